@@ -1,0 +1,374 @@
+#!/usr/bin/env python
+"""Dual-AR frames/s of the sm_100a path (and of the reference's CPU path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Workload: BASELINE config 2 (C2), the full-size S2-Pro-shaped f16 Dual-AR
+(36 Slow-AR layers, 4 Fast-AR layers, d 2560, vocab 155,776, 10 codebooks x
+4096), random-init weights written as a seeded synthetic GGUF, 512-token
+seeded prompt, greedy decode of 256 frames at batch 1.
+
+One step = one generate_codes call (prefill + 256 frames).  Reported:
+  value      frames/s of the decode loop, device time (CUDA events on the
+             library's stream around the frame graphs), weights and prompt
+             already resident; whole-job = all ranks' frames / max rank time.
+  e2e        frames/s through the C ABI with host buffers: prompt upload,
+             prefill, every frame, codes download, wall clock bracketed by
+             barrier + device synchronize, max over ranks.
+  roofline   the dominant kernel (the fused RMSNorm + w1/w3 + SwiGLU GEMV)
+             timed live on resident weights; achieved = algorithmic bytes per
+             launch / mean launch time, against MEASURED_PEAKS.json.
+  cpu_baseline  the CPU oracle (port of the reference's algorithm) on a
+             bounded sample of the same workload, rank 0, N = 1 only.
+Multi-GPU: every rank decodes its own utterance (independent replicas,
+weak scaling); the only collectives are the barrier and the max of the
+timings.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from fish_s2pro_b200 import configs  # noqa: E402
+
+METRIC = "Dual-AR frames/sec (batch 1)"
+UNIT = "frames/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="C2")
+    ap.add_argument("--frames", type=int, default=None, help="override frames per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model-dir", default=None, help="GGUF cache (default: synth.default_model_dir())")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def device_sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(f"/tmp/s2d_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        self.path.unlink(missing_ok=True)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        load = [s for s, p in zip(sm, power) if p > 300] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power)}
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle timing (port of the reference's algorithm)
+# ---------------------------------------------------------------------------
+
+def oracle_frames(model_path, wl, frames: int, warmup: int, prompt_len: int, seed: int = 0):
+    """The reference's generate_codes loop (generate.rs:117-221) on the CPU
+    oracle in reference-faithful mode (per-step f32 weight re-expansion,
+    per-codebook Fast-AR prefix recomputation, full-vocabulary LM head and
+    sort).  Returns (seconds per timed frame, threads, prefill seconds)."""
+    from oracle import oracle as o
+    m = wl.model
+    om = o.OracleModel(model_path, max_seq_len=prompt_len + frames + warmup + 4, mode=1)
+    gp = wl.gen_params(greedy=True)
+    prompt = wl.prompt()[:, :prompt_len]
+    flat = prompt.T.reshape(-1).astype(np.int32)
+    bias = o.build_semantic_bias(m.vocab, m.sem_begin, m.sem_end, gp["im_end_id"])
+    rng = o.SeededRng(seed)
+    t0 = time.perf_counter()
+    hidden, logits = om.eval(flat)
+    t_prefill = time.perf_counter() - t0
+    main = o.sample_token(o.apply_semantic_bias(logits, bias, True, gp["im_end_id"]),
+                          gp["temperature"], gp["top_p"], gp["top_k"], None, rng)
+    times = []
+    for f in range(warmup + frames):
+        t = time.perf_counter()
+        sem = main - m.sem_begin if m.sem_begin <= main <= m.sem_end else 0
+        cbs = om.generate_codebooks(hidden, sem, gp["temperature"], gp["top_p"], gp["top_k"], rng)
+        step = [main] + (cbs if m.sem_begin <= main <= m.sem_end else [0] * m.num_codebooks)
+        hidden, logits = om.eval(step)
+        main = o.sample_token(o.apply_semantic_bias(logits, bias, True, gp["im_end_id"]),
+                              gp["temperature"], gp["top_p"], gp["top_k"], None, rng)
+        if f >= warmup:
+            times.append(time.perf_counter() - t)
+    om.close()
+    return sum(times) / len(times), o.get_threads(), t_prefill
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+def ensure_model(d: Dist, wl, model_dir) -> Path:
+    from fish_s2pro_b200 import synth
+    if d.rank == 0 or d.local == 0:
+        path = synth.cached_gguf(wl.model, model_dir)
+    d.barrier()
+    path = synth.cached_gguf(wl.model, model_dir)
+    return path
+
+
+def run_ours(args, d: Dist):
+    from fish_s2pro_b200 import (FastArWeights, GenerateParams, PromptTensor, SeededRng,
+                                 SlowArState, build, generate_codes)
+    build.build_runtime()
+    wl = configs.WORKLOADS[args.workload]
+    frames = args.frames or wl.frames
+    m = wl.model
+    path = ensure_model(d, wl, args.model_dir)
+    st = SlowArState.open(path, max_seq_len=wl.prompt_len + frames + 8, device=d.local)
+    spec = st.graph_spec()
+    fw = FastArWeights.from_state(st)
+    prompt = configs.Workload(m, wl.prompt_len, frames, wl.prompt_seed + d.rank,
+                              wl.im_end_id).prompt()
+    gp = wl.gen_params(greedy=True)
+    gp["max_new_tokens"] = frames
+    gp["min_tokens_before_end"] = 2 * frames + 2
+    params = GenerateParams(frames, gp["temperature"], gp["top_p"], gp["top_k"],
+                            gp["min_tokens_before_end"])
+    pt = PromptTensor(prompt.shape[0], prompt.shape[1], prompt.reshape(-1))
+
+    def one(seed):
+        return generate_codes(st, gp["im_end_id"], spec, pt, params, fw, SeededRng(seed))
+
+    for i in range(args.warmup):
+        one(i)
+    # dominant kernel, timed live on the resident weights
+    kern = {}
+    for name in ("w13", "wqkv", "wo", "w2", "lm_head"):
+        ms, nb = st.profile_kernel(name, iters=144)
+        kern[name] = {"ms": ms, "bytes": nb, "gbs": nb / ms / 1e6}
+    clocks = Clocks(d.local)
+    d.barrier()
+    device_sync()
+    clocks.start()
+    t0 = time.perf_counter()
+    results = [one(100 + i) for i in range(args.steps)]
+    device_sync()
+    t1 = time.perf_counter()
+    d.barrier()
+    ck = clocks.stop()
+    wall = d.max(t1 - t0)
+    decode_s = d.max(sum(r.profile.decode_ms for r in results) / 1e3)
+    prefill_ms = d.max(statistics.mean(r.profile.prefill_ms for r in results))
+    my_frames = sum(r.n_frames for r in results)
+    frames_total = d.sum(my_frames)
+    launches = sum(r.profile.prefill_kernels + r.profile.kernels_per_frame *
+                   r.profile.frame_launches for r in results)
+    value = frames_total / decode_s
+    e2e = frames_total / wall
+    pk = peaks()
+    top = kern["w13"]
+    bpf = configs.weight_bytes_per_frame(m)
+    p_avg = wl.prompt_len + frames / 2
+    frame_bytes = sum(bpf.values()) + configs.kv_bytes_per_position(m) * p_avg
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": d.world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(wall / args.steps * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded random-init S2-Pro-shaped GGUF, seeded 512-id prompt)",
+        "config": {"workload": f"{args.workload}: full-size f16 S2-Pro-shaped Dual-AR, "
+                               f"{wl.prompt_len}-token prompt, greedy {frames} frames, batch 1",
+                   "global_batch": d.world, "seq_len": wl.prompt_len + frames,
+                   "parallelism": f"replicas x{d.world} (independent utterances)",
+                   "l2": "inputs larger than L2 (each frame streams ~14.8 GB of weights)"},
+        "e2e": {"value": round(e2e, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(prompt.nbytes),
+                "d2h_bytes_per_step": int(m.num_codebooks * frames * 4 + 40)},
+        "gpu_launches": int(launches),
+        "prefill_ms": round(prefill_ms, 2),
+        "frame_bytes": int(frame_bytes),
+        "frame_gbs": round(frame_bytes * value / d.world / 1e9, 1),
+        "frame_roofline_frac": round(frame_bytes * value / d.world / 1e9 / pk["hbm_gbs"], 3),
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<1,EPI_SWIGLU_SLOW> (ffn_norm+w1/w3+SwiGLU)",
+                     "achieved": round(top["gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(top["gbs"] / pk["hbm_gbs"], 3), "traffic": None,
+                     "peak_source": pk["source"],
+                     "bytes_per_launch": int(top["bytes"]),
+                     "kernels": {k: {"us": round(v["ms"] * 1e3, 2), "gbs": round(v["gbs"], 1)}
+                                 for k, v in kern.items()}},
+        "clocks": ck,
+    }
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        spf, cores, _ = oracle_frames(path, wl, frames=2, warmup=0, prompt_len=16)
+        line["cpu_baseline"] = {
+            "value": round(1.0 / spf, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": "2 decode frames after a 16-token prefill of the same C2 model, "
+                      "reference-faithful CPU oracle (f32 re-expansion per step, Fast-AR "
+                      "prefix recomputation, full-vocab LM head and sort)"}
+    st.close()
+    return line
+
+
+def run_reference(args, d: Dist):
+    """The reference's CPU implementation (oracle port, reference-faithful),
+    rank 0 only, on the same workload: each step is one decode frame after a
+    short prefill."""
+    wl = configs.WORKLOADS[args.workload]
+    if d.rank != 0:
+        return None
+    path = ensure_model(d, wl, args.model_dir)
+    prompt_len = 16
+    spf, cores, t_prefill = oracle_frames(path, wl, frames=max(args.steps, 1),
+                                          warmup=args.warmup, prompt_len=prompt_len)
+    v = round(1.0 / spf, 4)
+    return {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": d.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(spf * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random-init S2-Pro-shaped GGUF)",
+        "config": {"workload": f"{args.workload}: full-size f16 S2-Pro-shaped Dual-AR, greedy, "
+                               f"batch 1 (CPU sample: {prompt_len}-token prompt)",
+                   "global_batch": 1, "seq_len": prompt_len + args.steps + args.warmup,
+                   "parallelism": "host threads"},
+        "impl": "reference",
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} timed decode frames after {args.warmup} "
+                                   f"warm-up frames and a {prompt_len}-token prefill "
+                                   f"({t_prefill:.1f} s), reference-faithful CPU oracle"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+class _Single:
+    rank = 0
+    local = 0
+
+    def barrier(self):
+        pass
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        line = run_reference(args, _Single())
+        print(json.dumps(line), flush=True)
+        return 0
+    d = Dist(args.gpus)
+    try:
+        line = run_ours(args, d)
+        if d.rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        d.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

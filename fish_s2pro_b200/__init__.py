@@ -1,0 +1,30 @@
+"""fish_s2pro_b200 -- sm_100a Dual-AR token loop for fish-s2pro.
+
+The product is libs2d.so (C ABI: include/s2d.h).  This package holds its
+sources (csrc/), the in-tree build (build.py), the Python mirror of the
+reference's `rust-pure` interface (s2d.py), the workload configurations
+(configs.py) and the seeded synthetic GGUF writer (synth.py).
+"""
+from .s2d import (  # noqa: F401
+    LOGITS_ALLOWED,
+    LOGITS_FULL,
+    LOGITS_NONE,
+    CudaMatmulBackend,
+    DecodeProfile,
+    FastArWeights,
+    GenerateCodesResult,
+    GenerateParams,
+    GraphSpec,
+    PromptTensor,
+    S2dError,
+    SamplerParams,
+    SeededRng,
+    SlowArState,
+    SlowArStepResult,
+    forward_codebook_prefix,
+    generate_codebooks_for_semantic,
+    generate_codes,
+    lib,
+    sample_token,
+    transpose_to_time_major,
+)

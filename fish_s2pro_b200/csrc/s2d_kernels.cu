@@ -1,0 +1,914 @@
+// s2d_kernels.cu -- sm_100a kernels of the Dual-AR decode step.
+//
+// Each kernel replaces one or more functions of the reference's CPU path
+// (crate fish_s2_infer, paths relative to the reference repository root);
+// the mapping is given above each kernel.  Batch-1 decode is HBM-bound, so
+// the kernels are organised around streaming every weight byte exactly once
+// per pass with 16-byte coalesced loads, with the small activation vectors
+// staged in shared memory and everything elementwise fused into the
+// producing GEMV.
+#include <math.h>
+
+#include "s2d_common.cuh"
+#include "s2d_kernels.cuh"
+
+namespace s2d {
+
+// ---------------------------------------------------------------------------
+// GEMV: y = W . rmsnorm(x)  (+ residual | SwiGLU)
+//
+// Replaces CpuMatmulBackend::linear (backend.rs:55-73) for every linear of a
+// layer, matvec_f16_streaming (tensor.rs:220-264) for the tied LM head, and
+// fuses the neighbouring elementwise ops of the layer:
+//   prologue: rms_norm_f32 (backend.rs:84-102) of the input vector;
+//   EPI_RESID: the residual adds (slow_ar.rs:697-701, 839-843);
+//   EPI_SWIGLU_*: w1 and w3 in one pass plus swiglu_split
+//                 (slow_ar.rs:1215-1232 / fast_ar.rs:472-485).
+// One warp owns one output row at a time; lanes stride the row in 16-byte
+// chunks.  The activation vector is staged in shared memory in a layout where
+// chunk c's low and high halves are stored in separate planes, so the 32
+// lanes' float4 reads of a warp hit 32 distinct banks.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int gemv_row(const GemvArgs &a, int row) {
+    if (a.n_contig < 0) return row;
+    return row < a.n_contig ? a.row_base + row : a.extra_row;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+template <int M, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
+    constexpr int NW = kGemvThreads / kWarp;
+    constexpr bool DUAL = EPI == EPI_SWIGLU_SLOW || EPI == EPI_SWIGLU_FAST;
+    constexpr int U = (DUAL || M > 2) ? 4 : 8;
+    extern __shared__ float4 xs4[];
+    __shared__ float red[M][NW];
+    __shared__ float scl[M];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = a.K, N = a.N, nchunk = K >> 3;
+    const int gw = blockIdx.x * NW + warp, stride = gridDim.x * NW;
+
+    // Weights do not depend on the previous kernel: start pulling this warp's
+    // rows into L2 before waiting for the predecessor's activations.
+    if (lane == 0) {
+        for (int row = gw; row < N; row += stride) {
+            prefetch_l2(a.W + (size_t)gemv_row(a, row) * K, (uint32_t)K * 2u);
+            if (DUAL) prefetch_l2(a.W2 + (size_t)row * K, (uint32_t)K * 2u);
+        }
+    }
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.done && *a.done) return;
+
+    float *xs = reinterpret_cast<float *>(xs4);
+    if (a.norm_w) {
+        float ss[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) ss[m] = 0.f;
+        for (int i = tid; i < K; i += kGemvThreads) {
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                float v = a.x[(size_t)m * a.ldx + i];
+                ss[m] = fmaf(v, v, ss[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float s = warp_sum(ss[m]);
+            if (lane == 0) red[m][warp] = s;
+        }
+        __syncthreads();
+        if (tid < M) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) t += red[tid][w];
+            scl[tid] = 1.0f / sqrtf(t / (float)K + a.eps);
+        }
+        __syncthreads();
+    }
+    for (int i = tid; i < K; i += kGemvThreads) {
+        const int c = i >> 3, k = i & 7;
+        const int idx = (((k >> 2) * nchunk) + c) * 4 + (k & 3);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float v = a.x[(size_t)m * a.ldx + i];
+            if (a.norm_w) v = __fmul_rn(__fmul_rn(v, scl[m]), a.norm_w[i]);
+            xs[m * 2 * nchunk * 4 + idx] = v;
+            if (a.x_out && blockIdx.x == 0) a.x_out[(size_t)m * K + i] = v;
+        }
+    }
+    __syncthreads();
+
+    for (int row = gw; row < N; row += stride) {
+        const uint4 *w = reinterpret_cast<const uint4 *>(a.W + (size_t)gemv_row(a, row) * K);
+        const uint4 *w2 = DUAL ? reinterpret_cast<const uint4 *>(a.W2 + (size_t)row * K) : nullptr;
+        float acc[M], acc2[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[m] = 0.f, acc2[m] = 0.f;
+        for (int c0 = lane; c0 < nchunk; c0 += 32 * U) {
+            uint4 wv[U], wv2[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < nchunk) {
+                    wv[u] = ld_stream_u4(w + c);
+                    if (DUAL) wv2[u] = ld_stream_u4(w2 + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + 32 * u;
+                if (c < nchunk) {
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        const float4 xa = xs4[m * 2 * nchunk + c];
+                        const float4 xb = xs4[m * 2 * nchunk + nchunk + c];
+                        acc[m] = dot8(wv[u], xa, xb, acc[m]);
+                        if (DUAL) acc2[m] = dot8(wv2[u], xa, xb, acc2[m]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            acc[m] = warp_sum(acc[m]);
+            if (DUAL) acc2[m] = warp_sum(acc2[m]);
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            if (lane != m) continue;
+            float out;
+            if (EPI == EPI_STORE) {
+                out = acc[m];
+            } else if (EPI == EPI_RESID) {
+                out = __fadd_rn(a.resid[(size_t)m * a.ldr + row], acc[m]);
+            } else if (EPI == EPI_SWIGLU_SLOW) {
+                const float g = acc[m], up = acc2[m];
+                const float sig = 1.0f / (1.0f + expf(-g));
+                out = __fmul_rn(__fmul_rn(g, sig), up);
+            } else {
+                const float g = acc[m], up = acc2[m];
+                out = __fmul_rn(g / (1.0f + expf(-g)), up);
+            }
+            a.y[(size_t)m * a.ldy + row] = out;
+        }
+    }
+}
+
+template <int M, int EPI>
+static cudaError_t gemv_launch_t(const GemvArgs &a, cudaStream_t s, bool pdl) {
+    const int NW = kGemvThreads / kWarp;
+    int blocks = (a.N + NW - 1) / NW;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    const size_t smem = (size_t)M * a.K * sizeof(float);
+    return s2d_launch(gemv_kernel<M, EPI>, dim3(blocks), dim3(kGemvThreads), smem, s, pdl, a);
+}
+
+template <int M>
+static cudaError_t gemv_dispatch_epi(const GemvArgs &a, int epi, cudaStream_t s, bool pdl) {
+    switch (epi) {
+    case EPI_STORE: return gemv_launch_t<M, EPI_STORE>(a, s, pdl);
+    case EPI_RESID: return gemv_launch_t<M, EPI_RESID>(a, s, pdl);
+    case EPI_SWIGLU_SLOW: return gemv_launch_t<M, EPI_SWIGLU_SLOW>(a, s, pdl);
+    case EPI_SWIGLU_FAST: return gemv_launch_t<M, EPI_SWIGLU_FAST>(a, s, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv(const GemvArgs &a, int M, int epi, cudaStream_t s, bool pdl) {
+    if (a.K % 8 != 0 || a.K <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+    if ((size_t)M * a.K * sizeof(float) > 200 * 1024) return cudaErrorInvalidValue;
+    switch (M) {
+    case 1: return gemv_dispatch_epi<1>(a, epi, s, pdl);
+    case 2: return gemv_dispatch_epi<2>(a, epi, s, pdl);
+    case 4: return gemv_dispatch_epi<4>(a, epi, s, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int M>
+static cudaError_t gemv_cfg_m() {
+    cudaError_t e;
+    const int bytes = 200 * 1024;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<M, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<M, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    if ((e = cudaFuncSetAttribute(gemv_kernel<M, EPI_SWIGLU_SLOW>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes))) return e;
+    return cudaFuncSetAttribute(gemv_kernel<M, EPI_SWIGLU_FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+static cudaError_t sample_configure();
+
+cudaError_t configure_kernels() {
+    cudaError_t e;
+    if ((e = gemv_cfg_m<1>())) return e;
+    if ((e = gemv_cfg_m<2>())) return e;
+    if ((e = gemv_cfg_m<4>())) return e;
+    return sample_configure();
+}
+
+// ---------------------------------------------------------------------------
+// QK-norm + RoPE + KV write.
+// Replaces, per token: the Q/K/V split (slow_ar.rs:743-746), rms_norm_heads
+// of Q and K (backend.rs:104-121; Slow-AR only, slow_ar.rs:748-763),
+// apply_rope_normal (attention.rs:172-206) and SlowArKvCache::write_token
+// (attention.rs:56-76).  One warp per head; the head's elements stay in
+// registers.  RoPE angles use the host-computed powf table so the rotation
+// matches the reference's theta = pos / base^(pair/hd) to the last bit of
+// the denominator; products are rounded separately as in the reference.
+// ---------------------------------------------------------------------------
+
+template <typename KV>
+__device__ __forceinline__ KV to_kv(float v);
+template <>
+__device__ __forceinline__ __half to_kv<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float to_kv<float>(float v) { return v; }
+__device__ __forceinline__ float from_kv(__half v) { return __half2float(v); }
+__device__ __forceinline__ float from_kv(float v) { return v; }
+
+template <typename KV, int EPL>
+__global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.done && *a.done) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int head = blockIdx.x * (blockDim.x >> 5) + warp;
+    const int m = blockIdx.y;
+    if (head >= a.H + a.Hkv) return;
+    const int pos = a.pos_const + (a.pos_dev ? *a.pos_dev : 0) + m;
+    const int hd = a.hd;
+    const float *row = a.qkv + (size_t)m * a.ld_qkv;
+    const bool is_q = head < a.H;
+    const int h = is_q ? head : head - a.H;
+    const float *src = is_q ? row + h * hd : row + (a.H + h) * hd;
+    float v[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = src[lane * EPL + e];
+    const float *nw = is_q ? a.q_norm : a.k_norm;
+    if (nw) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
+        ss = warp_sum(ss);
+        const float scale = 1.0f / sqrtf(ss / (float)hd + a.eps);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], scale), nw[lane * EPL + e]);
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+        const int pair = lane * EPL + e;
+        const float theta = (float)pos / a.rope_denom[pair >> 1];
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const float x0 = v[e], x1 = v[e + 1];
+        v[e] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        v[e + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+    }
+    if (is_q) {
+        float *dst = a.q_out + (size_t)m * a.H * hd + h * hd + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e] = v[e];
+        return;
+    }
+    if (pos < 0 || pos >= a.max_seq) {
+        if (lane == 0 && a.error) atomicExch(a.error, 1);
+        return;
+    }
+    KV *kc = reinterpret_cast<KV *>(a.kcache) + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
+    KV *vc = reinterpret_cast<KV *>(a.vcache) + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
+    const float *vsrc = row + (a.H + a.Hkv + h) * hd + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        kc[e] = to_kv<KV>(v[e]);
+        vc[e] = to_kv<KV>(vsrc[e]);
+    }
+}
+
+template <typename KV>
+static cudaError_t rope_launch_t(const RopeArgs &a, cudaStream_t s, bool pdl) {
+    const int warps = 8;
+    dim3 grid((a.H + a.Hkv + warps - 1) / warps, a.M);
+    switch (a.hd / 32) {
+    case 2: return s2d_launch(rope_kv_kernel<KV, 2>, grid, dim3(warps * 32), 0, s, pdl, a);
+    case 4: return s2d_launch(rope_kv_kernel<KV, 4>, grid, dim3(warps * 32), 0, s, pdl, a);
+    case 8: return s2d_launch(rope_kv_kernel<KV, 8>, grid, dim3(warps * 32), 0, s, pdl, a);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_rope_kv(const RopeArgs &a, bool kv_half, cudaStream_t s, bool pdl) {
+    if (a.hd % 64 != 0 || a.hd > 256) return cudaErrorInvalidValue;
+    return kv_half ? rope_launch_t<__half>(a, s, pdl) : rope_launch_t<float>(a, s, pdl);
+}
+
+// ---------------------------------------------------------------------------
+// GQA decode attention, split over the sequence.
+// Replaces SlowArKvCache::decode_attention_with_backend (attention.rs:106-145)
+// + gqa_decode_attention / softmax_in_place (attention.rs:208-247, 296-309)
+// for one or more query tokens (prefill: each token sees its causal prefix,
+// slow_ar.rs:579-593).  Grid (split, kv head, token); one warp per query head
+// of the GQA group, so the group's K/V rows are read from HBM once and hit
+// L1 for the other heads.  Each split keeps an online softmax (max, sum,
+// weighted V) and writes it to scratch; the last split block to arrive (an
+// atomic counter per kv head and token) merges the partials and resets the
+// counter for the next launch.
+// ---------------------------------------------------------------------------
+
+template <typename KV, int EPL>
+__device__ __forceinline__ void load_kv(const KV *p, float *out);
+template <>
+__device__ __forceinline__ void load_kv<__half, 2>(const __half *p, float *o) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(p));
+    o[0] = f.x, o[1] = f.y;
+}
+template <>
+__device__ __forceinline__ void load_kv<__half, 4>(const __half *p, float *o) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    o[0] = f0.x, o[1] = f0.y, o[2] = f1.x, o[3] = f1.y;
+}
+template <>
+__device__ __forceinline__ void load_kv<__half, 8>(const __half *p, float *o) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        o[2 * i] = f.x, o[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load_kv<float, 2>(const float *p, float *o) {
+    const float2 f = *reinterpret_cast<const float2 *>(p);
+    o[0] = f.x, o[1] = f.y;
+}
+template <>
+__device__ __forceinline__ void load_kv<float, 4>(const float *p, float *o) {
+    const float4 f = *reinterpret_cast<const float4 *>(p);
+    o[0] = f.x, o[1] = f.y, o[2] = f.z, o[3] = f.w;
+}
+template <>
+__device__ __forceinline__ void load_kv<float, 8>(const float *p, float *o) {
+    const float4 f = *reinterpret_cast<const float4 *>(p);
+    const float4 g = *reinterpret_cast<const float4 *>(p + 4);
+    o[0] = f.x, o[1] = f.y, o[2] = f.z, o[3] = f.w, o[4] = g.x, o[5] = g.y, o[6] = g.z, o[7] = g.w;
+}
+
+template <typename KV, int EPL>
+__global__ void __launch_bounds__(512) attn_kernel(const AttnArgs a) {
+    __shared__ int s_last;
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.done && *a.done) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rep = blockDim.x >> 5;
+    const int sp = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+    const int h = kvh * rep + warp;
+    const int hd = a.hd, S = a.S;
+    const int pos = a.pos_const + (a.pos_dev ? *a.pos_dev : 0) + m;
+    int visible = pos + 1;
+    if (visible > a.max_seq) visible = a.max_seq;
+    const int chunk = (visible + S - 1) / S;
+    const int t0 = sp * chunk;
+    const int t1 = min(visible, t0 + chunk);
+    float q[EPL], acc[EPL];
+    const float *qp = a.q + (size_t)m * a.H * hd + h * hd + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) q[e] = qp[e], acc[e] = 0.f;
+    float mrun = -INFINITY, l = 0.f;
+    const KV *kb = reinterpret_cast<const KV *>(a.kcache) + (size_t)kvh * a.max_seq * hd + lane * EPL;
+    const KV *vb = reinterpret_cast<const KV *>(a.vcache) + (size_t)kvh * a.max_seq * hd + lane * EPL;
+    for (int t = t0; t < t1; ++t) {
+        float kf[EPL], vf[EPL];
+        load_kv<KV, EPL>(kb + (size_t)t * hd, kf);
+        load_kv<KV, EPL>(vb + (size_t)t * hd, vf);
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) d = fmaf(q[e], kf[e], d);
+        d = warp_sum(d);
+        const float sc = d * a.scale;
+        const float mn = fmaxf(mrun, sc);
+        const float corr = expf(mrun - mn);
+        const float p = expf(sc - mn);
+        l = fmaf(l, corr, p);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(acc[e], corr, p * vf[e]);
+        mrun = mn;
+    }
+    float *pp = a.part + (((size_t)m * a.H + h) * S + sp) * (hd + 2);
+    if (lane == 0) {
+        __stcg(pp, mrun);
+        __stcg(pp + 1, l);
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) __stcg(pp + 2 + lane * EPL + e, acc[e]);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&a.counters[m * a.Hkv + kvh], 1);
+        s_last = (prev == S - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float *base = a.part + ((size_t)m * a.H + h) * S * (hd + 2);
+    float gmax = -INFINITY;
+    for (int j = 0; j < S; ++j) gmax = fmaxf(gmax, __ldcg(base + (size_t)j * (hd + 2)));
+    float L = 0.f, o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = 0.f;
+    for (int j = 0; j < S; ++j) {
+        const float *pj = base + (size_t)j * (hd + 2);
+        const float f = expf(__ldcg(pj) - gmax);
+        L = fmaf(__ldcg(pj + 1), f, L);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] = fmaf(__ldcg(pj + 2 + lane * EPL + e), f, o[e]);
+    }
+    float *op = a.out + (size_t)m * a.H * hd + h * hd + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) op[e] = o[e] / L;
+    if (threadIdx.x == 0) a.counters[m * a.Hkv + kvh] = 0;
+}
+
+template <typename KV>
+static cudaError_t attn_launch_t(const AttnArgs &a, cudaStream_t s, bool pdl) {
+    const int rep = a.H / a.Hkv;
+    dim3 grid(a.S, a.Hkv, a.M);
+    switch (a.hd / 32) {
+    case 2: return s2d_launch(attn_kernel<KV, 2>, grid, dim3(rep * 32), 0, s, pdl, a);
+    case 4: return s2d_launch(attn_kernel<KV, 4>, grid, dim3(rep * 32), 0, s, pdl, a);
+    case 8: return s2d_launch(attn_kernel<KV, 8>, grid, dim3(rep * 32), 0, s, pdl, a);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_attention(const AttnArgs &a, bool kv_half, cudaStream_t s, bool pdl) {
+    if (a.Hkv <= 0 || a.H % a.Hkv || a.H / a.Hkv > 16 || a.hd % 64 || a.hd > 256 || a.S <= 0)
+        return cudaErrorInvalidValue;
+    return kv_half ? attn_launch_t<__half>(a, s, pdl) : attn_launch_t<float>(a, s, pdl);
+}
+
+// ---------------------------------------------------------------------------
+// Slow-AR input embedding.
+// Replaces build_step_input (generate.rs:300-344) and
+// embed_slow_ar_time_major (slow_ar.rs:1041-1133): semantic row plus, for a
+// semantic id, the codebook rows summed in codebook order, then scaled by
+// 1/sqrt(K+1).  The additions and the scaling are rounded exactly as the
+// reference does, so this kernel's output is bit-identical to it.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) embed_kernel(const EmbedArgs a) {
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.done && *a.done) return;
+    const int m = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.d) return;
+    const int cd = a.K + 1;
+    uint32_t main_id;
+    if (a.tokens) {
+        const int32_t t = a.tokens[(size_t)m * cd];
+        if (t < 0) {
+            if (i == 0) atomicExch(a.error, 2);
+            return;
+        }
+        main_id = (uint32_t)t;
+    } else {
+        main_id = a.st->main_token;
+    }
+    const bool is_sem = main_id >= a.sem_begin && main_id <= a.sem_end;
+    if (main_id >= (uint32_t)a.vocab) {
+        if (i == 0) atomicExch(a.error, 3);
+        return;
+    }
+    float h = h2f(a.emb[(size_t)main_id * a.d + i]);
+    if (is_sem) {
+        float sum = 0.f;
+        for (int cb = 0; cb < a.K; ++cb) {
+            const int32_t raw = a.tokens ? a.tokens[(size_t)m * cd + 1 + cb] : a.frame_codes[cb];
+            const int64_t cid = (int64_t)raw + (int64_t)cb * a.cb_size;
+            if (raw < 0 || cid >= a.cb_rows) {
+                if (i == 0) atomicExch(a.error, 4);
+                return;
+            }
+            sum = __fadd_rn(sum, h2f(a.cb_emb[(size_t)cid * a.d + i]));
+        }
+        h = __fadd_rn(h, sum);
+    }
+    if (a.scale_on) h = __fmul_rn(h, is_sem ? a.sem_scale : 1.0f);
+    a.out[(size_t)m * a.d + i] = h;
+}
+
+cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t s, bool pdl) {
+    dim3 grid((a.d + 255) / 256, a.M);
+    return s2d_launch(embed_kernel, grid, dim3(256), 0, s, pdl, a);
+}
+
+// ---------------------------------------------------------------------------
+// Fast-AR frame start: semantic_to_codebook_id (generate.rs:273-282) and the
+// first two positions of the Fast-AR sequence [slow_hidden, fast_emb[c0]]
+// (fast_ar.rs:393-403).  code 0 of the frame goes to the output codes
+// (generate.rs:176-191).
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) fast_init_kernel(const FastInitArgs a) {
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.st->done) return;
+    uint32_t code;
+    if (a.code_override) {
+        code = *a.code_override;
+    } else {
+        const uint32_t mt = a.st->main_token;
+        if (mt < a.sem_begin || mt > a.sem_end) code = 0;
+        else {
+            code = mt - a.sem_begin;
+            if (code >= (uint32_t)a.cb_size) code = (uint32_t)a.cb_size - 1;
+        }
+    }
+    if (code >= (uint32_t)a.cb_size) code = (uint32_t)a.cb_size - 1;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        a.frame_codes[0] = (int32_t)code;
+        if (a.codes_out) a.codes_out[a.st->step_index] = (int32_t)code;
+    }
+    if (i < a.d) {
+        a.fast_x[i] = a.slow_hidden[i];
+        a.fast_x[a.d + i] = h2f(a.fast_emb[(size_t)code * a.d + i]);
+    }
+}
+
+cudaError_t launch_fast_init(const FastInitArgs &a, cudaStream_t s, bool pdl) {
+    return s2d_launch(fast_init_kernel, dim3((a.d + 255) / 256), dim3(256), 0, s, pdl, a);
+}
+
+// ---------------------------------------------------------------------------
+// Device sampler: sample_token (sampling.rs:121-200) with apply_softmax
+// (:202-225), sample_discrete (:227-241) and the SeededRng LCG (:46-52), plus
+// the semantic masking of sample_semantic_token (generate.rs:284-298,
+// sampling.rs:76-100) and the loop bookkeeping of generate_codes
+// (generate.rs:165-211).
+//
+// Candidates are the unmasked rows only (the allowed semantic rows and
+// <|im_end|> for the Slow-AR head; every code for the Fast-AR head).  The
+// reference sorts the whole vocabulary; all other entries are -inf there, so
+// they sit after the finite entries in id order and carry zero probability.
+// The sampler reproduces the reference's item list exactly, including those
+// -inf entries when top-k/top-p reach them:
+//   greedy fast path: temperature 0, top_p <= 1 and a unique maximum (no
+//   other logit within 1e-6) -> the reference's draw always picks item 0;
+//   general path: one block bitonic-sorts (value desc, id asc) keys, which is
+//   the order of the reference's stable sort, then thread 0 runs the
+//   reference's sequential top-k / force-include / softmax / top-p /
+//   renormalise / draw steps with the same f32 sums.
+// Every call consumes exactly one RNG draw, like the reference.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t f2ord(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float rng_target(uint64_t *state) {
+    *state = *state * 6364136223846793005ull + 1ull;
+    const uint64_t mant = (*state >> 11) & ((1ull << 53) - 1ull);
+    const double draw = (double)mant / 9007199254740992.0;
+    float t = __double2float_rn(draw);
+    t = fminf(fmaxf(t, 0.0f), 1.0f - 1e-7f);
+    return t;
+}
+
+struct SampleShared {
+    float maxv;
+    int count;      // logits within 1e-6 of the max
+    int first_tie;  // candidate index of the (unique) maximum
+    int nfin;       // finite candidates
+    int kk;         // finite items inside top-k
+    int appended;   // force id appended after top-k
+    int nf;         // finite items in the list
+    int token;
+    int force_pos;
+    float force_v;
+    int general;
+};
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs a) {
+    extern __shared__ unsigned long long skeys[];  // [kSampleMax]
+    float *probs = reinterpret_cast<float *>(skeys + kSampleMax);  // [kSampleMax + 1]
+    __shared__ SampleShared sh;
+    __shared__ float rv[32];
+    __shared__ int ri[32], rj[32];
+    grid_dep_launch();
+    grid_dep_wait();
+    DevState *st = a.st;
+    if (a.mode != SAMPLE_PLAIN && st->done) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n = a.n;
+
+    bool block = false;
+    int64_t force = a.force_id;
+    int32_t new_npast = 0, new_step = 0;
+    if (a.mode == SAMPLE_SLOW_FIRST) {
+        block = 0u < a.min_tokens_before_end;
+        force = block ? -1 : (int64_t)a.im_end;
+    } else if (a.mode == SAMPLE_SLOW_STEP) {
+        new_npast = st->n_past + 1;
+        new_step = st->step_index + 1;
+        const uint32_t gen = (uint32_t)(new_npast - st->prompt_cols + new_step);
+        block = gen < a.min_tokens_before_end;
+        force = block ? -1 : (int64_t)a.im_end;
+    } else if (a.mode == SAMPLE_FAST) {
+        force = -1;
+    }
+    const bool slow = a.mode == SAMPLE_SLOW_FIRST || a.mode == SAMPLE_SLOW_STEP;
+    auto cid = [&](int r) -> uint32_t {
+        return a.n_contig < 0 ? (uint32_t)r : (r < a.n_contig ? a.id_base + (uint32_t)r : a.extra_id);
+    };
+    auto cval = [&](int r) -> float {
+        const float v = a.logits[r];
+        return (slow && block && cid(r) == a.im_end) ? -INFINITY : v;
+    };
+
+    // pass 1: max and finite count
+    float mx = -INFINITY;
+    int fin = 0;
+    for (int r = tid; r < n; r += kSampleThreads) {
+        const float v = cval(r);
+        mx = fmaxf(mx, v);
+        fin += v > -INFINITY;
+    }
+    mx = warp_max(mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) fin += __shfl_xor_sync(0xffffffffu, fin, o);
+    if (lane == 0) rv[warp] = mx, ri[warp] = fin;
+    __syncthreads();
+    if (tid == 0) {
+        float m2 = -INFINITY;
+        int f2 = 0;
+        for (int w = 0; w < kSampleThreads / 32; ++w) m2 = fmaxf(m2, rv[w]), f2 += ri[w];
+        sh.maxv = m2;
+        sh.nfin = f2;
+    }
+    __syncthreads();
+    // pass 2: entries within 1e-6 of the max
+    int cnt = 0, first = 0x7fffffff;
+    for (int r = tid; r < n; r += kSampleThreads) {
+        const float v = cval(r);
+        if (fabsf(v - sh.maxv) < 1e-6f) {
+            ++cnt;
+            first = min(first, r);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+        first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+    }
+    if (lane == 0) ri[warp] = cnt, rj[warp] = first;
+    __syncthreads();
+    const int64_t k_eff = a.top_k > 0 ? min((int64_t)a.top_k, a.vocab_full) : a.vocab_full;
+    if (tid == 0) {
+        int c2 = 0, f2 = 0x7fffffff;
+        for (int w = 0; w < kSampleThreads / 32; ++w) c2 += ri[w], f2 = min(f2, rj[w]);
+        sh.count = c2;
+        sh.first_tie = f2;
+        sh.general = !(a.temperature == 0.0f && a.top_p <= 1.0f && isfinite(sh.maxv) && c2 == 1 &&
+                       k_eff >= 1);
+        if (!sh.general) {
+            (void)rng_target(a.rng);
+            sh.token = (int)cid(f2);
+        }
+    }
+    __syncthreads();
+
+    if (sh.general) {
+        // bitonic sort of (value desc, id asc) keys
+        int np2 = 2;
+        while (np2 < n) np2 <<= 1;
+        for (int r = tid; r < np2; r += kSampleThreads) {
+            if (r < n) {
+                const float v = cval(r);
+                skeys[r] = ((unsigned long long)(~f2ord(v)) << 32) | cid(r);
+            } else {
+                skeys[r] = ~0ull;
+            }
+        }
+        __syncthreads();
+        for (int k = 2; k <= np2; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < np2; i += kSampleThreads) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long x = skeys[i], y = skeys[ixj];
+                        const bool up = (i & k) == 0;
+                        if ((x > y) == up) skeys[i] = y, skeys[ixj] = x;
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        // position of the force id among the sorted finite entries
+        if (tid == 0) sh.force_pos = 0x7fffffff, sh.force_v = -INFINITY;
+        __syncthreads();
+        if (force >= 0 && force < a.vocab_full) {
+            for (int r = tid; r < sh.nfin; r += kSampleThreads) {
+                if ((uint32_t)(skeys[r] & 0xffffffffu) == (uint32_t)force) {
+                    sh.force_pos = r;
+                    const uint32_t ord = ~(uint32_t)(skeys[r] >> 32);
+                    sh.force_v = __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
+                }
+            }
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const int64_t kk = min(k_eff, (int64_t)sh.nfin);
+            int appended = 0;
+            if (force >= 0 && sh.force_pos != 0x7fffffff && sh.force_v > -1e30f &&
+                (int64_t)sh.force_pos >= k_eff)
+                appended = 1;
+            sh.kk = (int)kk;
+            sh.appended = appended;
+            sh.nf = (int)kk + appended;
+        }
+        __syncthreads();
+        const int nf = sh.nf;
+        // item values and probabilities (apply_softmax), in parallel
+        const float top = nf > 0 ? sh.maxv : -INFINITY;
+        for (int i = tid; i < nf; i += kSampleThreads) {
+            float v;
+            if (i < sh.kk) {
+                const uint32_t ord = ~(uint32_t)(skeys[i] >> 32);
+                v = __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
+            } else {
+                v = sh.force_v;
+            }
+            probs[i] = a.temperature > 0.0f ? expf((v - top) / a.temperature)
+                                            : (fabsf(v - top) < 1e-6f ? 1.0f : 0.0f);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            const int64_t n_items = k_eff + sh.appended;
+            int64_t choice;
+            if (nf == 0) {
+                (void)rng_target(a.rng);
+                choice = n_items - 1;
+            } else {
+                float sum = 0.0f;
+                for (int i = 0; i < nf; ++i) sum += probs[i];
+                if (sum > 0.0f)
+                    for (int i = 0; i < nf; ++i) probs[i] /= sum;
+                const int64_t always_pos =
+                    force < 0 || sh.force_pos == 0x7fffffff || !(sh.force_v > -1e30f)
+                        ? -1
+                        : (sh.appended ? (int64_t)sh.kk : (int64_t)sh.force_pos);
+                int64_t p_idx = 0;
+                float cum = 0.0f;
+                bool broke = false;
+                for (int i = 0; i < nf; ++i) {
+                    cum += probs[i];
+                    p_idx = i + 1;
+                    if (cum >= a.top_p) {
+                        broke = true;
+                        break;
+                    }
+                }
+                if (!broke) p_idx = n_items;
+                if (p_idx == 0) p_idx = 1;
+                if (always_pos >= 0 && always_pos >= p_idx) p_idx = always_pos + 1;
+                const int lim = (int)min(p_idx, (int64_t)nf);
+                float sum_p = -0.0f;
+                for (int i = 0; i < lim; ++i) sum_p += probs[i];
+                if (sum_p > 0.0f)
+                    for (int i = 0; i < lim; ++i) probs[i] /= sum_p;
+                const float target = rng_target(a.rng);
+                choice = p_idx - 1;
+                float c2 = 0.0f;
+                for (int i = 0; i < lim; ++i) {
+                    c2 += probs[i];
+                    if (target < c2) {
+                        choice = i;
+                        break;
+                    }
+                }
+            }
+            if (choice < sh.kk) {
+                sh.token = (int)(uint32_t)(skeys[choice] & 0xffffffffu);
+            } else if (sh.appended && choice == sh.kk) {
+                sh.token = (int)force;
+            } else {
+                // the j-th -inf entry in id order: ids that are not finite candidates
+                const int64_t j = choice - sh.kk;
+                int64_t ans = j;
+                for (int it = 0; it < 64; ++it) {
+                    int64_t c = 0;
+                    for (int r = 0; r < sh.nfin; ++r)
+                        c += (int64_t)(uint32_t)(skeys[r] & 0xffffffffu) <= ans;
+                    if (j + c == ans) break;
+                    ans = j + c;
+                }
+                sh.token = (int)ans;
+            }
+        }
+        __syncthreads();
+    }
+
+    const uint32_t token = (uint32_t)sh.token;
+    if (tid == 0) {
+        if (a.out_token) *a.out_token = token;
+        if (a.mode == SAMPLE_SLOW_FIRST) {
+            st->main_token = token;
+            st->done = (token == a.im_end) || (a.max_new <= 0);
+        } else if (a.mode == SAMPLE_SLOW_STEP) {
+            st->n_past = new_npast;
+            st->step_index = new_step;
+            st->main_token = token;
+            st->done = (token == a.im_end) || (new_step >= a.max_new);
+        } else if (a.mode == SAMPLE_FAST) {
+            a.frame_codes[a.cb_index] = (int32_t)token;
+            if (a.codes_out) a.codes_out[(size_t)a.cb_index * a.max_new + st->step_index] = (int32_t)token;
+        }
+    }
+    if (a.mode == SAMPLE_FAST && a.fast_x_next) {
+        for (int i = tid; i < a.d; i += kSampleThreads)
+            a.fast_x_next[i] = h2f(a.fast_emb[(size_t)token * a.d + i]);
+    }
+}
+
+static constexpr size_t kSampleSmem =
+    kSampleMax * sizeof(unsigned long long) + (kSampleMax + 1) * sizeof(float);
+
+static cudaError_t sample_configure() {
+    return cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kSampleSmem);
+}
+
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl) {
+    if (a.n <= 0 || a.n > kSampleMax) return cudaErrorInvalidValue;
+    return s2d_launch(sample_kernel, dim3(1), dim3(kSampleThreads), kSampleSmem, s, pdl, a);
+}
+
+// ---------------------------------------------------------------------------
+// Small helpers: exact f16 expansion (tensor.rs:22-75), op-level head
+// RMSNorm (backend.rs:104-121), state initialisation.
+// ---------------------------------------------------------------------------
+
+__global__ void f16_to_f32_kernel(const uint16_t *src, float *dst, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = h2f(src[i]);
+}
+
+cudaError_t launch_f16_to_f32(const uint16_t *src, float *dst, int64_t n, cudaStream_t s) {
+    const int64_t want = (n + 255) / 256;
+    int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+    if (blocks < 1) blocks = 1;
+    f16_to_f32_kernel<<<blocks, 256, 0, s>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
+__global__ void rms_norm_heads_kernel(const float *x, const float *w, float *y, int hd, float eps) {
+    __shared__ float red[32];
+    const float *xh = x + (size_t)blockIdx.x * hd;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) ss = fmaf(xh[i], xh[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+        red[0] = 1.0f / sqrtf(t / (float)hd + eps);
+    }
+    __syncthreads();
+    const float scale = red[0];
+    for (int i = threadIdx.x; i < hd; i += blockDim.x)
+        y[(size_t)blockIdx.x * hd + i] = __fmul_rn(__fmul_rn(xh[i], scale), w[i]);
+}
+
+cudaError_t launch_rms_norm_heads(const float *x, const float *w, float *y, int64_t n, int hd,
+                                  float eps, cudaStream_t s) {
+    if (hd <= 0 || n % hd) return cudaErrorInvalidValue;
+    rms_norm_heads_kernel<<<(unsigned)(n / hd), 256, 0, s>>>(x, w, y, hd, eps);
+    return cudaGetLastError();
+}
+
+__global__ void set_state_kernel(DevState *st, int32_t n_past, int32_t prompt_cols, uint64_t rng) {
+    st->n_past = n_past;
+    st->step_index = 0;
+    st->done = 0;
+    st->main_token = 0;
+    st->rng = rng;
+    st->error = 0;
+    st->prompt_cols = prompt_cols;
+}
+
+cudaError_t launch_set_state(DevState *st, int32_t n_past, int32_t prompt_cols, uint64_t rng,
+                             cudaStream_t s) {
+    set_state_kernel<<<1, 1, 0, s>>>(st, n_past, prompt_cols, rng);
+    return cudaGetLastError();
+}
+
+}  // namespace s2d

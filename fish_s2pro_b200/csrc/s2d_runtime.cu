@@ -1,0 +1,1195 @@
+// s2d_runtime.cu -- handle, loader and C ABI of libs2d.so (include/s2d.h).
+//
+// The handle owns the HBM-resident weights (uploaded once at open), the
+// Slow-AR KV cache, the activation and scratch buffers, one CUDA stream, the
+// device-resident generation state and the captured frame graph.  The frame
+// graph is one full Dual-AR frame: Fast-AR codebooks 1..K-1 (9 sampled passes
+// over the 4 Fast-AR layers), the embedding-sum feedback, the 36-layer
+// Slow-AR step, the masked LM head and the semantic sampler; it is replayed
+// once per frame without any host round-trip.
+#include <cuda_fp16.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/s2d.h"
+#include "s2d_gguf.h"
+#include "s2d_kernels.cuh"
+
+using namespace s2d;
+
+namespace {
+
+constexpr int kMaxM = 4;  // tokens per GEMV pass (prefill chunk)
+
+struct LayerDev {
+    const uint16_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr, *w3 = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+
+struct TensorDev {
+    const GgufTensor *info = nullptr;
+    uint8_t *dev = nullptr;
+};
+
+struct ArShape {
+    int L, d, F, H, Hkv, hd, ctx;
+    float rope_base, eps;
+    bool qk_norm;
+    int qs() const { return H * hd; }
+    int kvs() const { return Hkv * hd; }
+    int qkv_out() const { return qs() + 2 * kvs(); }
+};
+
+struct GenKey {
+    uint32_t max_new = 0, min_tokens = 0, im_end = 0;
+    float temperature = 0, top_p = 0;
+    int32_t top_k = 0;
+    bool operator==(const GenKey &o) const {
+        return max_new == o.max_new && min_tokens == o.min_tokens && im_end == o.im_end &&
+               temperature == o.temperature && top_p == o.top_p && top_k == o.top_k;
+    }
+};
+
+}  // namespace
+
+struct S2dHandle {
+    std::string err;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    S2dConfig cfg{};
+    S2dGraphSpec spec{};
+    ArShape slow{}, fast{};
+    Gguf gguf;
+    std::vector<TensorDev> tensors;  // parallel to gguf.tensors
+    uint8_t *arena = nullptr;
+    float *norm_arena = nullptr;
+    std::vector<LayerDev> slow_layers, fast_layers;
+    const uint16_t *emb = nullptr, *cb_emb = nullptr, *fast_emb = nullptr, *fast_out = nullptr;
+    float *norm = nullptr, *fast_norm = nullptr;
+    float *rope_slow = nullptr, *rope_fast = nullptr;
+    __half *kv_slow = nullptr;  // [L][2][Hkv][max_seq][hd]
+    float *kv_fast = nullptr;   // [Lf][2][Hkv][ctx][hd]
+    float *x = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
+    float *fast_x = nullptr, *hidden_post = nullptr, *logits = nullptr, *logits_fast = nullptr;
+    float *part = nullptr;
+    int32_t *counters = nullptr;
+    int S_slow = 16, S_fast = 1;
+    DevState *st = nullptr;
+    int32_t *tokens_dev = nullptr;
+    size_t tokens_cap = 0;
+    int32_t *frame_codes = nullptr, *codes_out = nullptr;
+    size_t codes_cap = 0;
+    uint32_t *tok_out = nullptr;
+    uint32_t *code_override = nullptr;
+    int n_allowed_extra = 1;
+    int32_t n_past = 0;
+    // captured frame
+    cudaGraphExec_t frame_exec = nullptr;
+    GenKey frame_key;
+    uint32_t frame_kernels = 0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
+    bool pdl = true;
+    uint32_t launches = 0;  // kernels enqueued through this handle
+};
+
+namespace {
+
+int32_t set_err(S2dHandle *h, int32_t code, const std::string &msg) {
+    if (h) h->err = msg;
+    return code;
+}
+
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess)                                                                \
+            return set_err(h, S2D_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// ---------------------------------------------------------------------------
+// loading
+// ---------------------------------------------------------------------------
+
+// DualArGraphSpec::from_gguf (registry.rs:45-103), shape-parametric: the slow
+// head_dim is the q_norm length (the reference forces QK_NORM_SIZE,
+// registry.rs:46-52) and the S2-Pro constants of registry.rs:109-213 are
+// replaced by metadata/tensor consistency checks in bind_weights().
+int32_t read_spec(S2dHandle *h) {
+    const Gguf &g = h->gguf;
+    std::string e, arch;
+    if (!g.meta_str("general.architecture", &arch, &e)) return set_err(h, S2D_EIO, "missing general.architecture");
+    if (arch != "fish-speech")
+        return set_err(h, S2D_EINVAL, "expected fish-speech transformer GGUF, got " + arch);
+    uint32_t u[20];
+    float f[4];
+    bool b[6];
+    bool ok = g.meta_bool("fish_speech.attention_qk_norm", &b[0], &e) &&
+              g.meta_u32("fish-speech.context_length", &u[0], &e) &&
+              g.meta_u32("fish-speech.embedding_length", &u[1], &e) &&
+              g.meta_u32("fish-speech.feed_forward_length", &u[2], &e) &&
+              g.meta_u32("fish-speech.block_count", &u[3], &e) &&
+              g.meta_u32("fish-speech.attention.head_count", &u[4], &e) &&
+              g.meta_u32("fish-speech.attention.head_count_kv", &u[5], &e) &&
+              g.meta_f32("fish-speech.rope.freq_base", &f[0], &e) &&
+              g.meta_f32("fish-speech.attention.layer_norm_rms_epsilon", &f[1], &e) &&
+              g.meta_u32("fish_speech.fast_context_length", &u[6], &e) &&
+              g.meta_u32("fish_speech.fast_embedding_length", &u[7], &e) &&
+              g.meta_u32("fish_speech.fast_feed_forward_length", &u[8], &e) &&
+              g.meta_u32("fish_speech.fast_block_count", &u[9], &e) &&
+              g.meta_u32("fish_speech.fast_head_count", &u[10], &e) &&
+              g.meta_u32("fish_speech.fast_head_count_kv", &u[11], &e) &&
+              g.meta_u32("fish_speech.fast_head_dim", &u[12], &e) &&
+              g.meta_f32("fish_speech.fast_rope_freq_base", &f[2], &e) &&
+              g.meta_f32("fish_speech.fast_layer_norm_rms_eps", &f[3], &e) &&
+              g.meta_bool("fish_speech.fast_attention_qk_norm", &b[1], &e) &&
+              g.meta_u32("fish_speech.codebook_size", &u[13], &e) &&
+              g.meta_u32("fish_speech.num_codebooks", &u[14], &e) &&
+              g.meta_u32("fish_speech.semantic_begin_id", &u[15], &e) &&
+              g.meta_u32("fish_speech.semantic_end_id", &u[16], &e) &&
+              g.meta_bool("fish_speech.scale_codebook_embeddings", &b[2], &e) &&
+              g.meta_bool("fish_speech.tie_word_embeddings", &b[3], &e) &&
+              g.meta_bool("fish_speech.fast_project_in", &b[4], &e);
+    if (!ok) return set_err(h, S2D_EIO, e);
+    if (b[4]) return set_err(h, S2D_EINVAL, "fast_project_in is not supported (fast_ar.rs:366-370)");
+    if (!b[2] || !b[3])
+        return set_err(h, S2D_EINVAL, "scale_codebook_embeddings and tie_word_embeddings must be true");
+    if (b[1]) return set_err(h, S2D_EINVAL, "fast.attention_qk_norm must be false");
+    S2dGraphSpec &s = h->spec;
+    s.context_length = (int)u[0];
+    s.hidden = (int)u[1];
+    s.ffn = (int)u[2];
+    s.slow_layers = (int)u[3];
+    s.heads = (int)u[4];
+    s.kv_heads = (int)u[5];
+    s.rope_base = f[0];
+    s.rms_eps = f[1];
+    s.fast_context_length = (int)u[6];
+    s.fast_ffn = (int)u[8];
+    s.fast_layers = (int)u[9];
+    s.fast_heads = (int)u[10];
+    s.fast_kv_heads = (int)u[11];
+    s.fast_head_dim = (int)u[12];
+    s.fast_rope_base = f[2];
+    s.fast_rms_eps = f[3];
+    s.codebook_size = (int)u[13];
+    s.num_codebooks = (int)u[14];
+    s.semantic_begin_id = (int)u[15];
+    s.semantic_end_id = (int)u[16];
+    if (u[7] != u[1])
+        return set_err(h, S2D_EINVAL, "slow hidden size mismatch: fast embedding_length != slow (fast_ar.rs:380-387)");
+    if (!b[0]) {
+        s.head_dim = s.heads ? s.hidden / s.heads : 0;
+    } else {
+        const GgufTensor *qn = g.tensor("layers.0.attention.q_norm.weight");
+        if (!qn || qn->dims.size() != 1) return set_err(h, S2D_EIO, "missing layers.0.attention.q_norm.weight");
+        s.head_dim = (int)qn->dims[0];
+    }
+    if (s.kv_heads <= 0 || s.heads % s.kv_heads || s.fast_kv_heads <= 0 || s.fast_heads % s.fast_kv_heads)
+        return set_err(h, S2D_EINVAL, "invalid GQA head split");
+    if (s.head_dim % 64 || s.head_dim > 256 || s.fast_head_dim % 64 || s.fast_head_dim > 256)
+        return set_err(h, S2D_EINVAL, "head_dim must be a multiple of 64 and <= 256");
+    if (s.heads / s.kv_heads > 16 || s.fast_heads / s.fast_kv_heads > 16)
+        return set_err(h, S2D_EINVAL, "GQA group larger than 16 heads");
+    if (s.num_codebooks < 1 || s.fast_context_length < s.num_codebooks)
+        return set_err(h, S2D_EINVAL, "fast_context_length must cover num_codebooks");
+    h->slow = ArShape{s.slow_layers, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim,
+                      s.context_length, s.rope_base, s.rms_eps, b[0]};
+    h->fast = ArShape{s.fast_layers, s.hidden, s.fast_ffn, s.fast_heads, s.fast_kv_heads,
+                      s.fast_head_dim, s.fast_context_length, s.fast_rope_base, s.fast_rms_eps, false};
+    return S2D_OK;
+}
+
+const GgufTensor *need(S2dHandle *h, const std::string &name, std::vector<uint64_t> dims, int *rc) {
+    const GgufTensor *t = h->gguf.tensor(name);
+    if (!t) {
+        *rc = set_err(h, S2D_EIO, "missing " + name);
+        return nullptr;
+    }
+    if (t->dims != dims) {
+        std::string want, got;
+        for (auto d : dims) want += std::to_string(d) + ",";
+        for (auto d : t->dims) got += std::to_string(d) + ",";
+        *rc = set_err(h, S2D_EINVAL, name + " dimensions mismatch: expected [" + want + "] got [" + got + "]");
+        return nullptr;
+    }
+    return t;
+}
+
+int32_t upload_all(S2dHandle *h) {
+    // one arena for every tensor, each 256-byte aligned
+    size_t total = 0;
+    for (const auto &t : h->gguf.tensors) total += align256((size_t)t.bytes);
+    CK(cudaMalloc(&h->arena, total ? total : 256));
+    const size_t CH = 64u << 20;
+    uint8_t *stage[2] = {nullptr, nullptr};
+    cudaEvent_t done_ev[2] = {nullptr, nullptr};
+    CK(cudaMallocHost(&stage[0], CH));
+    CK(cudaMallocHost(&stage[1], CH));
+    CK(cudaEventCreateWithFlags(&done_ev[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&done_ev[1], cudaEventDisableTiming));
+    h->tensors.resize(h->gguf.tensors.size());
+    size_t off = 0;
+    int slot = 0;
+    bool used[2] = {false, false};
+    for (size_t i = 0; i < h->gguf.tensors.size(); ++i) {
+        const GgufTensor &t = h->gguf.tensors[i];
+        h->tensors[i].info = &t;
+        h->tensors[i].dev = h->arena + off;
+        for (size_t b = 0; b < t.bytes; b += CH) {
+            const size_t n = std::min<size_t>(CH, (size_t)t.bytes - b);
+            if (used[slot]) CK(cudaEventSynchronize(done_ev[slot]));
+            memcpy(stage[slot], t.data + b, n);
+            CK(cudaMemcpyAsync(h->arena + off + b, stage[slot], n, cudaMemcpyHostToDevice, h->stream));
+            CK(cudaEventRecord(done_ev[slot], h->stream));
+            used[slot] = true;
+            slot ^= 1;
+        }
+        off += align256((size_t)t.bytes);
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    cudaFreeHost(stage[0]);
+    cudaFreeHost(stage[1]);
+    cudaEventDestroy(done_ev[0]);
+    cudaEventDestroy(done_ev[1]);
+    return S2D_OK;
+}
+
+TensorDev *tdev(S2dHandle *h, const GgufTensor *t) {
+    return &h->tensors[(size_t)(t - h->gguf.tensors.data())];
+}
+
+// TransformerTensorRegistry (registry.rs:346-496, 515-552, 625-650): bind and
+// validate every required tensor.  Linear weights must be F16 in this
+// version; norms F16 or F32.
+int32_t bind_weights(S2dHandle *h) {
+    int rc = S2D_OK;
+    const S2dGraphSpec &s = h->spec;
+    const uint64_t d = (uint64_t)s.hidden, K = (uint64_t)s.num_codebooks, cb = (uint64_t)s.codebook_size;
+    const GgufTensor *emb = h->gguf.tensor("embeddings.weight");
+    if (!emb || emb->dims.size() != 2 || emb->dims[0] != d)
+        return set_err(h, S2D_EINVAL, "embeddings.weight expected [hidden, vocab]");
+    s2d::GgufTensor const *ce = h->gguf.tensor("codebook_embeddings.weight");
+    if (!ce || ce->dims.size() != 2 || ce->dims[0] != d)
+        return set_err(h, S2D_EINVAL, "codebook_embeddings.weight shape mismatch");
+    h->spec.vocab_size = (int)emb->dims[1];
+    h->spec.codebook_rows = (int)ce->dims[1];
+    const GgufTensor *fe = need(h, "fast_embeddings.weight", {d, cb}, &rc);
+    const GgufTensor *fo = need(h, "fast_output.weight", {d, cb}, &rc);
+    const GgufTensor *nw = need(h, "norm.weight", {d}, &rc);
+    const GgufTensor *fnw = need(h, "fast_norm.weight", {d}, &rc);
+    if (rc) return rc;
+    if (emb->type != 1 || ce->type != 1 || fe->type != 1)
+        return set_err(h, S2D_EINVAL, "embedding tables must be F16");
+    if ((uint64_t)s.codebook_rows < K * cb)
+        return set_err(h, S2D_EINVAL, "codebook_embeddings.weight has fewer than num_codebooks*codebook_size rows");
+    if (s.semantic_end_id < s.semantic_begin_id || s.semantic_end_id >= s.vocab_size)
+        return set_err(h, S2D_EINVAL, "semantic id range outside the vocabulary");
+    if (s.semantic_end_id - s.semantic_begin_id + 1 > kSampleMax - 1)
+        return set_err(h, S2D_EINVAL, "semantic range larger than the device sampler supports");
+    if (s.codebook_size > kSampleMax) return set_err(h, S2D_EINVAL, "codebook_size larger than the device sampler supports");
+
+    // norms: expanded to f32 once
+    std::vector<std::pair<const GgufTensor *, float **>> norms;
+    h->slow_layers.resize((size_t)s.slow_layers);
+    h->fast_layers.resize((size_t)s.fast_layers);
+    uint32_t linear_type = 0;
+    auto linear = [&](const std::string &name, const ArShape &a, uint64_t in, uint64_t out) -> const uint16_t * {
+        const GgufTensor *t = need(h, name, {in, out}, &rc);
+        if (!t) return nullptr;
+        if (t->type != 1) {
+            rc = set_err(h, S2D_EINVAL, name + ": only F16 linear weights are supported by this build");
+            return nullptr;
+        }
+        linear_type = t->type;
+        (void)a;
+        return reinterpret_cast<const uint16_t *>(tdev(h, t)->dev);
+    };
+    for (int l = 0; l < s.slow_layers && !rc; ++l) {
+        const ArShape &a = h->slow;
+        const std::string p = "layers." + std::to_string(l) + ".";
+        LayerDev &L = h->slow_layers[(size_t)l];
+        L.wqkv = linear(p + "attention.wqkv.weight", a, d, (uint64_t)a.qkv_out());
+        L.wo = linear(p + "attention.wo.weight", a, (uint64_t)a.qs(), d);
+        L.w1 = linear(p + "feed_forward.w1.weight", a, d, (uint64_t)a.F);
+        L.w2 = linear(p + "feed_forward.w2.weight", a, (uint64_t)a.F, d);
+        L.w3 = linear(p + "feed_forward.w3.weight", a, d, (uint64_t)a.F);
+        const GgufTensor *an = need(h, p + "attention_norm.weight", {d}, &rc);
+        const GgufTensor *fn = need(h, p + "ffn_norm.weight", {d}, &rc);
+        const GgufTensor *qn = need(h, p + "attention.q_norm.weight", {(uint64_t)a.hd}, &rc);
+        const GgufTensor *kn = need(h, p + "attention.k_norm.weight", {(uint64_t)a.hd}, &rc);
+        if (rc) break;
+        norms.push_back({an, &L.attn_norm});
+        norms.push_back({fn, &L.ffn_norm});
+        norms.push_back({qn, &L.q_norm});
+        norms.push_back({kn, &L.k_norm});
+    }
+    for (int l = 0; l < s.fast_layers && !rc; ++l) {
+        const ArShape &a = h->fast;
+        const std::string p = "fast_layers." + std::to_string(l) + ".";
+        LayerDev &L = h->fast_layers[(size_t)l];
+        L.wqkv = linear(p + "attention.wqkv.weight", a, d, (uint64_t)a.qkv_out());
+        L.wo = linear(p + "attention.wo.weight", a, (uint64_t)a.qs(), d);
+        L.w1 = linear(p + "feed_forward.w1.weight", a, d, (uint64_t)a.F);
+        L.w2 = linear(p + "feed_forward.w2.weight", a, (uint64_t)a.F, d);
+        L.w3 = linear(p + "feed_forward.w3.weight", a, d, (uint64_t)a.F);
+        const GgufTensor *an = need(h, p + "attention_norm.weight", {d}, &rc);
+        const GgufTensor *fn = need(h, p + "ffn_norm.weight", {d}, &rc);
+        if (rc) break;
+        norms.push_back({an, &L.attn_norm});
+        norms.push_back({fn, &L.ffn_norm});
+    }
+    if (rc) return rc;
+    h->fast_out = reinterpret_cast<const uint16_t *>(tdev(h, fo)->dev);
+    if (fo->type != 1) return set_err(h, S2D_EINVAL, "fast_output.weight: only F16 is supported by this build");
+    norms.push_back({nw, &h->norm});
+    norms.push_back({fnw, &h->fast_norm});
+    h->emb = reinterpret_cast<const uint16_t *>(tdev(h, emb)->dev);
+    h->cb_emb = reinterpret_cast<const uint16_t *>(tdev(h, ce)->dev);
+    h->fast_emb = reinterpret_cast<const uint16_t *>(tdev(h, fe)->dev);
+    h->spec.linear_type = (int)linear_type;
+    size_t nfloats = 0;
+    for (auto &pr : norms) nfloats += (size_t)(pr.first->elements + 63) / 64 * 64;
+    CK(cudaMalloc(&h->norm_arena, nfloats * sizeof(float)));
+    size_t off = 0;
+    for (auto &pr : norms) {
+        const GgufTensor *t = pr.first;
+        float *dst = h->norm_arena + off;
+        if (t->type == 1) CK(launch_f16_to_f32(reinterpret_cast<const uint16_t *>(tdev(h, t)->dev), dst, (int64_t)t->elements, h->stream));
+        else if (t->type == 0) CK(cudaMemcpyAsync(dst, tdev(h, t)->dev, t->elements * 4, cudaMemcpyDeviceToDevice, h->stream));
+        else return set_err(h, S2D_EINVAL, t->name + ": norm weights must be F16 or F32");
+        *pr.second = dst;
+        off += (size_t)(t->elements + 63) / 64 * 64;
+    }
+    return S2D_OK;
+}
+
+int32_t alloc_buffers(S2dHandle *h) {
+    const S2dGraphSpec &s = h->spec;
+    const ArShape &a = h->slow, &f = h->fast;
+    const int maxseq = h->cfg.max_seq;
+    // RoPE denominators rope_base^(pair/hd), computed with the host libm powf
+    // exactly as apply_rope_normal does (attention.rs:196-197).
+    std::vector<float> rs((size_t)a.hd / 2), rf((size_t)f.hd / 2);
+    for (int p = 0; p < a.hd; p += 2) rs[(size_t)p / 2] = powf(a.rope_base, (float)p / (float)a.hd);
+    for (int p = 0; p < f.hd; p += 2) rf[(size_t)p / 2] = powf(f.rope_base, (float)p / (float)f.hd);
+    CK(cudaMalloc(&h->rope_slow, rs.size() * sizeof(float)));
+    CK(cudaMalloc(&h->rope_fast, rf.size() * sizeof(float)));
+    CK(cudaMemcpy(h->rope_slow, rs.data(), rs.size() * sizeof(float), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(h->rope_fast, rf.data(), rf.size() * sizeof(float), cudaMemcpyHostToDevice));
+    const size_t kv_slow = (size_t)a.L * 2 * a.Hkv * maxseq * a.hd;
+    CK(cudaMalloc(&h->kv_slow, kv_slow * sizeof(__half)));
+    CK(cudaMemset(h->kv_slow, 0, kv_slow * sizeof(__half)));
+    const size_t kv_fast = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
+    CK(cudaMalloc(&h->kv_fast, std::max<size_t>(kv_fast, 1) * sizeof(float)));
+    CK(cudaMemset(h->kv_fast, 0, std::max<size_t>(kv_fast, 1) * sizeof(float)));
+    const int d = s.hidden;
+    const int qkv_out = std::max(a.qkv_out(), f.qkv_out());
+    const int qs = std::max(a.qs(), f.qs());
+    const int F = std::max(a.F, f.F);
+    CK(cudaMalloc(&h->x, (size_t)kMaxM * d * sizeof(float)));
+    CK(cudaMalloc(&h->qkv, (size_t)kMaxM * qkv_out * sizeof(float)));
+    CK(cudaMalloc(&h->q, (size_t)kMaxM * qs * sizeof(float)));
+    CK(cudaMalloc(&h->att, (size_t)kMaxM * qs * sizeof(float)));
+    CK(cudaMalloc(&h->act, (size_t)kMaxM * F * sizeof(float)));
+    CK(cudaMalloc(&h->fast_x, (size_t)(f.ctx + 1) * d * sizeof(float)));
+    CK(cudaMalloc(&h->hidden_post, (size_t)d * sizeof(float)));
+    CK(cudaMalloc(&h->logits, (size_t)s.vocab_size * sizeof(float)));
+    CK(cudaMalloc(&h->logits_fast, (size_t)std::max(s.codebook_size, kSampleMax) * sizeof(float)));
+    // attention split count: ~64 positions per split at full context
+    h->S_slow = std::min(128, std::max(8, (maxseq + 63) / 64));
+    h->S_fast = 1;
+    const int H = std::max(a.H, f.H), hd = std::max(a.hd, f.hd), Hkv = std::max(a.Hkv, f.Hkv);
+    CK(cudaMalloc(&h->part, (size_t)kMaxM * H * h->S_slow * (hd + 2) * sizeof(float)));
+    CK(cudaMalloc(&h->counters, (size_t)kMaxM * Hkv * sizeof(int32_t)));
+    CK(cudaMemset(h->counters, 0, (size_t)kMaxM * Hkv * sizeof(int32_t)));
+    CK(cudaMalloc(&h->st, sizeof(DevState)));
+    CK(cudaMemset(h->st, 0, sizeof(DevState)));
+    CK(cudaMalloc(&h->frame_codes, (size_t)std::max(s.num_codebooks, 1) * sizeof(int32_t)));
+    CK(cudaMalloc(&h->tok_out, sizeof(uint32_t)));
+    CK(cudaMalloc(&h->code_override, sizeof(uint32_t)));
+    return S2D_OK;
+}
+
+int32_t ensure_tokens(S2dHandle *h, size_t n) {
+    if (n <= h->tokens_cap) return S2D_OK;
+    if (h->tokens_dev) cudaFree(h->tokens_dev);
+    h->tokens_dev = nullptr;
+    h->tokens_cap = 0;
+    CK(cudaMalloc(&h->tokens_dev, n * sizeof(int32_t)));
+    h->tokens_cap = n;
+    return S2D_OK;
+}
+
+// ---------------------------------------------------------------------------
+// layer sequences
+// ---------------------------------------------------------------------------
+
+// One transformer layer over M consecutive tokens at rows x[0..M) of width d:
+// SlowArLayerSkeleton::forward_decode_token_with_backend +
+// forward_feed_forward_with_backend (slow_ar.rs:637-710) for the Slow-AR,
+// FastArLayerSkeleton::forward_prefill for the Fast-AR (fast_ar.rs:245-352).
+cudaError_t enqueue_layer(S2dHandle *h, bool is_fast, int l, float *x, int M,
+                          const int32_t *pos_dev, int pos_const, const int32_t *done) {
+    const ArShape &a = is_fast ? h->fast : h->slow;
+    const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
+    const int d = a.d;
+    cudaError_t e;
+    GemvArgs g{};
+    g.done = done;
+    g.n_contig = -1;
+    // attention_norm + WQKV
+    g.W = L.wqkv, g.x = x, g.ldx = d, g.norm_w = L.attn_norm, g.eps = a.eps;
+    g.y = h->qkv, g.ldy = a.qkv_out(), g.K = d, g.N = a.qkv_out();
+    if ((e = launch_gemv(g, M, EPI_STORE, h->stream, h->pdl))) return e;
+    // QK-norm + RoPE + KV write
+    RopeArgs r{};
+    r.qkv = h->qkv, r.ld_qkv = a.qkv_out(), r.q_out = h->q;
+    if (is_fast) {
+        float *base = h->kv_fast + (size_t)l * 2 * a.Hkv * a.ctx * a.hd;
+        r.kcache = base, r.vcache = base + (size_t)a.Hkv * a.ctx * a.hd, r.max_seq = a.ctx;
+        r.rope_denom = h->rope_fast;
+    } else {
+        __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
+        r.kcache = base, r.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd, r.max_seq = h->cfg.max_seq;
+        r.q_norm = L.q_norm, r.k_norm = L.k_norm, r.rope_denom = h->rope_slow;
+    }
+    r.eps = a.eps, r.pos_dev = pos_dev, r.pos_const = pos_const;
+    r.H = a.H, r.Hkv = a.Hkv, r.hd = a.hd, r.M = M, r.done = done, r.error = &h->st->error;
+    if ((e = launch_rope_kv(r, !is_fast, h->stream, h->pdl))) return e;
+    // GQA attention
+    AttnArgs t{};
+    t.q = h->q, t.kcache = r.kcache, t.vcache = r.vcache, t.max_seq = r.max_seq, t.out = h->att;
+    t.part = h->part, t.counters = h->counters, t.pos_dev = pos_dev, t.pos_const = pos_const;
+    t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd, t.S = is_fast ? h->S_fast : h->S_slow, t.M = M;
+    t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
+    t.done = done;
+    if ((e = launch_attention(t, !is_fast, h->stream, h->pdl))) return e;
+    // wo + residual
+    g = GemvArgs{};
+    g.done = done, g.n_contig = -1;
+    g.W = L.wo, g.x = h->att, g.ldx = a.qs(), g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
+    g.K = a.qs(), g.N = d;
+    if ((e = launch_gemv(g, M, EPI_RESID, h->stream, h->pdl))) return e;
+    // ffn_norm + w1/w3 + SwiGLU
+    g = GemvArgs{};
+    g.done = done, g.n_contig = -1;
+    g.W = L.w1, g.W2 = L.w3, g.x = x, g.ldx = d, g.norm_w = L.ffn_norm, g.eps = a.eps;
+    g.y = h->act, g.ldy = a.F, g.K = d, g.N = a.F;
+    if ((e = launch_gemv(g, M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, h->stream, h->pdl))) return e;
+    // w2 + residual
+    g = GemvArgs{};
+    g.done = done, g.n_contig = -1;
+    g.W = L.w2, g.x = h->act, g.ldx = a.F, g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
+    g.K = a.F, g.N = d;
+    h->launches += 6;
+    return launch_gemv(g, M, EPI_RESID, h->stream, h->pdl);
+}
+
+// Final norm + tied LM head (SlowArOutputHeadF16Weights::forward_logits,
+// slow_ar.rs:943-955) on the row `xrow`; writes the post-norm hidden.
+// full: every vocabulary row; otherwise the semantic rows + im_end only.
+cudaError_t enqueue_lm_head(S2dHandle *h, const float *xrow, bool full, uint32_t im_end,
+                            const int32_t *done) {
+    const S2dGraphSpec &s = h->spec;
+    GemvArgs g{};
+    g.done = done;
+    g.W = h->emb, g.x = xrow, g.ldx = s.hidden, g.norm_w = h->norm, g.eps = h->slow.eps;
+    g.y = h->logits, g.ldy = s.vocab_size, g.x_out = h->hidden_post, g.K = s.hidden;
+    if (full) {
+        g.n_contig = -1;
+        g.N = s.vocab_size;
+    } else {
+        const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+        const bool extra = (int64_t)im_end < s.vocab_size &&
+                           ((int)im_end < s.semantic_begin_id || (int)im_end > s.semantic_end_id);
+        g.row_base = s.semantic_begin_id;
+        g.n_contig = nsem;
+        g.extra_row = extra ? (int)im_end : s.semantic_begin_id;
+        g.N = nsem + (extra ? 1 : 0);
+        h->n_allowed_extra = extra ? 1 : 0;
+    }
+    h->launches += 1;
+    return launch_gemv(g, 1, EPI_STORE, h->stream, h->pdl);
+}
+
+cudaError_t enqueue_fast_head(S2dHandle *h, const float *xrow, const int32_t *done) {
+    GemvArgs g{};
+    g.done = done, g.n_contig = -1;
+    g.W = h->fast_out, g.x = xrow, g.ldx = h->fast.d, g.norm_w = h->fast_norm, g.eps = h->fast.eps;
+    g.y = h->logits_fast, g.ldy = h->spec.codebook_size, g.K = h->fast.d, g.N = h->spec.codebook_size;
+    h->launches += 1;
+    return launch_gemv(g, 1, EPI_STORE, h->stream, h->pdl);
+}
+
+SampleArgs slow_sample_args(S2dHandle *h, int mode, const GenKey &k) {
+    const S2dGraphSpec &s = h->spec;
+    SampleArgs a{};
+    a.logits = h->logits;
+    const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+    const bool extra = (int64_t)k.im_end < s.vocab_size &&
+                       ((int)k.im_end < s.semantic_begin_id || (int)k.im_end > s.semantic_end_id);
+    a.n = nsem + (extra ? 1 : 0);
+    a.n_contig = nsem;
+    a.id_base = (uint32_t)s.semantic_begin_id;
+    a.extra_id = k.im_end;
+    a.vocab_full = s.vocab_size;
+    a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k;
+    a.force_id = -1;
+    a.mode = mode;
+    a.im_end = k.im_end;
+    a.min_tokens_before_end = k.min_tokens;
+    a.max_new = (int)k.max_new;
+    a.st = h->st;
+    a.rng = &h->st->rng;
+    a.out_token = h->tok_out;
+    return a;
+}
+
+// Fast-AR codebooks 1..K-1 of one frame (generate_codebooks_for_semantic,
+// fast_ar.rs:440-470), with a KV cache over the frame's positions instead
+// of the reference's prefix recomputation (identical results: causal).
+cudaError_t enqueue_fast_frame(S2dHandle *h, const GenKey &k, bool with_override) {
+    const S2dGraphSpec &s = h->spec;
+    const int d = s.hidden, K = s.num_codebooks;
+    const int32_t *done = &h->st->done;
+    cudaError_t e;
+    FastInitArgs fi{};
+    fi.st = h->st, fi.slow_hidden = h->hidden_post, fi.fast_emb = h->fast_emb, fi.fast_x = h->fast_x;
+    fi.frame_codes = h->frame_codes, fi.codes_out = with_override ? nullptr : h->codes_out;
+    fi.max_new = (int)k.max_new, fi.d = d, fi.cb_size = s.codebook_size;
+    fi.sem_begin = (uint32_t)s.semantic_begin_id, fi.sem_end = (uint32_t)s.semantic_end_id;
+    fi.code_override = with_override ? h->code_override : nullptr;
+    h->launches += 1;
+    if ((e = launch_fast_init(fi, h->stream, h->pdl))) return e;
+    for (int cbk = 1; cbk < K; ++cbk) {
+        // positions processed this pass: 0 and 1 on the first pass, then cbk
+        const int p0 = cbk == 1 ? 0 : cbk;
+        const int M = cbk == 1 ? 2 : 1;
+        for (int l = 0; l < h->fast.L; ++l)
+            if ((e = enqueue_layer(h, true, l, h->fast_x + (size_t)p0 * d, M, nullptr, p0, done))) return e;
+        if ((e = enqueue_fast_head(h, h->fast_x + (size_t)cbk * d, done))) return e;
+        SampleArgs a{};
+        a.logits = h->logits_fast;
+        a.n = s.codebook_size;
+        a.n_contig = -1;
+        a.vocab_full = s.codebook_size;
+        a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k;
+        a.force_id = -1;
+        a.mode = SAMPLE_FAST;
+        a.max_new = (int)k.max_new;
+        a.st = h->st;
+        a.rng = &h->st->rng;
+        a.cb_index = cbk;
+        a.frame_codes = h->frame_codes;
+        a.codes_out = with_override ? nullptr : h->codes_out;
+        a.fast_emb = h->fast_emb;
+        a.fast_x_next = cbk + 1 < K ? h->fast_x + (size_t)(cbk + 1) * d : nullptr;
+        a.d = d;
+        a.out_token = h->tok_out;
+        h->launches += 1;
+        if ((e = launch_sample(a, h->stream, h->pdl))) return e;
+    }
+    return cudaSuccess;
+}
+
+// One full frame (the loop body of generate_codes, generate.rs:165-211).
+cudaError_t enqueue_frame(S2dHandle *h, const GenKey &k) {
+    const S2dGraphSpec &s = h->spec;
+    const int32_t *done = &h->st->done;
+    cudaError_t e;
+    if ((e = enqueue_fast_frame(h, k, false))) return e;
+    EmbedArgs ea{};
+    ea.tokens = nullptr, ea.st = h->st, ea.frame_codes = h->frame_codes;
+    ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = s.hidden, ea.K = s.num_codebooks;
+    ea.cb_size = s.codebook_size, ea.vocab = s.vocab_size, ea.cb_rows = s.codebook_rows;
+    ea.sem_begin = (uint32_t)s.semantic_begin_id, ea.sem_end = (uint32_t)s.semantic_end_id;
+    ea.scale_on = 1, ea.sem_scale = 1.0f / sqrtf((float)(s.num_codebooks + 1));
+    ea.out = h->x, ea.M = 1, ea.done = done, ea.error = &h->st->error;
+    h->launches += 1;
+    if ((e = launch_embed(ea, h->stream, h->pdl))) return e;
+    for (int l = 0; l < h->slow.L; ++l)
+        if ((e = enqueue_layer(h, false, l, h->x, 1, &h->st->n_past, 0, done))) return e;
+    if ((e = enqueue_lm_head(h, h->x, false, k.im_end, done))) return e;
+    SampleArgs a = slow_sample_args(h, SAMPLE_SLOW_STEP, k);
+    h->launches += 1;
+    return launch_sample(a, h->stream, h->pdl);
+}
+
+int32_t check_device_error(S2dHandle *h) {
+    int32_t err = 0;
+    CK(cudaMemcpyAsync(&err, &h->st->error, sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if (err) {
+        cudaMemsetAsync(&h->st->error, 0, sizeof(int32_t), h->stream);
+        return set_err(h, S2D_EDEVICE, "device error flag " + std::to_string(err) +
+                                           " (1: KV position out of range, 2-4: token id out of range)");
+    }
+    return S2D_OK;
+}
+
+// Slow-AR eval over n tokens at positions n_past.. (SlowArState::eval,
+// slow_ar.rs:456-527).  Leaves the post-norm hidden in hidden_post and the
+// logits in h->logits.
+int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t logits_mode,
+                  uint32_t im_end) {
+    const S2dGraphSpec &s = h->spec;
+    const int64_t cd = s.num_codebooks + 1;
+    if (n_flat <= 0 || n_flat % cd)
+        return set_err(h, S2D_EINVAL, "flat token length " + std::to_string(n_flat) +
+                                          " is not a multiple of codebook_dim " + std::to_string(cd));
+    const int64_t n = n_flat / cd;
+    if (h->n_past + n > h->cfg.max_seq)
+        return set_err(h, S2D_ESTATE, "KV cache overflow: n_past=" + std::to_string(h->n_past) +
+                                          " n_tokens=" + std::to_string(n) +
+                                          " max_seq_len=" + std::to_string(h->cfg.max_seq));
+    // embed_slow_ar_time_major's id checks (slow_ar.rs:1071-1105, tensor.rs:177-185)
+    for (int64_t t = 0; t < n; ++t) {
+        const int32_t id = flat[t * cd];
+        if (id < 0) return set_err(h, S2D_EINVAL, "semantic token id must be non-negative, got " + std::to_string(id));
+        if (id >= s.vocab_size)
+            return set_err(h, S2D_EINVAL, "embedding index " + std::to_string(id) + " out of range for vocab_dim " +
+                                              std::to_string(s.vocab_size));
+        if (id < s.semantic_begin_id || id > s.semantic_end_id) continue;
+        for (int cb = 0; cb < s.num_codebooks; ++cb) {
+            const int32_t raw = flat[t * cd + 1 + cb];
+            if (raw < 0) return set_err(h, S2D_EINVAL, "codebook token must be non-negative, got " + std::to_string(raw));
+            const int64_t cid = (int64_t)raw + (int64_t)cb * s.codebook_size;
+            if (cid >= s.codebook_rows)
+                return set_err(h, S2D_EINVAL, "embedding index " + std::to_string(cid) + " out of range for vocab_dim " +
+                                                  std::to_string(s.codebook_rows));
+        }
+    }
+    int32_t rc = ensure_tokens(h, (size_t)n_flat);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
+    for (int64_t c0 = 0; c0 < n;) {
+        int M = (int)std::min<int64_t>(kMaxM, n - c0);
+        if (M == 3) M = 2;  // GEMV instantiations: 1, 2, 4
+        EmbedArgs ea{};
+        ea.tokens = h->tokens_dev + c0 * cd, ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = s.hidden;
+        ea.K = s.num_codebooks, ea.cb_size = s.codebook_size, ea.vocab = s.vocab_size;
+        ea.cb_rows = s.codebook_rows, ea.sem_begin = (uint32_t)s.semantic_begin_id;
+        ea.sem_end = (uint32_t)s.semantic_end_id, ea.scale_on = 1;
+        ea.sem_scale = 1.0f / sqrtf((float)(s.num_codebooks + 1));
+        ea.out = h->x, ea.M = M, ea.error = &h->st->error;
+        h->launches += 1;
+        CK(launch_embed(ea, h->stream, false));
+        for (int l = 0; l < h->slow.L; ++l)
+            CK(enqueue_layer(h, false, l, h->x, M, nullptr, (int)(h->n_past + c0), nullptr));
+        if (c0 + M >= n) {
+            CK(enqueue_lm_head(h, h->x + (size_t)(M - 1) * s.hidden, logits_mode == S2D_LOGITS_FULL, im_end, nullptr));
+        }
+        c0 += M;
+    }
+    rc = check_device_error(h);
+    if (rc) return rc;
+    h->n_past += (int32_t)n;
+    return S2D_OK;
+}
+
+int32_t copy_eval_outputs(S2dHandle *h, float *out_hidden, float *out_logits, int32_t mode,
+                          uint32_t im_end) {
+    const S2dGraphSpec &s = h->spec;
+    if (out_hidden)
+        CK(cudaMemcpyAsync(out_hidden, h->hidden_post, (size_t)s.hidden * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    if (out_logits && mode == S2D_LOGITS_FULL)
+        CK(cudaMemcpyAsync(out_logits, h->logits, (size_t)s.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    if (out_logits && mode == S2D_LOGITS_ALLOWED) {
+        const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+        for (int i = 0; i < s.vocab_size; ++i) out_logits[i] = -INFINITY;
+        CK(cudaMemcpyAsync(out_logits + s.semantic_begin_id, h->logits, (size_t)nsem * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+        if (h->n_allowed_extra)
+            CK(cudaMemcpyAsync(out_logits + im_end, h->logits + nsem, sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    }
+    CK(cudaStreamSynchronize(h->stream));
+    return S2D_OK;
+}
+
+void free_handle(S2dHandle *h) {
+    if (!h) return;
+    if (h->device >= 0) cudaSetDevice(h->device);
+    if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
+    void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
+                    h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
+                    h->logits_fast, h->part, h->counters, h->st, h->tokens_dev, h->frame_codes,
+                    h->codes_out, h->tok_out, h->code_override};
+    for (void *p : bufs)
+        if (p) cudaFree(p);
+    if (h->ev0) cudaEventDestroy(h->ev0);
+    if (h->ev1) cudaEventDestroy(h->ev1);
+    if (h->ev2) cudaEventDestroy(h->ev2);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+
+extern "C" {
+
+int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *err, size_t err_cap) {
+    auto report = [&](S2dHandle *h, int32_t rc) {
+        if (err && err_cap) {
+            snprintf(err, err_cap, "%s", h ? h->err.c_str() : "out of memory");
+        }
+        free_handle(h);
+        return rc;
+    };
+    if (out) *out = nullptr;
+    if (!path || !out) {
+        if (err && err_cap) snprintf(err, err_cap, "s2d_open: path and out must not be NULL");
+        return S2D_EINVAL;
+    }
+    S2dHandle *h = new (std::nothrow) S2dHandle();
+    if (!h) return report(nullptr, S2D_ENOMEM);
+    h->cfg = cfg ? *cfg : S2dConfig{0, 4096, 1, 0};
+    if (h->cfg.max_seq <= 0) {
+        h->err = "max_seq_len must be non-zero";
+        return report(h, S2D_EINVAL);
+    }
+    h->device = h->cfg.device;
+    cudaError_t ce = cudaSetDevice(h->device);
+    if (ce) {
+        h->err = std::string("cudaSetDevice: ") + cudaGetErrorString(ce);
+        h->device = -1;
+        return report(h, S2D_ECUDA);
+    }
+    if ((ce = cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking)) ||
+        (ce = cudaEventCreate(&h->ev0)) || (ce = cudaEventCreate(&h->ev1)) ||
+        (ce = cudaEventCreate(&h->ev2)) || (ce = configure_kernels())) {
+        h->err = std::string("CUDA init: ") + cudaGetErrorString(ce);
+        return report(h, S2D_ECUDA);
+    }
+    std::string e;
+    if (!h->gguf.open(path, &e)) {
+        h->err = e;
+        return report(h, S2D_EIO);
+    }
+    int32_t rc;
+    if ((rc = read_spec(h))) return report(h, rc);
+    if ((rc = upload_all(h))) return report(h, rc);
+    if ((rc = bind_weights(h))) return report(h, rc);
+    if ((rc = alloc_buffers(h))) return report(h, rc);
+    if ((ce = cudaStreamSynchronize(h->stream))) {
+        h->err = std::string("CUDA: ") + cudaGetErrorString(ce);
+        return report(h, S2D_ECUDA);
+    }
+    *out = h;
+    return S2D_OK;
+}
+
+void s2d_close(S2dHandle *h) { free_handle(h); }
+
+const char *s2d_last_error(const S2dHandle *h) { return h ? h->err.c_str() : ""; }
+
+int32_t s2d_graph_spec(const S2dHandle *h, S2dGraphSpec *out) {
+    if (!h || !out) return S2D_EINVAL;
+    *out = h->spec;
+    return S2D_OK;
+}
+
+int32_t s2d_reset(S2dHandle *h, int32_t seq) {
+    if (!h) return S2D_EINVAL;
+    if (seq != 0) return set_err(h, S2D_EINVAL, "seq must be 0");
+    h->n_past = 0;
+    return S2D_OK;
+}
+
+int32_t s2d_n_past(const S2dHandle *h, int32_t seq, int32_t *out) {
+    if (!h || !out || seq != 0) return S2D_EINVAL;
+    *out = h->n_past;
+    return S2D_OK;
+}
+
+int32_t s2d_prefill(S2dHandle *h, int32_t seq, const int32_t *flat, int64_t n_flat, float *out_hidden,
+                    float *out_logits, int32_t logits_mode, uint32_t im_end) {
+    if (!h) return S2D_EINVAL;
+    if (seq != 0 || !flat) return set_err(h, S2D_EINVAL, "bad arguments");
+    CK(cudaSetDevice(h->device));
+    int32_t rc = slow_eval(h, flat, n_flat, logits_mode, im_end);
+    if (rc) return rc;
+    return copy_eval_outputs(h, out_hidden, out_logits, logits_mode, im_end);
+}
+
+int32_t s2d_step(S2dHandle *h, int32_t seq, const int32_t *step_input, int64_t n, float *out_hidden,
+                 float *out_logits, int32_t logits_mode, uint32_t im_end) {
+    if (!h) return S2D_EINVAL;
+    if (n != h->spec.num_codebooks + 1)
+        return set_err(h, S2D_EINVAL, "step token width mismatch: expected " +
+                                          std::to_string(h->spec.num_codebooks + 1) + ", got " + std::to_string(n));
+    return s2d_prefill(h, seq, step_input, n, out_hidden, out_logits, logits_mode, im_end);
+}
+
+int32_t s2d_fast_prefix_logits(S2dHandle *h, const float *slow_hidden, const uint32_t *prefix, int64_t n_prefix,
+                               float *out_logits) {
+    if (!h || !slow_hidden || (!prefix && n_prefix) || !out_logits) return S2D_EINVAL;
+    const S2dGraphSpec &s = h->spec;
+    if (n_prefix >= s.num_codebooks)
+        return set_err(h, S2D_EINVAL, "fast prefix too long: " + std::to_string(n_prefix) + " codes (max " +
+                                          std::to_string(s.num_codebooks - 1) + ")");
+    if (n_prefix + 1 > h->fast.ctx)
+        return set_err(h, S2D_EINVAL, "fast sequence length exceeds context_length");
+    CK(cudaSetDevice(h->device));
+    const int d = s.hidden;
+    CK(cudaMemcpyAsync(h->fast_x, slow_hidden, (size_t)d * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    for (int64_t i = 0; i < n_prefix; ++i) {
+        if (prefix[i] >= (uint32_t)s.codebook_size)
+            return set_err(h, S2D_EINVAL, "embedding index " + std::to_string(prefix[i]) + " out of range");
+        CK(launch_f16_to_f32(h->fast_emb + (size_t)prefix[i] * d, h->fast_x + (size_t)(1 + i) * d, d, h->stream));
+    }
+    const int n = (int)n_prefix + 1;
+    for (int c0 = 0; c0 < n;) {
+        int M = std::min(kMaxM, n - c0);
+        if (M == 3) M = 2;
+        for (int l = 0; l < h->fast.L; ++l)
+            CK(enqueue_layer(h, true, l, h->fast_x + (size_t)c0 * d, M, nullptr, c0, nullptr));
+        c0 += M;
+    }
+    CK(enqueue_fast_head(h, h->fast_x + (size_t)(n - 1) * d, nullptr));
+    CK(cudaMemcpyAsync(out_logits, h->logits_fast, (size_t)s.codebook_size * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return check_device_error(h);
+}
+
+int32_t s2d_generate_codebooks(S2dHandle *h, const float *slow_hidden, uint32_t semantic_code,
+                               const S2dSamplerParams *sp, uint64_t *rng_state, uint32_t *out_codes) {
+    if (!h || !slow_hidden || !sp || !rng_state || !out_codes) return S2D_EINVAL;
+    const S2dGraphSpec &s = h->spec;
+    if (semantic_code >= (uint32_t)s.codebook_size)
+        return set_err(h, S2D_EINVAL, "semantic_code " + std::to_string(semantic_code) + " >= codebook_size " +
+                                          std::to_string(s.codebook_size));
+    CK(cudaSetDevice(h->device));
+    GenKey k;
+    k.temperature = sp->temperature, k.top_p = sp->top_p, k.top_k = sp->top_k, k.max_new = 1;
+    CK(cudaMemcpyAsync(h->hidden_post, slow_hidden, (size_t)s.hidden * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(h->code_override, &semantic_code, sizeof(uint32_t), cudaMemcpyHostToDevice, h->stream));
+    CK(launch_set_state(h->st, 0, 0, *rng_state, h->stream));
+    CK(enqueue_fast_frame(h, k, true));
+    std::vector<int32_t> codes((size_t)s.num_codebooks);
+    DevState st{};
+    CK(cudaMemcpyAsync(codes.data(), h->frame_codes, codes.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(&st, h->st, sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    for (size_t i = 0; i < codes.size(); ++i) out_codes[i] = (uint32_t)codes[i];
+    *rng_state = st.rng;
+    return st.error ? set_err(h, S2D_EDEVICE, "device error flag") : S2D_OK;
+}
+
+int32_t s2d_sample_token(S2dHandle *h, const float *logits, int64_t n, const S2dSamplerParams *sp,
+                         int64_t always_include_id, uint64_t *rng_state, uint32_t *out_token) {
+    if (!h || !logits || !sp || !rng_state || !out_token) return S2D_EINVAL;
+    if (n <= 0 || n > kSampleMax) return set_err(h, S2D_EINVAL, "n must be in 1..8192");
+    CK(cudaSetDevice(h->device));
+    CK(cudaMemcpyAsync(h->logits_fast, logits, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    CK(launch_set_state(h->st, 0, 0, *rng_state, h->stream));
+    SampleArgs a{};
+    a.logits = h->logits_fast, a.n = (int)n, a.n_contig = -1, a.vocab_full = n;
+    a.temperature = sp->temperature, a.top_p = sp->top_p, a.top_k = sp->top_k;
+    a.force_id = always_include_id, a.mode = SAMPLE_PLAIN, a.st = h->st, a.rng = &h->st->rng;
+    a.out_token = h->tok_out;
+    CK(launch_sample(a, h->stream, false));
+    DevState st{};
+    CK(cudaMemcpyAsync(out_token, h->tok_out, sizeof(uint32_t), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(&st, h->st, sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    *rng_state = st.rng;
+    return S2D_OK;
+}
+
+int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, int32_t cols,
+                           const S2dGenParams *p, uint64_t *rng_state, int32_t *out_codes,
+                           uint32_t *out_n_frames, S2dProfile *profile) {
+    if (!h) return S2D_EINVAL;
+    if (!prompt || !p || !rng_state || !out_codes || !out_n_frames)
+        return set_err(h, S2D_EINVAL, "s2d_generate_codes: NULL argument");
+    const S2dGraphSpec &s = h->spec;
+    const int K = std::max(s.num_codebooks, 1);
+    if (rows != s.num_codebooks + 1) return set_err(h, S2D_EINVAL, "prompt rows must be num_codebooks+1");
+    if (cols <= 0) return set_err(h, S2D_EINVAL, "expected at least one token");
+    if ((int64_t)cols + (int64_t)p->max_new_tokens > h->cfg.max_seq)
+        return set_err(h, S2D_ESTATE, "prompt + max_new_tokens exceeds max_seq");
+    CK(cudaSetDevice(h->device));
+    // transpose_to_time_major (prompt.rs:77-103)
+    std::vector<int32_t> flat((size_t)rows * cols);
+    for (int t = 0; t < cols; ++t)
+        for (int r = 0; r < rows; ++r) {
+            const uint32_t v = prompt[(size_t)r * cols + t];
+            if (v > 0x7fffffffu) return set_err(h, S2D_EINVAL, "prompt token id does not fit i32");
+            flat[(size_t)t * rows + r] = (int32_t)v;
+        }
+    const size_t need_codes = (size_t)K * std::max<uint32_t>(p->max_new_tokens, 1);
+    if (need_codes > h->codes_cap) {
+        if (h->codes_out) cudaFree(h->codes_out);
+        h->codes_out = nullptr;
+        h->codes_cap = 0;
+        CK(cudaMalloc(&h->codes_out, need_codes * sizeof(int32_t)));
+        h->codes_cap = need_codes;
+        if (h->frame_exec) {  // captured frames point at the old buffer
+            cudaGraphExecDestroy(h->frame_exec);
+            h->frame_exec = nullptr;
+        }
+    }
+    CK(cudaMemsetAsync(h->codes_out, 0, need_codes * sizeof(int32_t), h->stream));
+    GenKey k;
+    k.max_new = p->max_new_tokens, k.min_tokens = p->min_tokens_before_end, k.im_end = p->im_end_id;
+    k.temperature = p->temperature, k.top_p = p->top_p, k.top_k = p->top_k;
+
+    // prefill + first semantic sample (generate.rs:126-162)
+    CK(cudaEventRecord(h->ev0, h->stream));
+    const uint32_t launches0 = h->launches;
+    h->n_past = 0;
+    int32_t rc = slow_eval(h, flat.data(), (int64_t)flat.size(), S2D_LOGITS_ALLOWED, p->im_end_id);
+    if (rc) return rc;
+    CK(launch_set_state(h->st, h->n_past, cols, *rng_state, h->stream));
+    SampleArgs first = slow_sample_args(h, SAMPLE_SLOW_FIRST, k);
+    CK(launch_sample(first, h->stream, false));
+    h->launches += 2;
+    const uint32_t prefill_kernels = h->launches - launches0;
+    CK(cudaEventRecord(h->ev1, h->stream));
+
+    // frames (generate.rs:165-211): one captured graph per frame
+    if (!h->frame_exec || !(h->frame_key == k)) {
+        if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
+        h->frame_exec = nullptr;
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        cudaError_t e = enqueue_frame(h, k);
+        cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
+        if (e || e2) {
+            if (graph) cudaGraphDestroy(graph);
+            return set_err(h, S2D_ECUDA, std::string("frame capture: ") + cudaGetErrorString(e ? e : e2));
+        }
+        size_t nn = 0;
+        cudaGraphGetNodes(graph, nullptr, &nn);
+        h->frame_kernels = (uint32_t)nn;
+        e = cudaGraphInstantiateWithFlags(&h->frame_exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e) return set_err(h, S2D_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        h->frame_key = k;
+    }
+    // Launch the frame graph up to max_new times; a frame whose state says
+    // `done` exits in every kernel, so frames past the end are no-ops.  The
+    // host polls `done` every few frames to stop launching early.
+    const uint32_t poll = 8;
+    DevState st{};
+    uint32_t launched = 0;
+    while (launched < p->max_new_tokens) {
+        const uint32_t batch = std::min(poll, p->max_new_tokens - launched);
+        for (uint32_t i = 0; i < batch; ++i) CK(cudaGraphLaunch(h->frame_exec, h->stream));
+        launched += batch;
+        CK(cudaMemcpyAsync(&st, h->st, sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+        CK(cudaStreamSynchronize(h->stream));
+        if (st.done || st.error) break;
+    }
+    CK(cudaEventRecord(h->ev2, h->stream));
+    CK(cudaMemcpyAsync(&st, h->st, sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    std::vector<int32_t> codes(need_codes);
+    CK(cudaMemcpyAsync(codes.data(), h->codes_out, need_codes * sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if (st.error) return set_err(h, S2D_EDEVICE, "device error flag " + std::to_string(st.error));
+    if (!st.done) return set_err(h, S2D_ESTATE, "generation did not finish");
+    const uint32_t frames = (uint32_t)st.step_index;
+    // compact_codes (generate.rs:346-390)
+    for (int cb = 0; cb < K; ++cb)
+        for (uint32_t t = 0; t < frames; ++t)
+            out_codes[(size_t)cb * frames + t] = codes[(size_t)cb * p->max_new_tokens + t];
+    *out_n_frames = frames;
+    *rng_state = st.rng;
+    h->n_past = st.n_past;
+    if (profile) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, h->ev0, h->ev1);
+        cudaEventElapsedTime(&b, h->ev1, h->ev2);
+        profile->prefill_ms = a;
+        profile->decode_ms = b;
+        profile->frames = frames;
+        profile->kernels_per_frame = h->frame_kernels;
+        profile->prefill_kernels = prefill_kernels;
+        profile->frame_launches = launched;
+    }
+    return S2D_OK;
+}
+
+int32_t s2d_dequant_tensor(S2dHandle *h, const char *name, float *out, int64_t n) {
+    if (!h || !name || !out) return S2D_EINVAL;
+    const GgufTensor *t = h->gguf.tensor(name);
+    if (!t) return set_err(h, S2D_EINVAL, std::string("tensor not found: ") + name);
+    if ((uint64_t)n != t->elements) return set_err(h, S2D_EINVAL, "element count mismatch");
+    CK(cudaSetDevice(h->device));
+    float *dst = nullptr;
+    CK(cudaMalloc(&dst, (size_t)n * sizeof(float)));
+    cudaError_t e;
+    if (t->type == 1) e = launch_f16_to_f32(reinterpret_cast<const uint16_t *>(tdev(h, t)->dev), dst, n, h->stream);
+    else if (t->type == 0) e = cudaMemcpyAsync(dst, tdev(h, t)->dev, (size_t)n * 4, cudaMemcpyDeviceToDevice, h->stream);
+    else e = cudaErrorNotSupported;
+    if (!e) e = cudaMemcpyAsync(out, dst, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
+    if (!e) e = cudaStreamSynchronize(h->stream);
+    cudaFree(dst);
+    if (e) return set_err(h, S2D_ECUDA, std::string("dequant: ") + cudaGetErrorString(e));
+    return S2D_OK;
+}
+
+int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *avg_ms, double *bytes) {
+    if (!h || !avg_ms || !bytes || iters <= 0) return S2D_EINVAL;
+    CK(cudaSetDevice(h->device));
+    const S2dGraphSpec &s = h->spec;
+    const ArShape &a = h->slow;
+    const int d = s.hidden;
+    // finite activations for the inputs the kernels read
+    CK(cudaMemsetAsync(h->x, 0, (size_t)kMaxM * d * sizeof(float), h->stream));
+    CK(cudaMemsetAsync(h->att, 0, (size_t)kMaxM * a.qs() * sizeof(float), h->stream));
+    CK(cudaMemsetAsync(h->act, 0, (size_t)kMaxM * a.F * sizeof(float), h->stream));
+    auto args = [&](int l, int *epi) {
+        const LayerDev &L = h->slow_layers[(size_t)l];
+        GemvArgs g{};
+        g.n_contig = -1;
+        switch (kernel) {
+        case S2D_KERNEL_WQKV:
+            g.W = L.wqkv, g.x = h->x, g.ldx = d, g.norm_w = L.attn_norm, g.eps = a.eps;
+            g.y = h->qkv, g.ldy = a.qkv_out(), g.K = d, g.N = a.qkv_out(), *epi = EPI_STORE;
+            break;
+        case S2D_KERNEL_WO:
+            g.W = L.wo, g.x = h->att, g.ldx = a.qs(), g.y = h->x, g.ldy = d, g.resid = h->x, g.ldr = d;
+            g.K = a.qs(), g.N = d, *epi = EPI_RESID;
+            break;
+        case S2D_KERNEL_W13:
+            g.W = L.w1, g.W2 = L.w3, g.x = h->x, g.ldx = d, g.norm_w = L.ffn_norm, g.eps = a.eps;
+            g.y = h->act, g.ldy = a.F, g.K = d, g.N = a.F, *epi = EPI_SWIGLU_SLOW;
+            break;
+        case S2D_KERNEL_W2:
+            g.W = L.w2, g.x = h->act, g.ldx = a.F, g.y = h->x, g.ldy = d, g.resid = h->x, g.ldr = d;
+            g.K = a.F, g.N = d, *epi = EPI_RESID;
+            break;
+        default: {
+            const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+            g.W = h->emb, g.x = h->x, g.ldx = d, g.norm_w = h->norm, g.eps = a.eps;
+            g.y = h->logits, g.ldy = s.vocab_size, g.x_out = h->hidden_post, g.K = d;
+            // a different block of rows per launch so that no launch hits L2
+            const int span = nsem + 1;
+            const int base = (int)(((int64_t)l * span) % std::max(1, s.vocab_size - span));
+            g.row_base = base, g.n_contig = nsem, g.extra_row = base + nsem;
+            g.N = span, *epi = EPI_STORE;
+        }
+        }
+        return g;
+    };
+    if (kernel < S2D_KERNEL_WQKV || kernel > S2D_KERNEL_LM_HEAD) return set_err(h, S2D_EINVAL, "unknown kernel");
+    int epi = 0;
+    GemvArgs g0 = args(0, &epi);
+    const double wbytes = (double)g0.K * g0.N * 2.0 * (g0.W2 ? 2 : 1);
+    *bytes = wbytes + (double)g0.K * 4.0 + (double)g0.N * 4.0 * (epi == EPI_RESID ? 2 : 1);
+    for (int i = 0; i < 3; ++i) CK(launch_gemv(args(i % a.L, &epi), 1, epi, h->stream, h->pdl));
+    CK(cudaEventRecord(h->ev0, h->stream));
+    for (int i = 0; i < iters; ++i) {
+        const int l = kernel == S2D_KERNEL_LM_HEAD ? i : i % a.L;
+        CK(launch_gemv(args(l, &epi), 1, epi, h->stream, h->pdl));
+    }
+    CK(cudaEventRecord(h->ev1, h->stream));
+    CK(cudaEventSynchronize(h->ev1));
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, h->ev0, h->ev1));
+    *avg_ms = ms / iters;
+    return S2D_OK;
+}
+
+// ---- op-level seam -------------------------------------------------------
+
+namespace {
+struct DevBuf {
+    void *p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+};
+}  // namespace
+
+int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *w, int64_t in_dim, int64_t out_dim,
+                          float *out) {
+    if (!input || !w || !out || in_dim <= 0 || out_dim <= 0) return set_err(h, S2D_EINVAL, "bad arguments");
+    if (in_dim % 8) return set_err(h, S2D_EINVAL, "in_dim must be a multiple of 8");
+    if (in_dim * 4 > 200 * 1024) return set_err(h, S2D_EINVAL, "in_dim too large for the op-level GEMV");
+    cudaStream_t st = h ? h->stream : nullptr;
+    if (h) CK(cudaSetDevice(h->device));
+    DevBuf x, W, y;
+    CK(configure_kernels());
+    CK(cudaMalloc(&x.p, (size_t)in_dim * 4));
+    CK(cudaMalloc(&W.p, (size_t)in_dim * out_dim * 2));
+    CK(cudaMalloc(&y.p, (size_t)out_dim * 4));
+    CK(cudaMemcpyAsync(x.p, input, (size_t)in_dim * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(W.p, w, (size_t)in_dim * out_dim * 2, cudaMemcpyHostToDevice, st));
+    GemvArgs g{};
+    g.W = (const uint16_t *)W.p, g.x = (const float *)x.p, g.ldx = (int)in_dim, g.y = (float *)y.p;
+    g.ldy = (int)out_dim, g.K = (int)in_dim, g.N = (int)out_dim, g.n_contig = -1;
+    CK(launch_gemv(g, 1, EPI_STORE, st, false));
+    CK(cudaMemcpyAsync(out, y.p, (size_t)out_dim * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return S2D_OK;
+}
+
+int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n, int64_t head_dim,
+                        float eps, float *out) {
+    if (!input || !weight || !out || n <= 0 || head_dim <= 0 || n % head_dim)
+        return set_err(h, S2D_EINVAL, "bad arguments");
+    cudaStream_t st = h ? h->stream : nullptr;
+    if (h) CK(cudaSetDevice(h->device));
+    DevBuf x, w, y;
+    CK(cudaMalloc(&x.p, (size_t)n * 4));
+    CK(cudaMalloc(&w.p, (size_t)head_dim * 4));
+    CK(cudaMalloc(&y.p, (size_t)n * 4));
+    CK(cudaMemcpyAsync(x.p, input, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(w.p, weight, (size_t)head_dim * 4, cudaMemcpyHostToDevice, st));
+    CK(launch_rms_norm_heads((const float *)x.p, (const float *)w.p, (float *)y.p, n, (int)head_dim, eps, st));
+    CK(cudaMemcpyAsync(out, y.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return S2D_OK;
+}
+
+int32_t s2d_op_gqa_decode_attention(S2dHandle *h, const float *query, const float *keys, const float *values,
+                                    int32_t H, int32_t Hkv, int32_t hd, int32_t T, float scale, float *out) {
+    if (!query || !keys || !values || !out || Hkv <= 0 || H % Hkv || hd <= 0 || T <= 0)
+        return set_err(h, S2D_EINVAL, "invalid GQA split or attention dims");
+    if (hd % 64 || hd > 256 || H / Hkv > 16) return set_err(h, S2D_EINVAL, "unsupported head_dim or group size");
+    cudaStream_t st = h ? h->stream : nullptr;
+    if (h) CK(cudaSetDevice(h->device));
+    // token-major [T][Hkv][hd] -> per-head [Hkv][T][hd]
+    std::vector<float> kt((size_t)Hkv * T * hd), vt((size_t)Hkv * T * hd);
+    for (int t = 0; t < T; ++t)
+        for (int k = 0; k < Hkv; ++k)
+            for (int e = 0; e < hd; ++e) {
+                kt[((size_t)k * T + t) * hd + e] = keys[((size_t)t * Hkv + k) * hd + e];
+                vt[((size_t)k * T + t) * hd + e] = values[((size_t)t * Hkv + k) * hd + e];
+            }
+    const int S = std::max(1, std::min(16, T / 8));
+    DevBuf q, K, V, o, part, cnt;
+    CK(cudaMalloc(&q.p, (size_t)H * hd * 4));
+    CK(cudaMalloc(&K.p, kt.size() * 4));
+    CK(cudaMalloc(&V.p, vt.size() * 4));
+    CK(cudaMalloc(&o.p, (size_t)H * hd * 4));
+    CK(cudaMalloc(&part.p, (size_t)H * S * (hd + 2) * 4));
+    CK(cudaMalloc(&cnt.p, (size_t)Hkv * 4));
+    CK(cudaMemsetAsync(cnt.p, 0, (size_t)Hkv * 4, st));
+    CK(cudaMemcpyAsync(q.p, query, (size_t)H * hd * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(K.p, kt.data(), kt.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(V.p, vt.data(), vt.size() * 4, cudaMemcpyHostToDevice, st));
+    AttnArgs a{};
+    a.q = (const float *)q.p, a.kcache = K.p, a.vcache = V.p, a.max_seq = T, a.out = (float *)o.p;
+    a.part = (float *)part.p, a.counters = (int32_t *)cnt.p, a.pos_const = T - 1;
+    a.H = H, a.Hkv = Hkv, a.hd = hd, a.S = S, a.M = 1, a.scale = scale;
+    CK(launch_attention(a, false, st, false));
+    CK(cudaMemcpyAsync(out, o.p, (size_t)H * hd * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return S2D_OK;
+}
+
+}  // extern "C"

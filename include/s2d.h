@@ -1,0 +1,205 @@
+/*
+ * s2d.h -- C ABI of libs2d.so, the sm_100a Dual-AR token loop for fish-s2pro.
+ *
+ * This is the drop-in boundary for the reference's `rust-pure` hot path
+ * (crate fish_s2_infer; paths below are relative to the reference repository
+ * root).  It follows the conventions of the reference's existing native ABI
+ * (crates/fish_s2_infer/ffi/s2_engine_ffi.h:10-37): opaque handle, plain C
+ * types, errors returned as a status with the message written into a caller
+ * buffer (s2_engine_ffi.cpp:16-22) or kept on the handle.  Caller-provided
+ * output buffers are used throughout, so nothing crosses allocators.
+ *
+ * Status codes: S2D_OK (0) on success, a negative S2D_E* on failure.
+ * Threading: a handle is not re-entrant; use one host thread per handle
+ * (the reference serialises the same way: engine.rs:159, server.rs:20).
+ * Every call is synchronous: it returns after its device work has finished.
+ */
+#ifndef S2D_H
+#define S2D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define S2D_OK 0
+#define S2D_EINVAL (-1)   /* bad argument, shape or token id          */
+#define S2D_EIO (-2)      /* GGUF file missing, truncated or malformed */
+#define S2D_ECUDA (-3)    /* a CUDA runtime call failed               */
+#define S2D_ENOMEM (-4)   /* device or host allocation failed         */
+#define S2D_ESTATE (-5)   /* KV cache overflow or call out of order   */
+#define S2D_EDEVICE (-6)  /* a kernel reported an error flag           */
+
+typedef struct S2dHandle S2dHandle;
+
+/* Open-time configuration (replaces the arguments of SlowArState::open,
+ * slow_ar.rs:387, and EngineConfig's device fields, engine.rs:83-127). */
+typedef struct S2dConfig {
+    int32_t device;       /* CUDA device ordinal                                   */
+    int32_t max_seq;      /* Slow-AR KV capacity in positions (SlowArState::open)   */
+    int32_t max_batch;    /* reserved: sequences per handle (1 in this version)      */
+    int32_t flags;        /* reserved, 0                                             */
+} S2dConfig;
+
+/* DualArGraphSpec (registry.rs:30-42, 216-231), shape-parametric. */
+typedef struct S2dGraphSpec {
+    int32_t slow_layers, hidden, ffn, heads, kv_heads, head_dim, context_length;
+    int32_t fast_layers, fast_ffn, fast_heads, fast_kv_heads, fast_head_dim, fast_context_length;
+    float rope_base, rms_eps, fast_rope_base, fast_rms_eps;
+    int32_t codebook_size, num_codebooks, semantic_begin_id, semantic_end_id;
+    int32_t vocab_size, codebook_rows;
+    int32_t linear_type; /* ggml type of the linear weights: 1 F16, 8 Q8_0, 12 Q4_K */
+} S2dGraphSpec;
+
+/* SamplerParams (sampling.rs:12-27). */
+typedef struct S2dSamplerParams {
+    float temperature;
+    float top_p;
+    int32_t top_k;
+} S2dSamplerParams;
+
+/* GenerateParams (generate.rs:13-32) plus the tokenizer's <|im_end|> id
+ * (S2TokenizerConfig.im_end_id, generate.rs:133-134). */
+typedef struct S2dGenParams {
+    uint32_t max_new_tokens;
+    float temperature;
+    float top_p;
+    int32_t top_k;
+    uint32_t min_tokens_before_end;
+    uint32_t im_end_id;
+} S2dGenParams;
+
+/* Timing of one generate call, measured with CUDA events on the handle's
+ * stream (the device-side counterpart of SlowArDecodeProfile,
+ * slow_ar.rs:248-319, which the reference fills with host timers). */
+typedef struct S2dProfile {
+    double prefill_ms;      /* prompt prefill + first semantic sample            */
+    double decode_ms;       /* all frames: Fast-AR codebooks + Slow-AR step      */
+    uint32_t frames;        /* frames produced                                   */
+    uint32_t kernels_per_frame; /* kernel launches in one captured frame       */
+    uint32_t prefill_kernels;   /* kernel launches of the prefill + first sample */
+    uint32_t frame_launches;    /* frame graphs launched (>= frames)            */
+} S2dProfile;
+
+/* Kernels that s2d_profile_kernel can time in isolation. */
+#define S2D_KERNEL_WQKV 0   /* attention_norm + WQKV GEMV            */
+#define S2D_KERNEL_WO 1     /* wo GEMV + residual                     */
+#define S2D_KERNEL_W13 2    /* ffn_norm + w1/w3 GEMV + SwiGLU          */
+#define S2D_KERNEL_W2 3     /* w2 GEMV + residual                     */
+#define S2D_KERNEL_LM_HEAD 4 /* final norm + masked LM head GEMV      */
+
+/* Logits requested from s2d_prefill / s2d_step. */
+#define S2D_LOGITS_NONE 0
+#define S2D_LOGITS_ALLOWED 1 /* semantic rows + im_end only; other entries -inf */
+#define S2D_LOGITS_FULL 2    /* all vocab_size rows (debug parity)            */
+
+/* ---- lifecycle ---------------------------------------------------------- */
+
+/* Replaces SlowArState::open + FastArWeights::from_gguf (slow_ar.rs:387-412,
+ * fast_ar.rs:202-223) and TransformerTensorRegistry::from_gguf
+ * (registry.rs:515-552): parses the transformer GGUF, validates names and
+ * shapes, uploads every tensor to HBM once. */
+int32_t s2d_open(const char *transformer_gguf, const S2dConfig *cfg, S2dHandle **out,
+                 char *err, size_t err_cap);
+/* Replaces s2_engine_destroy (s2_engine_ffi.h:26). NULL is ignored. */
+void s2d_close(S2dHandle *h);
+/* Message of the last failed call on this handle ("" if none). */
+const char *s2d_last_error(const S2dHandle *h);
+/* SlowArState::graph_spec (slow_ar.rs:418-420). */
+int32_t s2d_graph_spec(const S2dHandle *h, S2dGraphSpec *out);
+
+/* ---- Slow-AR state (SlowArState, slow_ar.rs:372-528) --------------------- */
+
+/* SlowArState::reset (slow_ar.rs:434-438). seq must be 0. */
+int32_t s2d_reset(S2dHandle *h, int32_t seq);
+/* SlowArState::n_past (slow_ar.rs:422-424). */
+int32_t s2d_n_past(const S2dHandle *h, int32_t seq, int32_t *out);
+/* SlowArState::prefill / eval (slow_ar.rs:440-442, 456-527): n_flat ids in
+ * time-major order (prompt.rs:77-103), a multiple of num_codebooks+1.
+ * out_hidden: hidden floats, the post-final-norm hidden of the last token
+ * (slow_ar.rs:515-526), or NULL.  out_logits: vocab_size floats or NULL,
+ * filled per logits_mode. */
+int32_t s2d_prefill(S2dHandle *h, int32_t seq, const int32_t *flat_tokens, int64_t n_flat,
+                    float *out_hidden, float *out_logits, int32_t logits_mode,
+                    uint32_t im_end_id);
+/* SlowArState::step (slow_ar.rs:444-454): exactly num_codebooks+1 ids. */
+int32_t s2d_step(S2dHandle *h, int32_t seq, const int32_t *step_input, int64_t n,
+                 float *out_hidden, float *out_logits, int32_t logits_mode, uint32_t im_end_id);
+
+/* ---- Fast-AR (fast_ar.rs) ------------------------------------------------ */
+
+/* forward_codebook_prefix (fast_ar.rs:360-437): slow_hidden (hidden floats),
+ * prefix codes (n_prefix < num_codebooks) -> codebook_size logits. */
+int32_t s2d_fast_prefix_logits(S2dHandle *h, const float *slow_hidden, const uint32_t *prefix,
+                               int64_t n_prefix, float *out_logits);
+/* generate_codebooks_for_semantic (fast_ar.rs:440-470): out_codes receives
+ * num_codebooks codes (out[0] = semantic_code).  *rng_state is the SeededRng
+ * state (sampling.rs:35-52), advanced in place. */
+int32_t s2d_generate_codebooks(S2dHandle *h, const float *slow_hidden, uint32_t semantic_code,
+                               const S2dSamplerParams *sampler, uint64_t *rng_state,
+                               uint32_t *out_codes);
+
+/* ---- the generation loop (generate.rs:117-221) --------------------------- */
+
+/* generate_codes: prompt is row-major (num_codebooks+1) x cols
+ * (PromptTensor, prompt.rs:59-67).  out_codes needs num_codebooks *
+ * max_new_tokens int32 and receives codebook-major codes compacted to
+ * *out_n_frames frames (generate.rs:346-390).  *rng_state is advanced like
+ * the reference's SeededRng.  profile may be NULL. */
+int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, int32_t cols,
+                           const S2dGenParams *params, uint64_t *rng_state, int32_t *out_codes,
+                           uint32_t *out_n_frames, S2dProfile *profile);
+
+/* ---- sampling (sampling.rs:121-241) ------------------------------------- */
+
+/* sample_token on the device sampler: logits (n floats, ids 0..n-1),
+ * always_include_id < 0 for None. */
+int32_t s2d_sample_token(S2dHandle *h, const float *logits, int64_t n,
+                         const S2dSamplerParams *sampler, int64_t always_include_id,
+                         uint64_t *rng_state, uint32_t *out_token);
+
+/* ---- weights ------------------------------------------------------------- */
+
+/* Dequantise one resident tensor to f32 on the device and copy it out
+ * (n = its element count).  The reference only decodes F16
+ * (F16TensorView::from_gguf, tensor.rs:22-45); Q8_0 / Q4_K follow ggml's
+ * block formats. */
+int32_t s2d_dequant_tensor(S2dHandle *h, const char *name, float *out, int64_t n);
+
+/* ---- measurement ----------------------------------------------------------
+ * No counterpart in the reference (which only has host timers,
+ * SlowArDecodeProfile, slow_ar.rs:248-319).  Times `iters` back-to-back
+ * launches of one decode kernel on the resident Slow-AR weights (cycling
+ * through the layers so that no launch finds its weights in L2) with CUDA
+ * events on the handle's stream.  *avg_ms: mean duration of one launch;
+ * *bytes: algorithmic HBM bytes of one launch (weights read once + the
+ * activation vector in and out). */
+int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *avg_ms,
+                           double *bytes);
+
+/* ---- op-level seam (MatmulBackend, backend.rs:5-39) ----------------------
+ * Host buffers in and out; each call uploads, runs one kernel and copies the
+ * result back.  Kept for op-level parity tests; the model path never uses
+ * them. */
+
+/* MatmulBackend::linear (backend.rs:55-73) with f16 weights [out_dim][in_dim]
+ * (GGUF little-endian bits), i.e. matvec_f16_streaming (tensor.rs:220-264). */
+int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *weight_f16,
+                          int64_t in_dim, int64_t out_dim, float *out);
+/* MatmulBackend::rms_norm / rms_norm_heads (backend.rs:84-121);
+ * head_dim == n gives the plain rms_norm. */
+int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n,
+                        int64_t head_dim, float eps, float *out);
+/* MatmulBackend::gqa_decode_attention (attention.rs:208-247): keys/values
+ * token-major [token_count][head_count_kv][head_dim]. */
+int32_t s2d_op_gqa_decode_attention(S2dHandle *h, const float *query, const float *keys,
+                                    const float *values, int32_t head_count,
+                                    int32_t head_count_kv, int32_t head_dim,
+                                    int32_t token_count, float attn_scale, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* S2D_H */
