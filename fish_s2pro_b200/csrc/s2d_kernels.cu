@@ -590,8 +590,10 @@ struct SampleShared {
     int appended;   // force id appended after top-k
     int nf;         // finite items in the list
     int token;
-    int force_pos;
+    int force_pos;  // sorted position of the force id if its logit is finite
     float force_v;
+    int fin_below;  // finite candidates with an id below the force id
+    long long always_pos;
     int general;
 };
 
@@ -627,9 +629,11 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
     auto cid = [&](int r) -> uint32_t {
         return a.n_contig < 0 ? (uint32_t)r : (r < a.n_contig ? a.id_base + (uint32_t)r : a.extra_id);
     };
+    // -0.0 is folded into +0.0: the reference's partial_cmp sees them equal,
+    // so their order must come from the id alone.
     auto cval = [&](int r) -> float {
         const float v = a.logits[r];
-        return (slow && block && cid(r) == a.im_end) ? -INFINITY : v;
+        return (slow && block && cid(r) == a.im_end) ? -INFINITY : (v == 0.0f ? 0.0f : v);
     };
 
     // pass 1: max and finite count
@@ -710,8 +714,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
                 __syncthreads();
             }
         }
-        // position of the force id among the sorted finite entries
-        if (tid == 0) sh.force_pos = 0x7fffffff, sh.force_v = -INFINITY;
+        // Position of the force id in the reference's sorted list: among the
+        // sorted finite entries if its logit is finite, otherwise among the
+        // -inf entries, which follow in id order (sampling.rs:146-168).
+        if (tid == 0) sh.force_pos = 0x7fffffff, sh.force_v = -INFINITY, sh.fin_below = 0;
         __syncthreads();
         if (force >= 0 && force < a.vocab_full) {
             for (int r = tid; r < sh.nfin; r += kSampleThreads) {
@@ -721,17 +727,32 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
                     sh.force_v = __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
                 }
             }
+            int below = 0;
+            for (int r = tid; r < n; r += kSampleThreads)
+                below += (cval(r) > -INFINITY) && ((int64_t)cid(r) < force);
+            if (below) atomicAdd(&sh.fin_below, below);
         }
         __syncthreads();
         if (tid == 0) {
             const int64_t kk = min(k_eff, (int64_t)sh.nfin);
             int appended = 0;
-            if (force >= 0 && sh.force_pos != 0x7fffffff && sh.force_v > -1e30f &&
-                (int64_t)sh.force_pos >= k_eff)
-                appended = 1;
+            int64_t always_pos = -1;
+            if (force >= 0 && force < a.vocab_full) {
+                const bool finite = sh.force_pos != 0x7fffffff;
+                const int64_t P = finite ? (int64_t)sh.force_pos
+                                         : (int64_t)sh.nfin + force - (int64_t)sh.fin_below;
+                if (!finite) sh.force_v = -INFINITY;
+                if (P < k_eff) {
+                    always_pos = P;
+                } else if (sh.force_v > -1e30f) {
+                    appended = 1;
+                    always_pos = kk;  // appended right after the top-k items
+                }
+            }
             sh.kk = (int)kk;
             sh.appended = appended;
             sh.nf = (int)kk + appended;
+            sh.always_pos = always_pos;
         }
         __syncthreads();
         const int nf = sh.nf;
@@ -760,10 +781,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
                 for (int i = 0; i < nf; ++i) sum += probs[i];
                 if (sum > 0.0f)
                     for (int i = 0; i < nf; ++i) probs[i] /= sum;
-                const int64_t always_pos =
-                    force < 0 || sh.force_pos == 0x7fffffff || !(sh.force_v > -1e30f)
-                        ? -1
-                        : (sh.appended ? (int64_t)sh.kk : (int64_t)sh.force_pos);
+                const int64_t always_pos = sh.always_pos;
                 int64_t p_idx = 0;
                 float cum = 0.0f;
                 bool broke = false;
