@@ -114,6 +114,10 @@ SIGNATURES = {
                                                      ctypes.c_int32, ctypes.c_int32,
                                                      ctypes.c_int32, ctypes.c_int32,
                                                      ctypes.c_float, _f32p]),
+    "s2d_op_gqa_decode_attention_noalloc": (ctypes.c_int32, [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

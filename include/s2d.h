@@ -199,6 +199,29 @@ int32_t s2d_op_gqa_decode_attention(S2dHandle *h, const float *query, const floa
                                     int32_t head_count_kv, int32_t head_dim,
                                     int32_t token_count, float attn_scale, float *out);
 
+/* Allocation-free variant of s2d_op_gqa_decode_attention.  It has no
+ * counterpart in the reference.  For callers that cannot call cudaMalloc: a
+ * real-time audio thread must not block in the CUDA allocator, and a host that
+ * gives this library a fixed memory budget owns every device allocation.
+ * query (head_count*head_dim), keys and values (head-major
+ * [head_count_kv][token_count][head_dim]) and out (head_count*head_dim) are
+ * the caller's DEVICE buffers, f32.  The split-K scratch is a fixed device
+ * array inside the library: 512 KiB of partials plus 64 counters, held by
+ * every GPU that loads the library until the process exits.  Calls needing
+ * more (head_count * splits * (head_dim+2) > 131072 floats, with
+ * splits = clamp(token_count/8, 1, 16), or head_count_kv > 64) are rejected
+ * with S2D_EINVAL.  The first call on a device looks the array's device
+ * address up (cudaGetSymbolAddress) and should come before any stream capture
+ * on that device.  All calls share the array, so calls that overlap on the
+ * GPU race.  The call is enqueued on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream) and returns after that stream has finished it.
+ * Errors are written into err. */
+int32_t s2d_op_gqa_decode_attention_noalloc(const float *query, const float *keys,
+                                            const float *values, int32_t head_count,
+                                            int32_t head_count_kv, int32_t head_dim,
+                                            int32_t token_count, float attn_scale, float *out,
+                                            void *stream, char *err, size_t err_cap);
+
 #ifdef __cplusplus
 }
 #endif
