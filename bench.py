@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--workload", default="C2")
     ap.add_argument("--frames", type=int, default=None, help="override frames per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-profile", action="store_true")
+    ap.add_argument("--prompt-len", type=int, default=None,
+                    help="override the prompt length (profiling runs only)")
     ap.add_argument("--model-dir", default=None, help="GGUF cache (default: synth.default_model_dir())")
     return ap.parse_args()
 
@@ -224,7 +227,9 @@ def run_ours(args, d: Dist):
     from fish_s2pro_b200 import (FastArWeights, GenerateParams, PromptTensor, SeededRng,
                                  SlowArState, build, generate_codes)
     build.build_runtime()
-    wl = configs.WORKLOADS[args.workload]
+    wl = {**configs.WORKLOADS, **configs.PROFILING}[args.workload]
+    if args.prompt_len:
+        wl = configs.Workload(wl.model, args.prompt_len, wl.frames, wl.prompt_seed, wl.im_end_id)
     frames = args.frames or wl.frames
     m = wl.model
     path = ensure_model(d, wl, args.model_dir)
@@ -247,7 +252,7 @@ def run_ours(args, d: Dist):
         one(i)
     # dominant kernel, timed live on the resident weights
     kern = {}
-    for name in ("w13", "wqkv", "wo", "w2", "lm_head"):
+    for name in (() if args.no_kernel_profile else ("w13", "wqkv", "wo", "w2", "lm_head")):
         ms, nb = st.profile_kernel(name, iters=144)
         kern[name] = {"ms": ms, "bytes": nb, "gbs": nb / ms / 1e6}
     clocks = Clocks(d.local)
@@ -270,7 +275,7 @@ def run_ours(args, d: Dist):
     value = frames_total / decode_s
     e2e = frames_total / wall
     pk = peaks()
-    top = kern["w13"]
+    top = kern.get("w13", {"ms": float("nan"), "bytes": 0.0, "gbs": float("nan")})
     bpf = configs.weight_bytes_per_frame(m)
     p_avg = wl.prompt_len + frames / 2
     frame_bytes = sum(bpf.values()) + configs.kv_bytes_per_position(m) * p_avg

@@ -123,6 +123,12 @@ C5 = Workload(s2pro(seed=4, linear_type=GGML_Q4_K), prompt_len=8192, frames=256,
 
 WORKLOADS = {"C1": C1, "C2": C2, "C3": C3, "C4": C4, "C5": C5}
 
+# Profiling case: C2's layer shapes with 4 Slow-AR and 1 Fast-AR layers (about
+# 2 GB on the device), small enough for full ncu captures of C2's kernels.
+C2S = Workload(s2pro(seed=1, slow_layers=4, fast_layers=1), prompt_len=64, frames=4,
+               prompt_seed=1, im_end_id=S2PRO_IM_END)
+PROFILING = {"C2S": C2S}
+
 
 def weight_bytes_per_frame(m: ModelConfig) -> dict:
     """Algorithmic HBM bytes of one batch-1 frame, excluding the KV term:
