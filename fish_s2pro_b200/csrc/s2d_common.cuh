@@ -43,21 +43,21 @@ __device__ __forceinline__ float warp_max(float v) {
 // crates/fish_s2_infer/src/tensor.rs:266-287, for every non-NaN input).
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
+// The f16 in the low / high half of a 32-bit word, as f32 (value operations
+// only, so the packed word never has to live in addressable memory).
+__device__ __forceinline__ float h_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+__device__ __forceinline__ float h_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
 // 8 f16 weights (one uint4) dotted with 8 f32 activations.
 __device__ __forceinline__ float dot8(const uint4 w, const float4 a, const float4 b, float acc) {
-    const __half2 *h = reinterpret_cast<const __half2 *>(&w);
-    float2 f0 = __half22float2(h[0]);
-    float2 f1 = __half22float2(h[1]);
-    float2 f2 = __half22float2(h[2]);
-    float2 f3 = __half22float2(h[3]);
-    acc = fmaf(f0.x, a.x, acc);
-    acc = fmaf(f0.y, a.y, acc);
-    acc = fmaf(f1.x, a.z, acc);
-    acc = fmaf(f1.y, a.w, acc);
-    acc = fmaf(f2.x, b.x, acc);
-    acc = fmaf(f2.y, b.y, acc);
-    acc = fmaf(f3.x, b.z, acc);
-    acc = fmaf(f3.y, b.w, acc);
+    acc = fmaf(h_lo(w.x), a.x, acc);
+    acc = fmaf(h_hi(w.x), a.y, acc);
+    acc = fmaf(h_lo(w.y), a.z, acc);
+    acc = fmaf(h_hi(w.y), a.w, acc);
+    acc = fmaf(h_lo(w.z), b.x, acc);
+    acc = fmaf(h_hi(w.z), b.y, acc);
+    acc = fmaf(h_lo(w.w), b.z, acc);
+    acc = fmaf(h_hi(w.w), b.w, acc);
     return acc;
 }
 

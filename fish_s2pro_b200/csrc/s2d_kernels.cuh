@@ -121,6 +121,128 @@ struct SampleArgs {
     uint32_t *out_token;    // optional result copy
 };
 
+// ---- persistent layer engine (s2d_engine.cu) -------------------------------
+
+enum EngineOpKind { OP_GEMV = 0, OP_ATTN = 1 };
+
+// One step of the engine's program.  A GEMV op reads its input vector(s) and
+// writes its outputs like gemv_kernel (GemvArgs fields); an ATTN op fuses
+// rope_kv_kernel and attn_kernel (RopeArgs / AttnArgs fields).
+struct EngineOp {
+    int kind, epi, M;
+    // GEMV
+    const uint16_t *W, *W2;
+    const float *x;
+    int ldx;
+    const float *norm_w;
+    float eps;
+    float *y;
+    int ldy;
+    const float *resid;
+    int ldr;
+    float *x_out;
+    int K, N;
+    int row_base, n_contig, extra_row;
+    // ATTN
+    const float *qkv;
+    int ld_qkv;
+    void *kcache, *vcache;
+    int max_seq, kv_half;
+    const float *q_norm, *k_norm, *rope_denom;
+    const int32_t *pos_dev;
+    int pos_const;
+    int H, Hkv, hd, S;
+    float scale;
+    float *att_out;
+    float *part;
+    int32_t *counters;
+    // GEMV weights in the engine's slot order (engine_relayout): the slot
+    // of row tile [tr0, tr0 + R) and K slice s starts at element
+    // Wt + tr0 * K * mats + s * R * kt * mats and holds [mat][R][kw].
+    const uint16_t *Wt;
+};
+
+struct EngineArgs {
+    const EngineOp *ops;
+    int n_ops;
+    int nslots, slot_bytes;            // shared-memory weight ring
+    int area_bytes;                    // staged inputs / attention tiles (multiple of 128)
+    uint32_t *barrier;                 // grid-barrier counter, zero at launch
+    const int32_t *done;               // DevState::done or nullptr
+    int32_t *error;                    // DevState::error
+    // Optional timeline (nullptr: off).  CTAs 0 and gridDim-1 record
+    // %globaltimer at each op: [cta][op][0] barrier passed, [1] input staged,
+    // [2] op finished by the consumers, [3] producer issued the op's last slot.
+    unsigned long long *trace;
+};
+
+constexpr int kEngineConsumerWarps = 8;
+constexpr int kEngineThreads = (kEngineConsumerWarps + 1) * 32;
+constexpr int kEngineSlotBytes = 24576;  // default ring slot size
+constexpr int kEngineSmemMax = 230400;  // dynamic smem, under the 227 KiB opt-in limit
+constexpr int kEngineTileRows = 32;      // output rows of one GEMV row tile
+constexpr int kEngineMaxSlots = 64;
+constexpr int kEngineBarrierBytes = 1024; // full + empty mbarriers of up to 64 slots
+constexpr int kEngineMaxK = 10240;        // longest GEMV input the consumers stage
+
+// Rows [*r0, *r1) of an N-row linear owned by CTA c of G.
+__host__ __device__ __forceinline__ void engine_cta_rows(int N, int c, int G, int *r0, int *r1) {
+    *r0 = (int)(((long long)N * c) / G);
+    *r1 = (int)(((long long)N * (c + 1)) / G);
+}
+
+// K-slice geometry of a GEMV: slices of kt columns (512 / mats, so that a
+// slice row is 64 / mats 16-byte chunks, two or one per consumer lane), the
+// last one possibly shorter, and row tiles of at most rmax rows so that a
+// slot of mats * rmax * kt f16 fits slot_bytes.
+struct SliceGeom {
+    int kt, nk, rmax;
+};
+__host__ __device__ inline SliceGeom engine_slice_geom(int mats, int K, int slot_bytes) {
+    SliceGeom g;
+    g.kt = 512 / mats < K ? 512 / mats : K;
+    g.nk = (K + g.kt - 1) / g.kt;
+    g.rmax = slot_bytes / (mats * g.kt * 2);
+    if (g.rmax > kEngineTileRows) g.rmax = kEngineTileRows;
+    if (g.rmax < 1) g.rmax = 1;
+    return g;
+}
+
+// Row tiles of a CTA's n rows: ceil(n / rmax) tiles of near-equal size; tile
+// t covers rows [*a, *b) relative to the CTA's first row.
+__host__ __device__ __forceinline__ int engine_tile_count(int n, int rmax) { return (n + rmax - 1) / rmax; }
+__host__ __device__ __forceinline__ void engine_tile_rows(int n, int t, int ntiles, int *a, int *b) {
+    *a = (int)(((long long)n * t) / ntiles);
+    *b = (int)(((long long)n * (t + 1)) / ntiles);
+}
+
+// Error codes the engine writes into DevState::error.
+constexpr int kErrEngineWeights = 16;  // a weight-ring wait ran out
+constexpr int kErrEngineGrid = 17;     // a grid-barrier wait ran out
+constexpr int kErrEngineAlign = 18;    // the shared-memory ring is not 128-byte aligned
+
+cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s);
+
+// Copies a linear's weights into the engine's slot order for a `grid`-CTA
+// launch with ring slots of slot_bytes: dst holds N * K * mats f16.  Output
+// row r reads source row (n_contig < 0 ? r : r < n_contig ? row_base + r :
+// extra_row) of W and row r of W2 (when W2 is not null).
+cudaError_t launch_engine_relayout(const uint16_t *W, const uint16_t *W2, int N, int K, int n_contig,
+                                   int row_base, int extra_row, int grid, int slot_bytes, uint16_t *dst,
+                                   cudaStream_t s);
+
+// Shared-memory bytes of one attention group of the engine: its warps' query
+// vectors, then up to kAttnCap cached K rows and V rows, each padded by 16
+// bytes so that lanes reading different rows hit different banks.
+constexpr int kAttnCap = 32;
+__host__ __device__ __forceinline__ int attn_row_bytes(int hd, int kvb) { return hd * kvb + 16; }
+__host__ __device__ __forceinline__ int attn_cap(int max_seq) {
+    return max_seq < kAttnCap ? max_seq : kAttnCap;
+}
+__host__ __device__ __forceinline__ int attn_group_bytes(int rep, int hd, int kvb, int max_seq) {
+    return (rep * hd * 4 + 2 * attn_cap(max_seq) * attn_row_bytes(hd, kvb) + 15) / 16 * 16;
+}
+
 constexpr int kSampleMax = 8192;
 constexpr int kSampleThreads = 1024;
 constexpr int kGemvThreads = 256;

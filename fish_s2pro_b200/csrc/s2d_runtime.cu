@@ -13,7 +13,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
 #include <memory>
+#include <tuple>
 #include <string>
 #include <vector>
 
@@ -44,6 +46,14 @@ struct ArShape {
     int qs() const { return H * hd; }
     int kvs() const { return Hkv * hd; }
     int qkv_out() const { return qs() + 2 * kvs(); }
+};
+
+// A program of the persistent layer engine (s2d_engine.cu), resident in HBM.
+struct EngineProgram {
+    EngineOp *ops = nullptr;
+    int n_ops = 0;
+    int nslots = 0, area_bytes = 0;
+    size_t smem = 0;
 };
 
 struct GenKey {
@@ -96,6 +106,17 @@ struct S2dHandle {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
     bool pdl = true;
     uint32_t launches = 0;  // kernels enqueued through this handle
+    // persistent layer engine
+    bool use_engine = true;
+    int num_sms = 0;
+    uint32_t *engine_bar = nullptr;
+    std::vector<EngineProgram> fast_progs;  // index = codebook being produced (1..K-1)
+    // engine weight copies in slot order, keyed by (W, W2, N, K, n_contig, row_base, extra_row)
+    std::map<std::tuple<const uint16_t *, const uint16_t *, int, int, int, int, int>, uint16_t *> tiled;
+    size_t tiled_bytes = 0;
+    int slot_bytes = kEngineSlotBytes;  // engine ring slot size (S2D_SLOT_KB)
+    EngineProgram slow_prog;
+    uint32_t slow_prog_im_end = 0xffffffffu;
 };
 
 namespace {
@@ -404,7 +425,8 @@ int32_t alloc_buffers(S2dHandle *h) {
     CK(cudaMalloc(&h->logits, (size_t)s.vocab_size * sizeof(float)));
     CK(cudaMalloc(&h->logits_fast, (size_t)std::max(s.codebook_size, kSampleMax) * sizeof(float)));
     // attention split count: ~64 positions per split at full context
-    h->S_slow = std::min(128, std::max(8, (maxseq + 63) / 64));
+    // attention splits: enough items to cover the SMs, ~32 positions per split at full context
+    h->S_slow = std::min(128, std::max(32, (maxseq + 31) / 32));
     h->S_fast = 1;
     const int H = std::max(a.H, f.H), hd = std::max(a.hd, f.hd), Hkv = std::max(a.Hkv, f.Hkv);
     CK(cudaMalloc(&h->part, (size_t)kMaxM * H * h->S_slow * (hd + 2) * sizeof(float)));
@@ -600,8 +622,198 @@ cudaError_t enqueue_fast_frame(S2dHandle *h, const GenKey &k, bool with_override
     return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------
+// persistent layer engine programs
+// ---------------------------------------------------------------------------
+
+// Whether the engine supports this model's shapes (else the per-op kernels run).
+bool engine_supported(const S2dHandle *h) {
+    for (const ArShape *a : {&h->slow, &h->fast}) {
+        const int rep = a->H / a->Hkv;
+        if (rep > kEngineConsumerWarps || kEngineConsumerWarps % rep || (a->hd != 64 && a->hd != 128)) return false;
+        if (a->d % 8 || a->qs() % 8 || a->F % 8) return false;
+        if (a->d > kEngineMaxK || a->qs() > kEngineMaxK || a->F > kEngineMaxK) return false;  // staged inputs
+    }
+    return h->num_sms > 0;
+}
+
+EngineOp gemv_op(int M, int epi, const uint16_t *W, const uint16_t *W2, const float *x, int ldx,
+                 const float *norm_w, float eps, float *y, int ldy, const float *resid, int K, int N) {
+    EngineOp o{};
+    o.kind = OP_GEMV, o.epi = epi, o.M = M, o.W = W, o.W2 = W2, o.x = x, o.ldx = ldx;
+    o.norm_w = norm_w, o.eps = eps, o.y = y, o.ldy = ldy, o.resid = resid, o.ldr = ldy;
+    o.K = K, o.N = N, o.n_contig = -1;
+    return o;
+}
+
+// The ops of one transformer layer over M tokens at rows x[0..M) (see
+// enqueue_layer for the per-op kernel version).
+void layer_ops(S2dHandle *h, bool is_fast, int l, float *x, int M, const int32_t *pos_dev,
+               int pos_const, std::vector<EngineOp> &ops) {
+    const ArShape &a = is_fast ? h->fast : h->slow;
+    const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
+    const int d = a.d;
+    ops.push_back(gemv_op(M, EPI_STORE, L.wqkv, nullptr, x, d, L.attn_norm, a.eps, h->qkv, a.qkv_out(),
+                          nullptr, d, a.qkv_out()));
+    EngineOp t{};
+    t.kind = OP_ATTN, t.M = M, t.qkv = h->qkv, t.ld_qkv = a.qkv_out();
+    if (is_fast) {
+        float *base = h->kv_fast + (size_t)l * 2 * a.Hkv * a.ctx * a.hd;
+        t.kcache = base, t.vcache = base + (size_t)a.Hkv * a.ctx * a.hd, t.max_seq = a.ctx, t.kv_half = 0;
+        t.rope_denom = h->rope_fast, t.S = h->S_fast;
+    } else {
+        __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
+        t.kcache = base, t.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd;
+        t.max_seq = h->cfg.max_seq, t.kv_half = 1;
+        t.q_norm = L.q_norm, t.k_norm = L.k_norm, t.rope_denom = h->rope_slow, t.S = h->S_slow;
+    }
+    t.eps = a.eps, t.pos_dev = pos_dev, t.pos_const = pos_const;
+    t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd, t.scale = 1.0f / sqrtf((float)a.hd);
+    t.att_out = h->att, t.part = h->part, t.counters = h->counters;
+    ops.push_back(t);
+    ops.push_back(gemv_op(M, EPI_RESID, L.wo, nullptr, h->att, a.qs(), nullptr, 0.f, x, d, x, a.qs(), d));
+    ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, x, d, L.ffn_norm, a.eps,
+                          h->act, a.F, nullptr, d, a.F));
+    ops.push_back(gemv_op(M, EPI_RESID, L.w2, nullptr, h->act, a.F, nullptr, 0.f, x, d, x, a.F, d));
+}
+
+// The weights of a GEMV op in the engine's slot order (engine_relayout),
+// built once per (matrices, row mapping) and kept for the handle's lifetime.
+int32_t tiled_weights(S2dHandle *h, EngineOp &o) {
+    const auto key = std::make_tuple(o.W, o.W2, o.N, o.K, o.n_contig, o.n_contig >= 0 ? o.row_base : 0,
+                                     o.n_contig >= 0 ? o.extra_row : 0);
+    auto it = h->tiled.find(key);
+    if (it == h->tiled.end()) {
+        uint16_t *dst = nullptr;
+        const size_t n = (size_t)o.N * o.K * (o.W2 ? 2 : 1);
+        CK(cudaMalloc(&dst, n * sizeof(uint16_t)));
+        it = h->tiled.emplace(key, dst).first;
+        CK(launch_engine_relayout(o.W, o.W2, o.N, o.K, o.n_contig, o.row_base, o.extra_row, h->num_sms,
+                                  h->slot_bytes, dst, h->stream));
+        h->tiled_bytes += n * sizeof(uint16_t);
+    }
+    o.Wt = it->second;
+    return S2D_OK;
+}
+
+int32_t upload_program(S2dHandle *h, const std::vector<EngineOp> &ops_in, EngineProgram *p) {
+    if (p->ops) cudaFree(p->ops);
+    p->ops = nullptr;
+    std::vector<EngineOp> ops = ops_in;
+    int ab = 0;  // shared area: a GEMV's staged inputs or an attention op's tiles
+    for (EngineOp &o : ops) {
+        if (o.kind == OP_GEMV) {
+            ab = std::max(ab, o.M * o.K * 4);
+            const int32_t rc = tiled_weights(h, o);
+            if (rc) return rc;
+        } else {
+            ab = std::max(ab, (kEngineConsumerWarps / (o.H / o.Hkv)) *
+                                  attn_group_bytes(o.H / o.Hkv, o.hd, o.kv_half ? 2 : 4, o.max_seq));
+        }
+    }
+    ab = (ab + 127) / 128 * 128;
+    const int ns = (int)std::min<long>(kEngineMaxSlots,
+                                       ((long)kEngineSmemMax - kEngineBarrierBytes - ab) / h->slot_bytes);
+    if (ns < 2) return set_err(h, S2D_EINVAL, "engine: inputs too large for shared memory");
+    CK(cudaMalloc(&p->ops, ops.size() * sizeof(EngineOp)));
+    CK(cudaMemcpy(p->ops, ops.data(), ops.size() * sizeof(EngineOp), cudaMemcpyHostToDevice));
+    p->n_ops = (int)ops.size();
+    p->area_bytes = ab;
+    p->nslots = ns;
+    p->smem = (size_t)kEngineBarrierBytes + (size_t)ab + (size_t)ns * h->slot_bytes;
+    if (p->smem > (size_t)kEngineSmemMax) return set_err(h, S2D_EINVAL, "engine: shared memory layout too large");
+    return S2D_OK;
+}
+
+// Fast-AR pass programs (codebook 1..K-1) and the Slow-AR step program.
+int32_t build_programs(S2dHandle *h, uint32_t im_end) {
+    const S2dGraphSpec &s = h->spec;
+    const int d = s.hidden, K = s.num_codebooks;
+    int32_t rc;
+    if (h->fast_progs.empty()) {
+        h->fast_progs.resize((size_t)std::max(K, 1));
+        for (int cbk = 1; cbk < K; ++cbk) {
+            const int p0 = cbk == 1 ? 0 : cbk, M = cbk == 1 ? 2 : 1;
+            std::vector<EngineOp> ops;
+            for (int l = 0; l < h->fast.L; ++l) layer_ops(h, true, l, h->fast_x + (size_t)p0 * d, M, nullptr, p0, ops);
+            ops.push_back(gemv_op(1, EPI_STORE, h->fast_out, nullptr, h->fast_x + (size_t)cbk * d, d, h->fast_norm,
+                                  h->fast.eps, h->logits_fast, s.codebook_size, nullptr, d, s.codebook_size));
+            if ((rc = upload_program(h, ops, &h->fast_progs[(size_t)cbk]))) return rc;
+        }
+    }
+    if (!h->slow_prog.ops || h->slow_prog_im_end != im_end) {
+        std::vector<EngineOp> ops;
+        for (int l = 0; l < h->slow.L; ++l) layer_ops(h, false, l, h->x, 1, &h->st->n_past, 0, ops);
+        const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+        const bool extra = (int64_t)im_end < s.vocab_size &&
+                           ((int)im_end < s.semantic_begin_id || (int)im_end > s.semantic_end_id);
+        EngineOp head = gemv_op(1, EPI_STORE, h->emb, nullptr, h->x, d, h->norm, h->slow.eps, h->logits,
+                                s.vocab_size, nullptr, d, nsem + (extra ? 1 : 0));
+        head.row_base = s.semantic_begin_id, head.n_contig = nsem;
+        head.extra_row = extra ? (int)im_end : s.semantic_begin_id;
+        head.x_out = h->hidden_post;
+        ops.push_back(head);
+        if ((rc = upload_program(h, ops, &h->slow_prog))) return rc;
+        h->slow_prog_im_end = im_end;
+        h->n_allowed_extra = extra ? 1 : 0;
+    }
+    return S2D_OK;
+}
+
+cudaError_t enqueue_engine(S2dHandle *h, const EngineProgram &p) {
+    cudaError_t e = cudaMemsetAsync(h->engine_bar, 0, sizeof(uint32_t), h->stream);
+    if (e) return e;
+    EngineArgs a{};
+    a.ops = p.ops, a.n_ops = p.n_ops, a.nslots = p.nslots, a.slot_bytes = h->slot_bytes;
+    a.area_bytes = p.area_bytes, a.barrier = h->engine_bar, a.done = &h->st->done, a.error = &h->st->error;
+    h->launches += 1;
+    return launch_engine(a, h->num_sms, p.smem, h->stream);
+}
+
+// One frame with the persistent engine: 9 Fast-AR pass programs and one
+// Slow-AR step program, with the samplers and the embedding between them.
+cudaError_t enqueue_frame_engine(S2dHandle *h, const GenKey &k) {
+    const S2dGraphSpec &s = h->spec;
+    const int d = s.hidden, K = s.num_codebooks;
+    const int32_t *done = &h->st->done;
+    cudaError_t e;
+    FastInitArgs fi{};
+    fi.st = h->st, fi.slow_hidden = h->hidden_post, fi.fast_emb = h->fast_emb, fi.fast_x = h->fast_x;
+    fi.frame_codes = h->frame_codes, fi.codes_out = h->codes_out;
+    fi.max_new = (int)k.max_new, fi.d = d, fi.cb_size = s.codebook_size;
+    fi.sem_begin = (uint32_t)s.semantic_begin_id, fi.sem_end = (uint32_t)s.semantic_end_id;
+    h->launches += 1;
+    if ((e = launch_fast_init(fi, h->stream, false))) return e;
+    for (int cbk = 1; cbk < K; ++cbk) {
+        if ((e = enqueue_engine(h, h->fast_progs[(size_t)cbk]))) return e;
+        SampleArgs a{};
+        a.logits = h->logits_fast, a.n = s.codebook_size, a.n_contig = -1, a.vocab_full = s.codebook_size;
+        a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
+        a.mode = SAMPLE_FAST, a.max_new = (int)k.max_new, a.st = h->st, a.rng = &h->st->rng;
+        a.cb_index = cbk, a.frame_codes = h->frame_codes, a.codes_out = h->codes_out;
+        a.fast_emb = h->fast_emb, a.fast_x_next = cbk + 1 < K ? h->fast_x + (size_t)(cbk + 1) * d : nullptr;
+        a.d = d, a.out_token = h->tok_out;
+        h->launches += 1;
+        if ((e = launch_sample(a, h->stream, false))) return e;
+    }
+    EmbedArgs ea{};
+    ea.tokens = nullptr, ea.st = h->st, ea.frame_codes = h->frame_codes;
+    ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = s.hidden, ea.K = s.num_codebooks;
+    ea.cb_size = s.codebook_size, ea.vocab = s.vocab_size, ea.cb_rows = s.codebook_rows;
+    ea.sem_begin = (uint32_t)s.semantic_begin_id, ea.sem_end = (uint32_t)s.semantic_end_id;
+    ea.scale_on = 1, ea.sem_scale = 1.0f / sqrtf((float)(s.num_codebooks + 1));
+    ea.out = h->x, ea.M = 1, ea.done = done, ea.error = &h->st->error;
+    h->launches += 1;
+    if ((e = launch_embed(ea, h->stream, false))) return e;
+    if ((e = enqueue_engine(h, h->slow_prog))) return e;
+    SampleArgs a = slow_sample_args(h, SAMPLE_SLOW_STEP, k);
+    h->launches += 1;
+    return launch_sample(a, h->stream, false);
+}
+
 // One full frame (the loop body of generate_codes, generate.rs:165-211).
 cudaError_t enqueue_frame(S2dHandle *h, const GenKey &k) {
+    if (h->use_engine) return enqueue_frame_engine(h, k);
     const S2dGraphSpec &s = h->spec;
     const int32_t *done = &h->st->done;
     cudaError_t e;
@@ -720,9 +932,12 @@ void free_handle(S2dHandle *h) {
     void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
                     h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
                     h->logits_fast, h->part, h->counters, h->st, h->tokens_dev, h->frame_codes,
-                    h->codes_out, h->tok_out, h->code_override};
+                    h->codes_out, h->tok_out, h->code_override, h->engine_bar, h->slow_prog.ops};
     for (void *p : bufs)
         if (p) cudaFree(p);
+    for (EngineProgram &p : h->fast_progs)
+        if (p.ops) cudaFree(p.ops);
+    for (auto &kv : h->tiled) cudaFree(kv.second);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
     if (h->ev2) cudaEventDestroy(h->ev2);
@@ -781,6 +996,21 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
     if ((rc = upload_all(h))) return report(h, rc);
     if ((rc = bind_weights(h))) return report(h, rc);
     if ((rc = alloc_buffers(h))) return report(h, rc);
+    {
+        int coop = 0;
+        cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->device);
+        if ((ce = cudaMalloc(&h->engine_bar, sizeof(uint32_t)))) {
+            h->err = std::string("cudaMalloc: ") + cudaGetErrorString(ce);
+            return report(h, S2D_ECUDA);
+        }
+        const char *env = getenv("S2D_ENGINE");
+        h->use_engine = coop && engine_supported(h) && !(env && env[0] == '0');
+        if (const char *kb = getenv("S2D_SLOT_KB")) {
+            const int v = atoi(kb);
+            if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
+        }
+    }
     if ((ce = cudaStreamSynchronize(h->stream))) {
         h->err = std::string("CUDA: ") + cudaGetErrorString(ce);
         return report(h, S2D_ECUDA);
@@ -960,6 +1190,7 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
 
     // frames (generate.rs:165-211): one captured graph per frame
     if (!h->frame_exec || !(h->frame_key == k)) {
+        if (h->use_engine && (rc = build_programs(h, k.im_end))) return rc;
         if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
         h->frame_exec = nullptr;
         cudaGraph_t graph = nullptr;
@@ -1101,6 +1332,42 @@ int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *
     CK(cudaEventElapsedTime(&ms, h->ev0, h->ev1));
     *avg_ms = ms / iters;
     return S2D_OK;
+}
+
+int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64_t trace_cap,
+                           int32_t *n_ops, double *ms) {
+    if (!h || !n_ops || !ms) return S2D_EINVAL;
+    if (!h->use_engine) return set_err(h, S2D_ESTATE, "the persistent engine is not in use");
+    CK(cudaSetDevice(h->device));
+    int32_t rc = build_programs(h, h->slow_prog.ops ? h->slow_prog_im_end : 0xffffffffu);
+    if (rc) return rc;
+    if (program < 0 || program >= (int)h->fast_progs.size()) return set_err(h, S2D_EINVAL, "no such program");
+    const EngineProgram &p = program == 0 ? h->slow_prog : h->fast_progs[(size_t)program];
+    if (!p.ops) return set_err(h, S2D_EINVAL, "no such program");
+    *n_ops = p.n_ops;
+    unsigned long long *dtr = nullptr;
+    const size_t need = (size_t)p.n_ops * 8;
+    if (trace) {
+        if ((int64_t)need > trace_cap) return set_err(h, S2D_EINVAL, "trace buffer too small");
+        CK(cudaMalloc(&dtr, need * sizeof(unsigned long long)));
+        CK(cudaMemsetAsync(dtr, 0, need * sizeof(unsigned long long), h->stream));
+    }
+    EngineArgs a{};
+    a.ops = p.ops, a.n_ops = p.n_ops, a.nslots = p.nslots, a.slot_bytes = h->slot_bytes;
+    a.area_bytes = p.area_bytes, a.barrier = h->engine_bar, a.done = nullptr, a.error = &h->st->error;
+    a.trace = dtr;
+    cudaError_t e = cudaMemsetAsync(h->engine_bar, 0, sizeof(uint32_t), h->stream);
+    if (!e) e = cudaEventRecord(h->ev0, h->stream);
+    if (!e) e = launch_engine(a, h->num_sms, p.smem, h->stream);
+    if (!e) e = cudaEventRecord(h->ev1, h->stream);
+    if (!e) e = cudaEventSynchronize(h->ev1);
+    float t = 0.f;
+    if (!e) e = cudaEventElapsedTime(&t, h->ev0, h->ev1);
+    if (!e && trace) e = cudaMemcpy(trace, dtr, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    if (dtr) cudaFree(dtr);
+    if (e) return set_err(h, S2D_ECUDA, std::string("profile_engine: ") + cudaGetErrorString(e));
+    *ms = t;
+    return check_device_error(h);
 }
 
 // ---- op-level seam -------------------------------------------------------

@@ -106,6 +106,8 @@ SIGNATURES = {
                                             ctypes.c_int64]),
     "s2d_profile_kernel": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                             _P(ctypes.c_double), _P(ctypes.c_double)]),
+    "s2d_profile_engine": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _u64p, ctypes.c_int64,
+                                            _i32p, _P(ctypes.c_double)]),
     "s2d_op_linear_f16": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _u16p, ctypes.c_int64,
                                            ctypes.c_int64, _f32p]),
     "s2d_op_rms_norm": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _f32p, ctypes.c_int64,
@@ -342,6 +344,19 @@ class SlowArState:
         self._check(lib().s2d_profile_kernel(self.handle, self.KERNELS[kernel], iters,
                                              ctypes.byref(ms), ctypes.byref(nb)))
         return float(ms.value), float(nb.value)
+
+    def profile_engine(self, program: int = 0, trace: bool = True):
+        """Run one persistent-engine program once (s2d_profile_engine).
+        Returns (ms, trace) with trace shaped [2 CTAs][n_ops][4] in ns."""
+        n = ctypes.c_int32()
+        ms = ctypes.c_double()
+        buf = np.zeros(8 * 4096, dtype=np.uint64) if trace else None
+        self._check(lib().s2d_profile_engine(self.handle, program,
+                                             _ptr(buf, ctypes.c_uint64) if trace else None,
+                                             buf.size if trace else 0, ctypes.byref(n),
+                                             ctypes.byref(ms)))
+        tr = buf[: n.value * 8].reshape(2, n.value, 4) if trace else None
+        return float(ms.value), tr
 
     def dequant_tensor(self, name: str, count: int) -> np.ndarray:
         out = np.empty(count, dtype=np.float32)
