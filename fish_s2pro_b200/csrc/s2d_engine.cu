@@ -12,11 +12,11 @@
 // every linear, in program order, into a ring of shared-memory slots with
 // cp.async.bulk and mbarrier completion.  Weights do not depend on
 // activations, so the producer runs ahead across op and layer boundaries,
-// limited only by the ring, and HBM stays busy while the consumers wait at a
-// grid barrier or run attention.  Warps 0-7 consume: for each op they wait at
-// a grid barrier for the previous op's outputs, stage the input vector (with
-// its RMSNorm) in shared memory, then every warp reads every slot, each warp
-// owning a few rows of the slot (see GemvTiling).
+// limited only by the ring, and HBM stays busy while the consumers wait for
+// inputs or run attention.  Warps 0-7 consume: for each op they poll its
+// input words (LL words, see EngineOp) until the producing op's tag appears,
+// stage the input vector (with its RMSNorm) in shared memory, then every
+// warp reads every slot, each warp owning a few rows of it (see GemvTiling).
 // Every wait is bounded: on timeout the kernel records an error code in
 // DevState::error and returns.
 #include <math.h>
@@ -31,7 +31,6 @@ namespace {
 // Bounds of every wait (about a second each): a healthy launch never comes
 // close; a broken one records an error and returns instead of hanging.
 constexpr uint32_t kMbarSpin = 1u << 20;   // try_wait rounds of <= 1 us each
-constexpr uint32_t kGridSpin = 1u << 22;   // grid-barrier polls with a short sleep
 
 __device__ __forceinline__ uint32_t saddr(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -72,11 +71,6 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // Wait for `parity` of an mbarrier, giving up (and flagging `code`) after a
 // bounded number of rounds or when another CTA has already flagged an error.
@@ -141,46 +135,191 @@ struct GemvTiling {
     }
 };
 
+// Attention splits of an ATTN op (shared by the consumers, which run the
+// items, and the producer, which streams their cache rows): one split per
+// kAttnSplitLen positions of the longest visible context, at most
+// kAttnMaxSplits and op.S, and few enough that every item has its own group
+// (split 0 waits for the others).
+constexpr int kAttnSplitLen = 32;
+constexpr int kAttnMaxSplits = 32;
+__device__ __forceinline__ int attn_splits(const EngineOp &op, int pos_base, int groups) {
+    int S = (min(pos_base + op.M, op.max_seq) + kAttnSplitLen - 1) / kAttnSplitLen;
+    S = min(min(S, kAttnMaxSplits), min(op.S, groups / (op.M * op.Hkv)));
+    return S < 1 ? 1 : S;
+}
+// Positions [*t0, *t1) of split sp of token m's visible context.
+__device__ __forceinline__ void attn_range(const EngineOp &op, int pos_base, int m, int sp, int S, int *t0, int *t1) {
+    const int visible = min(pos_base + m + 1, op.max_seq);
+    const int chunk = (visible + S - 1) / S;
+    *t0 = min(visible, sp * chunk);
+    *t1 = min(visible, *t0 + chunk);
+}
+__device__ __forceinline__ int attn_pos_base(const EngineOp &op) {
+    return op.pos_const + (op.pos_dev ? *reinterpret_cast<const volatile int32_t *>(op.pos_dev) : 0);
+}
+// First RoPE row a side block holds: the new positions, clamped to the table.
+__device__ __forceinline__ int attn_rope_r0(const EngineOp &op, int pos_base) { return min(pos_base, op.max_seq - 1); }
+
+// The ring slots of an ATTN op on this CTA: `rounds` rounds of one slot per
+// group (gpc groups), round k of a group carrying positions
+// [t0 + k * P, t0 + (k + 1) * P) of its item's range.
+struct AttnPlan {
+    int rep = 1, gpc = 1, kvb = 2, P = 1, S = 1, n_items = 0, rounds = 0, pos_base = 0;
+    __device__ void init(const EngineOp &op, int slot_bytes) {
+        rep = op.H / op.Hkv, gpc = kEngineConsumerWarps / rep, kvb = op.kv_half ? 2 : 4;
+        P = attn_slot_rows(op.hd, kvb, slot_bytes);
+        pos_base = attn_pos_base(op);
+        S = attn_splits(op, pos_base, gridDim.x * gpc);
+        n_items = op.M * op.Hkv * S;
+        const int vmax = min(pos_base + op.M, op.max_seq), chunk = (vmax + S - 1) / S;
+        rounds = max(1, (chunk + P - 1) / P);
+    }
+    __device__ int slots() const { return rounds * gpc; }
+};
+
+// One slot's bulk copies, in fixed places (a zero size: no copy), so that
+// the producer keeps them in registers: a weight slot uses copy 0; an
+// attention slot K rows (0), V rows (1), RoPE rows (2), Q gains (3) and K
+// gains (4).
+struct SlotCopies {
+    const void *src[5];
+    uint32_t off[5], bytes[5];
+    __device__ __forceinline__ void clear() {
+#pragma unroll
+        for (int q = 0; q < 5; ++q) src[q] = nullptr, off[q] = 0, bytes[q] = 0;
+    }
+    __device__ __forceinline__ uint32_t total() const {
+        uint32_t t = 0;
+#pragma unroll
+        for (int q = 0; q < 5; ++q) t += bytes[q];
+        return t;
+    }
+};
+
+// The copies of slot j (round j / gpc, group j % gpc) of an ATTN op.
+__device__ void attn_slot(const EngineOp &op, const AttnPlan &pl, int j, SlotCopies &c) {
+    const int k = j / pl.gpc, gg = j % pl.gpc, item = gg * gridDim.x + blockIdx.x;
+    if (item >= pl.n_items) return;
+    const int sp = item % pl.S, kvh = (item / pl.S) % op.Hkv, m = item / (pl.S * op.Hkv);
+    int t0, t1;
+    attn_range(op, pl.pos_base, m, sp, pl.S, &t0, &t1);
+    const int hd = op.hd, rowb = hd * pl.kvb, tile = attn_tile_bytes(pl.P, hd, pl.kvb);
+    const int c0 = t0 + k * pl.P, nc = min(min(t1, c0 + pl.P), pl.pos_base) - c0;
+    if (nc > 0) {
+        const size_t off = ((size_t)kvh * op.max_seq + c0) * rowb;
+        c.src[0] = reinterpret_cast<const uint8_t *>(op.kcache) + off, c.off[0] = 0, c.bytes[0] = (uint32_t)(nc * rowb);
+        c.src[1] = reinterpret_cast<const uint8_t *>(op.vcache) + off, c.off[1] = (uint32_t)tile;
+        c.bytes[1] = (uint32_t)(nc * rowb);
+    }
+    if (k == 0) {
+        const int r0 = attn_rope_r0(op, pl.pos_base), nr = min(op.M, op.max_seq - r0);
+        c.src[2] = op.rope_cs + (size_t)r0 * (hd >> 1), c.off[2] = (uint32_t)(2 * tile);
+        c.bytes[2] = (uint32_t)(nr * (hd >> 1) * 8);
+        if (op.q_norm) c.src[3] = op.q_norm, c.off[3] = (uint32_t)(2 * tile + 8 * hd), c.bytes[3] = (uint32_t)(hd * 4);
+        if (op.k_norm) c.src[4] = op.k_norm, c.off[4] = (uint32_t)(2 * tile + 12 * hd), c.bytes[4] = (uint32_t)(hd * 4);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // producer: lane 0 of the last warp
 // ---------------------------------------------------------------------------
 
-__device__ void producer(const EngineArgs &a, uint64_t *full, uint64_t *empty, uint8_t *ring) {
-    const int NS = a.nslots;
-    uint32_t g = 0;  // slots issued
-    int slot = 0;
-    uint32_t phase = 0;
-    for (int i = 0; i < a.n_ops; ++i) {
-        const EngineOp &op = a.ops[i];
-        if (op.kind != OP_GEMV) continue;
-        const GemvTiling T(op, a.slot_bytes);
-        const int K = T.K, mats = T.mats;
-        const SliceGeom sg = T.sg;
-        for (int t = 0; t < T.ntiles; ++t) {
-            int tr0, R;
-            T.tile(t, &tr0, &R);
-            const uint16_t *src = op.Wt + (size_t)tr0 * K * mats;
-            for (int s = 0; s < sg.nk; ++s, ++g) {
-                const int kw = min(sg.kt, K - s * sg.kt);
-                if (!mbar_wait(&empty[slot], phase ^ 1u, a.error, kErrEngineWeights)) goto drain;
-                const uint32_t bytes = (uint32_t)(mats * R * kw * 2);
-                mbar_arrive_expect_tx(&full[slot], bytes);
-                bulk_copy(ring + (size_t)slot * a.slot_bytes, src + (size_t)s * R * sg.kt * mats, bytes, &full[slot]);
-                if (++slot == NS) slot = 0, phase ^= 1u;
+// Walks this CTA's ring slots in program order: the weight slots of GEMV
+// ops and the cache-row slots of ATTN ops.
+struct SlotIter {
+    int i = -1, t = 0, s = 0;  // op, tile (ATTN: slot), slice of the next slot
+    bool attn = false;
+    int r0 = 0, n = 0, ntiles = 0, mats = 1, K = 0, tr0 = 0, R = 0;
+    SliceGeom sg{};
+    const uint16_t *Wt = nullptr;
+    AttnPlan *pl = nullptr;
+    __device__ void set_tile() {
+        int a0, b0;
+        engine_tile_rows(n, t, ntiles, &a0, &b0);
+        tr0 = r0 + a0, R = b0 - a0;
+    }
+    // Fills c with the next slot's copies and returns its op; -1 at the end.
+    __device__ int next(const EngineArgs &a, SlotCopies &c, AttnPlan &plan) {
+        for (;;) {
+            if (t < ntiles) {
+                const int opi = i;
+                c.clear();
+                if (attn) {
+                    attn_slot(a.ops[i], plan, t, c);
+                    ++t;
+                } else {
+                    const int kw = min(sg.kt, K - s * sg.kt);
+                    c.src[0] = Wt + (size_t)tr0 * K * mats + (size_t)s * R * sg.kt * mats;
+                    c.bytes[0] = (uint32_t)(mats * R * kw * 2);
+                    if (++s == sg.nk) {
+                        s = 0;
+                        if (++t < ntiles) set_tile();
+                    }
+                }
+                return opi;
+            }
+            if (++i >= a.n_ops) return -1;
+            const EngineOp &op = a.ops[i];
+            t = s = 0;
+            attn = op.kind != OP_GEMV;
+            if (attn) {
+                plan.init(op, a.slot_bytes);
+                ntiles = plan.slots();
+            } else {
+                const GemvTiling T(op, a.slot_bytes);
+                r0 = T.r0, n = T.n, ntiles = T.ntiles, mats = T.mats, K = T.K, sg = T.sg, Wt = op.Wt;
+                if (ntiles) set_tile();
             }
         }
-        if (a.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))
-            a.trace[((size_t)(blockIdx.x ? 1 : 0) * a.n_ops + i) * 4 + 3] = globaltimer();
     }
-drain:
+};
+
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ void producer(const EngineArgs &a, uint64_t *full, uint64_t *empty, uint8_t *ring) {
+    const int NS = a.nslots;
+    uint32_t g = 0;   // slots issued
+    uint32_t pf = 0;  // slots the prefetch cursor has passed
+    int slot = 0;
+    uint32_t phase = 0;
+    SlotIter cur, ahead;
+    AttnPlan cur_plan, ahead_plan;
+    SlotCopies c, pc;
+    for (;;) {
+        const int opi = cur.next(a, c, cur_plan);
+        if (opi < 0) break;
+        // keep the L2 prefetch cursor l2_lead slots ahead of the ring
+        while (a.l2_lead > 0 && pf <= g + (uint32_t)a.l2_lead) {
+            if (ahead.next(a, pc, ahead_plan) < 0) {
+                pf = 0xffffffffu;
+                break;
+            }
+            if (pf > g) {
+#pragma unroll
+                for (int q = 0; q < 5; ++q)
+                    if (pc.bytes[q]) prefetch_l2(pc.src[q], pc.bytes[q]);
+            }
+            ++pf;
+        }
+        if (!mbar_wait(&empty[slot], phase ^ 1u, a.error, kErrEngineWeights)) break;
+        uint8_t *dst = ring + (size_t)slot * a.slot_bytes;
+        mbar_arrive_expect_tx(&full[slot], c.total());  // 0 bytes: the phase completes here
+#pragma unroll
+        for (int q = 0; q < 5; ++q)
+            if (c.bytes[q]) bulk_copy(dst + c.off[q], c.src[q], c.bytes[q], &full[slot]);
+        ++g;
+        if (++slot == NS) slot = 0, phase ^= 1u;
+        if (a.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))
+            a.trace[((size_t)(blockIdx.x ? 1 : 0) * a.n_ops + opi) * 4 + 3] = globaltimer();
+    }
     // Do not leave the CTA while copies may still be landing in it: wait
     // (bounded, also after an error) for the last ring's worth of copies.
-    {
-        const uint32_t first = g > (uint32_t)NS ? g - (uint32_t)NS : 0u;
-        for (uint32_t q = first; q < g; ++q) {
-            const int slot = (int)(q % (uint32_t)NS);
-            if (!mbar_wait(&full[slot], (q / (uint32_t)NS) & 1u, a.error, kErrEngineWeights, false)) return;
-        }
+    const uint32_t first = g > (uint32_t)NS ? g - (uint32_t)NS : 0u;
+    for (uint32_t q = first; q < g; ++q) {
+        const int sl = (int)(q % (uint32_t)NS);
+        if (!mbar_wait(&full[sl], (q / (uint32_t)NS) & 1u, a.error, kErrEngineWeights, false)) return;
     }
 }
 
@@ -216,44 +355,151 @@ __global__ void relayout_kernel(const uint16_t *W, const uint16_t *W2, int N, in
 // consumers: warps 0-7
 // ---------------------------------------------------------------------------
 
+constexpr uint32_t kPollSpin = 1u << 21;  // polls of one LL word (an L2 round trip each)
+
 struct ConsumerShared {
     float red[2][kEngineConsumerWarps];
-    int ok;
-    int abort;  // a consumer warp's wait failed: all warps leave at the next barrier
-    int last[kEngineConsumerWarps];
+    uint32_t epoch;
+    int abort;  // a consumer wait failed: all warps leave after the current op
 };
+
+__device__ __forceinline__ unsigned long long ll_word(float v, uint32_t tag) {
+    return ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+}
+__device__ __forceinline__ void ll_store(uint64_t *p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load(const uint64_t *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ ulonglong2 ll_load2(const uint64_t *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool ll_fresh(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+__device__ __forceinline__ float ll_value(unsigned long long w) { return __uint_as_float((uint32_t)w); }
+
+// Wait until the N words w[i] = *addr(i) (addr(i) == nullptr: no word) carry
+// `tag`.  Words start as 0 (tag 0 is never used), so the first pass issues
+// every load at once and later passes re-read only the stale ones.  Bounded:
+// on timeout kErrEngineWait is flagged; when another CTA has flagged an
+// error the wait gives up; either way it returns false.
+template <int N, class Addr>
+__device__ __forceinline__ bool ll_wait(unsigned long long (&w)[N], Addr addr, uint32_t tag, int32_t *err) {
+    for (uint32_t spin = 0;; ++spin) {
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint64_t *p = addr(i);
+            if (p && !ll_fresh(w[i], tag)) {
+                all = false;
+                w[i] = ll_load(p);
+            }
+        }
+        if (all) return true;
+        if ((spin & 255u) == 255u && ld_volatile(err)) return false;
+        if (spin >= kPollSpin) {
+            atomicCAS(err, 0, kErrEngineWait);
+            return false;
+        }
+    }
+}
+template <int N, class Addr>
+__device__ __forceinline__ bool ll_wait2(ulonglong2 (&w)[N], Addr addr, uint32_t tag, int32_t *err) {
+    for (uint32_t spin = 0;; ++spin) {
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint64_t *p = addr(i);
+            if (p && !(ll_fresh(w[i].x, tag) && ll_fresh(w[i].y, tag))) {
+                all = false;
+                w[i] = ll_load2(p);
+            }
+        }
+        if (all) return true;
+        if ((spin & 255u) == 255u && ld_volatile(err)) return false;
+        if (spin >= kPollSpin) {
+            atomicCAS(err, 0, kErrEngineWait);
+            return false;
+        }
+    }
+}
+
+// One input value of an op: a float written before the launch (src < 0) or
+// an LL word of op src.
+__device__ __forceinline__ bool read_input(const void *base, size_t idx, int src, uint32_t epoch, float &v,
+                                           int32_t *err) {
+    if (src < 0) {
+        v = __ldcg(reinterpret_cast<const float *>(base) + idx);
+        return true;
+    }
+    const uint64_t *p = reinterpret_cast<const uint64_t *>(base) + idx;
+    unsigned long long w[1] = {0ull};
+    const bool ok = ll_wait(w, [&](int) { return p; }, engine_tag(epoch, src), err);
+    v = ll_value(w[0]);
+    return ok;
+}
 
 // Stage the op's M input vectors in shared memory as xs[m][K], normalised
 // when the op has an RMSNorm prologue; CTA 0 also writes them to x_out.
+// Returns false (for every thread) when an input wait failed.
 template <int M>
-__device__ void stage_x(const EngineOp &op, float *xs, ConsumerShared &cs) {
+__device__ bool stage_x(const EngineOp &op, float *xs, ConsumerShared &cs, int32_t *err) {
     constexpr int T = kEngineConsumerWarps * 32;
-    constexpr int J = kEngineMaxK / (T * 4);  // float4 per thread and token
-    static_assert(J * T * 4 == kEngineMaxK, "K bound");
+    constexpr int B = 8;  // 16-byte chunks in flight per thread
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = op.K, C = K >> 2;
+    const int K = op.K;
     float ss[M];
+    bool ok = true;
 #pragma unroll
     for (int m = 0; m < M; ++m) {
-        const float4 *src = reinterpret_cast<const float4 *>(op.x + (size_t)m * op.ldx);
-        float4 *dst = reinterpret_cast<float4 *>(xs + (size_t)m * K);
-        float4 v[J];
-#pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const int c = tid + j * T;
-            v[j] = c < C ? __ldcg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
         ss[m] = 0.f;
+        float *dst = xs + (size_t)m * K;
+        if (op.x_src < 0) {
+            const float4 *src = reinterpret_cast<const float4 *>(op.x) + (size_t)m * (op.ldx >> 2);
+            for (int c0 = tid; c0 < (K >> 2); c0 += B * T) {
+                float4 v[B];
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-            const int c = tid + j * T;
-            if (c < C) dst[c] = v[j];
-            ss[m] = fmaf(v[j].x, v[j].x, ss[m]);
-            ss[m] = fmaf(v[j].y, v[j].y, ss[m]);
-            ss[m] = fmaf(v[j].z, v[j].z, ss[m]);
-            ss[m] = fmaf(v[j].w, v[j].w, ss[m]);
+                for (int b = 0; b < B; ++b) {
+                    const int c = c0 + b * T;
+                    v[b] = c < (K >> 2) ? __ldcg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const int c = c0 + b * T;
+                    if (c < (K >> 2)) reinterpret_cast<float4 *>(dst)[c] = v[b];
+                    ss[m] = fmaf(v[b].x, v[b].x, ss[m]);
+                    ss[m] = fmaf(v[b].y, v[b].y, ss[m]);
+                    ss[m] = fmaf(v[b].z, v[b].z, ss[m]);
+                    ss[m] = fmaf(v[b].w, v[b].w, ss[m]);
+                }
+            }
+        } else {
+            const uint32_t tag = engine_tag(cs.epoch, op.x_src);
+            const uint64_t *src = reinterpret_cast<const uint64_t *>(op.x) + (size_t)m * op.ldx;
+            for (int c0 = tid; c0 < (K >> 1); c0 += B * T) {
+                ulonglong2 v[B];
+#pragma unroll
+                for (int b = 0; b < B; ++b) v[b] = make_ulonglong2(0ull, 0ull);
+                ok = ll_wait2(v, [&](int b) { return c0 + b * T < (K >> 1) ? src + 2 * (c0 + b * T) : nullptr; },
+                              tag, err) && ok;
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const int c = c0 + b * T;
+                    if (c < (K >> 1)) {
+                        const float f0 = ll_value(v[b].x), f1 = ll_value(v[b].y);
+                        reinterpret_cast<float2 *>(dst)[c] = make_float2(f0, f1);
+                        ss[m] = fmaf(f0, f0, ss[m]);
+                        ss[m] = fmaf(f1, f1, ss[m]);
+                    }
+                }
+            }
         }
     }
+    if (!ok) cs.abort = 1;
     float *x_out = blockIdx.x == 0 ? op.x_out : nullptr;
     if (op.norm_w) {
 #pragma unroll
@@ -270,7 +516,7 @@ __device__ void stage_x(const EngineOp &op, float *xs, ConsumerShared &cs) {
             for (int k = 0; k < kEngineConsumerWarps; ++k) t += cs.red[m][k];
             const float scale = 1.0f / sqrtf(t / (float)K + op.eps);
             float4 *row = reinterpret_cast<float4 *>(xs + (size_t)m * K);
-            for (int c = tid; c < C; c += T) {  // the elements this thread stored
+            for (int c = tid; c < (K >> 2); c += T) {
                 float4 v = row[c];
                 const float4 g = __ldg(nw + c);
                 v.x = __fmul_rn(__fmul_rn(v.x, scale), g.x);
@@ -281,13 +527,18 @@ __device__ void stage_x(const EngineOp &op, float *xs, ConsumerShared &cs) {
                 if (x_out) reinterpret_cast<float4 *>(x_out + (size_t)m * K)[c] = v;
             }
         }
-    } else if (x_out) {
+    } else {
+        consumers_sync();
+        if (x_out) {
 #pragma unroll
-        for (int m = 0; m < M; ++m)
-            for (int c = tid; c < C; c += T)
-                reinterpret_cast<float4 *>(x_out + (size_t)m * K)[c] = reinterpret_cast<const float4 *>(xs + (size_t)m * K)[c];
+            for (int m = 0; m < M; ++m)
+                for (int c = tid; c < (K >> 2); c += T)
+                    reinterpret_cast<float4 *>(x_out + (size_t)m * K)[c] =
+                        reinterpret_cast<const float4 *>(xs + (size_t)m * K)[c];
+        }
     }
     consumers_sync();  // xs is complete; cs.red may be rewritten by the next op
+    return !cs.abort;
 }
 
 __device__ __forceinline__ uint4 lds_u4(uint32_t addr) {
@@ -344,19 +595,22 @@ __device__ __forceinline__ void gemv_slot(uint32_t wbase, uint32_t rstride, uint
 // takes every slot: per 16-byte column chunk a lane loads the inputs once
 // and the chunk of each of its warp's rows.
 template <int M, int MATS>
-__device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, uint32_t &g, uint64_t *full,
-                             uint64_t *empty, const uint8_t *ring, const float *xs) {
+__device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch, uint32_t &g,
+                             uint64_t *full, uint64_t *empty, const uint8_t *ring, const float *xs) {
     constexpr int CH = 2 / MATS;  // chunks per lane and step: a slice row has 64 / MATS chunks
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int NS = a.nslots;
     const GemvTiling T(op, a.slot_bytes);
     const SliceGeom sg = T.sg;
-    const int K = T.K, epi = op.epi, ldy = op.ldy, ldr = op.ldr;
-    float *y = op.y;
-    const float *resid = op.resid;
+    const int K = T.K, epi = op.epi, ldy = op.ldy, ldr = op.ldr, resid_src = op.resid_src;
+    const bool y_ll = op.y_ll != 0;
+    void *y = op.y;
+    const void *resid = op.resid;
+    const uint32_t out_tag = engine_tag(epoch, opi);
     const uint32_t ring_s = saddr(ring), xs_s = saddr(xs), slot_bytes = (uint32_t)a.slot_bytes;
     int slot = (int)(g % (uint32_t)NS);
     uint32_t phase = (g / (uint32_t)NS) & 1u;
+    bool ok = true;
     for (int t = 0; t < T.ntiles; ++t) {
         int tr0, R;
         T.tile(t, &tr0, &R);
@@ -398,10 +652,10 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, uint32_t &
             for (int q = 0; q < MATS; ++q)
 #pragma unroll
                 for (int m = 0; m < M; ++m) {
-                    float t = acc[0][i][q][m];
+                    float s = acc[0][i][q][m];
 #pragma unroll
-                    for (int j = 1; j < CH; ++j) t += acc[j][i][q][m];
-                    v[q][m] = warp_sum(t);
+                    for (int j = 1; j < CH; ++j) s += acc[j][i][q][m];
+                    v[q][m] = warp_sum(s);
                 }
 #pragma unroll
             for (int m = 0; m < M; ++m) {
@@ -412,27 +666,30 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, uint32_t &
                 if (epi == EPI_STORE) {
                     out = g1;
                 } else if (epi == EPI_RESID) {
-                    out = __fadd_rn(__ldcg(resid + (size_t)m * ldr + row), g1);
+                    float r;
+                    ok = read_input(resid, (size_t)m * ldr + row, resid_src, epoch, r, a.error) && ok;
+                    out = __fadd_rn(r, g1);
                 } else if (epi == EPI_SWIGLU_SLOW) {
                     const float sig = 1.0f / (1.0f + expf(-g1));
                     out = __fmul_rn(__fmul_rn(g1, sig), g3);
                 } else {
                     out = __fmul_rn(g1 / (1.0f + expf(-g1)), g3);
                 }
-                y[(size_t)m * ldy + row] = out;
+                if (y_ll) ll_store(reinterpret_cast<uint64_t *>(y) + (size_t)m * ldy + row, out, out_tag);
+                else reinterpret_cast<float *>(y)[(size_t)m * ldy + row] = out;
             }
         }
     }
-    return true;
+    return ok;
 }
 
 template <int M>
-__device__ bool run_gemv(const EngineArgs &a, const EngineOp &op, uint32_t &g, uint64_t *full, uint64_t *empty,
-                         const uint8_t *ring, float *xs, ConsumerShared &cs, unsigned long long *tr) {
-    stage_x<M>(op, xs, cs);
+__device__ bool run_gemv(const EngineArgs &a, const EngineOp &op, int opi, uint32_t &g, uint64_t *full,
+                         uint64_t *empty, const uint8_t *ring, float *xs, ConsumerShared &cs, unsigned long long *tr) {
+    if (!stage_x<M>(op, xs, cs, a.error)) return false;
     if (tr) tr[1] = globaltimer();
-    return op.W2 ? consume_gemv<M, 2>(a, op, g, full, empty, ring, xs)
-                 : consume_gemv<M, 1>(a, op, g, full, empty, ring, xs);
+    return op.W2 ? consume_gemv<M, 2>(a, op, opi, cs.epoch, g, full, empty, ring, xs)
+                 : consume_gemv<M, 1>(a, op, opi, cs.epoch, g, full, empty, ring, xs);
 }
 
 template <typename KV>
@@ -444,31 +701,39 @@ __device__ __forceinline__ float kv_from<float>(float v) { return v; }
 __device__ __forceinline__ float kv_to(__half v) { return __half2float(v); }
 __device__ __forceinline__ float kv_to(float v) { return v; }
 
-// QK-norm (optional) + RoPE of one head held as EPL values per lane.
+// This lane's QK-norm gains and RoPE (cos, sin) pairs of one head, from the
+// group's side block in shared memory.
 template <int EPL>
-__device__ __forceinline__ void norm_rope(float *v, const float *nw, float eps, int hd, int pos,
-                                          const float *denom) {
-    const int lane = threadIdx.x & 31;
-    if (nw) {
-        float ss = 0.f;
+struct RopeNorm {
+    float g[EPL];
+    float2 cs[EPL / 2];
+    __device__ __forceinline__ void load(const float *gains, const float2 *rope_row) {
+        const int lane = threadIdx.x & 31;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
-        ss = warp_sum(ss);
-        const float scale = 1.0f / sqrtf(ss / (float)hd + eps);
+        for (int e = 0; e < EPL; ++e) g[e] = gains[lane * EPL + e];
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], scale), nw[lane * EPL + e]);
+        for (int e = 0; e < EPL; e += 2) cs[e / 2] = rope_row[(lane * EPL + e) >> 1];
     }
+    // QK-norm (when `norm`) + RoPE of one head held as EPL values per lane
+    __device__ __forceinline__ void apply(float *v, bool norm, float eps, int hd) const {
+        if (norm) {
+            float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < EPL; e += 2) {
-        const int pair = lane * EPL + e;
-        const float theta = (float)pos / denom[pair >> 1];
-        float sn, cs;
-        sincosf(theta, &sn, &cs);
-        const float x0 = v[e], x1 = v[e + 1];
-        v[e] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-        v[e + 1] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+            for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
+            ss = warp_sum(ss);
+            const float scale = 1.0f / sqrtf(ss / (float)hd + eps);
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) v[e] = __fmul_rn(__fmul_rn(v[e], scale), g[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) {
+            const float2 r = cs[e / 2];
+            const float x0 = v[e], x1 = v[e + 1];
+            v[e] = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
+            v[e + 1] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
+        }
     }
-}
+};
 
 template <typename KV>
 __device__ __forceinline__ float4 kv_load4(const uint8_t *p, int i);  // elements 4i..4i+3
@@ -482,223 +747,262 @@ __device__ __forceinline__ float4 kv_load4<float>(const uint8_t *p, int i) {
     return reinterpret_cast<const float4 *>(p)[i];
 }
 
-// Fused QK-norm + RoPE + KV write + split-K GQA attention (the ops of
+
+
+// This lane's EPL elements (lane * EPL ...) of a K or V row, as floats.
+template <typename KV, int EPL>
+__device__ __forceinline__ void kv_load_lane(const uint8_t *row, float (&v)[EPL]) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (EPL % 4 == 0) {
+#pragma unroll
+        for (int e = 0; e < EPL; e += 4) {
+            const float4 f = kv_load4<KV>(row, (lane * EPL + e) >> 2);
+            v[e] = f.x, v[e + 1] = f.y, v[e + 2] = f.z, v[e + 3] = f.w;
+        }
+    } else {
+        const KV *r = reinterpret_cast<const KV *>(row) + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) v[e] = kv_to(r[e]);
+    }
+}
+
+// Fused QK-norm + RoPE + KV write + split GQA attention (the ops of
 // rope_kv_kernel and attn_kernel).  Work items are (token, kv head, split);
 // a group of `rep` warps (one per query head of the GQA group) takes one
-// item.  Per sub-chunk of at most kAttnCap positions the group copies the
-// cached K/V rows into shared memory in one cooperative round trip and adds
-// the rows of the new tokens (recomputed from qkv, so no group reads a
-// position another group is still writing); scores are then computed with
-// one lane per position, P.V with each lane owning head dims.  The group of
-// split 0 writes its token's K/V to the cache.  The last group to finish a
-// (token, kv head) merges the S partial softmaxes.
-constexpr int kAttnSplitLen = 64;  // visible positions per attention split
-constexpr int kAttnLoads = 4;      // 16-byte cache loads per thread in flight
-
+// item.  Cached K/V rows stream through one or two shared-memory buffers of
+// kAttnRows rows with cp.async, the next sub-chunk's copies in flight while
+// the current one is scored; the new tokens' rows are rebuilt from the QKV
+// words, so no group reads a position another group is still writing.  The
+// group holding a token's own position writes it to the cache.  With S > 1
+// splits, split 0 merges the other splits' partials (LL words).
+// Fused QK-norm + RoPE + KV write + split GQA attention (the ops of
+// rope_kv_kernel and attn_kernel).  Work items are (token, kv head, split);
+// a group of `rep` warps (one per query head of the GQA group) takes one
+// item.  The item's cached K/V rows arrive through the weight ring (see
+// AttnPlan), round by round; every consumer warp waits on every slot, in
+// order, and the owning group reads it.  The new tokens' rows are rebuilt
+// from the QKV words, so no group reads a position another group is still
+// writing; the group holding a token's own position writes it to the cache.
+// With S > 1 splits, split 0 merges the other splits' partials (LL words).
 template <typename KV, int EPL>
-__device__ void consume_attn(const EngineOp &op, float *xs, ConsumerShared &cs) {
+__device__ bool consume_attn(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch, uint8_t *area,
+                             uint32_t g, uint64_t *full, uint64_t *empty, const uint8_t *ring,
+                             unsigned long long *tr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hd = op.hd, rep = op.H / op.Hkv, M = op.M;
-    const int gpc = kEngineConsumerWarps / rep;  // groups per CTA
-    const int gid = warp / rep, wr = warp % rep, gtid = wr * 32 + lane;
+    const int hd = op.hd, M = op.M;
+    AttnPlan pl;
+    pl.init(op, a.slot_bytes);
+    const int rep = pl.rep, gid = warp / rep, wr = warp % rep, gtid = wr * 32 + lane;
     const int bar_id = 2 + gid, bar_n = rep * 32;
     constexpr int kvb = (int)sizeof(KV);
-    const int cap = attn_cap(op.max_seq), rowb = attn_row_bytes(hd, kvb);
-    uint8_t *gbase = reinterpret_cast<uint8_t *>(xs) + (size_t)gid * attn_group_bytes(rep, hd, kvb, op.max_seq);
+    const int rowb = hd * kvb, tile = attn_tile_bytes(pl.P, hd, kvb);
+    uint8_t *gbase = area + (size_t)gid * attn_group_bytes(rep, hd, kvb);
     float *qsm = reinterpret_cast<float *>(gbase) + wr * hd;
-    uint8_t *kc = gbase + rep * hd * 4;
-    uint8_t *vc = kc + (size_t)cap * rowb;
-    const int pos_base = op.pos_const + (op.pos_dev ? __ldcg(op.pos_dev) : 0);
-    // splits of the visible positions: one per kAttnSplitLen of the longest
-    // token's context, at most the S that the partial buffers hold
-    int S = (min(pos_base + M, op.max_seq) + kAttnSplitLen - 1) / kAttnSplitLen;
-    S = S < 1 ? 1 : (S > op.S ? op.S : S);
-    const int n_items = M * op.Hkv * S;
-    const int units = hd * kvb / 16;  // 16-byte units per row
-    for (int item = blockIdx.x * gpc + gid; item < n_items; item += gridDim.x * gpc) {
-        const int sp = item % S, kvh = (item / S) % op.Hkv, m = item / (S * op.Hkv);
-        const int pos = pos_base + m;
-        const KV *kbase = reinterpret_cast<const KV *>(op.kcache) + (size_t)kvh * op.max_seq * hd;
-        const KV *vbase = reinterpret_cast<const KV *>(op.vcache) + (size_t)kvh * op.max_seq * hd;
-        // the query of this warp's head, normalised and rotated, into shared memory
-        const int h = kvh * rep + wr;
-        {
-            float q[EPL];
-            const float *qrow = op.qkv + (size_t)m * op.ld_qkv + h * hd + lane * EPL;
+    KV *newk = reinterpret_cast<KV *>(gbase + rep * hd * 4);  // [2][hd]
+    KV *newv = newk + 2 * hd;
+    const int pos_base = pl.pos_base, rope_r0 = attn_rope_r0(op, pos_base), S = pl.S;
+    const uint32_t in_tag = engine_tag(epoch, op.qkv_src), out_tag = engine_tag(epoch, opi);
+    const int NS = a.nslots;
+    int slot = (int)(g % (uint32_t)NS);
+    uint32_t phase = (g / (uint32_t)NS) & 1u;
+    const int item = gid * gridDim.x + blockIdx.x;  // CTA-major: items spread over the SMs first
+    const bool has = item < pl.n_items;
+    const int sp = has ? item % S : 0, kvh = has ? (item / S) % op.Hkv : 0, m = has ? item / (S * op.Hkv) : 0;
+    const int pos = pos_base + m, h = kvh * rep + wr;
+    int t0 = 0, t1 = 0;
+    if (has) attn_range(op, pos_base, m, sp, S, &t0, &t1);
+    KV *kbase = reinterpret_cast<KV *>(op.kcache) + (size_t)kvh * op.max_seq * hd;
+    KV *vbase = reinterpret_cast<KV *>(op.vcache) + (size_t)kvh * op.max_seq * hd;
+    bool ok = true;
+    float mrun = -INFINITY, l = 0.f, acc[EPL];
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) q[e] = __ldcg(qrow + e);
-            norm_rope<EPL>(q, op.q_norm, op.eps, hd, pos, op.rope_denom);
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int k = 0; k < pl.rounds; ++k) {
+        for (int gg = 0; gg < pl.gpc; ++gg) {
+            const bool got = mbar_wait(&full[slot], phase, a.error, kErrEngineWeights);
+            if (!__all_sync(0xffffffffu, got)) return false;
+            if (gg == gid && has) {
+                const uint8_t *sb = ring + (size_t)slot * a.slot_bytes;
+                if (k == 0) {
+                    // the side block: RoPE rows of the new positions, QK-norm gains
+                    const float2 *rope = reinterpret_cast<const float2 *>(sb + 2 * tile);
+                    const float *qn = reinterpret_cast<const float *>(sb + 2 * tile + 8 * hd), *kn = qn + hd;
+                    {
+                        RopeNorm<EPL> rn;
+                        rn.load(qn, rope + (size_t)(min(pos, op.max_seq - 1) - rope_r0) * (hd >> 1));
+                        float q[EPL];
+                        const uint64_t *qp = op.qkv + (size_t)m * op.ld_qkv + h * hd + lane * EPL;
+                        unsigned long long w[EPL];
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) qsm[lane * EPL + e] = q[e];
-        }
-        // split 0 stores this token's K/V in the cache
-        if (sp == 0 && wr == 0 && pos < op.max_seq) {
-            const float *row = op.qkv + (size_t)m * op.ld_qkv;
-            float kf[EPL];
+                        for (int e = 0; e < EPL; ++e) w[e] = 0ull;
+                        ok = ll_wait(w, [&](int e) { return qp + e; }, in_tag, a.error) && ok;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) kf[e] = __ldcg(row + (op.H + kvh) * hd + lane * EPL + e);
-            norm_rope<EPL>(kf, op.k_norm, op.eps, hd, pos, op.rope_denom);
-            KV *kd = const_cast<KV *>(kbase) + (size_t)pos * hd + lane * EPL;
-            KV *vd = const_cast<KV *>(vbase) + (size_t)pos * hd + lane * EPL;
+                        for (int e = 0; e < EPL; ++e) q[e] = ll_value(w[e]);
+                        rn.apply(q, op.q_norm != nullptr, op.eps, hd);
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                kd[e] = kv_from<KV>(kf[e]);
-                vd[e] = kv_from<KV>(__ldcg(row + (op.H + op.Hkv + kvh) * hd + lane * EPL + e));
-            }
-        }
-        int visible = pos + 1;
-        if (visible > op.max_seq) visible = op.max_seq;
-        const int chunk = (visible + S - 1) / S;
-        const int t0 = sp * chunk, t1 = min(visible, t0 + chunk);
-        float mrun = -INFINITY, l = 0.f, acc[EPL];
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-        for (int c0 = t0; c0 < t1; c0 += cap) {
-            const int c1 = min(t1, c0 + cap), n = c1 - c0;
-            group_sync(bar_id, bar_n);  // previous sub-chunk's readers are done; qsm is written
-            // cached rows [c0, min(c1, pos_base)) -> shared memory, all loads issued together
-            const int ncache = max(0, min(c1, pos_base) - c0);
-            const int total = 2 * ncache * units;
-            for (int u0 = 0; u0 < total; u0 += kAttnLoads * bar_n) {
-                uint4 v[kAttnLoads];
-#pragma unroll
-                for (int k = 0; k < kAttnLoads; ++k) {
-                    const int u = u0 + k * bar_n + gtid;
-                    if (u < total) {
-                        const int which = u >= ncache * units, r = (u % (ncache * units)) / units, c = u % units;
-                        const uint8_t *src = reinterpret_cast<const uint8_t *>(which ? vbase : kbase) +
-                                             ((size_t)(c0 + r) * hd) * kvb + (size_t)c * 16;
-                        v[k] = __ldcg(reinterpret_cast<const uint4 *>(src));
+                        for (int e = 0; e < EPL; ++e) qsm[lane * EPL + e] = q[e];
                     }
-                }
+                    // the new tokens' K/V rows this item sees, rebuilt by warp
+                    // 0; the row of the item's own position also goes to the cache
+                    if (wr == 0) {
+                        for (int mm = 0; mm < M; ++mm) {
+                            const int t = pos_base + mm;
+                            if (t < t0 || t >= t1) continue;
+                            RopeNorm<EPL> rn;
+                            rn.load(kn, rope + (size_t)(t - rope_r0) * (hd >> 1));
+                            const uint64_t *kp = op.qkv + (size_t)mm * op.ld_qkv + (op.H + kvh) * hd + lane * EPL;
+                            const uint64_t *vp = kp + (size_t)op.Hkv * hd;
+                            unsigned long long w[2 * EPL];
 #pragma unroll
-                for (int k = 0; k < kAttnLoads; ++k) {
-                    const int u = u0 + k * bar_n + gtid;
-                    if (u < total) {
-                        const int which = u >= ncache * units, r = (u % (ncache * units)) / units, c = u % units;
-                        *reinterpret_cast<uint4 *>((which ? vc : kc) + (size_t)r * rowb + (size_t)c * 16) = v[k];
+                            for (int e = 0; e < 2 * EPL; ++e) w[e] = 0ull;
+                            ok = ll_wait(w, [&](int e) { return e < EPL ? kp + e : vp + (e - EPL); }, in_tag,
+                                         a.error) && ok;
+                            float kf[EPL], vf[EPL];
+#pragma unroll
+                            for (int e = 0; e < EPL; ++e) kf[e] = ll_value(w[e]), vf[e] = ll_value(w[EPL + e]);
+                            rn.apply(kf, op.k_norm != nullptr, op.eps, hd);
+                            KV *kd = newk + mm * hd + lane * EPL, *vd = newv + mm * hd + lane * EPL;
+#pragma unroll
+                            for (int e = 0; e < EPL; ++e) kd[e] = kv_from<KV>(kf[e]), vd[e] = kv_from<KV>(vf[e]);
+                            if (t == pos) {
+                                KV *kc = kbase + (size_t)t * hd + lane * EPL, *vc = vbase + (size_t)t * hd + lane * EPL;
+#pragma unroll
+                                for (int e = 0; e < EPL; ++e) kc[e] = kd[e], vc[e] = vd[e];
+                            }
+                        }
                     }
+                    group_sync(bar_id, bar_n);  // qsm and the new rows are complete
+                    if (tr && gtid == 0) tr[1] = globaltimer();
                 }
-            }
-            // rows of the new tokens [pos_base, pos_base + M) that fall in this sub-chunk
-            if (wr == 0) {
-                for (int t = max(c0, pos_base); t < c1; ++t) {
-                    const int mm = t - pos_base;
-                    const float *row = op.qkv + (size_t)mm * op.ld_qkv;
-                    float kf[EPL];
-#pragma unroll
-                    for (int e = 0; e < EPL; ++e) kf[e] = __ldcg(row + (op.H + kvh) * hd + lane * EPL + e);
-                    norm_rope<EPL>(kf, op.k_norm, op.eps, hd, t, op.rope_denom);
-                    KV *kd = reinterpret_cast<KV *>(kc + (size_t)(t - c0) * rowb) + lane * EPL;
-                    KV *vd = reinterpret_cast<KV *>(vc + (size_t)(t - c0) * rowb) + lane * EPL;
-#pragma unroll
-                    for (int e = 0; e < EPL; ++e) {
-                        kd[e] = kv_from<KV>(kf[e]);
-                        vd[e] = kv_from<KV>(__ldcg(row + (op.H + op.Hkv + kvh) * hd + lane * EPL + e));
+                const int c0 = t0 + k * pl.P, c1 = min(t1, c0 + pl.P), n = max(0, c1 - c0);
+                const uint8_t *kt = sb, *vt = sb + tile;
+                // scores: lane j owns position c0 + j; lanes start at different
+                // 4-element groups of the row so that they hit different banks
+                float sc = -INFINITY;
+                if (lane < n) {
+                    const int t = c0 + lane;
+                    const uint8_t *krow = t < pos_base ? kt + (size_t)lane * rowb
+                                                       : reinterpret_cast<const uint8_t *>(newk + (t - pos_base) * hd);
+                    const float4 *q4 = reinterpret_cast<const float4 *>(qsm);
+                    const int ng = hd / 4;  // a power of two
+                    float d0 = 0.f, d1 = 0.f;
+                    for (int i = 0; i < ng; i += 2) {
+                        const int i0 = (i + lane) & (ng - 1), i1 = (i + 1 + lane) & (ng - 1);
+                        const float4 k0 = kv_load4<KV>(krow, i0), k1 = kv_load4<KV>(krow, i1);
+                        const float4 a0 = q4[i0], a1 = q4[i1];
+                        d0 = fmaf(a0.x, k0.x, d0);
+                        d0 = fmaf(a0.y, k0.y, d0);
+                        d0 = fmaf(a0.z, k0.z, d0);
+                        d0 = fmaf(a0.w, k0.w, d0);
+                        d1 = fmaf(a1.x, k1.x, d1);
+                        d1 = fmaf(a1.y, k1.y, d1);
+                        d1 = fmaf(a1.z, k1.z, d1);
+                        d1 = fmaf(a1.w, k1.w, d1);
                     }
+                    sc = (d0 + d1) * op.scale;
                 }
-            }
-            group_sync(bar_id, bar_n);
-            // scores: lane j owns position c0 + j
-            float sc = -INFINITY;
-            if (lane < n) {
-                const uint8_t *krow = kc + (size_t)lane * rowb;
-                const float4 *q4 = reinterpret_cast<const float4 *>(qsm);
-                float d = 0.f;
-                for (int i = 0; i < hd / 4; ++i) {
-                    const float4 kk = kv_load4<KV>(krow, i), qq = q4[i];
-                    d = fmaf(qq.x, kk.x, d);
-                    d = fmaf(qq.y, kk.y, d);
-                    d = fmaf(qq.z, kk.z, d);
-                    d = fmaf(qq.w, kk.w, d);
-                }
-                sc = d * op.scale;
-            }
-            const float mn = fmaxf(mrun, warp_max(sc));
-            const float corr = expf(mrun - mn);
-            const float p = lane < n ? expf(sc - mn) : 0.f;
-            l = fmaf(l, corr, warp_sum(p));
+                if (n > 0) {
+                    const float mn = fmaxf(mrun, warp_max(sc));
+                    const float corr = expf(mrun - mn);
+                    const float p = lane < n ? expf(sc - mn) : 0.f;
+                    l = fmaf(l, corr, warp_sum(p));
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] *= corr;
-            for (int j = 0; j < n; ++j) {
-                const float pj = __shfl_sync(0xffffffffu, p, j);
-                const KV *vr = reinterpret_cast<const KV *>(vc + (size_t)j * rowb) + lane * EPL;
+                    for (int e = 0; e < EPL; ++e) acc[e] *= corr;
+                    for (int j0 = 0; j0 < n; j0 += 4) {
+                        float pj[4], vv[4][EPL];
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj, kv_to(vr[e]), acc[e]);
-            }
-            mrun = mn;
-        }
-        if (S == 1) {  // one split: the group's softmax is final
-            float *outp = op.att_out + (size_t)m * op.H * hd + h * hd + lane * EPL;
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = j0 + u, t = c0 + j;
+                            pj[u] = __shfl_sync(0xffffffffu, p, j & 31);
+                            const uint8_t *vr = t < pos_base ? vt + (size_t)j * rowb
+                                                             : reinterpret_cast<const uint8_t *>(newv + (t - pos_base) * hd);
+                            if (j < n) {
+                                kv_load_lane<KV, EPL>(vr, vv[u]);
+                            } else {
+                                pj[u] = 0.f;
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) outp[e] = acc[e] / l;
-            continue;
-        }
-        float *pp = op.part + (((size_t)m * op.H + h) * S + sp) * (hd + 2);
-        if (lane == 0) __stcg(pp, mrun), __stcg(pp + 1, l);
+                                for (int e = 0; e < EPL; ++e) vv[u][e] = 0.f;
+                            }
+                        }
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) __stcg(pp + 2 + lane * EPL + e, acc[e]);
-        __threadfence();
-        group_sync(bar_id, bar_n);
-        if (wr == 0 && lane == 0) {
-            const int prev = atomicAdd(&op.counters[m * op.Hkv + kvh], 1);
-            cs.last[gid] = prev == S - 1;
-        }
-        group_sync(bar_id, bar_n);
-        if (cs.last[gid]) {
-            __threadfence();
-            // merge: the S partial (max, sum, P.V) loaded in parallel across lanes
-            const float *base = op.part + ((size_t)m * op.H + h) * S * (hd + 2);
-            float gmax = -INFINITY;
-            for (int j0 = 0; j0 < S; j0 += 32) {
-                const int j = j0 + lane;
-                gmax = fmaxf(gmax, j < S ? __ldcg(base + (size_t)j * (hd + 2)) : -INFINITY);
-            }
-            gmax = warp_max(gmax);
-            float L = 0.f, o[EPL];
+                        for (int u = 0; u < 4; ++u)
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) o[e] = 0.f;
-            for (int j0 = 0; j0 < S; j0 += 32) {
-                const int j = j0 + lane;
-                float f = 0.f, lj = 0.f;
-                if (j < S) {
-                    const float *pj = base + (size_t)j * (hd + 2);
-                    f = expf(__ldcg(pj) - gmax);
-                    lj = __ldcg(pj + 1);
-                }
-                L += warp_sum(lj * f);
-                const int nj = min(32, S - j0);
-                for (int jj = 0; jj < nj; jj += 4) {
-                    float a[4][EPL], fs[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        fs[k] = __shfl_sync(0xffffffffu, f, (jj + k) & 31);
-                        const float *pk = base + (size_t)(j0 + jj + k) * (hd + 2) + 2 + lane * EPL;
-#pragma unroll
-                        for (int e = 0; e < EPL; ++e) a[k][e] = jj + k < nj ? __ldcg(pk + e) : 0.f;
+                            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj[u], vv[u][e], acc[e]);
                     }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-#pragma unroll
-                        for (int e = 0; e < EPL; ++e) o[e] = fmaf(a[k][e], jj + k < nj ? fs[k] : 0.f, o[e]);
+                    mrun = mn;
                 }
             }
-            float *outp = op.att_out + (size_t)m * op.H * hd + h * hd + lane * EPL;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) outp[e] = o[e] / L;
-            if (wr == 0 && lane == 0) op.counters[m * op.Hkv + kvh] = 0;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == NS) slot = 0, phase ^= 1u;
         }
-        group_sync(bar_id, bar_n);
     }
+    if (!has) return ok;
+    uint64_t *outp = op.att_out + (size_t)m * op.H * hd + h * hd + lane * EPL;
+    if (S == 1) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ll_store(outp + e, acc[e] / l, out_tag);
+        return ok;
+    }
+    uint64_t *pbase = op.part + ((size_t)m * op.H + h) * op.S * (hd + 2);
+    if (sp != 0) {
+        uint64_t *pp = pbase + (size_t)sp * (hd + 2);
+        if (lane == 0) ll_store(pp, mrun, out_tag), ll_store(pp + 1, l, out_tag);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ll_store(pp + 2 + e * 32 + lane, acc[e], out_tag);  // lane-contiguous
+        return ok;
+    }
+    // split 0 merges the other splits of its (token, head): lane j reads
+    // split j + 1's (max, sum) and the lanes' dims of P.V come in batches
+    if (tr && gtid == 0) tr[3] = globaltimer();
+    float mj = -INFINITY, lj = 0.f;
+    {
+        const uint64_t *pj = lane < S - 1 ? pbase + (size_t)(lane + 1) * (hd + 2) : nullptr;
+        unsigned long long w[2] = {0ull, 0ull};
+        ok = ll_wait(w, [&](int i) { return pj ? pj + i : nullptr; }, out_tag, a.error) && ok;
+        if (pj) mj = ll_value(w[0]), lj = ll_value(w[1]);
+    }
+    const float gmax = fmaxf(mrun, warp_max(mj));
+    const float fj = lane < S - 1 ? expf(mj - gmax) : 0.f, fown = expf(mrun - gmax);
+    const float L = fmaf(l, fown, warp_sum(lj * fj));
+    float o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = acc[e] * fown;
+    constexpr int kB = 8;  // splits per batch of loads
+    for (int j0 = 1; j0 < S; j0 += kB) {
+        unsigned long long w[kB * EPL];
+#pragma unroll
+        for (int i = 0; i < kB * EPL; ++i) w[i] = 0ull;
+        ok = ll_wait(w,
+                     [&](int i) {
+                         const int j = j0 + i / EPL;
+                         return j < S ? pbase + (size_t)j * (hd + 2) + 2 + (i % EPL) * 32 + lane : nullptr;
+                     },
+                     out_tag, a.error) && ok;
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+            const float f = __shfl_sync(0xffffffffu, fj, (j0 + b - 1) & 31);
+            if (j0 + b < S) {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) o[e] = fmaf(ll_value(w[b * EPL + e]), f, o[e]);
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) ll_store(outp + e, o[e] / L, out_tag);
+    return ok;
 }
 
 // Not inlined: attention's register pressure stays out of the GEMV loops.
 template <typename KV>
-__device__ __noinline__ void consume_attn_dispatch(const EngineOp &op, float *xs, ConsumerShared &cs) {
+__device__ __noinline__ bool consume_attn_dispatch(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch,
+                                                   uint8_t *area, uint32_t g, uint64_t *full, uint64_t *empty,
+                                                   const uint8_t *ring, unsigned long long *tr) {
     switch (op.hd / 32) {
-    case 2: consume_attn<KV, 2>(op, xs, cs); break;
-    case 4: consume_attn<KV, 4>(op, xs, cs); break;
+    case 2: return consume_attn<KV, 2>(a, op, opi, epoch, area, g, full, empty, ring, tr);
+    case 4: return consume_attn<KV, 4>(a, op, opi, epoch, area, g, full, empty, ring, tr);
     }
+    return false;
 }
 
 }  // namespace
@@ -707,17 +1011,18 @@ __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineA
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ ConsumerShared cs;
     const int tid = threadIdx.x, warp = tid >> 5;
-    // [full | empty mbarriers] [staged inputs / attention tiles] [ring]
+    // [full | empty mbarriers] [staged inputs / attention groups] [ring]
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + a.nslots;
     uint8_t *area = smem + kEngineBarrierBytes;
     uint8_t *ring = area + a.area_bytes;
-    if ((saddr(ring) & 127u) != 0u) {  // TMA boxes land on 128-byte boundaries
+    if ((saddr(ring) & 127u) != 0u) {  // bulk copies land on 128-byte boundaries
         if (tid == 0) atomicCAS(a.error, 0, kErrEngineAlign);
         return;
     }
     if (tid == 0) {
         cs.abort = 0;
+        cs.epoch = *reinterpret_cast<volatile uint32_t *>(a.epoch);
         for (int i = 0; i < a.nslots; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kEngineConsumerWarps);
@@ -730,57 +1035,41 @@ __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineA
         if ((tid & 31) == 0) producer(a, full, empty, ring);
         return;
     }
-    uint32_t g = 0;
+    const uint32_t epoch = cs.epoch;
+    uint32_t g = 0;  // ring slots consumed
     for (int i = 0; i < a.n_ops; ++i) {
         const EngineOp &op = a.ops[i];
-        if (i > 0) {
-            // grid barrier: op i reads what op i-1 wrote on every CTA
-            consumers_sync();
-            if (tid == 0) {
-                int ok = cs.abort ? 0 : 1;
-                if (ok) {
-                    // release: the CTA's writes, ordered before this thread by
-                    // the barrier above, are visible to whoever acquires the count
-                    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.barrier) : "memory");
-                }
-                const uint32_t target = (uint32_t)i * gridDim.x;
-                uint32_t it = 0;
-                while (ok && ld_acquire(a.barrier) < target) {
-                    if (++it > kGridSpin) {
-                        atomicCAS(a.error, 0, kErrEngineGrid);
-                        ok = 0;
-                        break;
-                    }
-                    if ((it & 63u) == 0 && ld_volatile(a.error)) {
-                        ok = 0;
-                        break;
-                    }
-                }
-                cs.ok = ok;  // the acquire above orders the reads after the next barrier
-            }
-            consumers_sync();
-            if (!cs.ok) return;
-        }
         unsigned long long *tr = nullptr;
         if (a.trace && tid == 0 && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))
             tr = a.trace + ((size_t)(blockIdx.x ? 1 : 0) * a.n_ops + i) * 4;
         if (tr) tr[0] = globaltimer();
+        bool ok;
         if (op.kind == OP_GEMV) {
             float *xs = reinterpret_cast<float *>(area);
-            const bool okg = op.M == 2 ? run_gemv<2>(a, op, g, full, empty, ring, xs, cs, tr)
-                                       : run_gemv<1>(a, op, g, full, empty, ring, xs, cs, tr);
-            if (!okg) cs.abort = 1;
+            ok = op.M == 2 ? run_gemv<2>(a, op, i, g, full, empty, ring, xs, cs, tr)
+                           : run_gemv<1>(a, op, i, g, full, empty, ring, xs, cs, tr);
         } else {
-            if (tr) tr[1] = globaltimer();
-            float *xs = reinterpret_cast<float *>(area);
-            if (op.kv_half) consume_attn_dispatch<__half>(op, xs, cs);
-            else consume_attn_dispatch<float>(op, xs, cs);
+            // attention timeline (group 0 of the CTA): [1] inputs ready, [3] merge started
+            unsigned long long *atr = a.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)
+                                          ? a.trace + ((size_t)(blockIdx.x ? 1 : 0) * a.n_ops + i) * 4
+                                          : nullptr;
+            ok = op.kv_half ? consume_attn_dispatch<__half>(a, op, i, epoch, area, g, full, empty, ring, atr)
+                            : consume_attn_dispatch<float>(a, op, i, epoch, area, g, full, empty, ring, atr);
+            AttnPlan pl;
+            pl.init(op, a.slot_bytes);
+            g += (uint32_t)pl.slots();
         }
-        if (a.trace) {  // uniform: every consumer thread takes the barrier
-            consumers_sync();
-            if (tr) tr[2] = globaltimer();
-        }
+        if (!ok) cs.abort = 1;
+        consumers_sync();  // every consumer thread: the op is done (and the area reusable)
+        if (tr) tr[2] = globaltimer();
+        if (a.trace && tid == 0) a.trace[(size_t)a.n_ops * 8 + (size_t)i * gridDim.x + blockIdx.x] = globaltimer();
+        if (cs.abort) break;
     }
+    // Every CTA read the epoch before producing its first outputs, and CTA 0's
+    // last op consumed outputs of every CTA: the next launch may use e + 1.
+    // (Also after a failed wait, so that no later launch mistakes this one's
+    // words for its own.)
+    if (blockIdx.x == 0 && tid == 0) *reinterpret_cast<volatile uint32_t *>(a.epoch) = epoch + 1;
 }
 
 cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s) {

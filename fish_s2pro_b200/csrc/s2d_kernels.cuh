@@ -128,52 +128,67 @@ enum EngineOpKind { OP_GEMV = 0, OP_ATTN = 1 };
 // One step of the engine's program.  A GEMV op reads its input vector(s) and
 // writes its outputs like gemv_kernel (GemvArgs fields); an ATTN op fuses
 // rope_kv_kernel and attn_kernel (RopeArgs / AttnArgs fields).
+//
+// Values passed between ops of one launch are "LL words": 64-bit words
+// holding a float in the low half and a tag in the high half, written with a
+// single 64-bit store.  The tag of op i's outputs in a launch with epoch e is
+// engine_tag(e, i); a reader polls the words it needs until they carry the
+// producer's tag, so no grid-wide barrier separates the ops.  Inputs written
+// before the launch are plain floats (src index -1).
 struct EngineOp {
     int kind, epi, M;
     // GEMV
     const uint16_t *W, *W2;
-    const float *x;
-    int ldx;
+    const void *x;       // [M][ldx] floats, or LL words of op x_src
+    int ldx, x_src;
     const float *norm_w;
     float eps;
-    float *y;
-    int ldy;
-    const float *resid;
-    int ldr;
-    float *x_out;
+    void *y;             // [M][ldy] LL words when y_ll, else floats
+    int ldy, y_ll;
+    const void *resid;   // [M][ldr] (EPI_RESID) floats, or LL words of op resid_src; may alias y
+    int ldr, resid_src;
+    float *x_out;        // optional: CTA 0 writes the normalised input [M][K] as floats
     int K, N;
     int row_base, n_contig, extra_row;
     // ATTN
-    const float *qkv;
-    int ld_qkv;
+    const uint64_t *qkv; // LL words [M][ld_qkv] of op qkv_src: Q | K | V
+    int ld_qkv, qkv_src;
     void *kcache, *vcache;
     int max_seq, kv_half;
-    const float *q_norm, *k_norm, *rope_denom;
+    const float *q_norm, *k_norm;
+    const float2 *rope_cs;  // [max_seq][hd / 2] (cos, sin) of pos / rope_base^(2i / hd)
     const int32_t *pos_dev;
     int pos_const;
     int H, Hkv, hd, S;
     float scale;
-    float *att_out;
-    float *part;
-    int32_t *counters;
+    uint64_t *att_out;   // LL words [M][H * hd]
+    uint64_t *part;      // LL words [M][H][S][hd + 2]: split partials (max, sum, P.V with
+                         // element lane * hd/32 + e at 2 + e * 32 + lane)
     // GEMV weights in the engine's slot order (engine_relayout): the slot
     // of row tile [tr0, tr0 + R) and K slice s starts at element
     // Wt + tr0 * K * mats + s * R * kt * mats and holds [mat][R][kw].
     const uint16_t *Wt;
 };
 
+__host__ __device__ __forceinline__ uint32_t engine_tag(uint32_t epoch, int op) {
+    return (epoch << 8) | (uint32_t)op;
+}
+constexpr int kEngineMaxOps = 255;
+
 struct EngineArgs {
     const EngineOp *ops;
     int n_ops;
     int nslots, slot_bytes;            // shared-memory weight ring
     int area_bytes;                    // staged inputs / attention tiles (multiple of 128)
-    uint32_t *barrier;                 // grid-barrier counter, zero at launch
+    uint32_t *epoch;                   // launch epoch (>= 1): read at start, advanced by CTA 0 at exit
     const int32_t *done;               // DevState::done or nullptr
     int32_t *error;                    // DevState::error
     // Optional timeline (nullptr: off).  CTAs 0 and gridDim-1 record
-    // %globaltimer at each op: [cta][op][0] barrier passed, [1] input staged,
-    // [2] op finished by the consumers, [3] producer issued the op's last slot.
+    // %globaltimer at each op: [cta][op][0] op started, [1] inputs staged,
+    // [2] op finished by the consumers, [3] producer issued the op's last slot;
+    // then [op][cta] every CTA's finish time.
     unsigned long long *trace;
+    int l2_lead;  // weight slots the producer prefetches into L2 ahead of the ring
 };
 
 constexpr int kEngineConsumerWarps = 8;
@@ -218,7 +233,7 @@ __host__ __device__ __forceinline__ void engine_tile_rows(int n, int t, int ntil
 
 // Error codes the engine writes into DevState::error.
 constexpr int kErrEngineWeights = 16;  // a weight-ring wait ran out
-constexpr int kErrEngineGrid = 17;     // a grid-barrier wait ran out
+constexpr int kErrEngineWait = 17;     // a wait for another op's outputs ran out
 constexpr int kErrEngineAlign = 18;    // the shared-memory ring is not 128-byte aligned
 
 cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s);
@@ -231,17 +246,23 @@ cudaError_t launch_engine_relayout(const uint16_t *W, const uint16_t *W2, int N,
                                    int row_base, int extra_row, int grid, int slot_bytes, uint16_t *dst,
                                    cudaStream_t s);
 
-// Shared-memory bytes of one attention group of the engine: its warps' query
-// vectors, then up to kAttnCap cached K rows and V rows, each padded by 16
-// bytes so that lanes reading different rows hit different banks.
-constexpr int kAttnCap = 32;
-__host__ __device__ __forceinline__ int attn_row_bytes(int hd, int kvb) { return hd * kvb + 16; }
-__host__ __device__ __forceinline__ int attn_cap(int max_seq) {
-    return max_seq < kAttnCap ? max_seq : kAttnCap;
+// Attention in the engine.  A group's query vectors and the new tokens' K
+// and V rows (at most 2 tokens) sit in the shared area (attn_group_bytes per
+// group).  The cached K/V rows of a group's item come through the weight
+// ring, in program order, as slots of up to attn_slot_rows positions:
+// [K rows][V rows] (each tile 128-byte aligned), and in a group's first slot
+// a side block: the RoPE (cos, sin) rows of the new positions [2][hd/2], then
+// the Q and K norm gains [hd] each.
+__host__ __device__ __forceinline__ int attn_round(int b) { return (b + 127) / 128 * 128; }
+__host__ __device__ __forceinline__ int attn_group_bytes(int rep, int hd, int kvb) {
+    return attn_round(rep * hd * 4 + 4 * hd * kvb);
 }
-__host__ __device__ __forceinline__ int attn_group_bytes(int rep, int hd, int kvb, int max_seq) {
-    return (rep * hd * 4 + 2 * attn_cap(max_seq) * attn_row_bytes(hd, kvb) + 15) / 16 * 16;
+__host__ __device__ __forceinline__ int attn_side_bytes(int hd) { return 16 * hd; }
+__host__ __device__ __forceinline__ int attn_slot_rows(int hd, int kvb, int slot_bytes) {
+    const int p = (slot_bytes - attn_side_bytes(hd) - 256) / (2 * hd * kvb);
+    return p > 32 ? 32 : p;
 }
+__host__ __device__ __forceinline__ int attn_tile_bytes(int rows, int hd, int kvb) { return attn_round(rows * hd * kvb); }
 
 constexpr int kSampleMax = 8192;
 constexpr int kSampleThreads = 1024;

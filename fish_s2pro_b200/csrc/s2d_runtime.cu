@@ -109,12 +109,16 @@ struct S2dHandle {
     // persistent layer engine
     bool use_engine = true;
     int num_sms = 0;
-    uint32_t *engine_bar = nullptr;
+    uint32_t *engine_epoch = nullptr;  // launch epoch of the engine's LL words (starts at 1)
+    // engine activations as LL words: residual, QKV, attention out, SwiGLU out, split partials
+    uint64_t *ll_x = nullptr, *ll_qkv = nullptr, *ll_att = nullptr, *ll_act = nullptr, *ll_part = nullptr;
+    float2 *rope_cs_slow = nullptr, *rope_cs_fast = nullptr;  // [positions][hd / 2] (cos, sin)
     std::vector<EngineProgram> fast_progs;  // index = codebook being produced (1..K-1)
     // engine weight copies in slot order, keyed by (W, W2, N, K, n_contig, row_base, extra_row)
     std::map<std::tuple<const uint16_t *, const uint16_t *, int, int, int, int, int>, uint16_t *> tiled;
     size_t tiled_bytes = 0;
     int slot_bytes = kEngineSlotBytes;  // engine ring slot size (S2D_SLOT_KB)
+    int l2_lead = 0;                    // engine L2 prefetch lead in slots (S2D_L2_LEAD)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
 };
@@ -405,6 +409,24 @@ int32_t alloc_buffers(S2dHandle *h) {
     CK(cudaMalloc(&h->rope_fast, rf.size() * sizeof(float)));
     CK(cudaMemcpy(h->rope_slow, rs.data(), rs.size() * sizeof(float), cudaMemcpyHostToDevice));
     CK(cudaMemcpy(h->rope_fast, rf.data(), rf.size() * sizeof(float), cudaMemcpyHostToDevice));
+    // (cos, sin) of theta = pos / denominator for every position, theta in
+    // f32 as above, sin and cos rounded from double
+    auto rope_table = [](const std::vector<float> &den, int npos) {
+        std::vector<float2> t((size_t)npos * den.size());
+        for (int p = 0; p < npos; ++p)
+            for (size_t i = 0; i < den.size(); ++i) {
+                const float theta = (float)p / den[i];
+                t[(size_t)p * den.size() + i] = make_float2((float)cos((double)theta), (float)sin((double)theta));
+            }
+        return t;
+    };
+    {
+        const std::vector<float2> ts = rope_table(rs, maxseq), tf = rope_table(rf, f.ctx);
+        CK(cudaMalloc(&h->rope_cs_slow, std::max<size_t>(ts.size(), 1) * sizeof(float2)));
+        CK(cudaMalloc(&h->rope_cs_fast, std::max<size_t>(tf.size(), 1) * sizeof(float2)));
+        CK(cudaMemcpy(h->rope_cs_slow, ts.data(), ts.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(h->rope_cs_fast, tf.data(), tf.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
     const size_t kv_slow = (size_t)a.L * 2 * a.Hkv * maxseq * a.hd;
     CK(cudaMalloc(&h->kv_slow, kv_slow * sizeof(__half)));
     CK(cudaMemset(h->kv_slow, 0, kv_slow * sizeof(__half)));
@@ -431,6 +453,21 @@ int32_t alloc_buffers(S2dHandle *h) {
     const int H = std::max(a.H, f.H), hd = std::max(a.hd, f.hd), Hkv = std::max(a.Hkv, f.Hkv);
     CK(cudaMalloc(&h->part, (size_t)kMaxM * H * h->S_slow * (hd + 2) * sizeof(float)));
     CK(cudaMalloc(&h->counters, (size_t)kMaxM * Hkv * sizeof(int32_t)));
+    // engine LL words (at most 2 tokens per engine op); zero words carry tag 0,
+    // which no launch uses (epochs start at 1)
+    {
+        const size_t nx = (size_t)2 * d, nq = (size_t)2 * qkv_out, na = (size_t)2 * qs, nf = (size_t)2 * F;
+        const size_t np = (size_t)2 * H * h->S_slow * (hd + 2);
+        uint64_t **bufs[] = {&h->ll_x, &h->ll_qkv, &h->ll_att, &h->ll_act, &h->ll_part};
+        const size_t ns[] = {nx, nq, na, nf, np};
+        for (int i = 0; i < 5; ++i) {
+            CK(cudaMalloc(bufs[i], ns[i] * sizeof(uint64_t)));
+            CK(cudaMemset(*bufs[i], 0, ns[i] * sizeof(uint64_t)));
+        }
+        const uint32_t one = 1;
+        CK(cudaMalloc(&h->engine_epoch, sizeof(uint32_t)));
+        CK(cudaMemcpy(h->engine_epoch, &one, sizeof(uint32_t), cudaMemcpyHostToDevice));
+    }
     CK(cudaMemset(h->counters, 0, (size_t)kMaxM * Hkv * sizeof(int32_t)));
     CK(cudaMalloc(&h->st, sizeof(DevState)));
     CK(cudaMemset(h->st, 0, sizeof(DevState)));
@@ -628,53 +665,72 @@ cudaError_t enqueue_fast_frame(S2dHandle *h, const GenKey &k, bool with_override
 
 // Whether the engine supports this model's shapes (else the per-op kernels run).
 bool engine_supported(const S2dHandle *h) {
+    if (h->num_sms <= 0) return false;
     for (const ArShape *a : {&h->slow, &h->fast}) {
         const int rep = a->H / a->Hkv;
         if (rep > kEngineConsumerWarps || kEngineConsumerWarps % rep || (a->hd != 64 && a->hd != 128)) return false;
         if (a->d % 8 || a->qs() % 8 || a->F % 8) return false;
         if (a->d > kEngineMaxK || a->qs() > kEngineMaxK || a->F > kEngineMaxK) return false;  // staged inputs
+        // every CTA must own rows of every linear: a CTA's outputs are what
+        // orders its reads of a reused buffer before the buffer's next writer
+        if (a->d < h->num_sms || a->qkv_out() < h->num_sms || a->F < h->num_sms) return false;
+        if (a->L * 5 + 1 > kEngineMaxOps) return false;
     }
-    return h->num_sms > 0;
+    const S2dGraphSpec &s = h->spec;
+    return s.codebook_size >= h->num_sms && s.semantic_end_id - s.semantic_begin_id + 1 >= h->num_sms;
 }
 
-EngineOp gemv_op(int M, int epi, const uint16_t *W, const uint16_t *W2, const float *x, int ldx,
-                 const float *norm_w, float eps, float *y, int ldy, const float *resid, int K, int N) {
+// A GEMV op reading x (floats when x_src < 0, else LL words of op x_src) and
+// writing y (LL words when y_ll).
+EngineOp gemv_op(int M, int epi, const uint16_t *W, const uint16_t *W2, const void *x, int ldx, int x_src,
+                 const float *norm_w, float eps, void *y, int ldy, int y_ll, const void *resid, int resid_src,
+                 int K, int N) {
     EngineOp o{};
-    o.kind = OP_GEMV, o.epi = epi, o.M = M, o.W = W, o.W2 = W2, o.x = x, o.ldx = ldx;
-    o.norm_w = norm_w, o.eps = eps, o.y = y, o.ldy = ldy, o.resid = resid, o.ldr = ldy;
-    o.K = K, o.N = N, o.n_contig = -1;
+    o.kind = OP_GEMV, o.epi = epi, o.M = M, o.W = W, o.W2 = W2, o.x = x, o.ldx = ldx, o.x_src = x_src;
+    o.norm_w = norm_w, o.eps = eps, o.y = y, o.ldy = ldy, o.y_ll = y_ll, o.resid = resid, o.ldr = ldy;
+    o.resid_src = resid_src, o.K = K, o.N = N, o.n_contig = -1;
     return o;
 }
 
-// The ops of one transformer layer over M tokens at rows x[0..M) (see
-// enqueue_layer for the per-op kernel version).
-void layer_ops(S2dHandle *h, bool is_fast, int l, float *x, int M, const int32_t *pos_dev,
-               int pos_const, std::vector<EngineOp> &ops) {
+// The ops of one transformer layer over M tokens (see enqueue_layer for the
+// per-op kernel version).  The residual stream enters as `x` (floats [M][d]
+// when *x_src < 0, else the LL residual h->ll_x written by op *x_src) and
+// leaves in h->ll_x, written by the op whose index is stored in *x_src.
+void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, const int32_t *pos_dev,
+               int pos_const, std::vector<EngineOp> &ops, int *x_src) {
     const ArShape &a = is_fast ? h->fast : h->slow;
     const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
     const int d = a.d;
-    ops.push_back(gemv_op(M, EPI_STORE, L.wqkv, nullptr, x, d, L.attn_norm, a.eps, h->qkv, a.qkv_out(),
-                          nullptr, d, a.qkv_out()));
+    const void *x = *x_src < 0 ? static_cast<const void *>(x_in) : static_cast<const void *>(h->ll_x);
+    const int i_qkv = (int)ops.size();
+    ops.push_back(gemv_op(M, EPI_STORE, L.wqkv, nullptr, x, d, *x_src, L.attn_norm, a.eps, h->ll_qkv, a.qkv_out(), 1,
+                          nullptr, -1, d, a.qkv_out()));
     EngineOp t{};
-    t.kind = OP_ATTN, t.M = M, t.qkv = h->qkv, t.ld_qkv = a.qkv_out();
+    t.kind = OP_ATTN, t.M = M, t.qkv = h->ll_qkv, t.ld_qkv = a.qkv_out(), t.qkv_src = i_qkv;
     if (is_fast) {
         float *base = h->kv_fast + (size_t)l * 2 * a.Hkv * a.ctx * a.hd;
         t.kcache = base, t.vcache = base + (size_t)a.Hkv * a.ctx * a.hd, t.max_seq = a.ctx, t.kv_half = 0;
-        t.rope_denom = h->rope_fast, t.S = h->S_fast;
+        t.rope_cs = h->rope_cs_fast, t.S = h->S_fast;
     } else {
         __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
         t.kcache = base, t.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd;
         t.max_seq = h->cfg.max_seq, t.kv_half = 1;
-        t.q_norm = L.q_norm, t.k_norm = L.k_norm, t.rope_denom = h->rope_slow, t.S = h->S_slow;
+        t.q_norm = L.q_norm, t.k_norm = L.k_norm, t.rope_cs = h->rope_cs_slow, t.S = h->S_slow;
     }
     t.eps = a.eps, t.pos_dev = pos_dev, t.pos_const = pos_const;
     t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd, t.scale = 1.0f / sqrtf((float)a.hd);
-    t.att_out = h->att, t.part = h->part, t.counters = h->counters;
+    t.att_out = h->ll_att, t.part = h->ll_part;
+    const int i_att = (int)ops.size();
     ops.push_back(t);
-    ops.push_back(gemv_op(M, EPI_RESID, L.wo, nullptr, h->att, a.qs(), nullptr, 0.f, x, d, x, a.qs(), d));
-    ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, x, d, L.ffn_norm, a.eps,
-                          h->act, a.F, nullptr, d, a.F));
-    ops.push_back(gemv_op(M, EPI_RESID, L.w2, nullptr, h->act, a.F, nullptr, 0.f, x, d, x, a.F, d));
+    const int i_wo = (int)ops.size();
+    ops.push_back(gemv_op(M, EPI_RESID, L.wo, nullptr, h->ll_att, a.qs(), i_att, nullptr, 0.f, h->ll_x, d, 1, x,
+                          *x_src, a.qs(), d));
+    const int i_w13 = (int)ops.size();
+    ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, h->ll_x, d, i_wo, L.ffn_norm,
+                          a.eps, h->ll_act, a.F, 1, nullptr, -1, d, a.F));
+    *x_src = (int)ops.size();
+    ops.push_back(gemv_op(M, EPI_RESID, L.w2, nullptr, h->ll_act, a.F, i_w13, nullptr, 0.f, h->ll_x, d, 1, h->ll_x,
+                          i_wo, a.F, d));
 }
 
 // The weights of a GEMV op in the engine's slot order (engine_relayout),
@@ -700,15 +756,21 @@ int32_t upload_program(S2dHandle *h, const std::vector<EngineOp> &ops_in, Engine
     if (p->ops) cudaFree(p->ops);
     p->ops = nullptr;
     std::vector<EngineOp> ops = ops_in;
-    int ab = 0;  // shared area: a GEMV's staged inputs or an attention op's tiles
+    if ((int)ops.size() > kEngineMaxOps) return set_err(h, S2D_EINVAL, "engine: program too long");
+    // Shared area: a GEMV's staged inputs, or an attention op's groups (query
+    // vectors and new K/V rows); the cached K/V rows come through the ring.
+    int ab = 0;
     for (EngineOp &o : ops) {
         if (o.kind == OP_GEMV) {
             ab = std::max(ab, o.M * o.K * 4);
             const int32_t rc = tiled_weights(h, o);
             if (rc) return rc;
         } else {
-            ab = std::max(ab, (kEngineConsumerWarps / (o.H / o.Hkv)) *
-                                  attn_group_bytes(o.H / o.Hkv, o.hd, o.kv_half ? 2 : 4, o.max_seq));
+            if (o.M > 2) return set_err(h, S2D_EINVAL, "engine: attention over more than 2 tokens");
+            const int kvb = o.kv_half ? 2 : 4;
+            if (attn_slot_rows(o.hd, kvb, h->slot_bytes) < 1)
+                return set_err(h, S2D_EINVAL, "engine: ring slots too small for a cache row");
+            ab = std::max(ab, (kEngineConsumerWarps / (o.H / o.Hkv)) * attn_group_bytes(o.H / o.Hkv, o.hd, kvb));
         }
     }
     ab = (ab + 127) / 128 * 128;
@@ -735,20 +797,25 @@ int32_t build_programs(S2dHandle *h, uint32_t im_end) {
         for (int cbk = 1; cbk < K; ++cbk) {
             const int p0 = cbk == 1 ? 0 : cbk, M = cbk == 1 ? 2 : 1;
             std::vector<EngineOp> ops;
-            for (int l = 0; l < h->fast.L; ++l) layer_ops(h, true, l, h->fast_x + (size_t)p0 * d, M, nullptr, p0, ops);
-            ops.push_back(gemv_op(1, EPI_STORE, h->fast_out, nullptr, h->fast_x + (size_t)cbk * d, d, h->fast_norm,
-                                  h->fast.eps, h->logits_fast, s.codebook_size, nullptr, d, s.codebook_size));
+            int x_src = -1;
+            for (int l = 0; l < h->fast.L; ++l)
+                layer_ops(h, true, l, h->fast_x + (size_t)p0 * d, M, nullptr, p0, ops, &x_src);
+            // the head reads the residual of the pass's last token (position cbk)
+            ops.push_back(gemv_op(1, EPI_STORE, h->fast_out, nullptr, h->ll_x + (size_t)(M - 1) * d, d, x_src,
+                                  h->fast_norm, h->fast.eps, h->logits_fast, s.codebook_size, 0, nullptr, -1, d,
+                                  s.codebook_size));
             if ((rc = upload_program(h, ops, &h->fast_progs[(size_t)cbk]))) return rc;
         }
     }
     if (!h->slow_prog.ops || h->slow_prog_im_end != im_end) {
         std::vector<EngineOp> ops;
-        for (int l = 0; l < h->slow.L; ++l) layer_ops(h, false, l, h->x, 1, &h->st->n_past, 0, ops);
+        int x_src = -1;
+        for (int l = 0; l < h->slow.L; ++l) layer_ops(h, false, l, h->x, 1, &h->st->n_past, 0, ops, &x_src);
         const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
         const bool extra = (int64_t)im_end < s.vocab_size &&
                            ((int)im_end < s.semantic_begin_id || (int)im_end > s.semantic_end_id);
-        EngineOp head = gemv_op(1, EPI_STORE, h->emb, nullptr, h->x, d, h->norm, h->slow.eps, h->logits,
-                                s.vocab_size, nullptr, d, nsem + (extra ? 1 : 0));
+        EngineOp head = gemv_op(1, EPI_STORE, h->emb, nullptr, h->ll_x, d, x_src, h->norm, h->slow.eps, h->logits,
+                                s.vocab_size, 0, nullptr, -1, d, nsem + (extra ? 1 : 0));
         head.row_base = s.semantic_begin_id, head.n_contig = nsem;
         head.extra_row = extra ? (int)im_end : s.semantic_begin_id;
         head.x_out = h->hidden_post;
@@ -761,11 +828,10 @@ int32_t build_programs(S2dHandle *h, uint32_t im_end) {
 }
 
 cudaError_t enqueue_engine(S2dHandle *h, const EngineProgram &p) {
-    cudaError_t e = cudaMemsetAsync(h->engine_bar, 0, sizeof(uint32_t), h->stream);
-    if (e) return e;
     EngineArgs a{};
     a.ops = p.ops, a.n_ops = p.n_ops, a.nslots = p.nslots, a.slot_bytes = h->slot_bytes;
-    a.area_bytes = p.area_bytes, a.barrier = h->engine_bar, a.done = &h->st->done, a.error = &h->st->error;
+    a.area_bytes = p.area_bytes, a.epoch = h->engine_epoch, a.done = &h->st->done, a.error = &h->st->error;
+    a.l2_lead = h->l2_lead;
     h->launches += 1;
     return launch_engine(a, h->num_sms, p.smem, h->stream);
 }
@@ -932,7 +998,8 @@ void free_handle(S2dHandle *h) {
     void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
                     h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
                     h->logits_fast, h->part, h->counters, h->st, h->tokens_dev, h->frame_codes,
-                    h->codes_out, h->tok_out, h->code_override, h->engine_bar, h->slow_prog.ops};
+                    h->codes_out, h->tok_out, h->code_override, h->engine_epoch, h->slow_prog.ops,
+                    h->ll_x, h->ll_qkv, h->ll_att, h->ll_act, h->ll_part, h->rope_cs_slow, h->rope_cs_fast};
     for (void *p : bufs)
         if (p) cudaFree(p);
     for (EngineProgram &p : h->fast_progs)
@@ -1000,12 +1067,9 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
         int coop = 0;
         cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->device);
-        if ((ce = cudaMalloc(&h->engine_bar, sizeof(uint32_t)))) {
-            h->err = std::string("cudaMalloc: ") + cudaGetErrorString(ce);
-            return report(h, S2D_ECUDA);
-        }
         const char *env = getenv("S2D_ENGINE");
         h->use_engine = coop && engine_supported(h) && !(env && env[0] == '0');
+        if (const char *lead = getenv("S2D_L2_LEAD")) h->l2_lead = std::max(0, std::min(64, atoi(lead)));
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -1346,7 +1410,7 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
     if (!p.ops) return set_err(h, S2D_EINVAL, "no such program");
     *n_ops = p.n_ops;
     unsigned long long *dtr = nullptr;
-    const size_t need = (size_t)p.n_ops * 8;
+    const size_t need = (size_t)p.n_ops * (8 + h->num_sms);
     if (trace) {
         if ((int64_t)need > trace_cap) return set_err(h, S2D_EINVAL, "trace buffer too small");
         CK(cudaMalloc(&dtr, need * sizeof(unsigned long long)));
@@ -1354,10 +1418,10 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
     }
     EngineArgs a{};
     a.ops = p.ops, a.n_ops = p.n_ops, a.nslots = p.nslots, a.slot_bytes = h->slot_bytes;
-    a.area_bytes = p.area_bytes, a.barrier = h->engine_bar, a.done = nullptr, a.error = &h->st->error;
+    a.area_bytes = p.area_bytes, a.epoch = h->engine_epoch, a.done = nullptr, a.error = &h->st->error;
+    a.l2_lead = h->l2_lead;
     a.trace = dtr;
-    cudaError_t e = cudaMemsetAsync(h->engine_bar, 0, sizeof(uint32_t), h->stream);
-    if (!e) e = cudaEventRecord(h->ev0, h->stream);
+    cudaError_t e = cudaEventRecord(h->ev0, h->stream);
     if (!e) e = launch_engine(a, h->num_sms, p.smem, h->stream);
     if (!e) e = cudaEventRecord(h->ev1, h->stream);
     if (!e) e = cudaEventSynchronize(h->ev1);

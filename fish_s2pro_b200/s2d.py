@@ -345,18 +345,23 @@ class SlowArState:
                                              ctypes.byref(ms), ctypes.byref(nb)))
         return float(ms.value), float(nb.value)
 
-    def profile_engine(self, program: int = 0, trace: bool = True):
+    def profile_engine(self, program: int = 0, trace: bool = True, per_cta: bool = False):
         """Run one persistent-engine program once (s2d_profile_engine).
-        Returns (ms, trace) with trace shaped [2 CTAs][n_ops][4] in ns."""
+        Returns (ms, trace) with trace shaped [2 CTAs][n_ops][4] in ns; with
+        per_cta, (ms, trace, finish) where finish is [n_ops][CTAs] in ns."""
         n = ctypes.c_int32()
         ms = ctypes.c_double()
-        buf = np.zeros(8 * 4096, dtype=np.uint64) if trace else None
+        buf = np.zeros(264 * 256, dtype=np.uint64) if trace else None
         self._check(lib().s2d_profile_engine(self.handle, program,
                                              _ptr(buf, ctypes.c_uint64) if trace else None,
                                              buf.size if trace else 0, ctypes.byref(n),
                                              ctypes.byref(ms)))
         tr = buf[: n.value * 8].reshape(2, n.value, 4) if trace else None
-        return float(ms.value), tr
+        if not per_cta:
+            return float(ms.value), tr
+        g = (int(np.count_nonzero(buf[n.value * 8:])) + n.value - 1) // max(n.value, 1) if trace else 0
+        fin = buf[n.value * 8: n.value * (8 + g)].reshape(n.value, g) if trace else None
+        return float(ms.value), tr, fin
 
     def dequant_tensor(self, name: str, count: int) -> np.ndarray:
         out = np.empty(count, dtype=np.float32)

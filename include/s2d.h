@@ -183,10 +183,11 @@ int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *
  * on the handle's current state (call after s2d_generate_codes): program 0 is
  * the Slow-AR step (all layers + LM head), program k >= 1 the Fast-AR pass
  * that produces codebook k.  *ms: its CUDA-event duration.  If trace is not
- * NULL it receives n_ops*8 timestamps (ns, %globaltimer): for CTA 0 then the
- * last CTA, per op: barrier passed, input staged, op finished, producer done
- * issuing the op's weights.  *n_ops receives the program length.  No
- * counterpart in the reference. */
+ * NULL it receives n_ops*(8+G) timestamps (ns, %globaltimer), G = the SM
+ * count: first for CTA 0 then the last CTA, per op: op started, input staged,
+ * op finished, producer done issuing the op's weights; then per op, every
+ * CTA's finish time.  *n_ops receives the program length.  No counterpart in
+ * the reference. */
 int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64_t trace_cap,
                            int32_t *n_ops, double *ms);
 
