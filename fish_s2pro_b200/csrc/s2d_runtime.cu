@@ -7,6 +7,7 @@
 // over the 4 Fast-AR layers), the embedding-sum feedback, the 36-layer
 // Slow-AR step, the masked LM head and the semantic sampler; it is replayed
 // once per frame without any host round-trip.
+#include <cublas_v2.h>
 #include <cuda_fp16.h>
 #include <math.h>
 #include <stdio.h>
@@ -22,6 +23,7 @@
 #include "../../include/s2d.h"
 #include "s2d_gguf.h"
 #include "s2d_kernels.cuh"
+#include "s2d_prefill.cuh"
 
 using namespace s2d;
 
@@ -109,6 +111,12 @@ struct S2dHandle {
     // persistent layer engine
     bool use_engine = true;
     int num_sms = 0;
+    // batched prefill (s2d_prefill.cu): up to pf_cap tokens per layer pass
+    cublasHandle_t blas = nullptr;
+    int pf_cap = 0;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_act = nullptr;
+    float *pf_inv = nullptr, *pf_y2 = nullptr, *pf_y2b = nullptr;
+    __half *pf_xs = nullptr;
     uint32_t *engine_epoch = nullptr;  // launch epoch of the engine's LL words (starts at 1)
     // engine activations as LL words: residual, QKV, attention out, SwiGLU out, split partials
     uint64_t *ll_x = nullptr, *ll_qkv = nullptr, *ll_att = nullptr, *ll_act = nullptr, *ll_part = nullptr;
@@ -916,6 +924,86 @@ int32_t check_device_error(S2dHandle *h) {
 // Slow-AR eval over n tokens at positions n_past.. (SlowArState::eval,
 // slow_ar.rs:456-527).  Leaves the post-norm hidden in hidden_post and the
 // logits in h->logits.
+// Prefill chunk length of the batched path, and the smallest prompt it takes.
+constexpr int kPrefillChunk = 512;
+constexpr int kPrefillMin = 8;
+
+int32_t ensure_prefill(S2dHandle *h) {
+    if (h->pf_cap) return S2D_OK;
+    if (!h->blas) {
+        if (cublasCreate(&h->blas) != CUBLAS_STATUS_SUCCESS) return set_err(h, S2D_ECUDA, "cublasCreate failed");
+        if (cublasSetStream(h->blas, h->stream) != CUBLAS_STATUS_SUCCESS)
+            return set_err(h, S2D_ECUDA, "cublasSetStream failed");
+    }
+    const ArShape &a = h->slow;
+    const size_t T = kPrefillChunk, kmax = (size_t)std::max(std::max(a.d, a.qs()), a.F);
+    const size_t nmax = (size_t)std::max(std::max(a.d, a.qkv_out()), a.F);
+    CK(cudaMalloc(&h->pf_x, T * a.d * sizeof(float)));
+    CK(cudaMalloc(&h->pf_qkv, T * a.qkv_out() * sizeof(float)));
+    CK(cudaMalloc(&h->pf_q, T * a.qs() * sizeof(float)));
+    CK(cudaMalloc(&h->pf_att, T * a.qs() * sizeof(float)));
+    CK(cudaMalloc(&h->pf_act, T * a.F * sizeof(float)));
+    CK(cudaMalloc(&h->pf_inv, T * sizeof(float)));
+    CK(cudaMalloc(&h->pf_y2, 2 * T * nmax * sizeof(float)));
+    CK(cudaMalloc(&h->pf_y2b, 2 * T * nmax * sizeof(float)));
+    CK(cudaMalloc(&h->pf_xs, 2 * T * kmax * sizeof(__half)));
+    h->pf_cap = (int)T;
+    return S2D_OK;
+}
+
+// Y2 [2T][N] = xs [2T][K] (f16) x W^T, W [N][K] f16 row-major, f32 accumulation.
+int32_t prefill_gemm(S2dHandle *h, const uint16_t *W, int N, int K, int T, float *Y2) {
+    const float one = 1.0f, zero = 0.0f;
+    const cublasStatus_t st =
+        cublasGemmEx(h->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * T, K, &one, W, CUDA_R_16F, K, h->pf_xs, CUDA_R_16F, K,
+                     &zero, Y2, CUDA_R_32F, N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    if (st != CUBLAS_STATUS_SUCCESS) return set_err(h, S2D_ECUDA, "cublasGemmEx failed (" + std::to_string((int)st) + ")");
+    return S2D_OK;
+}
+
+// The Slow-AR layers over T (<= pf_cap) embedded tokens in pf_x at positions
+// pos0 .. pos0 + T - 1 (forward_slow_ar_block_prefill_layers_cached,
+// slow_ar.rs:1002-1039, a layer at a time over all the tokens).
+int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
+    const ArShape &a = h->slow;
+    const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F;
+    int32_t rc;
+    for (int l = 0; l < a.L; ++l) {
+        const LayerDev &L = h->slow_layers[(size_t)l];
+        // attention_norm + WQKV
+        CK(launch_split_rows(h->pf_x, d, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        if ((rc = prefill_gemm(h, L.wqkv, qo, d, T, h->pf_y2))) return rc;
+        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, T, qo, h->pf_qkv, qo, nullptr, 0, h->stream));
+        // QK-norm + RoPE + KV write for all T tokens
+        RopeArgs r{};
+        __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
+        r.qkv = h->pf_qkv, r.ld_qkv = qo, r.q_out = h->pf_q;
+        r.kcache = base, r.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd, r.max_seq = h->cfg.max_seq;
+        r.q_norm = L.q_norm, r.k_norm = L.k_norm, r.rope_denom = h->rope_slow;
+        r.eps = a.eps, r.pos_dev = nullptr, r.pos_const = pos0;
+        r.H = a.H, r.Hkv = a.Hkv, r.hd = a.hd, r.M = T, r.done = nullptr, r.error = &h->st->error;
+        CK(launch_rope_kv(r, true, h->stream, false));
+        // causal GQA attention over the cache
+        CK(launch_prefill_attention(h->pf_q, r.kcache, r.vcache, true, h->cfg.max_seq, h->pf_att, T, pos0, a.H,
+                                    a.Hkv, a.hd, 1.0f / sqrtf((float)a.hd), h->stream));
+        // wo + residual
+        CK(launch_split_rows(h->pf_att, qs, T, qs, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        if ((rc = prefill_gemm(h, L.wo, d, qs, T, h->pf_y2))) return rc;
+        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, h->pf_x, d, h->pf_x, d, h->stream));
+        // ffn_norm + w1 / w3 + SwiGLU
+        CK(launch_split_rows(h->pf_x, d, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        if ((rc = prefill_gemm(h, L.w1, F, d, T, h->pf_y2))) return rc;
+        if ((rc = prefill_gemm(h, L.w3, F, d, T, h->pf_y2b))) return rc;
+        CK(launch_combine(PF_SWIGLU_SLOW, h->pf_y2, h->pf_y2b, h->pf_inv, T, F, h->pf_act, F, nullptr, 0, h->stream));
+        // w2 + residual
+        CK(launch_split_rows(h->pf_act, F, T, F, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        if ((rc = prefill_gemm(h, L.w2, d, F, T, h->pf_y2))) return rc;
+        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, h->pf_x, d, h->pf_x, d, h->stream));
+        h->launches += 13;
+    }
+    return S2D_OK;
+}
+
 int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t logits_mode,
                   uint32_t im_end) {
     const S2dGraphSpec &s = h->spec;
@@ -948,6 +1036,29 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
     int32_t rc = ensure_tokens(h, (size_t)n_flat);
     if (rc) return rc;
     CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
+    if (n >= kPrefillMin && h->spec.linear_type == 1 /* F16 */) {
+        if ((rc = ensure_prefill(h))) return rc;
+        for (int64_t c0 = 0; c0 < n; c0 += h->pf_cap) {
+            const int T = (int)std::min<int64_t>(h->pf_cap, n - c0);
+            EmbedArgs ea{};
+            ea.tokens = h->tokens_dev + c0 * cd, ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = s.hidden;
+            ea.K = s.num_codebooks, ea.cb_size = s.codebook_size, ea.vocab = s.vocab_size;
+            ea.cb_rows = s.codebook_rows, ea.sem_begin = (uint32_t)s.semantic_begin_id;
+            ea.sem_end = (uint32_t)s.semantic_end_id, ea.scale_on = 1;
+            ea.sem_scale = 1.0f / sqrtf((float)(s.num_codebooks + 1));
+            ea.out = h->pf_x, ea.M = T, ea.error = &h->st->error;
+            h->launches += 1;
+            CK(launch_embed(ea, h->stream, false));
+            if ((rc = prefill_layers(h, T, (int)(h->n_past + c0)))) return rc;
+            if (c0 + T >= n)
+                CK(enqueue_lm_head(h, h->pf_x + (size_t)(T - 1) * s.hidden, logits_mode == S2D_LOGITS_FULL, im_end,
+                                   nullptr));
+        }
+        rc = check_device_error(h);
+        if (rc) return rc;
+        h->n_past += (int32_t)n;
+        return S2D_OK;
+    }
     for (int64_t c0 = 0; c0 < n;) {
         int M = (int)std::min<int64_t>(kMaxM, n - c0);
         if (M == 3) M = 2;  // GEMV instantiations: 1, 2, 4
@@ -1005,6 +1116,10 @@ void free_handle(S2dHandle *h) {
     for (EngineProgram &p : h->fast_progs)
         if (p.ops) cudaFree(p.ops);
     for (auto &kv : h->tiled) cudaFree(kv.second);
+    for (void *p : {(void *)h->pf_x, (void *)h->pf_qkv, (void *)h->pf_q, (void *)h->pf_att, (void *)h->pf_act,
+                    (void *)h->pf_inv, (void *)h->pf_y2, (void *)h->pf_y2b, (void *)h->pf_xs})
+        if (p) cudaFree(p);
+    if (h->blas) cublasDestroy(h->blas);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
     if (h->ev2) cudaEventDestroy(h->ev2);
