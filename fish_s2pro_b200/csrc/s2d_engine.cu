@@ -116,7 +116,7 @@ constexpr int kRowsPerWarp = kEngineTileRows / kEngineConsumerWarps;  // 4
 static_assert(kRowsPerWarp * kEngineConsumerWarps == kEngineTileRows, "tile mapping");
 
 struct GemvTiling {
-    int r0, n, ntiles, mats, K;
+    int r0, n, ntiles, mats, K, wt;
     SliceGeom sg;
     __device__ __forceinline__ GemvTiling(const EngineOp &op, int slot_bytes) {
         int r1;
@@ -124,7 +124,8 @@ struct GemvTiling {
         n = r1 - r0;
         mats = op.W2 ? 2 : 1;
         K = op.K;
-        sg = engine_slice_geom(mats, K, slot_bytes);
+        wt = op.wt;
+        sg = engine_slice_geom(mats, K, slot_bytes, op.wt);
         ntiles = engine_tile_count(n, sg.rmax);
     }
     // rows [*tr0, *tr0 + *R) of tile t
@@ -229,10 +230,9 @@ __device__ void attn_slot(const EngineOp &op, const AttnPlan &pl, int j, SlotCop
 struct SlotIter {
     int i = -1, t = 0, s = 0;  // op, tile (ATTN: slot), slice of the next slot
     bool attn = false;
-    int r0 = 0, n = 0, ntiles = 0, mats = 1, K = 0, tr0 = 0, R = 0;
+    int r0 = 0, n = 0, ntiles = 0, mats = 1, K = 0, tr0 = 0, R = 0, wt = 0;
     SliceGeom sg{};
-    const uint16_t *Wt = nullptr;
-    AttnPlan *pl = nullptr;
+    const uint8_t *Wt = nullptr;
     __device__ void set_tile() {
         int a0, b0;
         engine_tile_rows(n, t, ntiles, &a0, &b0);
@@ -249,8 +249,9 @@ struct SlotIter {
                     ++t;
                 } else {
                     const int kw = min(sg.kt, K - s * sg.kt);
-                    c.src[0] = Wt + (size_t)tr0 * K * mats + (size_t)s * R * sg.kt * mats;
-                    c.bytes[0] = (uint32_t)(mats * R * kw * 2);
+                    c.src[0] = Wt + (size_t)tr0 * engine_row_bytes(wt, K) * mats +
+                               (size_t)s * R * engine_row_bytes(wt, sg.kt) * mats;
+                    c.bytes[0] = (uint32_t)(mats * R * engine_row_bytes(wt, kw));
                     if (++s == sg.nk) {
                         s = 0;
                         if (++t < ntiles) set_tile();
@@ -267,7 +268,8 @@ struct SlotIter {
                 ntiles = plan.slots();
             } else {
                 const GemvTiling T(op, a.slot_bytes);
-                r0 = T.r0, n = T.n, ntiles = T.ntiles, mats = T.mats, K = T.K, sg = T.sg, Wt = op.Wt;
+                r0 = T.r0, n = T.n, ntiles = T.ntiles, mats = T.mats, K = T.K, sg = T.sg, wt = T.wt;
+                Wt = reinterpret_cast<const uint8_t *>(op.Wt);
                 if (ntiles) set_tile();
             }
         }
@@ -323,30 +325,68 @@ __device__ void producer(const EngineArgs &a, uint64_t *full, uint64_t *empty, u
     }
 }
 
-// Out-of-place copy of a linear's weights into slot order (see GemvTiling):
-// one block per output row.
-__global__ void relayout_kernel(const uint16_t *W, const uint16_t *W2, int N, int K, int n_contig, int row_base,
-                                int extra_row, int G, int slot_bytes, uint16_t *dst) {
+// The 6-bit scale and min of sub-block j of a ggml Q4_K superblock from its
+// 12 packed bytes (the published Q4_K block format).
+__device__ __forceinline__ void q4k_sub_scale(int j, const uint8_t *p, int *sc, int *mn) {
+    if (j < 4) {
+        *sc = p[j] & 63;
+        *mn = p[j + 4] & 63;
+    } else {
+        *sc = (p[j + 4] & 0x0f) | ((p[j - 4] >> 6) << 4);
+        *mn = (p[j + 4] >> 4) | ((p[j] >> 6) << 4);
+    }
+}
+
+// Out-of-place copy of a linear's weights into slot order (see GemvTiling
+// and EngineWeight): one block per output row, threads over 32-element
+// units (8-element ones for F16).
+__global__ void relayout_kernel(const uint8_t *W, const uint8_t *W2, int gtype, int wt, int N, int K, int n_contig,
+                                int row_base, int extra_row, int G, int slot_bytes, uint8_t *dst) {
     const int r = blockIdx.x;
     const int mats = W2 ? 2 : 1;
     // the CTA owning row r: the largest c with floor(N c / G) <= r
     const int c = (int)((((long long)r + 1) * G - 1) / N);
     int r0, r1;
     engine_cta_rows(N, c, G, &r0, &r1);
-    const SliceGeom sg = engine_slice_geom(mats, K, slot_bytes);
+    const SliceGeom sg = engine_slice_geom(mats, K, slot_bytes, wt);
     const int n = r1 - r0, nt = engine_tile_count(n, sg.rmax), rel = r - r0;
     const int t = (int)((((long long)rel + 1) * nt - 1) / n);
     int ta, tb;
     engine_tile_rows(n, t, nt, &ta, &tb);
     const int R = tb - ta, q = rel - ta, tr0 = r0 + ta;
     const int src_row = n_contig < 0 ? r : (r < n_contig ? row_base + r : extra_row);
-    uint16_t *tile = dst + (size_t)tr0 * K * mats;
-    for (int ch = threadIdx.x; ch < K / 8; ch += blockDim.x) {
-        const int col = ch * 8, s = col / sg.kt, kw = min(sg.kt, K - s * sg.kt), cc = col - s * sg.kt;
-        uint16_t *slot = tile + (size_t)s * R * sg.kt * mats;
+    uint8_t *tile = dst + (size_t)tr0 * engine_row_bytes(wt, K) * mats;
+    const size_t src_row_bytes = gtype == 1 ? (size_t)K * 2 : gtype == 8 ? (size_t)K / 32 * 34 : (size_t)K / 256 * 144;
+    const int unit = wt == EW_F16 ? 8 : 32;
+    for (int u = threadIdx.x; u < K / unit; u += blockDim.x) {
+        const int col = u * unit, s = col / sg.kt, kw = min(sg.kt, K - s * sg.kt), cc = col - s * sg.kt;
+        uint8_t *slot = tile + (size_t)s * R * engine_row_bytes(wt, sg.kt) * mats;
         for (int m = 0; m < mats; ++m) {
-            const uint16_t *src = (m ? W2 + (size_t)r * K : W + (size_t)src_row * K) + col;
-            *reinterpret_cast<uint4 *>(slot + ((size_t)m * R + q) * kw + cc) = *reinterpret_cast<const uint4 *>(src);
+            const uint8_t *srow = (m ? W2 + (size_t)r * src_row_bytes : W + (size_t)src_row * src_row_bytes);
+            uint8_t *drow = slot + ((size_t)m * R + q) * engine_row_bytes(wt, kw);
+            if (wt == EW_F16) {
+                *reinterpret_cast<uint4 *>(drow + (size_t)cc * 2) = *reinterpret_cast<const uint4 *>(srow + (size_t)col * 2);
+            } else if (wt == EW_Q8_0) {
+                const uint8_t *blk = srow + (size_t)u * 34;
+                for (int i = 0; i < 32; ++i) drow[cc + i] = blk[2 + i];
+                drow[kw + cc / 16] = blk[0], drow[kw + cc / 16 + 1] = blk[1];
+            } else {
+                // sub-block j of superblock sb: elements 32j.. of the superblock
+                const int sb = col / 256, j = (col % 256) / 32;
+                const uint8_t *blk = srow + (size_t)sb * 144;
+                const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(blk[2] | (blk[3] << 8))));
+                int sc, mn;
+                q4k_sub_scale(j, blk + 4, &sc, &mn);
+                const uint8_t *qs = blk + 16 + 32 * (j / 2);  // group j/2: low nibbles j even, high j odd
+                for (int i = 0; i < 16; ++i) {
+                    const int lo = (j & 1) ? qs[2 * i] >> 4 : qs[2 * i] & 0x0f;
+                    const int hi = (j & 1) ? qs[2 * i + 1] >> 4 : qs[2 * i + 1] & 0x0f;
+                    drow[cc / 2 + i] = (uint8_t)(lo | (hi << 4));
+                }
+                float2 ab = make_float2(d * (float)sc, dmin * (float)mn);
+                *reinterpret_cast<float2 *>(drow + kw / 2 + (cc / 32) * 8) = ab;
+            }
         }
     }
 }
@@ -591,6 +631,93 @@ __device__ __forceinline__ void gemv_slot(uint32_t wbase, uint32_t rstride, uint
     }
 }
 
+__device__ __forceinline__ uint2 lds_u2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ unsigned short lds_u16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
+
+// acc += sum over the 4 int8 of `q` of (d * q_i) * x_i (ggml Q8_0 value d*q).
+__device__ __forceinline__ float dot4_q8(uint32_t q, float d, float4 x, float acc) {
+    acc = fmaf(__fmul_rn((float)(int8_t)(q & 0xff), d), x.x, acc);
+    acc = fmaf(__fmul_rn((float)(int8_t)((q >> 8) & 0xff), d), x.y, acc);
+    acc = fmaf(__fmul_rn((float)(int8_t)((q >> 16) & 0xff), d), x.z, acc);
+    acc = fmaf(__fmul_rn((float)(int8_t)(q >> 24), d), x.w, acc);
+    return acc;
+}
+// acc += sum over the 8 nibbles of `q` (element 2i low, 2i+1 high of byte
+// i) of (a * n - b) * x (ggml Q4_K value (d*sc)*q - dmin*m).
+__device__ __forceinline__ float dot8_q4(uint32_t q, float a, float b, float4 x0, float4 x1, float acc) {
+    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fmaf(__fsub_rn(__fmul_rn(a, (float)((q >> (4 * i)) & 0xf)), b), xs[i], acc);
+    return acc;
+}
+
+// One slot's arithmetic for quantized weights (EW_Q8_0 / EW_Q4_K): like
+// gemv_slot over 16-column chunks; a row slice of kw columns holds the
+// chunk quants at q_off + chunk * qb and the scales at s_off.
+template <int WT, int NR, int M, int MATS, int CH>
+__device__ __forceinline__ void gemv_slot_q(uint32_t wbase, uint32_t rstride, uint32_t mstride, uint32_t xbase,
+                                            int K, int kw, int nch, int lane,
+                                            float (&acc)[CH][kRowsPerWarp][MATS][M]) {
+#pragma unroll 1
+    for (int c = lane; c < nch; c += 32 * CH) {
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+            const int cj = c + 32 * j;
+            if (j > 0 && cj >= nch) break;
+            float4 x[M][4];
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const uint32_t xa = xbase + (uint32_t)((m * K + cj * 16) * 4);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) x[m][v] = lds_f4(xa + 16 * v);
+            }
+#pragma unroll
+            for (int i = 0; i < NR; ++i)
+#pragma unroll
+                for (int q = 0; q < MATS; ++q) {
+                    const uint32_t row = wbase + i * rstride + q * mstride;
+                    if (WT == EW_Q8_0) {
+                        const uint4 w = lds_u4(row + (uint32_t)cj * 16);
+                        const float d = __half2float(__ushort_as_half(lds_u16(row + (uint32_t)(kw + (cj >> 1) * 2))));
+#pragma unroll
+                        for (int m = 0; m < M; ++m) {
+                            float t = acc[j][i][q][m];
+                            t = dot4_q8(w.x, d, x[m][0], t);
+                            t = dot4_q8(w.y, d, x[m][1], t);
+                            t = dot4_q8(w.z, d, x[m][2], t);
+                            t = dot4_q8(w.w, d, x[m][3], t);
+                            acc[j][i][q][m] = t;
+                        }
+                    } else {
+                        const uint2 w = lds_u2(row + (uint32_t)cj * 8);
+                        const uint32_t sa = row + (uint32_t)(kw / 2 + (cj >> 1) * 8);
+                        const float a = __uint_as_float(lds_u32(sa)), b = __uint_as_float(lds_u32(sa + 4));
+#pragma unroll
+                        for (int m = 0; m < M; ++m) {
+                            float t = acc[j][i][q][m];
+                            t = dot8_q4(w.x, a, b, x[m][0], x[m][1], t);
+                            t = dot8_q4(w.y, a, b, x[m][2], x[m][3], t);
+                            acc[j][i][q][m] = t;
+                        }
+                    }
+                }
+        }
+    }
+}
+
 // Consume this CTA's slots of one GEMV op (see GemvTiling).  Every warp
 // takes every slot: per 16-byte column chunk a lane loads the inputs once
 // and the chunk of each of its warp's rows.
@@ -628,15 +755,36 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, int opi, u
             const int k0 = s * sg.kt, kw = min(sg.kt, K - k0), nch = kw >> 3;
             const bool got = mbar_wait(&full[slot], phase, a.error, kErrEngineWeights);
             if (!__all_sync(0xffffffffu, got)) return false;
-            const uint32_t wbase = ring_s + (uint32_t)slot * slot_bytes + (uint32_t)(warp * kw * 2);
-            const uint32_t rstride = (uint32_t)(kEngineConsumerWarps * kw * 2), mstride = (uint32_t)(R * kw * 2);
+            const uint32_t rb = (uint32_t)engine_row_bytes(T.wt, kw);  // one row slice
+            const uint32_t wbase = ring_s + (uint32_t)slot * slot_bytes + (uint32_t)warp * rb;
+            const uint32_t rstride = (uint32_t)kEngineConsumerWarps * rb, mstride = (uint32_t)R * rb;
             const uint32_t xbase = xs_s + (uint32_t)(k0 * 4);
-            switch (nrw) {
-            case 4: gemv_slot<4, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
-            case 3: gemv_slot<3, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
-            case 2: gemv_slot<2, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
-            case 1: gemv_slot<1, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
-            default: break;
+            if (T.wt == EW_F16) {
+                switch (nrw) {
+                case 4: gemv_slot<4, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
+                case 3: gemv_slot<3, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
+                case 2: gemv_slot<2, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
+                case 1: gemv_slot<1, M, MATS, CH>(wbase, rstride, mstride, xbase, K, nch, lane, acc); break;
+                default: break;
+                }
+            } else if (T.wt == EW_Q8_0) {
+                const int nq = kw >> 4;
+                switch (nrw) {
+                case 4: gemv_slot_q<EW_Q8_0, 4, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 3: gemv_slot_q<EW_Q8_0, 3, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 2: gemv_slot_q<EW_Q8_0, 2, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 1: gemv_slot_q<EW_Q8_0, 1, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                default: break;
+                }
+            } else {
+                const int nq = kw >> 4;
+                switch (nrw) {
+                case 4: gemv_slot_q<EW_Q4_K, 4, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 3: gemv_slot_q<EW_Q4_K, 3, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 2: gemv_slot_q<EW_Q4_K, 2, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                case 1: gemv_slot_q<EW_Q4_K, 1, M, MATS, CH>(wbase, rstride, mstride, xbase, K, kw, nq, lane, acc); break;
+                default: break;
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -1093,11 +1241,29 @@ cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream
     return cudaLaunchKernelEx(&cfg, engine_kernel, a);
 }
 
-cudaError_t launch_engine_relayout(const uint16_t *W, const uint16_t *W2, int N, int K, int n_contig,
-                                   int row_base, int extra_row, int grid, int slot_bytes, uint16_t *dst,
+int engine_weight_format(int gtype) {
+    switch (gtype) {
+    case 1: return EW_F16;
+    case 8: return EW_Q8_0;
+    case 12: return EW_Q4_K;
+    }
+    return -1;
+}
+
+size_t engine_weight_bytes(int gtype, int N, int K, int mats) {
+    const int wt = engine_weight_format(gtype);
+    return wt < 0 ? 0 : (size_t)N * engine_row_bytes(wt, K) * mats;
+}
+
+cudaError_t launch_engine_relayout(const void *W, const void *W2, int gtype, int N, int K, int n_contig,
+                                   int row_base, int extra_row, int grid, int slot_bytes, void *dst,
                                    cudaStream_t s) {
-    if (N <= 0 || K <= 0 || K % 8 || grid <= 0) return cudaErrorInvalidValue;
-    relayout_kernel<<<N, 128, 0, s>>>(W, W2, N, K, n_contig, row_base, extra_row, grid, slot_bytes, dst);
+    const int wt = engine_weight_format(gtype);
+    if (wt < 0 || N <= 0 || K <= 0 || grid <= 0) return cudaErrorInvalidValue;
+    if (K % (wt == EW_F16 ? 8 : wt == EW_Q8_0 ? 256 : 256)) return cudaErrorInvalidValue;
+    relayout_kernel<<<N, 128, 0, s>>>(reinterpret_cast<const uint8_t *>(W), reinterpret_cast<const uint8_t *>(W2),
+                                      gtype, wt, N, K, n_contig, row_base, extra_row, grid, slot_bytes,
+                                      reinterpret_cast<uint8_t *>(dst));
     return cudaGetLastError();
 }
 

@@ -178,7 +178,138 @@ static cudaError_t gemv_dispatch_epi(const GemvArgs &a, int epi, cudaStream_t s,
     return cudaErrorInvalidValue;
 }
 
+// ---------------------------------------------------------------------------
+// Quantized linears for the per-op path (single steps, short prefills, the
+// op-level APIs): one block per output row, threads over 32-element ggml
+// sub-blocks, each weight dequantised as the block format defines
+// (EngineWeight) and multiplied with the (optionally RMS-normalised) input.
+// Not a hot path: decode frames run in the persistent engine.
+// ---------------------------------------------------------------------------
+
+// The 6-bit scale and min of sub-block j of a ggml Q4_K superblock.
+__device__ __forceinline__ void q4k_scale_min_dev(int j, const uint8_t *p, int *sc, int *mn) {
+    if (j < 4) {
+        *sc = p[j] & 63;
+        *mn = p[j + 4] & 63;
+    } else {
+        *sc = (p[j + 4] & 0x0f) | ((p[j - 4] >> 6) << 4);
+        *mn = (p[j + 4] >> 4) | ((p[j] >> 6) << 4);
+    }
+}
+__device__ __forceinline__ float f16_bits(const uint8_t *p) {
+    return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+// Element i (0..31) of 32-element sub-block `blk` of a ggml row.
+struct QuantSub {
+    float a, b;  // value = a * q - b (Q4_K) or q * a (Q8_0, b unused)
+    const uint8_t *q;
+    int shift;   // Q4_K nibble shift
+    __device__ QuantSub(int wq, const uint8_t *row, int blk) {
+        if (wq == 1) {
+            const uint8_t *p = row + (size_t)blk * 34;
+            a = f16_bits(p), b = 0.f, q = p + 2, shift = 0;
+        } else {
+            const uint8_t *p = row + (size_t)(blk / 8) * 144;
+            const int j = blk % 8;
+            int sc, mn;
+            q4k_scale_min_dev(j, p + 4, &sc, &mn);
+            a = f16_bits(p) * (float)sc, b = f16_bits(p + 2) * (float)mn;
+            q = p + 16 + 32 * (j / 2), shift = (j & 1) * 4;
+        }
+    }
+    __device__ __forceinline__ float at(int wq, int i) const {
+        if (wq == 1) return __fmul_rn((float)(int8_t)q[i], a);
+        return __fsub_rn(__fmul_rn(a, (float)((q[i] >> shift) & 0xf)), b);
+    }
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(128) gemv_quant_kernel(const GemvArgs a, int M) {
+    grid_dep_launch();
+    grid_dep_wait();
+    if (a.done && *a.done) return;
+    __shared__ float red[4];
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const int src = a.n_contig < 0 ? row : (row < a.n_contig ? a.row_base + row : a.extra_row);
+    const size_t rb = a.wq == 1 ? (size_t)a.K / 32 * 34 : (size_t)a.K / 256 * 144;
+    const uint8_t *wrow = reinterpret_cast<const uint8_t *>(a.W) + (size_t)src * rb;
+    const uint8_t *wrow2 = a.W2 ? reinterpret_cast<const uint8_t *>(a.W2) + (size_t)row * rb : nullptr;
+    auto block_sum = [&](float v) {
+        v = warp_sum(v);
+        if ((tid & 31) == 0) red[tid >> 5] = v;
+        __syncthreads();
+        const float t = red[0] + red[1] + red[2] + red[3];
+        __syncthreads();
+        return t;
+    };
+    for (int m = 0; m < M; ++m) {
+        const float *x = a.x + (size_t)m * a.ldx;
+        float scale = 1.f;
+        if (a.norm_w) {
+            float ss = 0.f;
+            for (int i = tid; i < a.K; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+            scale = 1.0f / sqrtf(block_sum(ss) / (float)a.K + a.eps);
+        }
+        float acc = 0.f, acc2 = 0.f;
+        for (int blk = tid; blk < a.K / 32; blk += blockDim.x) {
+            const QuantSub s1(a.wq, wrow, blk);
+            const QuantSub s2(a.wq, wrow2 ? wrow2 : wrow, blk);
+            for (int i = 0; i < 32; ++i) {
+                float xv = x[blk * 32 + i];
+                if (a.norm_w) xv = __fmul_rn(__fmul_rn(xv, scale), a.norm_w[blk * 32 + i]);
+                acc = fmaf(s1.at(a.wq, i), xv, acc);
+                if (wrow2) acc2 = fmaf(s2.at(a.wq, i), xv, acc2);
+            }
+        }
+        acc = block_sum(acc);
+        if (EPI == EPI_SWIGLU_SLOW || EPI == EPI_SWIGLU_FAST) acc2 = block_sum(acc2);
+        if (tid == 0) {
+            float out;
+            if (EPI == EPI_STORE) {
+                out = acc;
+            } else if (EPI == EPI_RESID) {
+                out = __fadd_rn(a.resid[(size_t)m * a.ldr + row], acc);
+            } else if (EPI == EPI_SWIGLU_SLOW) {
+                const float sig = 1.0f / (1.0f + expf(-acc));
+                out = __fmul_rn(__fmul_rn(acc, sig), acc2);
+            } else {
+                out = __fmul_rn(acc / (1.0f + expf(-acc)), acc2);
+            }
+            a.y[(size_t)m * a.ldy + row] = out;
+        }
+    }
+}
+
+// A tensor's ggml blocks are contiguous, so its elements are one long row.
+__global__ void dequant_kernel(int wq, const uint8_t *src, float *dst, int64_t n) {
+    const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= n / 32) return;
+    const uint8_t *base = src + (wq == 1 ? (size_t)(blk / 8) * 8 * 34 : (size_t)(blk / 8) * 144);
+    const QuantSub s(wq, base, (int)(blk % 8));
+    for (int i = 0; i < 32; ++i) dst[blk * 32 + i] = s.at(wq, i);
+}
+
+cudaError_t launch_dequant(int gtype, const void *src, float *dst, int64_t n, cudaStream_t s) {
+    const int wq = gtype == 8 ? 1 : gtype == 12 ? 2 : 0;
+    if (!wq || n % (wq == 1 ? 32 : 256)) return cudaErrorInvalidValue;
+    const int64_t blocks = n / 32;
+    dequant_kernel<<<(unsigned)((blocks + 255) / 256), 256, 0, s>>>(wq, reinterpret_cast<const uint8_t *>(src), dst, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_gemv(const GemvArgs &a, int M, int epi, cudaStream_t s, bool pdl) {
+    if (a.wq != 0) {
+        if (a.K % (a.wq == 1 ? 32 : 256)) return cudaErrorInvalidValue;
+        switch (epi) {
+        case EPI_STORE: return s2d_launch(gemv_quant_kernel<EPI_STORE>, dim3(a.N), dim3(128), 0, s, pdl, a, M);
+        case EPI_RESID: return s2d_launch(gemv_quant_kernel<EPI_RESID>, dim3(a.N), dim3(128), 0, s, pdl, a, M);
+        case EPI_SWIGLU_SLOW:
+            return s2d_launch(gemv_quant_kernel<EPI_SWIGLU_SLOW>, dim3(a.N), dim3(128), 0, s, pdl, a, M);
+        case EPI_SWIGLU_FAST:
+            return s2d_launch(gemv_quant_kernel<EPI_SWIGLU_FAST>, dim3(a.N), dim3(128), 0, s, pdl, a, M);
+        }
+        return cudaErrorInvalidValue;
+    }
     if (a.K % 8 != 0 || a.K <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     if ((size_t)M * a.K * sizeof(float) > 200 * 1024) return cudaErrorInvalidValue;
     switch (M) {

@@ -22,7 +22,7 @@ struct DevState {
 enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU_SLOW = 2, EPI_SWIGLU_FAST = 3 };
 
 struct GemvArgs {
-    const uint16_t *W;   // f16 bits, [N][K] row-major (GGUF dims [K, N])
+    const uint16_t *W;   // f16 bits, [N][K] row-major (GGUF dims [K, N]), or ggml blocks (wq)
     const uint16_t *W2;  // second matrix (w3) for the SwiGLU epilogue
     const float *x;      // [M][ldx] input activations
     int ldx;
@@ -36,6 +36,7 @@ struct GemvArgs {
     int K, N;
     int row_base, n_contig, extra_row;  // row remap when n_contig >= 0
     const int32_t *done; // early-exit flag (DevState::done) or nullptr
+    int wq;              // weight format: 0 f16 rows, 1 ggml Q8_0, 2 ggml Q4_K (EngineWeight)
 };
 
 struct RopeArgs {
@@ -168,6 +169,7 @@ struct EngineOp {
     // of row tile [tr0, tr0 + R) and K slice s starts at element
     // Wt + tr0 * K * mats + s * R * kt * mats and holds [mat][R][kw].
     const uint16_t *Wt;
+    int wt;              // EngineWeight of W (and W2)
 };
 
 __host__ __device__ __forceinline__ uint32_t engine_tag(uint32_t epoch, int op) {
@@ -206,18 +208,33 @@ __host__ __device__ __forceinline__ void engine_cta_rows(int N, int c, int G, in
     *r1 = (int)(((long long)N * (c + 1)) / G);
 }
 
-// K-slice geometry of a GEMV: slices of kt columns (512 / mats, so that a
-// slice row is 64 / mats 16-byte chunks, two or one per consumer lane), the
-// last one possibly shorter, and row tiles of at most rmax rows so that a
-// slot of mats * rmax * kt f16 fits slot_bytes.
+// Weight formats of the engine's GEMVs.  In slot order (engine_relayout) a
+// row slice of kw columns is: F16, kw f16 values; Q8_0 (ggml blocks of 32:
+// f16 scale d + 32 int8, value d*q), kw int8 quants then kw/32 f16 scales;
+// Q4_K (ggml superblocks of 256 in sub-blocks of 32, value (d*sc)*q -
+// dmin*m), kw/2 bytes of 4-bit quants (byte k: element 2k in the low
+// nibble, 2k+1 in the high one) then per sub-block the f32 pair
+// (d*sc, dmin*m).
+enum EngineWeight { EW_F16 = 0, EW_Q8_0 = 1, EW_Q4_K = 2 };
+__host__ __device__ __forceinline__ int engine_row_bytes(int wt, int kw) {
+    return wt == EW_F16 ? 2 * kw : wt == EW_Q8_0 ? kw + kw / 16 : kw / 2 + kw / 4;
+}
+// Columns per lane chunk: 8 f16 (16 bytes), 16 quantized weights.
+__host__ __device__ __forceinline__ int engine_chunk_cols(int wt) { return wt == EW_F16 ? 8 : 16; }
+
+// K-slice geometry of a GEMV: slices of kt columns (64 / mats lane chunks
+// per row: two or one per consumer lane), the last one possibly shorter,
+// and row tiles of at most rmax rows so that a slot of mats * rmax row
+// slices fits slot_bytes.
 struct SliceGeom {
     int kt, nk, rmax;
 };
-__host__ __device__ inline SliceGeom engine_slice_geom(int mats, int K, int slot_bytes) {
+__host__ __device__ inline SliceGeom engine_slice_geom(int mats, int K, int slot_bytes, int wt = EW_F16) {
     SliceGeom g;
-    g.kt = 512 / mats < K ? 512 / mats : K;
+    const int kt = 64 * engine_chunk_cols(wt) / mats;
+    g.kt = kt < K ? kt : K;
     g.nk = (K + g.kt - 1) / g.kt;
-    g.rmax = slot_bytes / (mats * g.kt * 2);
+    g.rmax = slot_bytes / (mats * engine_row_bytes(wt, g.kt));
     if (g.rmax > kEngineTileRows) g.rmax = kEngineTileRows;
     if (g.rmax < 1) g.rmax = 1;
     return g;
@@ -239,12 +256,17 @@ constexpr int kErrEngineAlign = 18;    // the shared-memory ring is not 128-byte
 cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s);
 
 // Copies a linear's weights into the engine's slot order for a `grid`-CTA
-// launch with ring slots of slot_bytes: dst holds N * K * mats f16.  Output
-// row r reads source row (n_contig < 0 ? r : r < n_contig ? row_base + r :
-// extra_row) of W and row r of W2 (when W2 is not null).
-cudaError_t launch_engine_relayout(const uint16_t *W, const uint16_t *W2, int N, int K, int n_contig,
-                                   int row_base, int extra_row, int grid, int slot_bytes, uint16_t *dst,
+// launch with ring slots of slot_bytes.  W and W2 are GGUF tensors of ggml
+// type gtype (F16, Q8_0 or Q4_K: rows of K elements); dst receives
+// N * engine_row_bytes(wt, K) * mats bytes in the EngineWeight format wt.
+// Output row r reads source row (n_contig < 0 ? r : r < n_contig ?
+// row_base + r : extra_row) of W and row r of W2 (when W2 is not null).
+cudaError_t launch_engine_relayout(const void *W, const void *W2, int gtype, int N, int K, int n_contig,
+                                   int row_base, int extra_row, int grid, int slot_bytes, void *dst,
                                    cudaStream_t s);
+// Bytes of the engine copy of an N x K linear of ggml type gtype.
+size_t engine_weight_bytes(int gtype, int N, int K, int mats);
+int engine_weight_format(int gtype);  // EngineWeight, or -1 if unsupported
 
 // Attention in the engine.  A group's query vectors and the new tokens' K
 // and V rows (at most 2 tokens) sit in the shared area (attn_group_bytes per
@@ -277,6 +299,9 @@ cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_fast_init(const FastInitArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_f16_to_f32(const uint16_t *src, float *dst, int64_t n, cudaStream_t s);
+// ggml Q8_0 / Q4_K blocks (gtype 8 / 12) of n elements -> f32 (the block
+// formulas d*q and (d*sc)*q - dmin*m, each rounded once in f32).
+cudaError_t launch_dequant(int gtype, const void *src, float *dst, int64_t n, cudaStream_t s);
 cudaError_t launch_rms_norm_heads(const float *x, const float *w, float *y, int64_t n, int hd,
                                   float eps, cudaStream_t s);
 cudaError_t launch_set_state(DevState *st, int32_t n_past, int32_t prompt_cols, uint64_t rng,

@@ -32,9 +32,13 @@ namespace {
 constexpr int kMaxM = 4;  // tokens per GEMV pass (prefill chunk)
 
 struct LayerDev {
+    // linears: f16 rows, or ggml Q8_0 / Q4_K blocks (wq, an EngineWeight)
     const uint16_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w2 = nullptr, *w3 = nullptr;
     float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    int wq = EW_F16;
 };
+
+int ggml_type_of(int wq) { return wq == EW_Q8_0 ? 8 : wq == EW_Q4_K ? 12 : 1; }
 
 struct TensorDev {
     const GgufTensor *info = nullptr;
@@ -83,6 +87,7 @@ struct S2dHandle {
     float *norm_arena = nullptr;
     std::vector<LayerDev> slow_layers, fast_layers;
     const uint16_t *emb = nullptr, *cb_emb = nullptr, *fast_emb = nullptr, *fast_out = nullptr;
+    int fast_out_wq = EW_F16;
     float *norm = nullptr, *fast_norm = nullptr;
     float *rope_slow = nullptr, *rope_fast = nullptr;
     __half *kv_slow = nullptr;  // [L][2][Hkv][max_seq][hd]
@@ -334,26 +339,33 @@ int32_t bind_weights(S2dHandle *h) {
     h->slow_layers.resize((size_t)s.slow_layers);
     h->fast_layers.resize((size_t)s.fast_layers);
     uint32_t linear_type = 0;
-    auto linear = [&](const std::string &name, const ArShape &a, uint64_t in, uint64_t out) -> const uint16_t * {
+    // F16, Q8_0 or Q4_K; the five linears of a layer share one format
+    auto linear = [&](const std::string &name, LayerDev &L, bool first, uint64_t in,
+                      uint64_t out) -> const uint16_t * {
         const GgufTensor *t = need(h, name, {in, out}, &rc);
         if (!t) return nullptr;
-        if (t->type != 1) {
-            rc = set_err(h, S2D_EINVAL, name + ": only F16 linear weights are supported by this build");
+        const int wq = engine_weight_format((int)t->type);
+        if (wq < 0 || (wq == EW_Q8_0 && in % 32) || (wq == EW_Q4_K && in % 256)) {
+            rc = set_err(h, S2D_EINVAL, name + ": linear weights must be F16, Q8_0 or Q4_K (rows of whole blocks)");
+            return nullptr;
+        }
+        if (first) L.wq = wq;
+        else if (L.wq != wq) {
+            rc = set_err(h, S2D_EINVAL, name + ": the linears of a layer must share one type");
             return nullptr;
         }
         linear_type = t->type;
-        (void)a;
         return reinterpret_cast<const uint16_t *>(tdev(h, t)->dev);
     };
     for (int l = 0; l < s.slow_layers && !rc; ++l) {
         const ArShape &a = h->slow;
         const std::string p = "layers." + std::to_string(l) + ".";
         LayerDev &L = h->slow_layers[(size_t)l];
-        L.wqkv = linear(p + "attention.wqkv.weight", a, d, (uint64_t)a.qkv_out());
-        L.wo = linear(p + "attention.wo.weight", a, (uint64_t)a.qs(), d);
-        L.w1 = linear(p + "feed_forward.w1.weight", a, d, (uint64_t)a.F);
-        L.w2 = linear(p + "feed_forward.w2.weight", a, (uint64_t)a.F, d);
-        L.w3 = linear(p + "feed_forward.w3.weight", a, d, (uint64_t)a.F);
+        L.wqkv = linear(p + "attention.wqkv.weight", L, true, d, (uint64_t)a.qkv_out());
+        L.wo = linear(p + "attention.wo.weight", L, false, (uint64_t)a.qs(), d);
+        L.w1 = linear(p + "feed_forward.w1.weight", L, false, d, (uint64_t)a.F);
+        L.w2 = linear(p + "feed_forward.w2.weight", L, false, (uint64_t)a.F, d);
+        L.w3 = linear(p + "feed_forward.w3.weight", L, false, d, (uint64_t)a.F);
         const GgufTensor *an = need(h, p + "attention_norm.weight", {d}, &rc);
         const GgufTensor *fn = need(h, p + "ffn_norm.weight", {d}, &rc);
         const GgufTensor *qn = need(h, p + "attention.q_norm.weight", {(uint64_t)a.hd}, &rc);
@@ -368,11 +380,11 @@ int32_t bind_weights(S2dHandle *h) {
         const ArShape &a = h->fast;
         const std::string p = "fast_layers." + std::to_string(l) + ".";
         LayerDev &L = h->fast_layers[(size_t)l];
-        L.wqkv = linear(p + "attention.wqkv.weight", a, d, (uint64_t)a.qkv_out());
-        L.wo = linear(p + "attention.wo.weight", a, (uint64_t)a.qs(), d);
-        L.w1 = linear(p + "feed_forward.w1.weight", a, d, (uint64_t)a.F);
-        L.w2 = linear(p + "feed_forward.w2.weight", a, (uint64_t)a.F, d);
-        L.w3 = linear(p + "feed_forward.w3.weight", a, d, (uint64_t)a.F);
+        L.wqkv = linear(p + "attention.wqkv.weight", L, true, d, (uint64_t)a.qkv_out());
+        L.wo = linear(p + "attention.wo.weight", L, false, (uint64_t)a.qs(), d);
+        L.w1 = linear(p + "feed_forward.w1.weight", L, false, d, (uint64_t)a.F);
+        L.w2 = linear(p + "feed_forward.w2.weight", L, false, (uint64_t)a.F, d);
+        L.w3 = linear(p + "feed_forward.w3.weight", L, false, d, (uint64_t)a.F);
         const GgufTensor *an = need(h, p + "attention_norm.weight", {d}, &rc);
         const GgufTensor *fn = need(h, p + "ffn_norm.weight", {d}, &rc);
         if (rc) break;
@@ -381,7 +393,9 @@ int32_t bind_weights(S2dHandle *h) {
     }
     if (rc) return rc;
     h->fast_out = reinterpret_cast<const uint16_t *>(tdev(h, fo)->dev);
-    if (fo->type != 1) return set_err(h, S2D_EINVAL, "fast_output.weight: only F16 is supported by this build");
+    h->fast_out_wq = engine_weight_format((int)fo->type);
+    if (h->fast_out_wq < 0 || (h->fast_out_wq == EW_Q8_0 && s.hidden % 32) || (h->fast_out_wq == EW_Q4_K && s.hidden % 256))
+        return set_err(h, S2D_EINVAL, "fast_output.weight must be F16, Q8_0 or Q4_K");
     norms.push_back({nw, &h->norm});
     norms.push_back({fnw, &h->fast_norm});
     h->emb = reinterpret_cast<const uint16_t *>(tdev(h, emb)->dev);
@@ -514,7 +528,7 @@ cudaError_t enqueue_layer(S2dHandle *h, bool is_fast, int l, float *x, int M,
     g.n_contig = -1;
     // attention_norm + WQKV
     g.W = L.wqkv, g.x = x, g.ldx = d, g.norm_w = L.attn_norm, g.eps = a.eps;
-    g.y = h->qkv, g.ldy = a.qkv_out(), g.K = d, g.N = a.qkv_out();
+    g.y = h->qkv, g.ldy = a.qkv_out(), g.K = d, g.N = a.qkv_out(), g.wq = L.wq;
     if ((e = launch_gemv(g, M, EPI_STORE, h->stream, h->pdl))) return e;
     // QK-norm + RoPE + KV write
     RopeArgs r{};
@@ -543,19 +557,19 @@ cudaError_t enqueue_layer(S2dHandle *h, bool is_fast, int l, float *x, int M,
     g = GemvArgs{};
     g.done = done, g.n_contig = -1;
     g.W = L.wo, g.x = h->att, g.ldx = a.qs(), g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
-    g.K = a.qs(), g.N = d;
+    g.K = a.qs(), g.N = d, g.wq = L.wq;
     if ((e = launch_gemv(g, M, EPI_RESID, h->stream, h->pdl))) return e;
     // ffn_norm + w1/w3 + SwiGLU
     g = GemvArgs{};
     g.done = done, g.n_contig = -1;
     g.W = L.w1, g.W2 = L.w3, g.x = x, g.ldx = d, g.norm_w = L.ffn_norm, g.eps = a.eps;
-    g.y = h->act, g.ldy = a.F, g.K = d, g.N = a.F;
+    g.y = h->act, g.ldy = a.F, g.K = d, g.N = a.F, g.wq = L.wq;
     if ((e = launch_gemv(g, M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, h->stream, h->pdl))) return e;
     // w2 + residual
     g = GemvArgs{};
     g.done = done, g.n_contig = -1;
     g.W = L.w2, g.x = h->act, g.ldx = a.F, g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
-    g.K = a.F, g.N = d;
+    g.K = a.F, g.N = d, g.wq = L.wq;
     h->launches += 6;
     return launch_gemv(g, M, EPI_RESID, h->stream, h->pdl);
 }
@@ -592,6 +606,7 @@ cudaError_t enqueue_fast_head(S2dHandle *h, const float *xrow, const int32_t *do
     g.done = done, g.n_contig = -1;
     g.W = h->fast_out, g.x = xrow, g.ldx = h->fast.d, g.norm_w = h->fast_norm, g.eps = h->fast.eps;
     g.y = h->logits_fast, g.ldy = h->spec.codebook_size, g.K = h->fast.d, g.N = h->spec.codebook_size;
+    g.wq = h->fast_out_wq;
     h->launches += 1;
     return launch_gemv(g, 1, EPI_STORE, h->stream, h->pdl);
 }
@@ -692,8 +707,9 @@ bool engine_supported(const S2dHandle *h) {
 // writing y (LL words when y_ll).
 EngineOp gemv_op(int M, int epi, const uint16_t *W, const uint16_t *W2, const void *x, int ldx, int x_src,
                  const float *norm_w, float eps, void *y, int ldy, int y_ll, const void *resid, int resid_src,
-                 int K, int N) {
+                 int K, int N, int wt = EW_F16) {
     EngineOp o{};
+    o.wt = wt;
     o.kind = OP_GEMV, o.epi = epi, o.M = M, o.W = W, o.W2 = W2, o.x = x, o.ldx = ldx, o.x_src = x_src;
     o.norm_w = norm_w, o.eps = eps, o.y = y, o.ldy = ldy, o.y_ll = y_ll, o.resid = resid, o.ldr = ldy;
     o.resid_src = resid_src, o.K = K, o.N = N, o.n_contig = -1;
@@ -712,7 +728,7 @@ void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, cons
     const void *x = *x_src < 0 ? static_cast<const void *>(x_in) : static_cast<const void *>(h->ll_x);
     const int i_qkv = (int)ops.size();
     ops.push_back(gemv_op(M, EPI_STORE, L.wqkv, nullptr, x, d, *x_src, L.attn_norm, a.eps, h->ll_qkv, a.qkv_out(), 1,
-                          nullptr, -1, d, a.qkv_out()));
+                          nullptr, -1, d, a.qkv_out(), L.wq));
     EngineOp t{};
     t.kind = OP_ATTN, t.M = M, t.qkv = h->ll_qkv, t.ld_qkv = a.qkv_out(), t.qkv_src = i_qkv;
     if (is_fast) {
@@ -732,13 +748,13 @@ void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, cons
     ops.push_back(t);
     const int i_wo = (int)ops.size();
     ops.push_back(gemv_op(M, EPI_RESID, L.wo, nullptr, h->ll_att, a.qs(), i_att, nullptr, 0.f, h->ll_x, d, 1, x,
-                          *x_src, a.qs(), d));
+                          *x_src, a.qs(), d, L.wq));
     const int i_w13 = (int)ops.size();
     ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, h->ll_x, d, i_wo, L.ffn_norm,
-                          a.eps, h->ll_act, a.F, 1, nullptr, -1, d, a.F));
+                          a.eps, h->ll_act, a.F, 1, nullptr, -1, d, a.F, L.wq));
     *x_src = (int)ops.size();
     ops.push_back(gemv_op(M, EPI_RESID, L.w2, nullptr, h->ll_act, a.F, i_w13, nullptr, 0.f, h->ll_x, d, 1, h->ll_x,
-                          i_wo, a.F, d));
+                          i_wo, a.F, d, L.wq));
 }
 
 // The weights of a GEMV op in the engine's slot order (engine_relayout),
@@ -749,12 +765,13 @@ int32_t tiled_weights(S2dHandle *h, EngineOp &o) {
     auto it = h->tiled.find(key);
     if (it == h->tiled.end()) {
         uint16_t *dst = nullptr;
-        const size_t n = (size_t)o.N * o.K * (o.W2 ? 2 : 1);
-        CK(cudaMalloc(&dst, n * sizeof(uint16_t)));
+        const int gtype = ggml_type_of(o.wt);
+        const size_t n = engine_weight_bytes(gtype, o.N, o.K, o.W2 ? 2 : 1);
+        CK(cudaMalloc(&dst, n));
         it = h->tiled.emplace(key, dst).first;
-        CK(launch_engine_relayout(o.W, o.W2, o.N, o.K, o.n_contig, o.row_base, o.extra_row, h->num_sms,
+        CK(launch_engine_relayout(o.W, o.W2, gtype, o.N, o.K, o.n_contig, o.row_base, o.extra_row, h->num_sms,
                                   h->slot_bytes, dst, h->stream));
-        h->tiled_bytes += n * sizeof(uint16_t);
+        h->tiled_bytes += n;
     }
     o.Wt = it->second;
     return S2D_OK;
@@ -811,7 +828,7 @@ int32_t build_programs(S2dHandle *h, uint32_t im_end) {
             // the head reads the residual of the pass's last token (position cbk)
             ops.push_back(gemv_op(1, EPI_STORE, h->fast_out, nullptr, h->ll_x + (size_t)(M - 1) * d, d, x_src,
                                   h->fast_norm, h->fast.eps, h->logits_fast, s.codebook_size, 0, nullptr, -1, d,
-                                  s.codebook_size));
+                                  s.codebook_size, h->fast_out_wq));
             if ((rc = upload_program(h, ops, &h->fast_progs[(size_t)cbk]))) return rc;
         }
     }
@@ -1442,6 +1459,7 @@ int32_t s2d_dequant_tensor(S2dHandle *h, const char *name, float *out, int64_t n
     cudaError_t e;
     if (t->type == 1) e = launch_f16_to_f32(reinterpret_cast<const uint16_t *>(tdev(h, t)->dev), dst, n, h->stream);
     else if (t->type == 0) e = cudaMemcpyAsync(dst, tdev(h, t)->dev, (size_t)n * 4, cudaMemcpyDeviceToDevice, h->stream);
+    else if (t->type == 8 || t->type == 12) e = launch_dequant((int)t->type, tdev(h, t)->dev, dst, n, h->stream);
     else e = cudaErrorNotSupported;
     if (!e) e = cudaMemcpyAsync(out, dst, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
     if (!e) e = cudaStreamSynchronize(h->stream);
@@ -1495,6 +1513,8 @@ int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *
         return g;
     };
     if (kernel < S2D_KERNEL_WQKV || kernel > S2D_KERNEL_LM_HEAD) return set_err(h, S2D_EINVAL, "unknown kernel");
+    if (kernel != S2D_KERNEL_LM_HEAD && h->slow_layers[0].wq != EW_F16)
+        return set_err(h, S2D_EINVAL, "profile_kernel times the f16 GEMV kernels; this model's linears are quantized");
     int epi = 0;
     GemvArgs g0 = args(0, &epi);
     const double wbytes = (double)g0.K * g0.N * 2.0 * (g0.W2 ? 2 : 1);
