@@ -24,6 +24,9 @@ from .s2d import (  # noqa: F401
     forward_codebook_prefix,
     generate_codebooks_for_semantic,
     generate_codes,
+    generate_codes_batch,
+    RNG_PHILOX,
+    RNG_SEEDED,
     lib,
     sample_token,
     transpose_to_time_major,

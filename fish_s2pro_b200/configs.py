@@ -61,6 +61,7 @@ class Workload:
     prompt_seed: int
     im_end_id: int
     batch: int = 1
+    prompt_len_min: int = 0  # batch > 1: prompt lengths uniform in [prompt_len_min, prompt_len]
 
     def prompt(self) -> np.ndarray:
         """Row-major (num_codebooks+1) x prompt_len prompt (PromptTensor,
@@ -71,6 +72,21 @@ class Workload:
         p = np.zeros((m.num_codebooks + 1, self.prompt_len), dtype=np.uint32)
         p[0] = rng.integers(0, m.sem_begin, size=self.prompt_len, dtype=np.uint32)
         return p
+
+    def batch_prompts(self) -> list:
+        """The `batch` prompts of a batched workload: lengths uniform in
+        [prompt_len_min, prompt_len] and text ids uniform over the text
+        vocabulary, both from prompt_seed; codebook rows 0."""
+        rng = np.random.default_rng(self.prompt_seed)
+        m = self.model
+        lo = self.prompt_len_min or self.prompt_len
+        lens = rng.integers(lo, self.prompt_len + 1, size=self.batch)
+        out = []
+        for n in lens:
+            p = np.zeros((m.num_codebooks + 1, int(n)), dtype=np.uint32)
+            p[0] = rng.integers(0, m.sem_begin, size=int(n), dtype=np.uint32)
+            out.append(p)
+        return out
 
     def gen_params(self, greedy: bool = True) -> dict:
         """Greedy decoding as in the reference's own greedy tests
@@ -117,7 +133,7 @@ C2 = Workload(s2pro(seed=1), prompt_len=512, frames=256, prompt_seed=1, im_end_i
 C3 = Workload(s2pro(seed=2, linear_type=GGML_Q8_0), prompt_len=512, frames=256, prompt_seed=2,
               im_end_id=S2PRO_IM_END)
 C4 = Workload(s2pro(seed=3), prompt_len=1024, frames=512, prompt_seed=3, im_end_id=S2PRO_IM_END,
-              batch=64)
+              batch=64, prompt_len_min=128)
 C5 = Workload(s2pro(seed=4, linear_type=GGML_Q4_K), prompt_len=8192, frames=256, prompt_seed=4,
               im_end_id=S2PRO_IM_END)
 

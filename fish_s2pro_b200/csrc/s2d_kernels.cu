@@ -369,7 +369,10 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
     const int head = blockIdx.x * (blockDim.x >> 5) + warp;
     const int m = blockIdx.y;
     if (head >= a.H + a.Hkv) return;
-    const int pos = a.pos_const + (a.pos_dev ? *a.pos_dev : 0) + m;
+    const int rps = a.rows_per_seq > 0 ? a.rows_per_seq : a.M;
+    const int seq = m / rps, j = m - seq * rps;
+    if (a.st_b && a.st_b[seq].done) return;
+    const int pos = a.pos_const + (a.st_b && a.st_pos ? a.st_b[seq].n_past : (a.pos_dev ? *a.pos_dev : 0)) + j;
     const int hd = a.hd;
     const float *row = a.qkv + (size_t)m * a.ld_qkv;
     const bool is_q = head < a.H;
@@ -408,8 +411,9 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
         if (lane == 0 && a.error) atomicExch(a.error, 1);
         return;
     }
-    KV *kc = reinterpret_cast<KV *>(a.kcache) + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
-    KV *vc = reinterpret_cast<KV *>(a.vcache) + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
+    const size_t so = (size_t)seq * a.kv_seq_stride;
+    KV *kc = reinterpret_cast<KV *>(a.kcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
+    KV *vc = reinterpret_cast<KV *>(a.vcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
     const float *vsrc = row + (a.H + a.Hkv + h) * hd + lane * EPL;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
@@ -608,7 +612,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedArgs a) {
         }
         main_id = (uint32_t)t;
     } else {
-        main_id = a.st->main_token;
+        main_id = a.st[a.batched ? m : 0].main_token;
     }
     const bool is_sem = main_id >= a.sem_begin && main_id <= a.sem_end;
     if (main_id >= (uint32_t)a.vocab) {
@@ -619,7 +623,8 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedArgs a) {
     if (is_sem) {
         float sum = 0.f;
         for (int cb = 0; cb < a.K; ++cb) {
-            const int32_t raw = a.tokens ? a.tokens[(size_t)m * cd + 1 + cb] : a.frame_codes[cb];
+            const int32_t raw = a.tokens ? a.tokens[(size_t)m * cd + 1 + cb]
+                                         : a.frame_codes[(a.batched ? (size_t)m * a.K : 0) + cb];
             const int64_t cid = (int64_t)raw + (int64_t)cb * a.cb_size;
             if (raw < 0 || cid >= a.cb_rows) {
                 if (i == 0) atomicExch(a.error, 4);
@@ -648,12 +653,18 @@ cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t s, bool pdl) {
 __global__ void __launch_bounds__(256) fast_init_kernel(const FastInitArgs a) {
     grid_dep_launch();
     grid_dep_wait();
-    if (a.st->done) return;
+    const size_t sq = a.batched ? blockIdx.y : 0;
+    const DevState *st = a.st + sq;
+    if (st->done) return;
+    float *fast_x = a.fast_x + sq * a.fast_x_stride;
+    int32_t *frame_codes = a.frame_codes + sq * a.frame_stride;
+    int32_t *codes_out = a.codes_out ? a.codes_out + sq * a.codes_stride : nullptr;
+    const float *slow_hidden = a.slow_hidden + sq * a.hidden_stride;
     uint32_t code;
     if (a.code_override) {
         code = *a.code_override;
     } else {
-        const uint32_t mt = a.st->main_token;
+        const uint32_t mt = st->main_token;
         if (mt < a.sem_begin || mt > a.sem_end) code = 0;
         else {
             code = mt - a.sem_begin;
@@ -663,17 +674,22 @@ __global__ void __launch_bounds__(256) fast_init_kernel(const FastInitArgs a) {
     if (code >= (uint32_t)a.cb_size) code = (uint32_t)a.cb_size - 1;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (blockIdx.x == 0 && threadIdx.x == 0) {
-        a.frame_codes[0] = (int32_t)code;
-        if (a.codes_out) a.codes_out[a.st->step_index] = (int32_t)code;
+        frame_codes[0] = (int32_t)code;
+        if (codes_out) codes_out[st->step_index] = (int32_t)code;
     }
     if (i < a.d) {
-        a.fast_x[i] = a.slow_hidden[i];
-        a.fast_x[a.d + i] = h2f(a.fast_emb[(size_t)code * a.d + i]);
+        fast_x[i] = slow_hidden[i];
+        fast_x[a.d + i] = h2f(a.fast_emb[(size_t)code * a.d + i]);
     }
 }
 
 cudaError_t launch_fast_init(const FastInitArgs &a, cudaStream_t s, bool pdl) {
     return s2d_launch(fast_init_kernel, dim3((a.d + 255) / 256), dim3(256), 0, s, pdl, a);
+}
+
+cudaError_t launch_fast_init_batch(const FastInitArgs &a, int n_seq, cudaStream_t s) {
+    if (!a.batched || n_seq <= 0 || n_seq > 65535) return cudaErrorInvalidValue;
+    return s2d_launch(fast_init_kernel, dim3((a.d + 255) / 256, n_seq), dim3(256), 0, s, false, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -703,13 +719,43 @@ __device__ __forceinline__ uint32_t f2ord(float v) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-__device__ __forceinline__ float rng_target(uint64_t *state) {
-    *state = *state * 6364136223846793005ull + 1ull;
-    const uint64_t mant = (*state >> 11) & ((1ull << 53) - 1ull);
+__device__ __forceinline__ float draw_to_target(uint64_t bits) {
+    const uint64_t mant = (bits >> 11) & ((1ull << 53) - 1ull);
     const double draw = (double)mant / 9007199254740992.0;
     float t = __double2float_rn(draw);
     t = fminf(fmaxf(t, 0.0f), 1.0f - 1e-7f);
     return t;
+}
+
+__device__ __forceinline__ float rng_target(uint64_t *state) {
+    *state = *state * 6364136223846793005ull + 1ull;
+    return draw_to_target(*state);
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3", SC 2011): ten rounds of two 32x32->64 multiplies with the
+// Weyl-sequence key schedule.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+        c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+        k.x += 0x9E3779B9u;
+        k.y += 0xBB67AE85u;
+    }
+    return c;
+}
+
+// One draw in [0, 1 - 1e-7]: the LCG step, or Philox on the counter
+// (draw index, sequence) with the draw index advanced.
+__device__ __forceinline__ float rng_draw(uint64_t *state, int kind, uint64_t key, uint32_t seq) {
+    if (kind != RNG_PHILOX) return rng_target(state);
+    const uint64_t n = *state;
+    *state = n + 1;
+    const uint4 r = philox4x32_10(make_uint4((uint32_t)n, (uint32_t)(n >> 32), seq, 0u),
+                                  make_uint2((uint32_t)key, (uint32_t)(key >> 32)));
+    return draw_to_target(((uint64_t)r.y << 32) | r.x);
 }
 
 struct SampleShared {
@@ -736,8 +782,15 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
     __shared__ int ri[32], rj[32];
     grid_dep_launch();
     grid_dep_wait();
-    DevState *st = a.st;
+    const uint32_t sq = a.batched ? blockIdx.x : 0u, rseq = a.rng_seq + sq;
+    DevState *st = a.st ? a.st + sq : nullptr;
     if (a.mode != SAMPLE_PLAIN && st->done) return;
+    const float *logits = a.logits + sq * a.logits_stride;
+    uint64_t *rng = a.batched ? &st->rng : a.rng;
+    int32_t *frame_codes = a.frame_codes ? a.frame_codes + sq * a.frame_stride : nullptr;
+    int32_t *codes_out = a.codes_out ? a.codes_out + sq * a.codes_stride : nullptr;
+    float *fast_x_next = a.fast_x_next ? a.fast_x_next + sq * a.fast_x_stride : nullptr;
+    uint32_t *out_token = a.out_token ? a.out_token + sq : nullptr;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int n = a.n;
 
@@ -763,7 +816,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
     // -0.0 is folded into +0.0: the reference's partial_cmp sees them equal,
     // so their order must come from the id alone.
     auto cval = [&](int r) -> float {
-        const float v = a.logits[r];
+        const float v = logits[r];
         return (slow && block && cid(r) == a.im_end) ? -INFINITY : (v == 0.0f ? 0.0f : v);
     };
 
@@ -813,7 +866,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
         sh.general = !(a.temperature == 0.0f && a.top_p <= 1.0f && isfinite(sh.maxv) && c2 == 1 &&
                        k_eff >= 1);
         if (!sh.general) {
-            (void)rng_target(a.rng);
+            (void)rng_draw(rng, a.rng_kind, a.philox_key, rseq);
             sh.token = (int)cid(f2);
         }
     }
@@ -905,7 +958,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
             const int64_t n_items = k_eff + sh.appended;
             int64_t choice;
             if (nf == 0) {
-                (void)rng_target(a.rng);
+                (void)rng_draw(rng, a.rng_kind, a.philox_key, rseq);
                 choice = n_items - 1;
             } else {
                 float sum = 0.0f;
@@ -932,7 +985,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
                 for (int i = 0; i < lim; ++i) sum_p += probs[i];
                 if (sum_p > 0.0f)
                     for (int i = 0; i < lim; ++i) probs[i] /= sum_p;
-                const float target = rng_target(a.rng);
+                const float target = rng_draw(rng, a.rng_kind, a.philox_key, rseq);
                 choice = p_idx - 1;
                 float c2 = 0.0f;
                 for (int i = 0; i < lim; ++i) {
@@ -966,7 +1019,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
 
     const uint32_t token = (uint32_t)sh.token;
     if (tid == 0) {
-        if (a.out_token) *a.out_token = token;
+        if (out_token) *out_token = token;
         if (a.mode == SAMPLE_SLOW_FIRST) {
             st->main_token = token;
             st->done = (token == a.im_end) || (a.max_new <= 0);
@@ -976,13 +1029,13 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
             st->main_token = token;
             st->done = (token == a.im_end) || (new_step >= a.max_new);
         } else if (a.mode == SAMPLE_FAST) {
-            a.frame_codes[a.cb_index] = (int32_t)token;
-            if (a.codes_out) a.codes_out[(size_t)a.cb_index * a.max_new + st->step_index] = (int32_t)token;
+            frame_codes[a.cb_index] = (int32_t)token;
+            if (codes_out) codes_out[(size_t)a.cb_index * a.max_new + st->step_index] = (int32_t)token;
         }
     }
-    if (a.mode == SAMPLE_FAST && a.fast_x_next) {
+    if (a.mode == SAMPLE_FAST && fast_x_next) {
         for (int i = tid; i < a.d; i += kSampleThreads)
-            a.fast_x_next[i] = h2f(a.fast_emb[(size_t)token * a.d + i]);
+            fast_x_next[i] = h2f(a.fast_emb[(size_t)token * a.d + i]);
     }
 }
 
@@ -995,8 +1048,22 @@ static cudaError_t sample_configure() {
 }
 
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl) {
-    if (a.n <= 0 || a.n > kSampleMax) return cudaErrorInvalidValue;
+    if (a.n <= 0 || a.n > kSampleMax || a.batched) return cudaErrorInvalidValue;
     return s2d_launch(sample_kernel, dim3(1), dim3(kSampleThreads), kSampleSmem, s, pdl, a);
+}
+
+__global__ void philox_kernel(uint4 c, uint2 k, uint4 *out) { *out = philox4x32_10(c, k); }
+
+cudaError_t launch_philox(const uint32_t counter[4], const uint32_t key[2], uint32_t *out_dev, cudaStream_t s) {
+    philox_kernel<<<1, 1, 0, s>>>(make_uint4(counter[0], counter[1], counter[2], counter[3]),
+                                  make_uint2(key[0], key[1]), reinterpret_cast<uint4 *>(out_dev));
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sample_batch(const SampleArgs &a, int n_seq, cudaStream_t s) {
+    if (a.n <= 0 || a.n > kSampleMax || !a.batched || !a.st || a.mode == SAMPLE_PLAIN || n_seq <= 0)
+        return cudaErrorInvalidValue;
+    return s2d_launch(sample_kernel, dim3(n_seq), dim3(kSampleThreads), kSampleSmem, s, false, a);
 }
 
 // ---------------------------------------------------------------------------

@@ -53,6 +53,15 @@ struct RopeArgs {
     int H, Hkv, hd, M;
     const int32_t *done;
     int32_t *error;
+    // Batched rows (0 = one sequence): row m belongs to sequence
+    // m / rows_per_seq at position pos_const + j (j = m % rows_per_seq), plus
+    // st_b[seq].n_past when st_pos is set; a sequence whose st_b[seq].done
+    // is set writes nothing.  Sequence s's caches start kv_seq_stride
+    // elements after sequence s-1's.
+    int rows_per_seq;
+    const DevState *st_b;
+    int st_pos;
+    size_t kv_seq_stride;
 };
 
 struct AttnArgs {
@@ -82,6 +91,7 @@ struct EmbedArgs {
     int M;
     const int32_t *done;
     int32_t *error;
+    int batched;             // with tokens == nullptr: row m is sequence m (st[m], frame_codes + m*K)
 };
 
 struct FastInitArgs {
@@ -94,7 +104,16 @@ struct FastInitArgs {
     int max_new, d, cb_size;
     uint32_t sem_begin, sem_end;
     const uint32_t *code_override; // tests: fixed semantic code (nullptr in the loop)
+    // batched (grid.y = sequences): per-sequence strides of slow_hidden,
+    // fast_x, frame_codes and codes_out; st is then an array
+    int batched;
+    size_t hidden_stride, fast_x_stride, codes_stride, frame_stride;
 };
+
+// Random draws of the sampler: the reference's SeededRng LCG (state in
+// *rng), or Philox4x32-10 keyed by philox_key with the sequence index and
+// the draw counter (*rng) as the counter.
+enum RngKind { RNG_SEEDED = 0, RNG_PHILOX = 1 };
 
 enum SampleMode { SAMPLE_PLAIN = 0, SAMPLE_SLOW_FIRST = 1, SAMPLE_SLOW_STEP = 2, SAMPLE_FAST = 3 };
 
@@ -120,6 +139,14 @@ struct SampleArgs {
     float *fast_x_next;     // SAMPLE_FAST: row to receive fast_emb[code]
     int d;
     uint32_t *out_token;    // optional result copy
+    int rng_kind;           // RngKind
+    uint64_t philox_key;
+    uint32_t rng_seq;       // Philox sequence index of block 0
+    // batched (one block per sequence, grid.x = sequences): st is an array
+    // and the rng is st[seq].rng; logits, frame_codes, codes_out, fast_x_next
+    // and out_token advance by these strides per sequence
+    int batched;
+    size_t logits_stride, codes_stride, fast_x_stride, frame_stride;
 };
 
 // ---- persistent layer engine (s2d_engine.cu) -------------------------------
@@ -297,7 +324,12 @@ cudaError_t launch_rope_kv(const RopeArgs &a, bool kv_half, cudaStream_t s, bool
 cudaError_t launch_attention(const AttnArgs &a, bool kv_half, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_fast_init(const FastInitArgs &a, cudaStream_t s, bool pdl);
+cudaError_t launch_fast_init_batch(const FastInitArgs &a, int n_seq, cudaStream_t s);
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t s, bool pdl);
+// The sampler's Philox4x32-10 block function on one counter (out_dev: 4 words).
+cudaError_t launch_philox(const uint32_t counter[4], const uint32_t key[2], uint32_t *out_dev, cudaStream_t s);
+// Batched sampler: one block per sequence (a.batched set).
+cudaError_t launch_sample_batch(const SampleArgs &a, int n_seq, cudaStream_t s);
 cudaError_t launch_f16_to_f32(const uint16_t *src, float *dst, int64_t n, cudaStream_t s);
 // ggml Q8_0 / Q4_K blocks (gtype 8 / 12) of n elements -> f32 (the block
 // formulas d*q and (d*sc)*q - dmin*m, each rounded once in f32).

@@ -120,67 +120,168 @@ __global__ void combine_kernel(const float *Y2, const float *Y2b, const float *i
     y[(size_t)t * ldy + n] = out;
 }
 
-// Causal GQA attention over the cache for T query tokens at positions
-// pos0 .. pos0+T-1 (gqa_decode_attention per token, attention.rs:208-247,
-// with the causal prefix of forward_prefill_sequence, slow_ar.rs:579-593).
-// Grid (token, kv head); warp r of the block is query head kvh*rep + r.  The
-// block copies 32 cached K and V rows at a time into shared memory; lane j
-// scores position c0 + j, then every lane accumulates its head dims.
+// ---------------------------------------------------------------------------
+// GQA attention of many query rows over their sequences' caches
+// (gqa_decode_attention + softmax_in_place per row, attention.rs:208-309; the
+// causal prefix of forward_prefill_sequence, slow_ar.rs:579-593).  A row is a
+// (sequence, position) pair: the T tokens of one prompt (prefill), one token
+// of each of B sequences (batched Slow-AR step), or the Fast-AR positions of
+// B frames.  Grid (row, kv head, split); warp r of a block is query head
+// kvh*rep + r, so the group's K/V rows are fetched once for its rep heads.
+// The block stages 32 cached K and V rows at a time in shared memory with
+// cp.async (two stages for f16 caches, so the next chunk streams while this
+// one is scored); lane j scores position c0 + j, then every lane accumulates
+// its head dims.  With S > 1 splits each block writes its (max, sum, weighted
+// V) partial and the last block of the (row, kv head) to arrive merges them.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// q (shared, hd floats) . K row (shared, hd elements), 16-byte reads.
+__device__ __forceinline__ float dot_row(const float *q, const __half *k, int hd) {
+    float d0 = 0.f, d1 = 0.f;
+    for (int i = 0; i < hd; i += 8) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(k + i);
+        d0 = fmaf(q[i], h_lo(u.x), d0);
+        d1 = fmaf(q[i + 1], h_hi(u.x), d1);
+        d0 = fmaf(q[i + 2], h_lo(u.y), d0);
+        d1 = fmaf(q[i + 3], h_hi(u.y), d1);
+        d0 = fmaf(q[i + 4], h_lo(u.z), d0);
+        d1 = fmaf(q[i + 5], h_hi(u.z), d1);
+        d0 = fmaf(q[i + 6], h_lo(u.w), d0);
+        d1 = fmaf(q[i + 7], h_hi(u.w), d1);
+    }
+    return d0 + d1;
+}
+__device__ __forceinline__ float dot_row(const float *q, const float *k, int hd) {
+    float d0 = 0.f, d1 = 0.f;
+    for (int i = 0; i < hd; i += 4) {
+        const float4 u = *reinterpret_cast<const float4 *>(k + i);
+        d0 = fmaf(q[i], u.x, d0);
+        d1 = fmaf(q[i + 1], u.y, d1);
+        d0 = fmaf(q[i + 2], u.z, d0);
+        d1 = fmaf(q[i + 3], u.w, d1);
+    }
+    return d0 + d1;
+}
+
 template <typename KV, int EPL>
-__global__ void prefill_attn_kernel(const float *q, const void *kcache, const void *vcache, int max_seq, float *out,
-                                    int pos0, int H, int Hkv, int hd, float scale) {
+__device__ __forceinline__ void load_v(const KV *p, float *o) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = float(p[e]);
+}
+
+template <typename KV, int EPL, int NST>
+__global__ void __launch_bounds__(256) rows_attn_kernel(const RowsAttnArgs a) {
     extern __shared__ __align__(16) uint8_t sm[];
-    const int rep = H / Hkv;
-    const int m = blockIdx.x, kvh = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ int s_last;
+    const int rep = blockDim.x >> 5;
+    const int m = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = kvh * rep + warp;
-    const int kvb = (int)sizeof(KV), rowb = hd * kvb;
-    uint8_t *kt = sm, *vt = sm + 32 * (rowb + 16);
-    float *qs = reinterpret_cast<float *>(vt + 32 * (rowb + 16)) + warp * hd;
-    const int visible = min(pos0 + m + 1, max_seq);
-    const float *qrow = q + (size_t)m * H * hd + h * hd;
+    const int hd = a.hd, rowb = hd * (int)sizeof(KV), pitch = rowb + 16;
+    const int seq = m / a.rows_per_seq, j = m - seq * a.rows_per_seq;
+    if (a.st && a.st[seq].done) return;  // every split of the row returns: no counter use
+    const int pos = a.pos_const + (a.st && a.st_pos ? a.st[seq].n_past : 0) + j;
+    const int visible = max(1, min(pos + 1, a.max_seq));
+    const int nch = (visible + 31) / 32, cps = (nch + a.S - 1) / a.S;
+    const int t0 = min(visible, sp * cps * 32), t1 = min(visible, t0 + cps * 32);
+    float *qs = reinterpret_cast<float *>(sm + (size_t)NST * 2 * 32 * pitch) + warp * hd;
+    const float *qrow = a.q + (size_t)m * a.H * hd + (size_t)h * hd;
     for (int i = lane; i < hd; i += 32) qs[i] = qrow[i];
-    const uint8_t *kb = reinterpret_cast<const uint8_t *>(kcache) + (size_t)kvh * max_seq * rowb;
-    const uint8_t *vb = reinterpret_cast<const uint8_t *>(vcache) + (size_t)kvh * max_seq * rowb;
-    const int units = rowb / 16, nthr = blockDim.x;
+    const size_t so = (size_t)seq * a.kv_seq_stride * sizeof(KV) + (size_t)kvh * a.max_seq * rowb;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + so;
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
+    const int units = rowb / 16;
+    auto issue = [&](int c0, int stg) {
+        const int n = min(32, t1 - c0);
+        uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
+        for (int u = threadIdx.x; u < 2 * n * units; u += blockDim.x) {
+            const int which = u >= n * units, uu = which ? u - n * units : u;
+            const int r = uu / units, c = uu - r * units;
+            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + (size_t)(c0 + r) * rowb + c * 16);
+        }
+        cp_async_commit();
+    };
     float mrun = -INFINITY, l = 0.f, acc[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    for (int c0 = 0; c0 < visible; c0 += 32) {
-        const int n = min(32, visible - c0);
-        __syncthreads();  // the previous chunk's readers are done (and qs is written)
-        for (int u = threadIdx.x; u < 2 * n * units; u += nthr) {
-            const int which = u >= n * units, r = (u % (n * units)) / units, c = u % units;
-            const uint4 v = __ldg(reinterpret_cast<const uint4 *>((which ? vb : kb) + (size_t)(c0 + r) * rowb) + c);
-            *reinterpret_cast<uint4 *>((which ? vt : kt) + (size_t)r * (rowb + 16) + c * 16) = v;
+    if (t0 < t1) issue(t0, 0);
+    for (int c0 = t0, it = 0; c0 < t1; c0 += 32, ++it) {
+        const int stg = NST == 2 ? (it & 1) : 0;
+        if (NST == 1) {
+            if (it > 0) issue(c0, 0);
+            cp_async_wait<0>();
+        } else if (c0 + 32 < t1) {
+            issue(c0 + 32, stg ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
-        __syncthreads();
+        __syncthreads();  // this chunk (and, on the first pass, qs) visible to every warp
+        const int n = min(32, t1 - c0);
+        const uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
         float sc = -INFINITY;
-        if (lane < n) {
-            const KV *kr = reinterpret_cast<const KV *>(kt + (size_t)lane * (rowb + 16));
-            float d0 = 0.f, d1 = 0.f;
-            for (int i = 0; i < hd; i += 2) {
-                d0 = fmaf(qs[i], float(kr[i]), d0);
-                d1 = fmaf(qs[i + 1], float(kr[i + 1]), d1);
-            }
-            sc = (d0 + d1) * scale;
-        }
+        if (lane < n) sc = dot_row(qs, reinterpret_cast<const KV *>(kt + lane * pitch), hd) * a.scale;
         const float mn = fmaxf(mrun, warp_max(sc));
         const float corr = expf(mrun - mn);
         const float p = lane < n ? expf(sc - mn) : 0.f;
         l = fmaf(l, corr, warp_sum(p));
 #pragma unroll
         for (int e = 0; e < EPL; ++e) acc[e] *= corr;
-        for (int j = 0; j < n; ++j) {
-            const float pj = __shfl_sync(0xffffffffu, p, j);
-            const KV *vr = reinterpret_cast<const KV *>(vt + (size_t)j * (rowb + 16)) + lane * EPL;
+        for (int jj = 0; jj < n; ++jj) {
+            const float pj = __shfl_sync(0xffffffffu, p, jj);
+            float vf[EPL];
+            load_v<KV, EPL>(reinterpret_cast<const KV *>(vt + jj * pitch) + lane * EPL, vf);
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj, float(vr[e]), acc[e]);
+            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj, vf[e], acc[e]);
         }
         mrun = mn;
+        if (NST == 1 || c0 + 32 < t1) __syncthreads();  // readers done before the stage is refilled
     }
-    float *o = out + (size_t)m * H * hd + h * hd + lane * EPL;
+    if (a.S == 1) {
+        float *o = a.out + (size_t)m * a.H * hd + (size_t)h * hd + lane * EPL;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) o[e] = acc[e] / l;
+        for (int e = 0; e < EPL; ++e) o[e] = acc[e] / l;
+        return;
+    }
+    float *pp = a.part + (((size_t)m * a.H + h) * a.S + sp) * (hd + 2);
+    if (lane == 0) {
+        __stcg(pp, mrun);
+        __stcg(pp + 1, l);
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) __stcg(pp + 2 + lane * EPL + e, acc[e]);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[(size_t)m * a.Hkv + kvh], 1) == a.S - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const float *base = a.part + ((size_t)m * a.H + h) * a.S * (hd + 2);
+    float gmax = -INFINITY;
+    for (int s2 = 0; s2 < a.S; ++s2) gmax = fmaxf(gmax, __ldcg(base + (size_t)s2 * (hd + 2)));
+    float L = 0.f, o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = 0.f;
+    for (int s2 = 0; s2 < a.S; ++s2) {
+        const float *pj = base + (size_t)s2 * (hd + 2);
+        const float f = expf(__ldcg(pj) - gmax);
+        L = fmaf(__ldcg(pj + 1), f, L);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] = fmaf(__ldcg(pj + 2 + lane * EPL + e), f, o[e]);
+    }
+    float *op = a.out + (size_t)m * a.H * hd + (size_t)h * hd + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) op[e] = o[e] / L;
+    if (threadIdx.x == 0) a.counters[(size_t)m * a.Hkv + kvh] = 0;
 }
 
 }  // namespace
@@ -220,23 +321,30 @@ cudaError_t launch_combine(int epi, const float *Y2, const float *Y2b, const flo
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_attention(const float *q, const void *kcache, const void *vcache, bool kv_half, int max_seq,
-                                     float *out, int T, int pos0, int H, int Hkv, int hd, float scale,
-                                     cudaStream_t s) {
-    if (T <= 0) return cudaSuccess;
-    const int rep = H / Hkv;
-    if (rep * Hkv != H || rep > 32 || (hd != 64 && hd != 128)) return cudaErrorInvalidValue;
-    const int kvb = kv_half ? 2 : 4;
-    const size_t smem = (size_t)2 * 32 * (hd * kvb + 16) + (size_t)rep * hd * 4;
-    const dim3 grid(T, Hkv), block(rep * 32);
-    if (kv_half) {
-        if (hd == 64) prefill_attn_kernel<__half, 2><<<grid, block, smem, s>>>(q, kcache, vcache, max_seq, out, pos0, H, Hkv, hd, scale);
-        else prefill_attn_kernel<__half, 4><<<grid, block, smem, s>>>(q, kcache, vcache, max_seq, out, pos0, H, Hkv, hd, scale);
-    } else {
-        if (hd == 64) prefill_attn_kernel<float, 2><<<grid, block, smem, s>>>(q, kcache, vcache, max_seq, out, pos0, H, Hkv, hd, scale);
-        else prefill_attn_kernel<float, 4><<<grid, block, smem, s>>>(q, kcache, vcache, max_seq, out, pos0, H, Hkv, hd, scale);
+template <typename KV, int EPL, int NST>
+static cudaError_t rows_attn_launch(const RowsAttnArgs &a, cudaStream_t s) {
+    const int rep = a.H / a.Hkv;
+    const int pitch = a.hd * (int)sizeof(KV) + 16;
+    const size_t smem = (size_t)NST * 2 * 32 * pitch + (size_t)rep * a.hd * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(rows_attn_kernel<KV, EPL, NST>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        if (e) return e;
+        configured = true;
     }
+    if (smem > 96 * 1024) return cudaErrorInvalidValue;
+    rows_attn_kernel<KV, EPL, NST><<<dim3(a.T, a.Hkv, a.S), rep * 32, smem, s>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s) {
+    if (a.T <= 0) return cudaSuccess;
+    if (a.Hkv <= 0 || a.H % a.Hkv || a.H / a.Hkv > 8 || (a.hd != 64 && a.hd != 128) || a.rows_per_seq <= 0 ||
+        a.S <= 0 || a.S > 65535 || a.T > 0x7fffffff || a.max_seq <= 0 || (a.S > 1 && (!a.part || !a.counters)))
+        return cudaErrorInvalidValue;
+    if (kv_half) return a.hd == 64 ? rows_attn_launch<__half, 2, 2>(a, s) : rows_attn_launch<__half, 4, 2>(a, s);
+    return a.hd == 64 ? rows_attn_launch<float, 2, 1>(a, s) : rows_attn_launch<float, 4, 1>(a, s);
 }
 
 }  // namespace s2d

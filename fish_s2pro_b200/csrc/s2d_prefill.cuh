@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "s2d_kernels.cuh"
+
 namespace s2d {
 
 // Epilogues of a GEMM over stacked hi/lo activation rows.
@@ -22,11 +24,29 @@ cudaError_t launch_split_rows(const float *x, int ldx, int T, int K, const float
 cudaError_t launch_combine(int epi, const float *Y2, const float *Y2b, const float *inv, int T, int N, float *y,
                            int ldy, const float *resid, int ldr, cudaStream_t s);
 
-// Causal GQA attention of T query tokens at positions pos0 + t over a
-// layer's cache [Hkv][max_seq][hd] (every position up to pos0 + T - 1
-// written): q [T][H*hd] (already normalised and rotated) -> out [T][H*hd].
-cudaError_t launch_prefill_attention(const float *q, const void *kcache, const void *vcache, bool kv_half, int max_seq,
-                                     float *out, int T, int pos0, int H, int Hkv, int hd, float scale,
-                                     cudaStream_t s);
+// GQA attention of T query rows over their sequences' caches.  Row m is
+// sequence m / rows_per_seq at position pos_const + (m % rows_per_seq), plus
+// st[seq].n_past when st_pos is set (rows of a finished sequence,
+// st[seq].done, are skipped).  Sequence s's layer caches [Hkv][max_seq][hd] (f16 or f32)
+// start kv_seq_stride elements after sequence s-1's; a row attends positions
+// 0 .. its own, which must all be written.  q [T][H*hd] is normalised and
+// rotated; out [T][H*hd].
+struct RowsAttnArgs {
+    const float *q;
+    const void *kcache, *vcache;
+    size_t kv_seq_stride;
+    int max_seq;
+    float *out;
+    int T, rows_per_seq;
+    const DevState *st;
+    int st_pos;
+    int pos_const;
+    int H, Hkv, hd;
+    float scale;
+    int S;               // splits of each row's positions (1: no merge)
+    float *part;         // S > 1: [T][H][S][hd + 2]
+    int32_t *counters;   // S > 1: [T][Hkv], zero between launches (left zero)
+};
+cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
 
 }  // namespace s2d

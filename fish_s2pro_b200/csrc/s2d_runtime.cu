@@ -118,6 +118,7 @@ struct S2dHandle {
     int num_sms = 0;
     // batched prefill (s2d_prefill.cu): up to pf_cap tokens per layer pass
     cublasHandle_t blas = nullptr;
+    void *blas_ws = nullptr;
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_act = nullptr;
     float *pf_inv = nullptr, *pf_y2 = nullptr, *pf_y2b = nullptr;
@@ -134,6 +135,29 @@ struct S2dHandle {
     int l2_lead = 0;                    // engine L2 prefetch lead in slots (S2D_L2_LEAD)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
+    // batched generation (s2d_generate_codes_batch): kv_slow holds max_batch
+    // sequences of kv_slow_seq elements each (sequence 0 is the one of the
+    // single-sequence calls)
+    int max_batch = 1;
+    size_t kv_slow_seq = 0;
+    DevState *st_b = nullptr;             // [max_batch]
+    float *bx = nullptr;                  // [max_batch][d] Slow-AR residual rows
+    float *fx = nullptr;                  // [max_batch][2][d] Fast-AR rows of a pass
+    float *hidden_b = nullptr;            // [max_batch][d] post-norm hidden
+    float *logits_b = nullptr;            // [max_batch][n_sem + 1]
+    float *logits_fast_b = nullptr;       // [max_batch][codebook_size]
+    float *kv_fast_b = nullptr;           // [max_batch][Lf][2][Hkv][ctx][hd]
+    int32_t *frame_codes_b = nullptr;     // [max_batch][K]
+    int32_t *codes_b = nullptr;           // [max_batch][K][max_new]
+    size_t codes_b_cap = 0;
+    float *ra_part = nullptr;             // rows attention split partials
+    int32_t *ra_counters = nullptr;
+    int ra_rows = 0, ra_smax = 0;
+    cudaGraphExec_t batch_exec = nullptr;
+    GenKey batch_key;
+    int batch_n = 0, batch_rng_kind = -1;
+    uint64_t batch_philox = 0;
+    uint32_t batch_kernels = 0;
 };
 
 namespace {
@@ -449,7 +473,8 @@ int32_t alloc_buffers(S2dHandle *h) {
         CK(cudaMemcpy(h->rope_cs_slow, ts.data(), ts.size() * sizeof(float2), cudaMemcpyHostToDevice));
         CK(cudaMemcpy(h->rope_cs_fast, tf.data(), tf.size() * sizeof(float2), cudaMemcpyHostToDevice));
     }
-    const size_t kv_slow = (size_t)a.L * 2 * a.Hkv * maxseq * a.hd;
+    h->kv_slow_seq = (size_t)a.L * 2 * a.Hkv * maxseq * a.hd;
+    const size_t kv_slow = h->kv_slow_seq * (size_t)h->max_batch;
     CK(cudaMalloc(&h->kv_slow, kv_slow * sizeof(__half)));
     CK(cudaMemset(h->kv_slow, 0, kv_slow * sizeof(__half)));
     const size_t kv_fast = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
@@ -943,6 +968,7 @@ int32_t check_device_error(S2dHandle *h) {
 // logits in h->logits.
 // Prefill chunk length of the batched path, and the smallest prompt it takes.
 constexpr int kPrefillChunk = 512;
+constexpr size_t kBlasWorkspace = (size_t)32 << 20;
 constexpr int kPrefillMin = 8;
 
 int32_t ensure_prefill(S2dHandle *h) {
@@ -951,15 +977,27 @@ int32_t ensure_prefill(S2dHandle *h) {
         if (cublasCreate(&h->blas) != CUBLAS_STATUS_SUCCESS) return set_err(h, S2D_ECUDA, "cublasCreate failed");
         if (cublasSetStream(h->blas, h->stream) != CUBLAS_STATUS_SUCCESS)
             return set_err(h, S2D_ECUDA, "cublasSetStream failed");
+        // a workspace of our own, so that GEMMs captured into the batched
+        // frame graph never allocate
+        CK(cudaMalloc(&h->blas_ws, kBlasWorkspace));
+        if (cublasSetWorkspace(h->blas, h->blas_ws, kBlasWorkspace) != CUBLAS_STATUS_SUCCESS)
+            return set_err(h, S2D_ECUDA, "cublasSetWorkspace failed");
     }
-    const ArShape &a = h->slow;
-    const size_t T = kPrefillChunk, kmax = (size_t)std::max(std::max(a.d, a.qs()), a.F);
-    const size_t nmax = (size_t)std::max(std::max(a.d, a.qkv_out()), a.F);
-    CK(cudaMalloc(&h->pf_x, T * a.d * sizeof(float)));
-    CK(cudaMalloc(&h->pf_qkv, T * a.qkv_out() * sizeof(float)));
-    CK(cudaMalloc(&h->pf_q, T * a.qs() * sizeof(float)));
-    CK(cudaMalloc(&h->pf_att, T * a.qs() * sizeof(float)));
-    CK(cudaMalloc(&h->pf_act, T * a.F * sizeof(float)));
+    // row buffers for both stacks (the batched Fast-AR passes use them too)
+    // and the heads (masked LM head, fast_output)
+    const ArShape &a = h->slow, &f = h->fast;
+    const S2dGraphSpec &sp = h->spec;
+    const size_t T = kPrefillChunk;
+    const size_t d = (size_t)std::max(a.d, f.d), qo = (size_t)std::max(a.qkv_out(), f.qkv_out());
+    const size_t qs = (size_t)std::max(a.qs(), f.qs()), F = (size_t)std::max(a.F, f.F);
+    const size_t kmax = std::max(std::max(d, qs), F);
+    const size_t heads_n = (size_t)std::max(sp.semantic_end_id - sp.semantic_begin_id + 2, sp.codebook_size);
+    const size_t nmax = std::max(std::max(std::max(d, qo), F), heads_n);
+    CK(cudaMalloc(&h->pf_x, T * d * sizeof(float)));
+    CK(cudaMalloc(&h->pf_qkv, T * qo * sizeof(float)));
+    CK(cudaMalloc(&h->pf_q, T * qs * sizeof(float)));
+    CK(cudaMalloc(&h->pf_att, T * qs * sizeof(float)));
+    CK(cudaMalloc(&h->pf_act, T * F * sizeof(float)));
     CK(cudaMalloc(&h->pf_inv, T * sizeof(float)));
     CK(cudaMalloc(&h->pf_y2, 2 * T * nmax * sizeof(float)));
     CK(cudaMalloc(&h->pf_y2b, 2 * T * nmax * sizeof(float)));
@@ -978,47 +1016,82 @@ int32_t prefill_gemm(S2dHandle *h, const uint16_t *W, int N, int K, int T, float
     return S2D_OK;
 }
 
-// The Slow-AR layers over T (<= pf_cap) embedded tokens in pf_x at positions
-// pos0 .. pos0 + T - 1 (forward_slow_ar_block_prefill_layers_cached,
-// slow_ar.rs:1002-1039, a layer at a time over all the tokens).
-int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
-    const ArShape &a = h->slow;
-    const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F;
+// Rows of one layered pass (rows_layers): T rows of the residual x, row m
+// of sequence m / rps at position pos_const + m % rps (+ st[seq].n_past with
+// st_pos); sequence s's KV cache starts kv_seq_stride elements after
+// sequence 0's (kv).  Rows of finished sequences (st[seq].done) write no KV.
+struct RowsPlan {
+    int T = 0, rps = 1, pos_const = 0, st_pos = 0, S = 1;
+    const DevState *st = nullptr;
+    void *kv = nullptr;
+    size_t kv_seq_stride = 0;
+    int max_seq = 0;
+};
+
+// Every layer of the Slow-AR (is_fast false) or the Fast-AR over T rows of
+// x [T][ldx] in place, a layer at a time: the linears are GEMMs over the
+// stacked hi/lo rows, RoPE + KV write and GQA attention are per row
+// (SlowArLayerSkeleton::forward_decode_token_with_backend +
+// forward_feed_forward_with_backend, slow_ar.rs:637-710, for each row;
+// forward_slow_ar_block_prefill_layers_cached, slow_ar.rs:1002-1039, when the
+// rows are one prompt; FastArLayerSkeleton::forward_prefill,
+// fast_ar.rs:245-352, for the Fast-AR).
+int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPlan &rp) {
+    const ArShape &a = is_fast ? h->fast : h->slow;
+    const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F, T = rp.T;
+    const size_t kvb = is_fast ? sizeof(float) : sizeof(__half);
+    const size_t layer_bytes = (size_t)2 * a.Hkv * rp.max_seq * a.hd * kvb;
     int32_t rc;
     for (int l = 0; l < a.L; ++l) {
-        const LayerDev &L = h->slow_layers[(size_t)l];
+        const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
         // attention_norm + WQKV
-        CK(launch_split_rows(h->pf_x, d, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        CK(launch_split_rows(x, ldx, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
         if ((rc = prefill_gemm(h, L.wqkv, qo, d, T, h->pf_y2))) return rc;
         CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, T, qo, h->pf_qkv, qo, nullptr, 0, h->stream));
-        // QK-norm + RoPE + KV write for all T tokens
+        // QK-norm (Slow-AR) + RoPE + KV write for every row
+        uint8_t *base = reinterpret_cast<uint8_t *>(rp.kv) + (size_t)l * layer_bytes;
         RopeArgs r{};
-        __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
         r.qkv = h->pf_qkv, r.ld_qkv = qo, r.q_out = h->pf_q;
-        r.kcache = base, r.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd, r.max_seq = h->cfg.max_seq;
-        r.q_norm = L.q_norm, r.k_norm = L.k_norm, r.rope_denom = h->rope_slow;
-        r.eps = a.eps, r.pos_dev = nullptr, r.pos_const = pos0;
+        r.kcache = base, r.vcache = base + layer_bytes / 2, r.max_seq = rp.max_seq;
+        if (!is_fast) r.q_norm = L.q_norm, r.k_norm = L.k_norm;
+        r.rope_denom = is_fast ? h->rope_fast : h->rope_slow;
+        r.eps = a.eps, r.pos_dev = nullptr, r.pos_const = rp.pos_const;
         r.H = a.H, r.Hkv = a.Hkv, r.hd = a.hd, r.M = T, r.done = nullptr, r.error = &h->st->error;
-        CK(launch_rope_kv(r, true, h->stream, false));
-        // causal GQA attention over the cache
-        CK(launch_prefill_attention(h->pf_q, r.kcache, r.vcache, true, h->cfg.max_seq, h->pf_att, T, pos0, a.H,
-                                    a.Hkv, a.hd, 1.0f / sqrtf((float)a.hd), h->stream));
+        r.rows_per_seq = rp.rps, r.st_b = rp.st, r.st_pos = rp.st_pos, r.kv_seq_stride = rp.kv_seq_stride;
+        CK(launch_rope_kv(r, !is_fast, h->stream, false));
+        // GQA attention of every row over its sequence's cache
+        RowsAttnArgs t{};
+        t.q = h->pf_q, t.kcache = r.kcache, t.vcache = r.vcache, t.kv_seq_stride = rp.kv_seq_stride;
+        t.max_seq = rp.max_seq, t.out = h->pf_att, t.T = T, t.rows_per_seq = rp.rps, t.st = rp.st;
+        t.st_pos = rp.st_pos, t.pos_const = rp.pos_const, t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd;
+        t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
+        t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters;
+        CK(launch_rows_attention(t, !is_fast, h->stream));
         // wo + residual
         CK(launch_split_rows(h->pf_att, qs, T, qs, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
         if ((rc = prefill_gemm(h, L.wo, d, qs, T, h->pf_y2))) return rc;
-        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, h->pf_x, d, h->pf_x, d, h->stream));
+        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
         // ffn_norm + w1 / w3 + SwiGLU
-        CK(launch_split_rows(h->pf_x, d, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        CK(launch_split_rows(x, ldx, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
         if ((rc = prefill_gemm(h, L.w1, F, d, T, h->pf_y2))) return rc;
         if ((rc = prefill_gemm(h, L.w3, F, d, T, h->pf_y2b))) return rc;
-        CK(launch_combine(PF_SWIGLU_SLOW, h->pf_y2, h->pf_y2b, h->pf_inv, T, F, h->pf_act, F, nullptr, 0, h->stream));
+        CK(launch_combine(is_fast ? PF_SWIGLU_FAST : PF_SWIGLU_SLOW, h->pf_y2, h->pf_y2b, h->pf_inv, T, F,
+                          h->pf_act, F, nullptr, 0, h->stream));
         // w2 + residual
         CK(launch_split_rows(h->pf_act, F, T, F, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
         if ((rc = prefill_gemm(h, L.w2, d, F, T, h->pf_y2))) return rc;
-        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, h->pf_x, d, h->pf_x, d, h->stream));
-        h->launches += 13;
+        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
+        h->launches += 10;  // own kernels; the GEMMs are cuBLAS's
     }
     return S2D_OK;
+}
+
+// The Slow-AR layers over T (<= pf_cap) embedded tokens in pf_x at positions
+// pos0 .. pos0 + T - 1 of sequence 0's cache.
+int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
+    RowsPlan rp;
+    rp.T = T, rp.rps = T, rp.pos_const = pos0, rp.kv = h->kv_slow, rp.max_seq = h->cfg.max_seq;
+    return rows_layers(h, false, h->pf_x, h->slow.d, rp);
 }
 
 int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t logits_mode,
@@ -1119,10 +1192,157 @@ int32_t copy_eval_outputs(S2dHandle *h, float *out_hidden, float *out_logits, in
     return S2D_OK;
 }
 
+// ---------------------------------------------------------------------------
+// batched generation: B independent sequences advance one frame per graph
+// launch, every linear a GEMM over the B (or 2B) rows of the frame
+// ---------------------------------------------------------------------------
+
+constexpr int kBatchMaxSeq = kPrefillChunk / 2;  // rows of the first Fast-AR pass fit one row block
+
+int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
+    const S2dGraphSpec &s = h->spec;
+    const ArShape &a = h->slow, &f = h->fast;
+    const size_t B = (size_t)h->max_batch, d = (size_t)s.hidden, K = (size_t)std::max(s.num_codebooks, 1);
+    int32_t rc;
+    if ((rc = ensure_prefill(h))) return rc;
+    if (!h->st_b) {
+        const size_t nsem = (size_t)(s.semantic_end_id - s.semantic_begin_id + 1);
+        const size_t kvf = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
+        CK(cudaMalloc(&h->st_b, B * sizeof(DevState)));
+        CK(cudaMemset(h->st_b, 0, B * sizeof(DevState)));
+        CK(cudaMalloc(&h->bx, B * d * sizeof(float)));
+        CK(cudaMemset(h->bx, 0, B * d * sizeof(float)));
+        CK(cudaMalloc(&h->fx, B * 2 * d * sizeof(float)));
+        CK(cudaMemset(h->fx, 0, B * 2 * d * sizeof(float)));
+        CK(cudaMalloc(&h->hidden_b, B * d * sizeof(float)));
+        CK(cudaMemset(h->hidden_b, 0, B * d * sizeof(float)));
+        CK(cudaMalloc(&h->logits_b, B * (nsem + 1) * sizeof(float)));
+        CK(cudaMalloc(&h->logits_fast_b, B * (size_t)s.codebook_size * sizeof(float)));
+        CK(cudaMalloc(&h->kv_fast_b, std::max<size_t>(B * kvf, 1) * sizeof(float)));
+        CK(cudaMemset(h->kv_fast_b, 0, std::max<size_t>(B * kvf, 1) * sizeof(float)));
+        CK(cudaMalloc(&h->frame_codes_b, B * K * sizeof(int32_t)));
+        CK(cudaMemset(h->frame_codes_b, 0, B * K * sizeof(int32_t)));
+        // split partials of the rows attention: up to 2 rows per sequence
+        h->ra_rows = (int)(2 * B), h->ra_smax = 16;
+        const size_t H = (size_t)std::max(a.H, f.H), Hkv = (size_t)std::max(a.Hkv, f.Hkv);
+        const size_t hd = (size_t)std::max(a.hd, f.hd);
+        CK(cudaMalloc(&h->ra_part, (size_t)h->ra_rows * H * h->ra_smax * (hd + 2) * sizeof(float)));
+        CK(cudaMalloc(&h->ra_counters, (size_t)h->ra_rows * Hkv * sizeof(int32_t)));
+        CK(cudaMemset(h->ra_counters, 0, (size_t)h->ra_rows * Hkv * sizeof(int32_t)));
+    }
+    const size_t need = B * K * std::max<uint32_t>(max_new, 1);
+    if (need > h->codes_b_cap) {
+        if (h->codes_b) cudaFree(h->codes_b);
+        h->codes_b = nullptr;
+        h->codes_b_cap = 0;
+        CK(cudaMalloc(&h->codes_b, need * sizeof(int32_t)));
+        h->codes_b_cap = need;
+        if (h->batch_exec) {  // the captured frame points at the old buffer
+            cudaGraphExecDestroy(h->batch_exec);
+            h->batch_exec = nullptr;
+        }
+    }
+    return S2D_OK;
+}
+
+// Attention splits of the batched Slow-AR step: enough blocks for ~8 per SM.
+int batch_splits(const S2dHandle *h, int B) {
+    const int blocks = B * h->slow.Hkv;
+    return std::max(1, std::min(h->ra_smax, (8 * std::max(h->num_sms, 1) + blocks - 1) / blocks));
+}
+
+// One frame of B sequences (the loop body of generate_codes,
+// generate.rs:165-211, for each sequence): Fast-AR codebooks 1..K-1 over all
+// sequences' rows, the embedding-sum feedback, the Slow-AR step over B rows,
+// the masked LM head and the semantic sampler.  Finished sequences keep their
+// state and caches (every kernel that writes them checks the sequence's done
+// flag).
+int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, uint64_t philox_key) {
+    const S2dGraphSpec &s = h->spec;
+    const int d = s.hidden, K = s.num_codebooks, cb = s.codebook_size;
+    const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
+    const bool extra = (int64_t)k.im_end < s.vocab_size &&
+                       ((int)k.im_end < s.semantic_begin_id || (int)k.im_end > s.semantic_end_id);
+    const size_t codes_stride = (size_t)K * k.max_new;
+    const ArShape &f = h->fast;
+    int32_t rc;
+    FastInitArgs fi{};
+    fi.st = h->st_b, fi.slow_hidden = h->hidden_b, fi.fast_emb = h->fast_emb, fi.fast_x = h->fx;
+    fi.frame_codes = h->frame_codes_b, fi.codes_out = h->codes_b;
+    fi.max_new = (int)k.max_new, fi.d = d, fi.cb_size = cb;
+    fi.sem_begin = (uint32_t)s.semantic_begin_id, fi.sem_end = (uint32_t)s.semantic_end_id;
+    fi.batched = 1, fi.hidden_stride = (size_t)d, fi.fast_x_stride = (size_t)2 * d;
+    fi.codes_stride = codes_stride, fi.frame_stride = (size_t)K;
+    CK(launch_fast_init_batch(fi, B, h->stream));
+    h->launches += 1;
+    for (int cbk = 1; cbk < K; ++cbk) {
+        // positions 0 and 1 on the first pass (rows (seq, 0), (seq, 1) of fx),
+        // then position cbk in row (seq, 0)
+        const int M = cbk == 1 ? 2 : 1;
+        RowsPlan rp;
+        rp.T = B * M, rp.rps = M, rp.pos_const = cbk == 1 ? 0 : cbk, rp.st = h->st_b, rp.st_pos = 0, rp.S = 1;
+        rp.kv = h->kv_fast_b, rp.kv_seq_stride = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd, rp.max_seq = f.ctx;
+        if ((rc = rows_layers(h, true, h->fx, M == 2 ? d : 2 * d, rp))) return rc;
+        // fast_norm + fast_output on each sequence's last row
+        CK(launch_split_rows(h->fx + (size_t)(M - 1) * d, 2 * d, B, d, h->fast_norm, f.eps, h->pf_xs, h->pf_inv,
+                             nullptr, h->stream));
+        if ((rc = prefill_gemm(h, h->fast_out, cb, d, B, h->pf_y2))) return rc;
+        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, cb, h->logits_fast_b, cb, nullptr, 0,
+                          h->stream));
+        SampleArgs a{};
+        a.logits = h->logits_fast_b, a.n = cb, a.n_contig = -1, a.vocab_full = cb;
+        a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
+        a.mode = SAMPLE_FAST, a.max_new = (int)k.max_new, a.st = h->st_b, a.cb_index = cbk;
+        a.frame_codes = h->frame_codes_b, a.codes_out = h->codes_b, a.fast_emb = h->fast_emb;
+        a.fast_x_next = cbk + 1 < K ? h->fx : nullptr, a.d = d;
+        a.rng_kind = rng_kind, a.philox_key = philox_key;
+        a.batched = 1, a.logits_stride = (size_t)cb, a.codes_stride = codes_stride;
+        a.fast_x_stride = (size_t)2 * d, a.frame_stride = (size_t)K;
+        CK(launch_sample_batch(a, B, h->stream));
+        h->launches += 3;
+    }
+    // step input embedding (build_step_input + embed_slow_ar_time_major)
+    EmbedArgs ea{};
+    ea.tokens = nullptr, ea.st = h->st_b, ea.frame_codes = h->frame_codes_b, ea.batched = 1;
+    ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = d, ea.K = K;
+    ea.cb_size = cb, ea.vocab = s.vocab_size, ea.cb_rows = s.codebook_rows;
+    ea.sem_begin = (uint32_t)s.semantic_begin_id, ea.sem_end = (uint32_t)s.semantic_end_id;
+    ea.scale_on = 1, ea.sem_scale = 1.0f / sqrtf((float)(K + 1));
+    ea.out = h->bx, ea.M = B, ea.done = nullptr, ea.error = &h->st->error;
+    CK(launch_embed(ea, h->stream, false));
+    // Slow-AR step: one row per sequence at its own position
+    RowsPlan rp;
+    rp.T = B, rp.rps = 1, rp.pos_const = 0, rp.st = h->st_b, rp.st_pos = 1, rp.S = batch_splits(h, B);
+    rp.kv = h->kv_slow, rp.kv_seq_stride = h->kv_slow_seq, rp.max_seq = h->cfg.max_seq;
+    if ((rc = rows_layers(h, false, h->bx, d, rp))) return rc;
+    // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
+    CK(launch_split_rows(h->bx, d, B, d, h->norm, h->slow.eps, h->pf_xs, h->pf_inv, h->hidden_b, h->stream));
+    if ((rc = prefill_gemm(h, h->emb + (size_t)s.semantic_begin_id * d, nsem, d, B, h->pf_y2))) return rc;
+    CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, nsem, h->logits_b, nsem + 1, nullptr, 0,
+                      h->stream));
+    if (extra) {
+        if ((rc = prefill_gemm(h, h->emb + (size_t)k.im_end * d, 1, d, B, h->pf_y2))) return rc;
+        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, 1, h->logits_b + nsem, nsem + 1, nullptr, 0,
+                          h->stream));
+    }
+    SampleArgs a = slow_sample_args(h, SAMPLE_SLOW_STEP, k);
+    a.logits = h->logits_b, a.st = h->st_b, a.rng = nullptr, a.out_token = nullptr;
+    a.rng_kind = rng_kind, a.philox_key = philox_key;
+    a.batched = 1, a.logits_stride = (size_t)nsem + 1;
+    CK(launch_sample_batch(a, B, h->stream));
+    h->launches += 4 + (extra ? 1 : 0);
+    return S2D_OK;
+}
+
 void free_handle(S2dHandle *h) {
     if (!h) return;
     if (h->device >= 0) cudaSetDevice(h->device);
     if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
+    if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
+    for (void *p : {(void *)h->st_b, (void *)h->bx, (void *)h->fx, (void *)h->hidden_b, (void *)h->logits_b,
+                    (void *)h->logits_fast_b, (void *)h->kv_fast_b, (void *)h->frame_codes_b, (void *)h->codes_b,
+                    (void *)h->ra_part, (void *)h->ra_counters})
+        if (p) cudaFree(p);
     void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
                     h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
                     h->logits_fast, h->part, h->counters, h->st, h->tokens_dev, h->frame_codes,
@@ -1137,6 +1357,7 @@ void free_handle(S2dHandle *h) {
                     (void *)h->pf_inv, (void *)h->pf_y2, (void *)h->pf_y2b, (void *)h->pf_xs})
         if (p) cudaFree(p);
     if (h->blas) cublasDestroy(h->blas);
+    if (h->blas_ws) cudaFree(h->blas_ws);
     if (h->ev0) cudaEventDestroy(h->ev0);
     if (h->ev1) cudaEventDestroy(h->ev1);
     if (h->ev2) cudaEventDestroy(h->ev2);
@@ -1172,6 +1393,11 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
         h->err = "max_seq_len must be non-zero";
         return report(h, S2D_EINVAL);
     }
+    if (h->cfg.max_batch > 4096) {
+        h->err = "max_batch must be at most 4096";
+        return report(h, S2D_EINVAL);
+    }
+    h->max_batch = std::max(1, h->cfg.max_batch);
     h->device = h->cfg.device;
     cudaError_t ce = cudaSetDevice(h->device);
     if (ce) {
@@ -1446,6 +1672,156 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
         profile->frame_launches = launched;
     }
     return S2D_OK;
+}
+
+int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *const *prompts,
+                                 const int32_t *cols, int32_t rows, const S2dGenParams *p, int32_t rng_kind,
+                                 uint64_t philox_key, uint64_t *rng_states, int32_t *out_codes,
+                                 uint32_t *out_n_frames, S2dProfile *profile) {
+    if (!h) return S2D_EINVAL;
+    if (!prompts || !cols || !p || !rng_states || !out_codes || !out_n_frames)
+        return set_err(h, S2D_EINVAL, "s2d_generate_codes_batch: NULL argument");
+    const S2dGraphSpec &s = h->spec;
+    const int K = std::max(s.num_codebooks, 1);
+    if (n_seq <= 0 || n_seq > h->max_batch || n_seq > kBatchMaxSeq)
+        return set_err(h, S2D_EINVAL, "n_seq must be in 1..min(max_batch, " + std::to_string(kBatchMaxSeq) +
+                                          "), max_batch = " + std::to_string(h->max_batch));
+    if (rng_kind != S2D_RNG_SEEDED && rng_kind != S2D_RNG_PHILOX) return set_err(h, S2D_EINVAL, "unknown rng_kind");
+    if (rows != s.num_codebooks + 1) return set_err(h, S2D_EINVAL, "prompt rows must be num_codebooks+1");
+    if (s.linear_type != 1) return set_err(h, S2D_EINVAL, "batched generation needs f16 linear weights");
+    if (h->fast_out_wq != EW_F16) return set_err(h, S2D_EINVAL, "batched generation needs an f16 fast_output");
+    for (int i = 0; i < n_seq; ++i) {
+        if (!prompts[i]) return set_err(h, S2D_EINVAL, "prompt " + std::to_string(i) + " is NULL");
+        if (cols[i] <= 0) return set_err(h, S2D_EINVAL, "expected at least one token in prompt " + std::to_string(i));
+        if ((int64_t)cols[i] + (int64_t)p->max_new_tokens > h->cfg.max_seq)
+            return set_err(h, S2D_ESTATE, "prompt " + std::to_string(i) + " + max_new_tokens exceeds max_seq");
+    }
+    CK(cudaSetDevice(h->device));
+    int32_t rc;
+    if ((rc = ensure_batch(h, p->max_new_tokens))) return rc;
+    const size_t codes_stride = (size_t)K * std::max<uint32_t>(p->max_new_tokens, 1);
+    CK(cudaMemsetAsync(h->codes_b, 0, (size_t)n_seq * codes_stride * sizeof(int32_t), h->stream));
+    GenKey k;
+    k.max_new = p->max_new_tokens, k.min_tokens = p->min_tokens_before_end, k.im_end = p->im_end_id;
+    k.temperature = p->temperature, k.top_p = p->top_p, k.top_k = p->top_k;
+
+    // each sequence's prefill + first semantic sample (generate.rs:126-162),
+    // into its own KV cache
+    CK(cudaEventRecord(h->ev0, h->stream));
+    const uint32_t launches0 = h->launches;
+    __half *kv0 = h->kv_slow;
+    for (int i = 0; i < n_seq; ++i) {
+        std::vector<int32_t> flat((size_t)rows * cols[i]);
+        for (int t = 0; t < cols[i]; ++t)
+            for (int r = 0; r < rows; ++r) {
+                const uint32_t v = prompts[i][(size_t)r * cols[i] + t];
+                if (v > 0x7fffffffu) {
+                    h->kv_slow = kv0;
+                    h->n_past = 0;
+                    return set_err(h, S2D_EINVAL, "prompt token id does not fit i32");
+                }
+                flat[(size_t)t * rows + r] = (int32_t)v;
+            }
+        h->kv_slow = kv0 + (size_t)i * h->kv_slow_seq;
+        h->n_past = 0;
+        rc = slow_eval(h, flat.data(), (int64_t)flat.size(), S2D_LOGITS_ALLOWED, p->im_end_id);
+        h->kv_slow = kv0;
+        if (rc) {
+            h->n_past = 0;
+            return rc;
+        }
+        CK(launch_set_state(h->st_b + i, h->n_past, cols[i], rng_states[i], h->stream));
+        SampleArgs first = slow_sample_args(h, SAMPLE_SLOW_FIRST, k);
+        first.st = h->st_b + i, first.rng = &h->st_b[i].rng, first.out_token = nullptr;
+        first.rng_kind = rng_kind, first.philox_key = philox_key, first.rng_seq = (uint32_t)i;
+        CK(launch_sample(first, h->stream, false));
+        CK(cudaMemcpyAsync(h->hidden_b + (size_t)i * s.hidden, h->hidden_post, (size_t)s.hidden * sizeof(float),
+                           cudaMemcpyDeviceToDevice, h->stream));
+        h->launches += 2;
+    }
+    h->n_past = 0;  // sequence 0's cache now holds batch sequence 0
+    const uint32_t prefill_kernels = h->launches - launches0;
+    CK(cudaEventRecord(h->ev1, h->stream));
+
+    // frames: one captured graph advances every sequence by one frame
+    if (!h->batch_exec || !(h->batch_key == k) || h->batch_n != n_seq || h->batch_rng_kind != rng_kind ||
+        h->batch_philox != philox_key) {
+        if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
+        h->batch_exec = nullptr;
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        const uint32_t l0 = h->launches;
+        rc = enqueue_frame_batch(h, k, n_seq, rng_kind, philox_key);
+        h->batch_kernels = h->launches - l0;
+        cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
+        if (rc || e2) {
+            if (graph) cudaGraphDestroy(graph);
+            if (rc) return rc;
+            return set_err(h, S2D_ECUDA, std::string("batch frame capture: ") + cudaGetErrorString(e2));
+        }
+        cudaError_t e = cudaGraphInstantiateWithFlags(&h->batch_exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e) return set_err(h, S2D_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        h->batch_key = k, h->batch_n = n_seq, h->batch_rng_kind = rng_kind, h->batch_philox = philox_key;
+    }
+    const uint32_t poll = 8;
+    std::vector<DevState> st((size_t)n_seq);
+    uint32_t launched = 0;
+    while (launched < p->max_new_tokens) {
+        const uint32_t batch = std::min(poll, p->max_new_tokens - launched);
+        for (uint32_t i = 0; i < batch; ++i) CK(cudaGraphLaunch(h->batch_exec, h->stream));
+        launched += batch;
+        CK(cudaMemcpyAsync(st.data(), h->st_b, st.size() * sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+        CK(cudaStreamSynchronize(h->stream));
+        bool all_done = true, err = false;
+        for (const DevState &x : st) all_done &= x.done != 0, err |= x.error != 0;
+        if (all_done || err) break;
+    }
+    CK(cudaEventRecord(h->ev2, h->stream));
+    CK(cudaMemcpyAsync(st.data(), h->st_b, st.size() * sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    std::vector<int32_t> codes((size_t)n_seq * codes_stride);
+    CK(cudaMemcpyAsync(codes.data(), h->codes_b, codes.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if ((rc = check_device_error(h))) return rc;
+    uint32_t total = 0;
+    for (int i = 0; i < n_seq; ++i) {
+        if (st[(size_t)i].error)
+            return set_err(h, S2D_EDEVICE, "sequence " + std::to_string(i) + ": device error flag " +
+                                               std::to_string(st[(size_t)i].error));
+        if (!st[(size_t)i].done)
+            return set_err(h, S2D_ESTATE, "sequence " + std::to_string(i) + ": generation did not finish");
+        const uint32_t frames = (uint32_t)st[(size_t)i].step_index;
+        // compact_codes (generate.rs:346-390), per sequence
+        int32_t *dst = out_codes + (size_t)i * codes_stride;
+        const int32_t *src = codes.data() + (size_t)i * codes_stride;
+        for (int cb = 0; cb < K; ++cb)
+            for (uint32_t t = 0; t < frames; ++t) dst[(size_t)cb * frames + t] = src[(size_t)cb * p->max_new_tokens + t];
+        out_n_frames[i] = frames;
+        rng_states[i] = st[(size_t)i].rng;
+        total += frames;
+    }
+    if (profile) {
+        float a = 0, b = 0;
+        cudaEventElapsedTime(&a, h->ev0, h->ev1);
+        cudaEventElapsedTime(&b, h->ev1, h->ev2);
+        profile->prefill_ms = a;
+        profile->decode_ms = b;
+        profile->frames = total;
+        profile->kernels_per_frame = h->batch_kernels;
+        profile->prefill_kernels = prefill_kernels;
+        profile->frame_launches = launched;
+    }
+    return S2D_OK;
+}
+
+int32_t s2d_philox4x32_10(const uint32_t *counter, const uint32_t *key, uint32_t *out) {
+    if (!counter || !key || !out) return S2D_EINVAL;
+    uint32_t *dev = nullptr;
+    if (cudaMalloc(&dev, 4 * sizeof(uint32_t)) != cudaSuccess) return S2D_ENOMEM;
+    cudaError_t e = launch_philox(counter, key, dev, nullptr);
+    if (!e) e = cudaMemcpy(out, dev, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    cudaFree(dev);
+    return e ? S2D_ECUDA : S2D_OK;
 }
 
 int32_t s2d_dequant_tensor(S2dHandle *h, const char *name, float *out, int64_t n) {

@@ -100,6 +100,11 @@ SIGNATURES = {
                                                 _P(_Sampler), _u64p, _u32p]),
     "s2d_generate_codes": (ctypes.c_int32, [ctypes.c_void_p, _u32p, ctypes.c_int32, ctypes.c_int32,
                                             _P(_GenParams), _u64p, _i32p, _u32p, _P(_Profile)]),
+    "s2d_generate_codes_batch": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32,
+                                                  _P(ctypes.c_void_p), _i32p, ctypes.c_int32,
+                                                  _P(_GenParams), ctypes.c_int32, ctypes.c_uint64,
+                                                  _u64p, _i32p, _u32p, _P(_Profile)]),
+    "s2d_philox4x32_10": (ctypes.c_int32, [_u32p, _u32p, _u32p]),
     "s2d_sample_token": (ctypes.c_int32, [ctypes.c_void_p, _f32p, ctypes.c_int64, _P(_Sampler),
                                           ctypes.c_int64, _u64p, _u32p]),
     "s2d_dequant_tensor": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_char_p, _f32p,
@@ -263,12 +268,15 @@ class SlowArState:
         self._spec = GraphSpec(**{f: getattr(spec, f) for f, _ in _Spec._fields_})
 
     @classmethod
-    def open(cls, transformer_path, max_seq_len: int = 32768, device: int = 0) -> "SlowArState":
+    def open(cls, transformer_path, max_seq_len: int = 32768, device: int = 0,
+             max_batch: int = 1) -> "SlowArState":
+        """max_batch: sequences of generate_codes_batch (each with its own KV
+        cache of max_seq_len positions)."""
         if max_seq_len <= 0:
             raise S2dError(-1, "max_seq_len must be non-zero")
         h = ctypes.c_void_p()
         err = ctypes.create_string_buffer(1024)
-        cfg = _Config(device=device, max_seq=max_seq_len, max_batch=1, flags=0)
+        cfg = _Config(device=device, max_seq=max_seq_len, max_batch=max_batch, flags=0)
         rc = lib().s2d_open(str(transformer_path).encode(), ctypes.byref(cfg), ctypes.byref(h),
                             err, len(err))
         if rc != 0:
@@ -455,6 +463,57 @@ def generate_codes(state: SlowArState, tokenizer, graph: GraphSpec, prompt: Prom
         profile=DecodeProfile(prof.prefill_ms, prof.decode_ms, prof.frames,
                               prof.kernels_per_frame, prof.prefill_kernels,
                               prof.frame_launches))
+
+
+RNG_SEEDED = 0  # the reference's SeededRng per sequence
+RNG_PHILOX = 1  # Philox4x32-10, counter (draw index, sequence)
+
+
+def generate_codes_batch(state: SlowArState, tokenizer, graph: GraphSpec,
+                         prompts: Sequence[PromptTensor], params: GenerateParams,
+                         fast_weights: FastArWeights, rngs: Sequence[SeededRng],
+                         rng_kind: int = RNG_SEEDED, philox_key: int = 0):
+    """generate_codes (generate.rs:117-221) over independent prompts at once,
+    one result per prompt.  With RNG_SEEDED, rngs[i] is sequence i's
+    SeededRng; with RNG_PHILOX its state is sequence i's draw counter.  The
+    handle must have been opened with max_batch >= len(prompts)."""
+    im_end = int(getattr(tokenizer, "im_end_id", tokenizer))
+    n = len(prompts)
+    if n != len(rngs):
+        raise S2dError(-1, "one rng per prompt")
+    rows = {p.rows for p in prompts}
+    if len(rows) != 1:
+        raise S2dError(-1, "prompts must share the row count (num_codebooks+1)")
+    datas = []
+    for p in prompts:
+        d = np.ascontiguousarray(np.asarray(p.data, dtype=np.uint32).reshape(-1))
+        if d.size != p.rows * p.cols:
+            raise S2dError(-1, "prompt data length mismatch")
+        datas.append(d)
+    ptrs = (ctypes.c_void_p * n)(*[d.ctypes.data for d in datas])
+    cols = np.array([p.cols for p in prompts], dtype=np.int32)
+    k = max(graph.num_codebooks, 1)
+    stride = k * max(params.max_new_tokens, 1)
+    codes = np.zeros(n * stride, dtype=np.int32)
+    frames = np.zeros(n, dtype=np.uint32)
+    states = np.array([r.state for r in rngs], dtype=np.uint64)
+    gp = _GenParams(params.max_new_tokens, params.temperature, params.top_p, params.top_k,
+                    params.min_tokens_before_end, im_end)
+    prof = _Profile()
+    state._check(lib().s2d_generate_codes_batch(
+        state.handle, n, ptrs, _ptr(cols, ctypes.c_int32), rows.pop(), ctypes.byref(gp),
+        rng_kind, ctypes.c_uint64(philox_key), _ptr(states, ctypes.c_uint64),
+        _ptr(codes, ctypes.c_int32), _ptr(frames, ctypes.c_uint32), ctypes.byref(prof)))
+    out = []
+    for i in range(n):
+        rngs[i].state = int(states[i])
+        f = int(frames[i])
+        out.append(GenerateCodesResult(
+            codes=codes[i * stride: i * stride + k * f].copy(), num_codebooks=k, n_frames=f,
+            profile=DecodeProfile(prof.prefill_ms, prof.decode_ms, prof.frames,
+                                  prof.kernels_per_frame, prof.prefill_kernels,
+                                  prof.frame_launches)))
+    return out
 
 
 # ---------------------------------------------------------------------------

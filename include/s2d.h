@@ -39,7 +39,8 @@ typedef struct S2dHandle S2dHandle;
 typedef struct S2dConfig {
     int32_t device;       /* CUDA device ordinal                                   */
     int32_t max_seq;      /* Slow-AR KV capacity in positions (SlowArState::open)   */
-    int32_t max_batch;    /* reserved: sequences per handle (1 in this version)      */
+    int32_t max_batch;    /* sequences of s2d_generate_codes_batch (<= 0: 1); each
+                             holds its own Slow-AR KV cache of max_seq positions   */
     int32_t flags;        /* reserved, 0                                             */
 } S2dConfig;
 
@@ -151,6 +152,32 @@ int32_t s2d_generate_codebooks(S2dHandle *h, const float *slow_hidden, uint32_t 
 int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, int32_t cols,
                            const S2dGenParams *params, uint64_t *rng_state, int32_t *out_codes,
                            uint32_t *out_n_frames, S2dProfile *profile);
+
+/* Random draws of the batched sampler. */
+#define S2D_RNG_SEEDED 0 /* the reference's SeededRng LCG; rng_states[i] is its state        */
+#define S2D_RNG_PHILOX 1 /* Philox4x32-10, key philox_key, counter (rng_states[i], i):      */
+                         /* rng_states[i] counts sequence i's draws                         */
+
+/* generate_codes over n_seq independent prompts at once (the batched
+ * variant of generate.rs:117-221; the reference has none).  prompts[i] is
+ * row-major rows x cols[i] (rows = num_codebooks+1); every sequence shares
+ * params.  Sequence i's codes go to out_codes + i*num_codebooks*max_new_tokens,
+ * codebook-major and compacted to out_n_frames[i] frames; rng_states[i] is
+ * advanced in place.  With S2D_RNG_SEEDED sequence i produces the codes of
+ * s2d_generate_codes on prompt i with state rng_states[i] (up to rounding
+ * of the batched GEMMs).  Needs n_seq <= max_batch (S2dConfig), f16 linears,
+ * and cols[i] + max_new_tokens <= max_seq.  Resets the single-sequence
+ * state (n_past = 0): sequence 0's cache is reused.  profile (may be NULL)
+ * counts frames over all sequences. */
+int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *const *prompts,
+                                 const int32_t *cols, int32_t rows, const S2dGenParams *params,
+                                 int32_t rng_kind, uint64_t philox_key, uint64_t *rng_states,
+                                 int32_t *out_codes, uint32_t *out_n_frames, S2dProfile *profile);
+
+/* The batched sampler's Philox4x32-10 block function, run on the current
+ * device: out = philox(counter[4], key[2]).  For checking the generator
+ * against the published known-answer vectors. */
+int32_t s2d_philox4x32_10(const uint32_t *counter, const uint32_t *key, uint32_t *out);
 
 /* ---- sampling (sampling.rs:121-241) ------------------------------------- */
 
