@@ -48,6 +48,9 @@ from fish_s2pro_b200 import configs  # noqa: E402
 
 METRIC = "Dual-AR frames/sec (batch 1)"
 METRIC_BATCH = "Dual-AR frames/sec (batch 64)"
+# arithmetic of the linears: f16 weights, or ggml blocks dequantised in
+# registers; activations and accumulation are f32 throughout
+WTYPE = {configs.GGML_F16: "f16", configs.GGML_Q8_0: "q8_0", configs.GGML_Q4_K: "q4_k"}
 UNIT = "frames/s"
 # DRAM traffic of one Slow-AR step program over its algorithmic bytes, from an
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of the 4-layer
@@ -298,9 +301,9 @@ def run_ours(args, d: Dist):
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": d.world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(wall / args.steps * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded random-init S2-Pro-shaped GGUF, seeded 512-id prompt)",
-        "config": {"workload": f"{args.workload}: full-size f16 S2-Pro-shaped Dual-AR, "
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": WTYPE[m.linear_type],
+        "data": f"synthetic (seeded random-init S2-Pro-shaped GGUF, seeded {wl.prompt_len}-id prompt)",
+        "config": {"workload": f"{args.workload}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, "
                                f"{wl.prompt_len}-token prompt, greedy {frames} frames, batch 1",
                    "global_batch": d.world, "seq_len": wl.prompt_len + frames,
                    "parallelism": f"replicas x{d.world} (independent utterances)",
@@ -316,7 +319,8 @@ def run_ours(args, d: Dist):
         "roofline": {"bound": "hbm", "kernel": "engine_kernel, Slow-AR step program (36 layers + masked LM head)",
                      "achieved": round(top["gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(top["gbs"] / pk["hbm_gbs"], 3),
-                     "traffic": int(top["bytes"] * ENGINE_TRAFFIC_RATIO) if top["bytes"] else None,
+                     "traffic": (int(top["bytes"] * ENGINE_TRAFFIC_RATIO)
+                                 if top["bytes"] and m.linear_type == configs.GGML_F16 else None),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 4-layer "
                                        "C2S Slow-AR step (1.019 x its algorithmic bytes), scaled to "
                                        "this step's algorithmic bytes",
@@ -391,6 +395,8 @@ def run_batch(args, d: Dist, wl):
     step_s = decode_s / (args.steps * frames) / 1.0
     achieved = step_bytes / step_s / 1e9
     h2d = int(sum(p.nbytes for p in ps))
+    breakdown = {} if args.no_kernel_profile else {
+        k: round(v, 3) for k, v in st.profile_batch(B).items()}
     line = {
         "metric": METRIC_BATCH, "value": round(value, 1), "unit": UNIT, "n_gpus": d.world,
         "steps": args.steps, "warmup": args.warmup,
@@ -414,7 +420,8 @@ def run_batch(args, d: Dist, wl):
                                                "stacked rows, rows attention, samplers)",
                      "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None,
-                     "peak_source": pk["source"], "bytes_per_launch": int(step_bytes)},
+                     "peak_source": pk["source"], "bytes_per_launch": int(step_bytes),
+                     "frame_ms_by_kernel": breakdown},
         "clocks": ck,
     }
     st.close()

@@ -289,6 +289,31 @@ __global__ void dequant_kernel(int wq, const uint8_t *src, float *dst, int64_t n
     for (int i = 0; i < 32; ++i) dst[blk * 32 + i] = s.at(wq, i);
 }
 
+// The same values rounded to f16 (round to nearest even), for the tensor-core
+// prefill of quantized models.
+__global__ void dequant_f16_kernel(int wq, const uint8_t *src, __half *dst, int64_t n) {
+    const int64_t blk = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (blk >= n / 32) return;
+    const uint8_t *base = src + (wq == 1 ? (size_t)(blk / 8) * 8 * 34 : (size_t)(blk / 8) * 144);
+    const QuantSub s(wq, base, (int)(blk % 8));
+    __align__(16) __half v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __float2half_rn(s.at(wq, i));
+    uint4 *d4 = reinterpret_cast<uint4 *>(dst + blk * 32);
+    const uint4 *v4 = reinterpret_cast<const uint4 *>(v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d4[i] = v4[i];
+}
+
+cudaError_t launch_dequant_f16(int wq, const void *src, __half *dst, int64_t n, cudaStream_t s) {
+    if ((wq != 1 && wq != 2) || n % (wq == 1 ? 32 : 256) || (reinterpret_cast<uintptr_t>(dst) & 15))
+        return cudaErrorInvalidValue;
+    const int64_t blocks = n / 32;
+    dequant_f16_kernel<<<(unsigned)((blocks + 255) / 256), 256, 0, s>>>(wq, reinterpret_cast<const uint8_t *>(src),
+                                                                       dst, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dequant(int gtype, const void *src, float *dst, int64_t n, cudaStream_t s) {
     const int wq = gtype == 8 ? 1 : gtype == 12 ? 2 : 0;
     if (!wq || n % (wq == 1 ? 32 : 256)) return cudaErrorInvalidValue;

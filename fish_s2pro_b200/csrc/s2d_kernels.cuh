@@ -1,6 +1,7 @@
 // s2d_kernels.cuh -- kernel argument blocks and host launchers.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -334,6 +335,8 @@ cudaError_t launch_f16_to_f32(const uint16_t *src, float *dst, int64_t n, cudaSt
 // ggml Q8_0 / Q4_K blocks (gtype 8 / 12) of n elements -> f32 (the block
 // formulas d*q and (d*sc)*q - dmin*m, each rounded once in f32).
 cudaError_t launch_dequant(int gtype, const void *src, float *dst, int64_t n, cudaStream_t s);
+// Q8_0 (wq 1) / Q4_K (wq 2) blocks -> f16 values (n elements, dst 16-byte aligned).
+cudaError_t launch_dequant_f16(int wq, const void *src, __half *dst, int64_t n, cudaStream_t s);
 cudaError_t launch_rms_norm_heads(const float *x, const float *w, float *y, int64_t n, int hd,
                                   float eps, cudaStream_t s);
 cudaError_t launch_set_state(DevState *st, int32_t n_past, int32_t prompt_cols, uint64_t rng,

@@ -119,6 +119,9 @@ struct S2dHandle {
     // batched prefill (s2d_prefill.cu): up to pf_cap tokens per layer pass
     cublasHandle_t blas = nullptr;
     void *blas_ws = nullptr;
+    // quantized models: one layer's linears dequantised to f16 for the
+    // tensor-core rows path (wqkv, wo, w1, w3, w2)
+    __half *qscratch[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_act = nullptr;
     float *pf_inv = nullptr, *pf_y2 = nullptr, *pf_y2b = nullptr;
@@ -154,6 +157,10 @@ struct S2dHandle {
     int32_t *ra_counters = nullptr;
     int ra_rows = 0, ra_smax = 0;
     cudaGraphExec_t batch_exec = nullptr;
+    // s2d_profile_batch: events recorded after each launch, tagged with the
+    // launch's category (null outside profiling); codes are not stored
+    std::vector<std::pair<int, cudaEvent_t>> *marks = nullptr;
+    bool batch_profile = false;
     GenKey batch_key;
     int batch_n = 0, batch_rng_kind = -1;
     uint64_t batch_philox = 0;
@@ -1016,6 +1023,19 @@ int32_t prefill_gemm(S2dHandle *h, const uint16_t *W, int N, int K, int T, float
     return S2D_OK;
 }
 
+// Kernel categories of s2d_profile_batch (S2D_PROF_* in include/s2d.h).
+enum ProfCat { PC_SPLIT = 0, PC_GEMM = 1, PC_COMBINE = 2, PC_ROPE = 3, PC_ATTN = 4, PC_SAMPLE = 5, PC_OTHER = 6,
+               PC_COUNT = 7 };
+
+// While profiling, an event after the launch just enqueued, tagged cat.
+void mark(S2dHandle *h, int cat) {
+    if (!h->marks) return;
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return;
+    cudaEventRecord(e, h->stream);
+    h->marks->emplace_back(cat, e);
+}
+
 // Rows of one layered pass (rows_layers): T rows of the residual x, row m
 // of sequence m / rps at position pos_const + m % rps (+ st[seq].n_past with
 // st_pos); sequence s's KV cache starts kv_seq_stride elements after
@@ -1036,6 +1056,29 @@ struct RowsPlan {
 // forward_slow_ar_block_prefill_layers_cached, slow_ar.rs:1002-1039, when the
 // rows are one prompt; FastArLayerSkeleton::forward_prefill,
 // fast_ar.rs:245-352, for the Fast-AR).
+// A quantized layer's linears as f16 rows in qscratch (rounded to nearest):
+// L's weight pointers are redirected there.
+int32_t dequant_layer(S2dHandle *h, const ArShape &a, LayerDev *L) {
+    if (!h->qscratch[0]) {
+        const ArShape &sl = h->slow, &fa = h->fast;
+        const size_t d = (size_t)std::max(sl.d, fa.d);
+        const size_t n[5] = {(size_t)std::max(sl.qkv_out(), fa.qkv_out()) * d,
+                             d * (size_t)std::max(sl.qs(), fa.qs()), (size_t)std::max(sl.F, fa.F) * d,
+                             (size_t)std::max(sl.F, fa.F) * d, d * (size_t)std::max(sl.F, fa.F)};
+        for (int i = 0; i < 5; ++i) CK(cudaMalloc(&h->qscratch[i], n[i] * sizeof(__half)));
+    }
+    const uint16_t **w[5] = {&L->wqkv, &L->wo, &L->w1, &L->w3, &L->w2};
+    const int64_t n[5] = {(int64_t)a.qkv_out() * a.d, (int64_t)a.d * a.qs(), (int64_t)a.F * a.d,
+                          (int64_t)a.F * a.d, (int64_t)a.d * a.F};
+    for (int i = 0; i < 5; ++i) {
+        CK(launch_dequant_f16(L->wq, *w[i], h->qscratch[i], n[i], h->stream));
+        *w[i] = reinterpret_cast<const uint16_t *>(h->qscratch[i]);
+    }
+    L->wq = EW_F16;
+    h->launches += 5;
+    return S2D_OK;
+}
+
 int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPlan &rp) {
     const ArShape &a = is_fast ? h->fast : h->slow;
     const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F, T = rp.T;
@@ -1043,11 +1086,15 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
     const size_t layer_bytes = (size_t)2 * a.Hkv * rp.max_seq * a.hd * kvb;
     int32_t rc;
     for (int l = 0; l < a.L; ++l) {
-        const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
+        LayerDev L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
+        if (L.wq != EW_F16 && (rc = dequant_layer(h, a, &L))) return rc;
         // attention_norm + WQKV
         CK(launch_split_rows(x, ldx, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.wqkv, qo, d, T, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, T, qo, h->pf_qkv, qo, nullptr, 0, h->stream));
+        mark(h, PC_COMBINE);
         // QK-norm (Slow-AR) + RoPE + KV write for every row
         uint8_t *base = reinterpret_cast<uint8_t *>(rp.kv) + (size_t)l * layer_bytes;
         RopeArgs r{};
@@ -1059,6 +1106,7 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         r.H = a.H, r.Hkv = a.Hkv, r.hd = a.hd, r.M = T, r.done = nullptr, r.error = &h->st->error;
         r.rows_per_seq = rp.rps, r.st_b = rp.st, r.st_pos = rp.st_pos, r.kv_seq_stride = rp.kv_seq_stride;
         CK(launch_rope_kv(r, !is_fast, h->stream, false));
+        mark(h, PC_ROPE);
         // GQA attention of every row over its sequence's cache
         RowsAttnArgs t{};
         t.q = h->pf_q, t.kcache = r.kcache, t.vcache = r.vcache, t.kv_seq_stride = rp.kv_seq_stride;
@@ -1067,20 +1115,31 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters;
         CK(launch_rows_attention(t, !is_fast, h->stream));
+        mark(h, PC_ATTN);
         // wo + residual
         CK(launch_split_rows(h->pf_att, qs, T, qs, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.wo, d, qs, T, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
+        mark(h, PC_COMBINE);
         // ffn_norm + w1 / w3 + SwiGLU
         CK(launch_split_rows(x, ldx, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.w1, F, d, T, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         if ((rc = prefill_gemm(h, L.w3, F, d, T, h->pf_y2b))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(is_fast ? PF_SWIGLU_FAST : PF_SWIGLU_SLOW, h->pf_y2, h->pf_y2b, h->pf_inv, T, F,
                           h->pf_act, F, nullptr, 0, h->stream));
+        mark(h, PC_COMBINE);
         // w2 + residual
         CK(launch_split_rows(h->pf_act, F, T, F, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.w2, d, F, T, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
+        mark(h, PC_COMBINE);
         h->launches += 10;  // own kernels; the GEMMs are cuBLAS's
     }
     return S2D_OK;
@@ -1126,7 +1185,7 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
     int32_t rc = ensure_tokens(h, (size_t)n_flat);
     if (rc) return rc;
     CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
-    if (n >= kPrefillMin && h->spec.linear_type == 1 /* F16 */) {
+    if (n >= kPrefillMin) {
         if ((rc = ensure_prefill(h))) return rc;
         for (int64_t c0 = 0; c0 < n; c0 += h->pf_cap) {
             const int T = (int)std::min<int64_t>(h->pf_cap, n - c0);
@@ -1268,12 +1327,13 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     int32_t rc;
     FastInitArgs fi{};
     fi.st = h->st_b, fi.slow_hidden = h->hidden_b, fi.fast_emb = h->fast_emb, fi.fast_x = h->fx;
-    fi.frame_codes = h->frame_codes_b, fi.codes_out = h->codes_b;
+    fi.frame_codes = h->frame_codes_b, fi.codes_out = h->batch_profile ? nullptr : h->codes_b;
     fi.max_new = (int)k.max_new, fi.d = d, fi.cb_size = cb;
     fi.sem_begin = (uint32_t)s.semantic_begin_id, fi.sem_end = (uint32_t)s.semantic_end_id;
     fi.batched = 1, fi.hidden_stride = (size_t)d, fi.fast_x_stride = (size_t)2 * d;
     fi.codes_stride = codes_stride, fi.frame_stride = (size_t)K;
     CK(launch_fast_init_batch(fi, B, h->stream));
+    mark(h, PC_OTHER);
     h->launches += 1;
     for (int cbk = 1; cbk < K; ++cbk) {
         // positions 0 and 1 on the first pass (rows (seq, 0), (seq, 1) of fx),
@@ -1286,19 +1346,24 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
         // fast_norm + fast_output on each sequence's last row
         CK(launch_split_rows(h->fx + (size_t)(M - 1) * d, 2 * d, B, d, h->fast_norm, f.eps, h->pf_xs, h->pf_inv,
                              nullptr, h->stream));
+        mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, h->fast_out, cb, d, B, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, cb, h->logits_fast_b, cb, nullptr, 0,
                           h->stream));
+        mark(h, PC_COMBINE);
         SampleArgs a{};
         a.logits = h->logits_fast_b, a.n = cb, a.n_contig = -1, a.vocab_full = cb;
         a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
         a.mode = SAMPLE_FAST, a.max_new = (int)k.max_new, a.st = h->st_b, a.cb_index = cbk;
-        a.frame_codes = h->frame_codes_b, a.codes_out = h->codes_b, a.fast_emb = h->fast_emb;
+        a.frame_codes = h->frame_codes_b, a.codes_out = h->batch_profile ? nullptr : h->codes_b;
+        a.fast_emb = h->fast_emb;
         a.fast_x_next = cbk + 1 < K ? h->fx : nullptr, a.d = d;
         a.rng_kind = rng_kind, a.philox_key = philox_key;
         a.batched = 1, a.logits_stride = (size_t)cb, a.codes_stride = codes_stride;
         a.fast_x_stride = (size_t)2 * d, a.frame_stride = (size_t)K;
         CK(launch_sample_batch(a, B, h->stream));
+        mark(h, PC_SAMPLE);
         h->launches += 3;
     }
     // step input embedding (build_step_input + embed_slow_ar_time_major)
@@ -1310,6 +1375,7 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     ea.scale_on = 1, ea.sem_scale = 1.0f / sqrtf((float)(K + 1));
     ea.out = h->bx, ea.M = B, ea.done = nullptr, ea.error = &h->st->error;
     CK(launch_embed(ea, h->stream, false));
+    mark(h, PC_OTHER);
     // Slow-AR step: one row per sequence at its own position
     RowsPlan rp;
     rp.T = B, rp.rps = 1, rp.pos_const = 0, rp.st = h->st_b, rp.st_pos = 1, rp.S = batch_splits(h, B);
@@ -1317,19 +1383,25 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     if ((rc = rows_layers(h, false, h->bx, d, rp))) return rc;
     // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
     CK(launch_split_rows(h->bx, d, B, d, h->norm, h->slow.eps, h->pf_xs, h->pf_inv, h->hidden_b, h->stream));
+    mark(h, PC_SPLIT);
     if ((rc = prefill_gemm(h, h->emb + (size_t)s.semantic_begin_id * d, nsem, d, B, h->pf_y2))) return rc;
+    mark(h, PC_GEMM);
     CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, nsem, h->logits_b, nsem + 1, nullptr, 0,
                       h->stream));
+    mark(h, PC_COMBINE);
     if (extra) {
         if ((rc = prefill_gemm(h, h->emb + (size_t)k.im_end * d, 1, d, B, h->pf_y2))) return rc;
+        mark(h, PC_GEMM);
         CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, 1, h->logits_b + nsem, nsem + 1, nullptr, 0,
                           h->stream));
+        mark(h, PC_COMBINE);
     }
     SampleArgs a = slow_sample_args(h, SAMPLE_SLOW_STEP, k);
     a.logits = h->logits_b, a.st = h->st_b, a.rng = nullptr, a.out_token = nullptr;
     a.rng_kind = rng_kind, a.philox_key = philox_key;
     a.batched = 1, a.logits_stride = (size_t)nsem + 1;
     CK(launch_sample_batch(a, B, h->stream));
+    mark(h, PC_SAMPLE);
     h->launches += 4 + (extra ? 1 : 0);
     return S2D_OK;
 }
@@ -1355,6 +1427,8 @@ void free_handle(S2dHandle *h) {
     for (auto &kv : h->tiled) cudaFree(kv.second);
     for (void *p : {(void *)h->pf_x, (void *)h->pf_qkv, (void *)h->pf_q, (void *)h->pf_att, (void *)h->pf_act,
                     (void *)h->pf_inv, (void *)h->pf_y2, (void *)h->pf_y2b, (void *)h->pf_xs})
+        if (p) cudaFree(p);
+    for (__half *p : h->qscratch)
         if (p) cudaFree(p);
     if (h->blas) cublasDestroy(h->blas);
     if (h->blas_ws) cudaFree(h->blas_ws);
@@ -1811,6 +1885,46 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
         profile->prefill_kernels = prefill_kernels;
         profile->frame_launches = launched;
     }
+    return S2D_OK;
+}
+
+int32_t s2d_profile_batch(S2dHandle *h, int32_t n_seq, double *out_ms, int32_t n_out) {
+    if (!h || !out_ms || n_out <= 0) return S2D_EINVAL;
+    if (!h->st_b || h->batch_n <= 0)
+        return set_err(h, S2D_ESTATE, "s2d_profile_batch needs a previous s2d_generate_codes_batch call");
+    if (n_seq <= 0 || n_seq > h->batch_n)
+        return set_err(h, S2D_EINVAL, "n_seq must be in 1..the last batch's sequence count");
+    CK(cudaSetDevice(h->device));
+    // every sequence active again for one more frame (codes are not stored)
+    for (int i = 0; i < n_seq; ++i) CK(cudaMemsetAsync(&h->st_b[i].done, 0, sizeof(int32_t), h->stream));
+    std::vector<std::pair<int, cudaEvent_t>> marks;
+    cudaEvent_t start = nullptr;
+    CK(cudaEventCreate(&start));
+    CK(cudaEventRecord(start, h->stream));
+    h->marks = &marks;
+    h->batch_profile = true;
+    const int32_t rc = enqueue_frame_batch(h, h->batch_key, n_seq, h->batch_rng_kind, h->batch_philox);
+    h->marks = nullptr;
+    h->batch_profile = false;
+    cudaError_t e = cudaStreamSynchronize(h->stream);
+    double sums[PC_COUNT + 1] = {0};
+    cudaEvent_t prev = start;
+    for (auto &m : marks) {
+        float ms = 0.f;
+        if (!e) cudaEventElapsedTime(&ms, prev, m.second);
+        sums[m.first] += ms;
+        sums[PC_COUNT] += ms;
+        prev = m.second;
+    }
+    for (auto &m : marks) cudaEventDestroy(m.second);
+    cudaEventDestroy(start);
+    // this extra frame may reach max_seq for some sequence: not an error here
+    cudaMemsetAsync(&h->st->error, 0, sizeof(int32_t), h->stream);
+    for (int i = 0; i < n_seq; ++i) cudaMemsetAsync(&h->st_b[i].done, 0xff, sizeof(int32_t), h->stream);
+    cudaStreamSynchronize(h->stream);
+    if (rc) return rc;
+    if (e) return set_err(h, S2D_ECUDA, std::string("profile_batch: ") + cudaGetErrorString(e));
+    for (int i = 0; i < n_out && i <= PC_COUNT; ++i) out_ms[i] = sums[i];
     return S2D_OK;
 }
 

@@ -105,6 +105,8 @@ SIGNATURES = {
                                                   _P(_GenParams), ctypes.c_int32, ctypes.c_uint64,
                                                   _u64p, _i32p, _u32p, _P(_Profile)]),
     "s2d_philox4x32_10": (ctypes.c_int32, [_u32p, _u32p, _u32p]),
+    "s2d_profile_batch": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _P(ctypes.c_double),
+                                           ctypes.c_int32]),
     "s2d_sample_token": (ctypes.c_int32, [ctypes.c_void_p, _f32p, ctypes.c_int64, _P(_Sampler),
                                           ctypes.c_int64, _u64p, _u32p]),
     "s2d_dequant_tensor": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_char_p, _f32p,
@@ -370,6 +372,15 @@ class SlowArState:
         g = (int(np.count_nonzero(buf[n.value * 8:])) + n.value - 1) // max(n.value, 1) if trace else 0
         fin = buf[n.value * 8: n.value * (8 + g)].reshape(n.value, g) if trace else None
         return float(ms.value), tr, fin
+
+    PROFILE_BATCH_KEYS = ("split", "gemm", "combine", "rope", "attention", "sample", "other", "total")
+
+    def profile_batch(self, n_seq: int) -> dict:
+        """ms of one batched frame per kernel category (s2d_profile_batch),
+        after generate_codes_batch."""
+        out = (ctypes.c_double * len(self.PROFILE_BATCH_KEYS))()
+        self._check(lib().s2d_profile_batch(self._h, n_seq, out, len(out)))
+        return dict(zip(self.PROFILE_BATCH_KEYS, list(out)))
 
     def dequant_tensor(self, name: str, count: int) -> np.ndarray:
         out = np.empty(count, dtype=np.float32)

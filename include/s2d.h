@@ -174,6 +174,22 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
                                  int32_t rng_kind, uint64_t philox_key, uint64_t *rng_states,
                                  int32_t *out_codes, uint32_t *out_n_frames, S2dProfile *profile);
 
+/* Device time of one batched frame by kernel category: the frame of the
+ * last s2d_generate_codes_batch call (its first n_seq sequences), replayed
+ * once outside its graph with a CUDA event after every launch; each gap is
+ * charged to the launch it ends.  Every sequence runs the frame (codes are
+ * not stored); afterwards every sequence is marked finished.  out_ms[i] for
+ * i < n_out: S2D_PROF_* below, out_ms[S2D_PROF_TOTAL] the whole frame. */
+#define S2D_PROF_SPLIT 0    /* RMSNorm + hi/lo row split before each GEMM  */
+#define S2D_PROF_GEMM 1     /* tensor-core GEMMs over the stacked rows     */
+#define S2D_PROF_COMBINE 2  /* hi + lo, residual / SwiGLU epilogues        */
+#define S2D_PROF_ROPE 3     /* QK-norm + RoPE + KV writes                  */
+#define S2D_PROF_ATTN 4     /* GQA attention of every row                  */
+#define S2D_PROF_SAMPLE 5   /* samplers                                    */
+#define S2D_PROF_OTHER 6    /* embedding feedback, Fast-AR frame start     */
+#define S2D_PROF_TOTAL 7
+int32_t s2d_profile_batch(S2dHandle *h, int32_t n_seq, double *out_ms, int32_t n_out);
+
 /* The batched sampler's Philox4x32-10 block function, run on the current
  * device: out = philox(counter[4], key[2]).  For checking the generator
  * against the published known-answer vectors. */
