@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--prompt-len", type=int, default=None,
                     help="override the prompt length (profiling runs only)")
     ap.add_argument("--model-dir", default=None, help="GGUF cache (default: synth.default_model_dir())")
+    ap.add_argument("--tp", action="store_true",
+                    help="under torchrun: all ranks form one tensor-parallel Slow-AR decoding one "
+                         "utterance (strong scaling) instead of independent replicas")
     return ap.parse_args()
 
 
@@ -114,6 +117,14 @@ class Dist:
         t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
         return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        """Rank 0's bytes on every rank."""
+        if not self.pg:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
 
     def close(self):
         if self.pg:
@@ -245,10 +256,15 @@ def run_ours(args, d: Dist):
     frames = args.frames or wl.frames
     m = wl.model
     path = ensure_model(d, wl, args.model_dir)
-    st = SlowArState.open(path, max_seq_len=wl.prompt_len + frames + 8, device=d.local)
+    tp = None
+    if args.tp and d.world > 1:
+        from fish_s2pro_b200 import nccl_unique_id
+        tp = (d.world, d.rank, d.bcast_bytes(nccl_unique_id() if d.rank == 0 else None))
+    st = SlowArState.open(path, max_seq_len=wl.prompt_len + frames + 8, device=d.local, tp=tp)
     spec = st.graph_spec()
     fw = FastArWeights.from_state(st)
-    prompt = configs.Workload(m, wl.prompt_len, frames, wl.prompt_seed + d.rank,
+    # replicas decode their own prompts; tensor-parallel ranks share one
+    prompt = configs.Workload(m, wl.prompt_len, frames, wl.prompt_seed + (0 if tp else d.rank),
                               wl.im_end_id).prompt()
     gp = wl.gen_params(greedy=True)
     gp["max_new_tokens"] = frames
@@ -276,7 +292,7 @@ def run_ours(args, d: Dist):
     decode_s = d.max(sum(r.profile.decode_ms for r in results) / 1e3)
     prefill_ms = d.max(statistics.mean(r.profile.prefill_ms for r in results))
     my_frames = sum(r.n_frames for r in results)
-    frames_total = d.sum(my_frames)
+    frames_total = my_frames if tp else d.sum(my_frames)
     launches = sum(r.profile.prefill_kernels + r.profile.kernels_per_frame *
                    r.profile.frame_launches for r in results)
     value = frames_total / decode_s
@@ -286,7 +302,7 @@ def run_ours(args, d: Dist):
     # the engine's programs, timed live after the timed steps on the state
     # they left (n_past = prompt + frames): median of 7 launches each
     kern = {}
-    if not args.no_kernel_profile:
+    if not args.no_kernel_profile and not tp:  # the engine is single-GPU
         n_past = st.n_past()
         kv_pos = configs.kv_bytes_per_position(m)
         passes = m.num_codebooks - 1
@@ -297,16 +313,28 @@ def run_ours(args, d: Dist):
     top = kern.get("slow_step", {"ms": float("nan"), "bytes": 0.0, "gbs": float("nan")})
     p_avg = wl.prompt_len + frames / 2
     frame_bytes = sum(bpf.values()) + configs.kv_bytes_per_position(m) * p_avg
+    # HBM bytes each GPU streams per second: a replica streams whole frames;
+    # a tensor-parallel rank its share of the Slow-AR and KV plus the
+    # replicated LM head and Fast-AR
+    if tp:
+        rank_bytes = ((bpf["slow"] + configs.kv_bytes_per_position(m) * p_avg) / d.world
+                      + bpf["lm_head"] + bpf["fast"] + bpf["embed_rows"])
+        gpu_gbs = rank_bytes * value / 1e9
+    else:
+        gpu_gbs = frame_bytes * value / d.world / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": d.world,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(wall / args.steps * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": WTYPE[m.linear_type],
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": WTYPE[m.linear_type],
         "data": f"synthetic (seeded random-init S2-Pro-shaped GGUF, seeded {wl.prompt_len}-id prompt)",
         "config": {"workload": f"{args.workload}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, "
                                f"{wl.prompt_len}-token prompt, greedy {frames} frames, batch 1",
                    "global_batch": d.world, "seq_len": wl.prompt_len + frames,
-                   "parallelism": f"replicas x{d.world} (independent utterances)",
+                   "parallelism": (f"tp{d.world} (Slow-AR heads and FFN columns sharded, NCCL "
+                                   "allreduce after wo and w2; Fast-AR replicated)") if tp
+                                  else f"replicas x{d.world} (independent utterances)",
                    "l2": "inputs larger than L2 (each frame streams ~14.8 GB of weights)"},
         "e2e": {"value": round(e2e, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(prompt.nbytes),
@@ -314,8 +342,8 @@ def run_ours(args, d: Dist):
         "gpu_launches": int(launches),
         "prefill_ms": round(prefill_ms, 2),
         "frame_bytes": int(frame_bytes),
-        "frame_gbs": round(frame_bytes * value / d.world / 1e9, 1),
-        "frame_roofline_frac": round(frame_bytes * value / d.world / 1e9 / pk["hbm_gbs"], 3),
+        "frame_gbs": round(gpu_gbs, 1),
+        "frame_roofline_frac": round(gpu_gbs / pk["hbm_gbs"], 3),
         "roofline": {"bound": "hbm", "kernel": "engine_kernel, Slow-AR step program (36 layers + masked LM head)",
                      "achieved": round(top["gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(top["gbs"] / pk["hbm_gbs"], 3),

@@ -28,6 +28,8 @@ from .s2d import (  # noqa: F401
     RNG_PHILOX,
     RNG_SEEDED,
     lib,
+    nccl_unique_id,
+    tp_plan,
     sample_token,
     transpose_to_time_major,
 )

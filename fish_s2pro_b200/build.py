@@ -59,7 +59,7 @@ def build_runtime(force: bool = False, verbose_ptxas: bool = False) -> Path:
         _nvcc(), *NVCC_ARCH, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
         "-Xcompiler", "-fPIC", "-shared", "-o", str(LIB),
         *[str(CSRC / s) for s in CUDA_SOURCES],
-        f"-L{CUDA_LIB}", "-lcublas", "-Xlinker", f"-rpath={CUDA_LIB}",
+        f"-L{CUDA_LIB}", "-lcublas", "-ldl", "-Xlinker", f"-rpath={CUDA_LIB}",
     ]
     if verbose_ptxas:
         cmd[1:1] = ["-Xptxas", "-v"]

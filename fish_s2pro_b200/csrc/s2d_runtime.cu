@@ -8,6 +8,8 @@
 // Slow-AR step, the masked LM head and the semantic sampler; it is replayed
 // once per frame without any host round-trip.
 #include <cublas_v2.h>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <cuda_fp16.h>
 #include <math.h>
 #include <stdio.h>
@@ -136,8 +138,16 @@ struct S2dHandle {
     size_t tiled_bytes = 0;
     int slot_bytes = kEngineSlotBytes;  // engine ring slot size (S2D_SLOT_KB)
     int l2_lead = 0;                    // engine L2 prefetch lead in slots (S2D_L2_LEAD)
+    int engine_att_splits = 0;          // cap on the Slow-AR attention splits (S2D_ATT_SPLITS; 0: none)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
+    // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
+    // Slow-AR layer (heads of wqkv / wo / the KV cache, an FFN slice of
+    // w1 / w3 / w2) and the communicator of the two per-layer allreduces
+    int tp = 1, tp_rank = 0;
+    ncclComm_t comm = nullptr;
+    uint8_t *shard_arena = nullptr;
+    S2dTpShard shard{};
     // batched generation (s2d_generate_codes_batch): kv_slow holds max_batch
     // sequences of kv_slow_seq elements each (sequence 0 is the one of the
     // single-sequence calls)
@@ -449,6 +459,126 @@ int32_t bind_weights(S2dHandle *h) {
     return S2D_OK;
 }
 
+// Bytes of `cols` consecutive values of a row in ggml type `gtype`
+// (F16, Q8_0 blocks of 32, Q4_K superblocks of 256).
+size_t ggml_row_bytes(int gtype, int64_t cols) {
+    if (gtype == 8) return (size_t)cols / 32 * 34;
+    if (gtype == 12) return (size_t)cols / 256 * 144;
+    return (size_t)cols * 2;
+}
+
+// This rank's shard of the Slow-AR (tp_plan): rank r of n takes query heads
+// [r*H/n, (r+1)*H/n) with their KV heads and the FFN columns of units
+// [r*U/n, (r+1)*U/n), a unit being the block width of the weight type (8
+// for F16, 32 for Q8_0, 256 for Q4_K) so that w2's column slices are whole
+// blocks; a Q4_K FFN may split unevenly.
+int32_t tp_plan(const S2dGraphSpec &s, int n, int r, S2dTpShard *out) {
+    if (n < 1 || r < 0 || r >= n) return S2D_EINVAL;
+    if (s.heads % n || s.kv_heads % n) return S2D_EINVAL;
+    const int unit = s.linear_type == 8 ? 32 : s.linear_type == 12 ? 256 : 8;
+    if (s.ffn % unit || (s.heads / n * s.head_dim) % unit) return S2D_EINVAL;
+    const int units = s.ffn / unit;
+    if (units < n) return S2D_EINVAL;
+    S2dTpShard t{};
+    t.heads = s.heads / n, t.kv_heads = s.kv_heads / n;
+    t.head0 = r * t.heads, t.kv_head0 = r * t.kv_heads;
+    t.ffn0 = (int32_t)((int64_t)r * units / n) * unit;
+    t.ffn = (int32_t)((int64_t)(r + 1) * units / n) * unit - t.ffn0;
+    *out = t;
+    return S2D_OK;
+}
+
+// Copy this rank's shard of every Slow-AR linear out of the file-layout
+// arena (rows of wqkv / w1 / w3, column slices of wo / w2) and narrow the
+// Slow-AR shape to it.
+int32_t shard_slow_weights(S2dHandle *h) {
+    const S2dGraphSpec &s = h->spec;
+    int32_t rc;
+    if ((rc = tp_plan(s, h->tp, h->tp_rank, &h->shard)))
+        return set_err(h, rc, "no tensor-parallel split of this model over " + std::to_string(h->tp) +
+                                  " ranks (heads, kv heads and the FFN must divide into whole blocks)");
+    const S2dTpShard &t = h->shard;
+    const int gt = s.linear_type, hd = s.head_dim;
+    const int64_t d = s.hidden, qs = (int64_t)s.heads * hd, kvs = (int64_t)s.kv_heads * hd;
+    const int64_t qs_r = (int64_t)t.heads * hd, kvs_r = (int64_t)t.kv_heads * hd, F_r = t.ffn;
+    const size_t rd = ggml_row_bytes(gt, d);
+    const size_t b_qkv = (size_t)(qs_r + 2 * kvs_r) * rd, b_wo = (size_t)d * ggml_row_bytes(gt, qs_r);
+    const size_t b_w13 = (size_t)F_r * rd, b_w2 = (size_t)d * ggml_row_bytes(gt, F_r);
+    auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t per_layer = al(b_qkv) + al(b_wo) + 2 * al(b_w13) + al(b_w2);
+    CK(cudaMalloc(&h->shard_arena, per_layer * (size_t)s.slow_layers));
+    for (int l = 0; l < s.slow_layers; ++l) {
+        LayerDev &L = h->slow_layers[(size_t)l];
+        uint8_t *p = h->shard_arena + per_layer * (size_t)l;
+        uint8_t *qkv = p, *wo = qkv + al(b_qkv), *w1 = wo + al(b_wo), *w3 = w1 + al(b_w13), *w2 = w3 + al(b_w13);
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(L.wqkv);
+        // [Q heads | K heads | V heads] of this rank, rows of d values
+        CK(cudaMemcpyAsync(qkv, src + (size_t)t.head0 * hd * rd, (size_t)qs_r * rd, cudaMemcpyDeviceToDevice, h->stream));
+        CK(cudaMemcpyAsync(qkv + (size_t)qs_r * rd, src + (size_t)(qs + (int64_t)t.kv_head0 * hd) * rd,
+                           (size_t)kvs_r * rd, cudaMemcpyDeviceToDevice, h->stream));
+        CK(cudaMemcpyAsync(qkv + (size_t)(qs_r + kvs_r) * rd, src + (size_t)(qs + kvs + (int64_t)t.kv_head0 * hd) * rd,
+                           (size_t)kvs_r * rd, cudaMemcpyDeviceToDevice, h->stream));
+        // wo and w2: d rows, this rank's input columns
+        CK(cudaMemcpy2DAsync(wo, ggml_row_bytes(gt, qs_r),
+                             reinterpret_cast<const uint8_t *>(L.wo) + ggml_row_bytes(gt, (int64_t)t.head0 * hd),
+                             ggml_row_bytes(gt, qs), ggml_row_bytes(gt, qs_r), (size_t)d, cudaMemcpyDeviceToDevice,
+                             h->stream));
+        CK(cudaMemcpy2DAsync(w2, ggml_row_bytes(gt, F_r), reinterpret_cast<const uint8_t *>(L.w2) + ggml_row_bytes(gt, t.ffn0),
+                             ggml_row_bytes(gt, s.ffn), ggml_row_bytes(gt, F_r), (size_t)d, cudaMemcpyDeviceToDevice,
+                             h->stream));
+        // w1 and w3: this rank's FFN rows
+        CK(cudaMemcpyAsync(w1, reinterpret_cast<const uint8_t *>(L.w1) + (size_t)t.ffn0 * rd, b_w13,
+                           cudaMemcpyDeviceToDevice, h->stream));
+        CK(cudaMemcpyAsync(w3, reinterpret_cast<const uint8_t *>(L.w3) + (size_t)t.ffn0 * rd, b_w13,
+                           cudaMemcpyDeviceToDevice, h->stream));
+        L.wqkv = reinterpret_cast<const uint16_t *>(qkv), L.wo = reinterpret_cast<const uint16_t *>(wo);
+        L.w1 = reinterpret_cast<const uint16_t *>(w1), L.w3 = reinterpret_cast<const uint16_t *>(w3);
+        L.w2 = reinterpret_cast<const uint16_t *>(w2);
+    }
+    h->slow.H = t.heads, h->slow.Hkv = t.kv_heads, h->slow.F = t.ffn;
+    return S2D_OK;
+}
+
+// NCCL, loaded on first use (tensor parallelism only): dlopen of
+// S2D_NCCL_LIB, else libnccl.so.2, which is the copy already in the process
+// when one is (a framework's), so that loading this library never puts a
+// second NCCL beside it.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+const NcclApi &nccl() {
+    static NcclApi api = [] {
+        NcclApi a;
+        const char *env = getenv("S2D_NCCL_LIB");
+        void *lib = dlopen(env && env[0] ? env : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!lib) return a;
+        a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(lib, "ncclGetUniqueId"));
+        a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(lib, "ncclCommInitRank"));
+        a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(lib, "ncclAllReduce"));
+        a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(lib, "ncclCommDestroy"));
+        a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(lib, "ncclGetErrorString"));
+        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+        return a;
+    }();
+    return api;
+}
+
+// The Slow-AR residual exchange of tensor parallelism: every rank's
+// wo / w2 output over its input columns, summed in place (rank 0's carries
+// the residual, the others' only their partial sums).
+cudaError_t tp_allreduce(S2dHandle *h, float *x, size_t n) {
+    if (h->tp <= 1) return cudaSuccess;
+    const ncclResult_t r = nccl().all_reduce(x, x, n, ncclFloat32, ncclSum, h->comm, h->stream);
+    return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
 int32_t alloc_buffers(S2dHandle *h) {
     const S2dGraphSpec &s = h->spec;
     const ArShape &a = h->slow, &f = h->fast;
@@ -590,7 +720,12 @@ cudaError_t enqueue_layer(S2dHandle *h, bool is_fast, int l, float *x, int M,
     g.done = done, g.n_contig = -1;
     g.W = L.wo, g.x = h->att, g.ldx = a.qs(), g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
     g.K = a.qs(), g.N = d, g.wq = L.wq;
-    if ((e = launch_gemv(g, M, EPI_RESID, h->stream, h->pdl))) return e;
+    // tensor parallel: rank 0 adds the residual, every rank's partial sums
+    // are then summed in place
+    const bool part = !is_fast && h->tp > 1;
+    const int resid_epi = part && h->tp_rank != 0 ? EPI_STORE : EPI_RESID;
+    if ((e = launch_gemv(g, M, resid_epi, h->stream, h->pdl))) return e;
+    if (part && (e = tp_allreduce(h, x, (size_t)M * d))) return e;
     // ffn_norm + w1/w3 + SwiGLU
     g = GemvArgs{};
     g.done = done, g.n_contig = -1;
@@ -603,7 +738,8 @@ cudaError_t enqueue_layer(S2dHandle *h, bool is_fast, int l, float *x, int M,
     g.W = L.w2, g.x = h->act, g.ldx = a.F, g.y = x, g.ldy = d, g.resid = x, g.ldr = d;
     g.K = a.F, g.N = d, g.wq = L.wq;
     h->launches += 6;
-    return launch_gemv(g, M, EPI_RESID, h->stream, h->pdl);
+    if ((e = launch_gemv(g, M, resid_epi, h->stream, h->pdl))) return e;
+    return part ? tp_allreduce(h, x, (size_t)M * d) : cudaSuccess;
 }
 
 // Final norm + tied LM head (SlowArOutputHeadF16Weights::forward_logits,
@@ -771,7 +907,8 @@ void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, cons
         __half *base = h->kv_slow + (size_t)l * 2 * a.Hkv * h->cfg.max_seq * a.hd;
         t.kcache = base, t.vcache = base + (size_t)a.Hkv * h->cfg.max_seq * a.hd;
         t.max_seq = h->cfg.max_seq, t.kv_half = 1;
-        t.q_norm = L.q_norm, t.k_norm = L.k_norm, t.rope_cs = h->rope_cs_slow, t.S = h->S_slow;
+        t.q_norm = L.q_norm, t.k_norm = L.k_norm, t.rope_cs = h->rope_cs_slow;
+        t.S = h->engine_att_splits > 0 ? std::min(h->engine_att_splits, h->S_slow) : h->S_slow;
     }
     t.eps = a.eps, t.pos_dev = pos_dev, t.pos_const = pos_const;
     t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd, t.scale = 1.0f / sqrtf((float)a.hd);
@@ -1084,6 +1221,11 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
     const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F, T = rp.T;
     const size_t kvb = is_fast ? sizeof(float) : sizeof(__half);
     const size_t layer_bytes = (size_t)2 * a.Hkv * rp.max_seq * a.hd * kvb;
+    // tensor parallel (Slow-AR rows in one block of d floats each): rank 0
+    // adds the residual, the others store their partial sums; summed in place
+    const bool part = !is_fast && h->tp > 1;
+    const int resid_epi = part && h->tp_rank != 0 ? PF_STORE : PF_RESID;
+    if (part && ldx != d) return set_err(h, S2D_EINVAL, "tensor-parallel rows must be contiguous");
     int32_t rc;
     for (int l = 0; l < a.L; ++l) {
         LayerDev L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
@@ -1121,8 +1263,9 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.wo, d, qs, T, h->pf_y2))) return rc;
         mark(h, PC_GEMM);
-        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
+        CK(launch_combine(resid_epi, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
         mark(h, PC_COMBINE);
+        if (part) CK(tp_allreduce(h, x, (size_t)T * d));
         // ffn_norm + w1 / w3 + SwiGLU
         CK(launch_split_rows(x, ldx, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
         mark(h, PC_SPLIT);
@@ -1138,8 +1281,9 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         mark(h, PC_SPLIT);
         if ((rc = prefill_gemm(h, L.w2, d, F, T, h->pf_y2))) return rc;
         mark(h, PC_GEMM);
-        CK(launch_combine(PF_RESID, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
+        CK(launch_combine(resid_epi, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
         mark(h, PC_COMBINE);
+        if (part) CK(tp_allreduce(h, x, (size_t)T * d));
         h->launches += 10;  // own kernels; the GEMMs are cuBLAS's
     }
     return S2D_OK;
@@ -1409,8 +1553,13 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
 void free_handle(S2dHandle *h) {
     if (!h) return;
     if (h->device >= 0) cudaSetDevice(h->device);
+    // graphs that hold NCCL calls go before the communicator
     if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
     if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
+    h->frame_exec = nullptr, h->batch_exec = nullptr;
+    if (h->stream) cudaStreamSynchronize(h->stream);
+    if (h->comm) nccl().comm_destroy(h->comm);
+    if (h->shard_arena) cudaFree(h->shard_arena);
     for (void *p : {(void *)h->st_b, (void *)h->bx, (void *)h->fx, (void *)h->hidden_b, (void *)h->logits_b,
                     (void *)h->logits_fast_b, (void *)h->kv_fast_b, (void *)h->frame_codes_b, (void *)h->codes_b,
                     (void *)h->ra_part, (void *)h->ra_counters})
@@ -1447,7 +1596,9 @@ void free_handle(S2dHandle *h) {
 
 extern "C" {
 
-int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *err, size_t err_cap) {
+namespace {
+int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int32_t tp_rank, const uint8_t *nccl_id,
+                    S2dHandle **out, char *err, size_t err_cap) {
     auto report = [&](S2dHandle *h, int32_t rc) {
         if (err && err_cap) {
             snprintf(err, err_cap, "%s", h ? h->err.c_str() : "out of memory");
@@ -1472,6 +1623,11 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
         return report(h, S2D_EINVAL);
     }
     h->max_batch = std::max(1, h->cfg.max_batch);
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || (tp_size > 1 && !nccl_id)) {
+        h->err = "invalid tensor-parallel rank, size or NCCL id";
+        return report(h, S2D_EINVAL);
+    }
+    h->tp = tp_size, h->tp_rank = tp_rank;
     h->device = h->cfg.device;
     cudaError_t ce = cudaSetDevice(h->device);
     if (ce) {
@@ -1494,14 +1650,30 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
     if ((rc = read_spec(h))) return report(h, rc);
     if ((rc = upload_all(h))) return report(h, rc);
     if ((rc = bind_weights(h))) return report(h, rc);
+    if (h->tp > 1) {
+        if ((rc = shard_slow_weights(h))) return report(h, rc);
+        if (!nccl().ok) {
+            h->err = "NCCL (libnccl.so.2, or S2D_NCCL_LIB) could not be loaded";
+            return report(h, S2D_ECUDA);
+        }
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof(id));
+        const ncclResult_t nr = nccl().comm_init_rank(&h->comm, h->tp, id, h->tp_rank);
+        if (nr != ncclSuccess) {
+            h->comm = nullptr;
+            h->err = std::string("ncclCommInitRank: ") + nccl().error_string(nr);
+            return report(h, S2D_ECUDA);
+        }
+    }
     if ((rc = alloc_buffers(h))) return report(h, rc);
     {
         int coop = 0;
         cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->device);
         const char *env = getenv("S2D_ENGINE");
-        h->use_engine = coop && engine_supported(h) && !(env && env[0] == '0');
+        h->use_engine = coop && h->tp == 1 && engine_supported(h) && !(env && env[0] == '0');
         if (const char *lead = getenv("S2D_L2_LEAD")) h->l2_lead = std::max(0, std::min(64, atoi(lead)));
+        if (const char *sp = getenv("S2D_ATT_SPLITS")) h->engine_att_splits = std::max(0, atoi(sp));
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -1512,6 +1684,29 @@ int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *
         return report(h, S2D_ECUDA);
     }
     *out = h;
+    return S2D_OK;
+}
+}  // namespace
+
+int32_t s2d_open(const char *path, const S2dConfig *cfg, S2dHandle **out, char *err, size_t err_cap) {
+    return open_handle(path, cfg, 1, 0, nullptr, out, err, err_cap);
+}
+
+int32_t s2d_open_tp(const char *path, const S2dConfig *cfg, int32_t tp_size, int32_t tp_rank, const uint8_t *nccl_id,
+                    S2dHandle **out, char *err, size_t err_cap) {
+    return open_handle(path, cfg, tp_size, tp_rank, nccl_id, out, err, err_cap);
+}
+
+int32_t s2d_tp_plan(const S2dGraphSpec *spec, int32_t tp_size, int32_t tp_rank, S2dTpShard *out) {
+    if (!spec || !out) return S2D_EINVAL;
+    return tp_plan(*spec, tp_size, tp_rank, out);
+}
+
+int32_t s2d_nccl_unique_id(uint8_t *out, size_t cap) {
+    if (!out || cap < sizeof(ncclUniqueId)) return S2D_EINVAL;
+    ncclUniqueId id;
+    if (!nccl().ok || nccl().get_unique_id(&id) != ncclSuccess) return S2D_ECUDA;
+    memcpy(out, &id, sizeof(id));
     return S2D_OK;
 }
 

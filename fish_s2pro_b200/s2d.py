@@ -68,6 +68,10 @@ class _GenParams(ctypes.Structure):
                 ("min_tokens_before_end", ctypes.c_uint32), ("im_end_id", ctypes.c_uint32)]
 
 
+class _TpShard(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_int32) for f in ("heads", "kv_heads", "head0", "kv_head0", "ffn", "ffn0")]
+
+
 class _Profile(ctypes.Structure):
     _fields_ = [("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double),
                 ("frames", ctypes.c_uint32), ("kernels_per_frame", ctypes.c_uint32),
@@ -85,6 +89,11 @@ _u64p = _P(ctypes.c_uint64)
 SIGNATURES = {
     "s2d_open": (ctypes.c_int32, [ctypes.c_char_p, _P(_Config), _P(ctypes.c_void_p),
                                   ctypes.c_char_p, ctypes.c_size_t]),
+    "s2d_open_tp": (ctypes.c_int32, [ctypes.c_char_p, _P(_Config), ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_char_p, _P(ctypes.c_void_p), ctypes.c_char_p,
+                                     ctypes.c_size_t]),
+    "s2d_tp_plan": (ctypes.c_int32, [_P(_Spec), ctypes.c_int32, ctypes.c_int32, _P(_TpShard)]),
+    "s2d_nccl_unique_id": (ctypes.c_int32, [ctypes.c_char_p, ctypes.c_size_t]),
     "s2d_close": (None, [ctypes.c_void_p]),
     "s2d_last_error": (ctypes.c_char_p, [ctypes.c_void_p]),
     "s2d_graph_spec": (ctypes.c_int32, [ctypes.c_void_p, _P(_Spec)]),
@@ -271,16 +280,23 @@ class SlowArState:
 
     @classmethod
     def open(cls, transformer_path, max_seq_len: int = 32768, device: int = 0,
-             max_batch: int = 1) -> "SlowArState":
+             max_batch: int = 1, tp: Optional[tuple] = None) -> "SlowArState":
         """max_batch: sequences of generate_codes_batch (each with its own KV
-        cache of max_seq_len positions)."""
+        cache of max_seq_len positions).  tp: (tp_size, tp_rank, nccl_id) to
+        open one rank of a tensor-parallel Slow-AR (collective over the
+        ranks; nccl_id from nccl_unique_id() on one rank)."""
         if max_seq_len <= 0:
             raise S2dError(-1, "max_seq_len must be non-zero")
         h = ctypes.c_void_p()
         err = ctypes.create_string_buffer(1024)
         cfg = _Config(device=device, max_seq=max_seq_len, max_batch=max_batch, flags=0)
-        rc = lib().s2d_open(str(transformer_path).encode(), ctypes.byref(cfg), ctypes.byref(h),
-                            err, len(err))
+        if tp is not None and tp[0] > 1:
+            size, rank, nid = tp
+            rc = lib().s2d_open_tp(str(transformer_path).encode(), ctypes.byref(cfg), size, rank,
+                                   bytes(nid), ctypes.byref(h), err, len(err))
+        else:
+            rc = lib().s2d_open(str(transformer_path).encode(), ctypes.byref(cfg), ctypes.byref(h),
+                                err, len(err))
         if rc != 0:
             raise S2dError(rc, err.value.decode(errors="replace"))
         return cls(h, str(transformer_path))
@@ -474,6 +490,26 @@ def generate_codes(state: SlowArState, tokenizer, graph: GraphSpec, prompt: Prom
         profile=DecodeProfile(prof.prefill_ms, prof.decode_ms, prof.frames,
                               prof.kernels_per_frame, prof.prefill_kernels,
                               prof.frame_launches))
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id for SlowArState.open(tp=...)."""
+    buf = ctypes.create_string_buffer(128)
+    rc = lib().s2d_nccl_unique_id(buf, len(buf))
+    if rc != 0:
+        raise S2dError(rc, "ncclGetUniqueId failed")
+    return buf.raw
+
+
+def tp_plan(spec: GraphSpec, tp_size: int, tp_rank: int) -> dict:
+    """Rank tp_rank's shard of the Slow-AR under tp_size-way tensor
+    parallelism (s2d_tp_plan): its query / KV heads and FFN columns."""
+    c = _Spec(**{f: getattr(spec, f) for f, _ in _Spec._fields_})
+    out = _TpShard()
+    rc = lib().s2d_tp_plan(ctypes.byref(c), tp_size, tp_rank, ctypes.byref(out))
+    if rc != 0:
+        raise S2dError(rc, f"no {tp_size}-way split of this model")
+    return {f: getattr(out, f) for f, _ in _TpShard._fields_}
 
 
 RNG_SEEDED = 0  # the reference's SeededRng per sequence

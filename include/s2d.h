@@ -96,6 +96,13 @@ typedef struct S2dProfile {
 #define S2D_LOGITS_ALLOWED 1 /* semantic rows + im_end only; other entries -inf */
 #define S2D_LOGITS_FULL 2    /* all vocab_size rows (debug parity)            */
 
+/* One rank's shard of the Slow-AR under tensor parallelism (s2d_tp_plan). */
+typedef struct S2dTpShard {
+    int32_t heads, kv_heads;  /* query / KV heads of this rank                     */
+    int32_t head0, kv_head0;  /* its first query / KV head                          */
+    int32_t ffn, ffn0;        /* its FFN columns [ffn0, ffn0 + ffn)                 */
+} S2dTpShard;
+
 /* ---- lifecycle ---------------------------------------------------------- */
 
 /* Replaces SlowArState::open + FastArWeights::from_gguf (slow_ar.rs:387-412,
@@ -104,6 +111,29 @@ typedef struct S2dProfile {
  * shapes, uploads every tensor to HBM once. */
 int32_t s2d_open(const char *transformer_gguf, const S2dConfig *cfg, S2dHandle **out,
                  char *err, size_t err_cap);
+/* ---- Slow-AR tensor parallelism ------------------------------------------
+ * tp_size ranks (one process or thread per GPU) open the same GGUF with
+ * s2d_open_tp; rank r keeps query heads [r*H/n, (r+1)*H/n) of wqkv / wo and
+ * the KV cache with their KV heads, and an FFN slice of w1 / w3 / w2 (whole
+ * weight blocks; a Q4_K FFN may split unevenly).  The two Slow-AR residual
+ * additions of each layer become an NCCL allreduce over the ranks; the LM
+ * head, the samplers and the Fast-AR run replicated, so every rank returns
+ * the same results.  Every rank must make the same calls in the same order
+ * (prefill, step, generate_codes, the batched variant).  The persistent
+ * decode engine is single-GPU: a tensor-parallel handle decodes with the
+ * per-op kernels captured into the frame graph together with the NCCL calls. */
+
+/* The shard of rank tp_rank of tp_size for this graph (spec.linear_type sets
+ * the block width).  S2D_EINVAL if the model does not split that way. */
+int32_t s2d_tp_plan(const S2dGraphSpec *spec, int32_t tp_size, int32_t tp_rank, S2dTpShard *out);
+/* A fresh NCCL unique id (cap >= 128 bytes) for s2d_open_tp; one rank makes
+ * it and hands it to the others by any host channel. */
+int32_t s2d_nccl_unique_id(uint8_t *out, size_t cap);
+/* s2d_open for rank tp_rank of tp_size (collective: blocks until every rank
+ * has joined the communicator).  tp_size 1 is s2d_open. */
+int32_t s2d_open_tp(const char *transformer_gguf, const S2dConfig *cfg, int32_t tp_size, int32_t tp_rank,
+                    const uint8_t *nccl_id, S2dHandle **out, char *err, size_t err_cap);
+
 /* Replaces s2_engine_destroy (s2_engine_ffi.h:26). NULL is ignored. */
 void s2d_close(S2dHandle *h);
 /* Message of the last failed call on this handle ("" if none). */
