@@ -23,7 +23,7 @@ namespace s2d {
 
 namespace {
 
-constexpr int kSplitThreads = 256;
+constexpr int kSplitThreads = 1024;  // one block per row: short passes over the row
 
 __device__ __forceinline__ float block_sum(float v, float *red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -46,22 +46,12 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return t;
 }
 
-// One block per row t of x [T][ldx]: optional RMSNorm (gain w), then the
-// scaled hi/lo split into xs rows t and T + t ([2T][K] f16); inv[t] undoes
-// the scaling.  With w, the normalised row is also written to xn (if set).
-__global__ void __launch_bounds__(kSplitThreads) split_rows_kernel(const float *x, int ldx, int T, int K,
-                                                                   const float *w, float eps, __half *xs,
-                                                                   float *inv, float *xn) {
-    extern __shared__ float row[];  // [K]
-    __shared__ float red[kSplitThreads / 32];
-    const int t = blockIdx.x;
-    const float *src = x + (size_t)t * ldx;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = src[i];
-        row[i] = v;
-        ss = fmaf(v, v, ss);
-    }
+// The second half of a row split, on row t held in shared memory (`row`,
+// K values, with the sum of their squares in ss): optional RMSNorm with gain
+// w (the normalised row also to xn when set), then the power-of-two scaled
+// f16 hi / lo halves into xs rows t and T + t, and inv[t] = 1 / scale.
+__device__ void split_row_tail(float *row, float ss, int t, int T, int K, const float *w, float eps, __half *xs,
+                               float *inv, float *xn, float *red) {
     float scale = 1.0f;
     if (w) scale = 1.0f / sqrtf(block_sum(ss, red) / (float)K + eps);
     else __syncthreads();
@@ -91,6 +81,62 @@ __global__ void __launch_bounds__(kSplitThreads) split_rows_kernel(const float *
         hi[i] = h;
         lo[i] = __float2half_rn(v - __half2float(h));
     }
+}
+
+// One block per row t of x [T][ldx]: optional RMSNorm (gain w), then the
+// scaled hi/lo split into xs rows t and T + t ([2T][K] f16); inv[t] undoes
+// the scaling.  With w, the normalised row is also written to xn (if set).
+__global__ void __launch_bounds__(kSplitThreads) split_rows_kernel(const float *x, int ldx, int T, int K,
+                                                                   const float *w, float eps, __half *xs,
+                                                                   float *inv, float *xn) {
+    extern __shared__ float row[];  // [K]
+    __shared__ float red[kSplitThreads / 32];
+    const int t = blockIdx.x;
+    const float *src = x + (size_t)t * ldx;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = src[i];
+        row[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    split_row_tail(row, ss, t, T, K, w, eps, xs, inv, xn, red);
+}
+
+template <int EPI>
+__device__ __forceinline__ float combine_one(const float *Y2, const float *Y2b, float s, size_t top, size_t bot,
+                                             const float *resid) {
+    const float v = __fadd_rn(Y2[top], Y2[bot]) * s;
+    if (EPI == PF_STORE) return v;
+    if (EPI == PF_RESID) return __fadd_rn(*resid, v);
+    const float u = __fadd_rn(Y2b[top], Y2b[bot]) * s;
+    if (EPI == PF_SWIGLU_SLOW) {
+        const float sig = 1.0f / (1.0f + expf(-v));
+        return __fmul_rn(__fmul_rn(v, sig), u);
+    }
+    return __fmul_rn(v / (1.0f + expf(-v)), u);
+}
+
+// combine_kernel then split_rows_kernel on the same row, in one pass: one
+// block per row t; y (optional) receives the combined row, the split goes to
+// xs / inv (inv[t] is read before it is replaced).
+template <int EPI>
+__global__ void __launch_bounds__(kSplitThreads) combine_split_kernel(const float *Y2, const float *Y2b, float *inv,
+                                                                      int T, int N, float *y, int ldy,
+                                                                      const float *resid, int ldr, const float *w,
+                                                                      float eps, __half *xs) {
+    extern __shared__ float row[];  // [N]
+    __shared__ float red[kSplitThreads / 32];
+    const int t = blockIdx.x;
+    const float s = inv[t];
+    float ss = 0.f;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+        const float v = combine_one<EPI>(Y2, Y2b, s, (size_t)t * N + n, ((size_t)T + t) * N + n,
+                                         resid + (size_t)t * ldr + n);
+        row[n] = v;
+        if (y) y[(size_t)t * ldy + n] = v;
+        ss = fmaf(v, v, ss);
+    }
+    split_row_tail(row, ss, t, T, N, w, eps, xs, inv, nullptr, red);
 }
 
 // y[t][n] (ldy) from the GEMM of the stacked rows: (Y2[t][n] + Y2[T+t][n]) *
@@ -298,6 +344,44 @@ cudaError_t launch_split_rows(const float *x, int ldx, int T, int K, const float
     }
     if (smem > 64 * 1024) return cudaErrorInvalidValue;
     split_rows_kernel<<<T, kSplitThreads, smem, s>>>(x, ldx, T, K, norm_w, eps, xs, inv, xn);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine_split(int epi, const float *Y2, const float *Y2b, float *inv, int T, int N, float *y,
+                                 int ldy, const float *resid, int ldr, const float *norm_w, float eps, __half *xs,
+                                 cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    const size_t smem = (size_t)N * sizeof(float);
+    if (smem > 64 * 1024 || (epi == PF_RESID && !resid)) return cudaErrorInvalidValue;
+    static bool configured = false;
+    if (!configured) {
+        const void *ks[] = {(const void *)combine_split_kernel<PF_STORE>, (const void *)combine_split_kernel<PF_RESID>,
+                            (const void *)combine_split_kernel<PF_SWIGLU_SLOW>,
+                            (const void *)combine_split_kernel<PF_SWIGLU_FAST>};
+        for (const void *k : ks) {
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+            if (e) return e;
+        }
+        configured = true;
+    }
+    const float *r = resid ? resid : Y2;
+    switch (epi) {
+    case PF_STORE:
+        combine_split_kernel<PF_STORE><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs);
+        break;
+    case PF_RESID:
+        combine_split_kernel<PF_RESID><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs);
+        break;
+    case PF_SWIGLU_SLOW:
+        combine_split_kernel<PF_SWIGLU_SLOW><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w,
+                                                                            eps, xs);
+        break;
+    case PF_SWIGLU_FAST:
+        combine_split_kernel<PF_SWIGLU_FAST><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w,
+                                                                            eps, xs);
+        break;
+    default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
 

@@ -24,6 +24,14 @@ cudaError_t launch_split_rows(const float *x, int ldx, int T, int K, const float
 cudaError_t launch_combine(int epi, const float *Y2, const float *Y2b, const float *inv, int T, int N, float *y,
                            int ldy, const float *resid, int ldr, cudaStream_t s);
 
+// launch_combine then launch_split_rows on its output, in one pass per row:
+// y[t] (optional, ldy) = epilogue of the stacked GEMM rows; then RMSNorm
+// (norm_w optional) and the hi/lo split of that row into xs, inv[t] replaced
+// by the new row scale.  N <= 16384.
+cudaError_t launch_combine_split(int epi, const float *Y2, const float *Y2b, float *inv, int T, int N, float *y,
+                                 int ldy, const float *resid, int ldr, const float *norm_w, float eps, __half *xs,
+                                 cudaStream_t s);
+
 // GQA attention of T query rows over their sequences' caches.  Row m is
 // sequence m / rows_per_seq at position pos_const + (m % rows_per_seq), plus
 // st[seq].n_past when st_pos is set (rows of a finished sequence,

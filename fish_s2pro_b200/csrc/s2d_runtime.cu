@@ -26,6 +26,7 @@
 #include "s2d_gguf.h"
 #include "s2d_kernels.cuh"
 #include "s2d_prefill.cuh"
+#include "s2d_tcgemm.cuh"
 
 using namespace s2d;
 
@@ -139,12 +140,16 @@ struct S2dHandle {
     int slot_bytes = kEngineSlotBytes;  // engine ring slot size (S2D_SLOT_KB)
     int l2_lead = 0;                    // engine L2 prefetch lead in slots (S2D_L2_LEAD)
     int engine_att_splits = 0;          // cap on the Slow-AR attention splits (S2D_ATT_SPLITS; 0: none)
+    int attn_blocks_per_sm = 16;        // batched step: rows-attention blocks per SM (S2D_BATCH_ATT_BLOCKS)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
     // Slow-AR layer (heads of wqkv / wo / the KV cache, an FFN slice of
     // w1 / w3 / w2) and the communicator of the two per-layer allreduces
     int tp = 1, tp_rank = 0;
+    // rows-path linears on the tcgen05 GEMM (S2D_TCGEMM=1); by default on
+    // cuBLAS + the combine pass, which measures faster for now
+    bool use_tc = false;
     ncclComm_t comm = nullptr;
     uint8_t *shard_arena = nullptr;
     S2dTpShard shard{};
@@ -1173,6 +1178,32 @@ void mark(S2dHandle *h, int cat) {
     h->marks->emplace_back(cat, e);
 }
 
+// y = epilogue(W . x) over the T rows split into pf_xs / pf_inv: the tcgen05
+// GEMM with the epilogue fused when it takes the shape, else cuBLAS over the
+// stacked rows followed by the combine pass.  W2 is the up projection of the
+// SwiGLU forms.
+int32_t rows_linear(S2dHandle *h, const uint16_t *W, const uint16_t *W2, int N, int K, int T, int epi, float *y,
+                    int ldy, const float *resid, int ldr) {
+    TcGemm g;
+    g.W = W, g.W2 = W2, g.N = N, g.K = K, g.xs = h->pf_xs, g.T = T, g.inv = h->pf_inv, g.epi = epi;
+    g.y = y, g.ldy = ldy, g.resid = resid, g.ldr = ldr, g.num_sms = h->num_sms > 0 ? h->num_sms : 148;
+    g.error = &h->st->error;
+    if (h->use_tc && tc_gemm_supported(g)) {
+        CK(launch_tc_gemm(g, h->stream));
+        mark(h, PC_GEMM);
+        h->launches += 1;
+        return S2D_OK;
+    }
+    int32_t rc;
+    if ((rc = prefill_gemm(h, W, N, K, T, h->pf_y2))) return rc;
+    if (W2 && (rc = prefill_gemm(h, W2, N, K, T, h->pf_y2b))) return rc;
+    mark(h, PC_GEMM);
+    CK(launch_combine(epi, h->pf_y2, W2 ? h->pf_y2b : nullptr, h->pf_inv, T, N, y, ldy, resid, ldr, h->stream));
+    mark(h, PC_COMBINE);
+    h->launches += 1;
+    return S2D_OK;
+}
+
 // Rows of one layered pass (rows_layers): T rows of the residual x, row m
 // of sequence m / rps at position pos_const + m % rps (+ st[seq].n_past with
 // st_pos); sequence s's KV cache starts kv_seq_stride elements after
@@ -1226,17 +1257,44 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
     const bool part = !is_fast && h->tp > 1;
     const int resid_epi = part && h->tp_rank != 0 ? PF_STORE : PF_RESID;
     if (part && ldx != d) return set_err(h, S2D_EINVAL, "tensor-parallel rows must be contiguous");
+    // on the cuBLAS path without an exchange between them, each combine pass
+    // also makes the next GEMM's row split (one pass per row instead of two)
+    const bool fuse = !h->use_tc && !part;
+    // the rows' split for `lin` (N outputs, K inputs) followed by the next
+    // GEMM's split of the result (norm_w optional); y may be null when fused
+    auto linear_then_split = [&](const uint16_t *W, const uint16_t *W2, int N, int K, int epi, float *y, int ldy,
+                                 const float *resid, int ldr, const float *norm_w) -> int32_t {
+        int32_t r2;
+        if (fuse) {
+            if ((r2 = prefill_gemm(h, W, N, K, T, h->pf_y2))) return r2;
+            if (W2 && (r2 = prefill_gemm(h, W2, N, K, T, h->pf_y2b))) return r2;
+            mark(h, PC_GEMM);
+            CK(launch_combine_split(epi, h->pf_y2, W2 ? h->pf_y2b : nullptr, h->pf_inv, T, N, y, ldy, resid, ldr,
+                                    norm_w, a.eps, h->pf_xs, h->stream));
+            mark(h, PC_COMBINE);
+            h->launches += 1;
+            return S2D_OK;
+        }
+        if ((r2 = rows_linear(h, W, W2, N, K, T, epi, y, ldy, resid, ldr))) return r2;
+        if (part && epi == resid_epi) CK(tp_allreduce(h, y, (size_t)T * d));
+        CK(launch_split_rows(y, ldy, T, N, norm_w, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+        mark(h, PC_SPLIT);
+        h->launches += 1;
+        return S2D_OK;
+    };
     int32_t rc;
+    bool presplit = false;  // pf_xs / pf_inv already hold this layer's attention-norm split
     for (int l = 0; l < a.L; ++l) {
         LayerDev L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
         if (L.wq != EW_F16 && (rc = dequant_layer(h, a, &L))) return rc;
         // attention_norm + WQKV
-        CK(launch_split_rows(x, ldx, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
-        mark(h, PC_SPLIT);
-        if ((rc = prefill_gemm(h, L.wqkv, qo, d, T, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, T, qo, h->pf_qkv, qo, nullptr, 0, h->stream));
-        mark(h, PC_COMBINE);
+        if (!presplit) {
+            CK(launch_split_rows(x, ldx, T, d, L.attn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
+            mark(h, PC_SPLIT);
+            h->launches += 1;
+        }
+        presplit = false;
+        if ((rc = rows_linear(h, L.wqkv, nullptr, qo, d, T, PF_STORE, h->pf_qkv, qo, nullptr, 0))) return rc;
         // QK-norm (Slow-AR) + RoPE + KV write for every row
         uint8_t *base = reinterpret_cast<uint8_t *>(rp.kv) + (size_t)l * layer_bytes;
         RopeArgs r{};
@@ -1258,33 +1316,24 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters;
         CK(launch_rows_attention(t, !is_fast, h->stream));
         mark(h, PC_ATTN);
-        // wo + residual
+        // wo + residual, then the ffn_norm split
         CK(launch_split_rows(h->pf_att, qs, T, qs, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
         mark(h, PC_SPLIT);
-        if ((rc = prefill_gemm(h, L.wo, d, qs, T, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(resid_epi, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
-        mark(h, PC_COMBINE);
-        if (part) CK(tp_allreduce(h, x, (size_t)T * d));
-        // ffn_norm + w1 / w3 + SwiGLU
-        CK(launch_split_rows(x, ldx, T, d, L.ffn_norm, a.eps, h->pf_xs, h->pf_inv, nullptr, h->stream));
-        mark(h, PC_SPLIT);
-        if ((rc = prefill_gemm(h, L.w1, F, d, T, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        if ((rc = prefill_gemm(h, L.w3, F, d, T, h->pf_y2b))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(is_fast ? PF_SWIGLU_FAST : PF_SWIGLU_SLOW, h->pf_y2, h->pf_y2b, h->pf_inv, T, F,
-                          h->pf_act, F, nullptr, 0, h->stream));
-        mark(h, PC_COMBINE);
-        // w2 + residual
-        CK(launch_split_rows(h->pf_act, F, T, F, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr, h->stream));
-        mark(h, PC_SPLIT);
-        if ((rc = prefill_gemm(h, L.w2, d, F, T, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(resid_epi, h->pf_y2, nullptr, h->pf_inv, T, d, x, ldx, x, ldx, h->stream));
-        mark(h, PC_COMBINE);
-        if (part) CK(tp_allreduce(h, x, (size_t)T * d));
-        h->launches += 10;  // own kernels; the GEMMs are cuBLAS's
+        if ((rc = linear_then_split(L.wo, nullptr, d, qs, resid_epi, x, ldx, x, ldx, L.ffn_norm))) return rc;
+        // w1 / w3 + SwiGLU, then the split for w2 (the SwiGLU row is not kept when fused)
+        if ((rc = linear_then_split(L.w1, L.w3, F, d, is_fast ? PF_SWIGLU_FAST : PF_SWIGLU_SLOW,
+                                    fuse ? nullptr : h->pf_act, F, nullptr, 0, nullptr)))
+            return rc;
+        // w2 + residual (with the next layer's attention-norm split when fused)
+        if (fuse && l + 1 < a.L) {
+            const LayerDev &N2 = is_fast ? h->fast_layers[(size_t)l + 1] : h->slow_layers[(size_t)l + 1];
+            if ((rc = linear_then_split(L.w2, nullptr, d, F, resid_epi, x, ldx, x, ldx, N2.attn_norm))) return rc;
+            presplit = true;
+        } else {
+            if ((rc = rows_linear(h, L.w2, nullptr, d, F, T, resid_epi, x, ldx, x, ldx))) return rc;
+            if (part) CK(tp_allreduce(h, x, (size_t)T * d));
+        }
+        h->launches += 3;  // rope, attention, the attention split
     }
     return S2D_OK;
 }
@@ -1451,7 +1500,7 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
 // Attention splits of the batched Slow-AR step: enough blocks for ~8 per SM.
 int batch_splits(const S2dHandle *h, int B) {
     const int blocks = B * h->slow.Hkv;
-    return std::max(1, std::min(h->ra_smax, (8 * std::max(h->num_sms, 1) + blocks - 1) / blocks));
+    return std::max(1, std::min(h->ra_smax, (h->attn_blocks_per_sm * std::max(h->num_sms, 1) + blocks - 1) / blocks));
 }
 
 // One frame of B sequences (the loop body of generate_codes,
@@ -1491,11 +1540,8 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
         CK(launch_split_rows(h->fx + (size_t)(M - 1) * d, 2 * d, B, d, h->fast_norm, f.eps, h->pf_xs, h->pf_inv,
                              nullptr, h->stream));
         mark(h, PC_SPLIT);
-        if ((rc = prefill_gemm(h, h->fast_out, cb, d, B, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, cb, h->logits_fast_b, cb, nullptr, 0,
-                          h->stream));
-        mark(h, PC_COMBINE);
+        if ((rc = rows_linear(h, h->fast_out, nullptr, cb, d, B, PF_STORE, h->logits_fast_b, cb, nullptr, 0)))
+            return rc;
         SampleArgs a{};
         a.logits = h->logits_fast_b, a.n = cb, a.n_contig = -1, a.vocab_full = cb;
         a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
@@ -1528,18 +1574,13 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
     CK(launch_split_rows(h->bx, d, B, d, h->norm, h->slow.eps, h->pf_xs, h->pf_inv, h->hidden_b, h->stream));
     mark(h, PC_SPLIT);
-    if ((rc = prefill_gemm(h, h->emb + (size_t)s.semantic_begin_id * d, nsem, d, B, h->pf_y2))) return rc;
-    mark(h, PC_GEMM);
-    CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, nsem, h->logits_b, nsem + 1, nullptr, 0,
-                      h->stream));
-    mark(h, PC_COMBINE);
-    if (extra) {
-        if ((rc = prefill_gemm(h, h->emb + (size_t)k.im_end * d, 1, d, B, h->pf_y2))) return rc;
-        mark(h, PC_GEMM);
-        CK(launch_combine(PF_STORE, h->pf_y2, nullptr, h->pf_inv, B, 1, h->logits_b + nsem, nsem + 1, nullptr, 0,
-                          h->stream));
-        mark(h, PC_COMBINE);
-    }
+    if ((rc = rows_linear(h, h->emb + (size_t)s.semantic_begin_id * d, nullptr, nsem, d, B, PF_STORE, h->logits_b,
+                          nsem + 1, nullptr, 0)))
+        return rc;
+    if (extra &&
+        (rc = rows_linear(h, h->emb + (size_t)k.im_end * d, nullptr, 1, d, B, PF_STORE, h->logits_b + nsem, nsem + 1,
+                          nullptr, 0)))
+        return rc;
     SampleArgs a = slow_sample_args(h, SAMPLE_SLOW_STEP, k);
     a.logits = h->logits_b, a.st = h->st_b, a.rng = nullptr, a.out_token = nullptr;
     a.rng_kind = rng_kind, a.philox_key = philox_key;
@@ -1674,6 +1715,8 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         h->use_engine = coop && h->tp == 1 && engine_supported(h) && !(env && env[0] == '0');
         if (const char *lead = getenv("S2D_L2_LEAD")) h->l2_lead = std::max(0, std::min(64, atoi(lead)));
         if (const char *sp = getenv("S2D_ATT_SPLITS")) h->engine_att_splits = std::max(0, atoi(sp));
+        if (const char *tc = getenv("S2D_TCGEMM")) h->use_tc = tc[0] == '1';
+        if (const char *ab = getenv("S2D_BATCH_ATT_BLOCKS")) h->attn_blocks_per_sm = std::max(1, std::min(64, atoi(ab)));
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -2286,6 +2329,60 @@ int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *w, i
     CK(cudaMemcpyAsync(out, y.p, (size_t)out_dim * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return S2D_OK;
+}
+
+int32_t s2d_op_rows_linear_f16(S2dHandle *h, const float *x, int64_t T, int64_t K, const uint16_t *w,
+                               const uint16_t *w2, int64_t N, const float *resid, int32_t epi, int32_t impl, float *y) {
+    if (!h) return S2D_EINVAL;
+    if (!x || !w || !y || T <= 0 || K <= 0 || N <= 0 || epi < 0 || epi > 3 || (epi >= 2) != (w2 != nullptr) ||
+        (epi == 1 && !resid))
+        return set_err(h, S2D_EINVAL, "s2d_op_rows_linear_f16: bad arguments");
+    if (T > kPrefillChunk) return set_err(h, S2D_EINVAL, "at most 512 rows per call");
+    if (K % 8 || K * 4 > 64 * 1024) return set_err(h, S2D_EINVAL, "K must be a multiple of 8 and at most 16384");
+    CK(cudaSetDevice(h->device));
+    int32_t rc;
+    if ((rc = ensure_prefill(h))) return rc;  // the cuBLAS handle
+    // row buffers of this call's size, in place of the handle's for its duration
+    DevBuf dx, dw, dw2, dy, xs, inv, y2, y2b;
+    CK(cudaMalloc(&xs.p, (size_t)2 * T * K * sizeof(__half)));
+    CK(cudaMalloc(&inv.p, (size_t)T * sizeof(float)));
+    CK(cudaMalloc(&y2.p, (size_t)2 * T * N * sizeof(float)));
+    CK(cudaMalloc(&y2b.p, (size_t)2 * T * N * sizeof(float)));
+    struct Swap {
+        S2dHandle *h;
+        __half *xs;
+        float *inv, *y2, *y2b;
+        ~Swap() { h->pf_xs = xs, h->pf_inv = inv, h->pf_y2 = y2, h->pf_y2b = y2b; }
+    } keep{h, h->pf_xs, h->pf_inv, h->pf_y2, h->pf_y2b};
+    h->pf_xs = (__half *)xs.p, h->pf_inv = (float *)inv.p, h->pf_y2 = (float *)y2.p, h->pf_y2b = (float *)y2b.p;
+    CK(cudaMalloc(&dx.p, (size_t)T * K * 4));
+    CK(cudaMalloc(&dw.p, (size_t)N * K * 2));
+    if (w2) CK(cudaMalloc(&dw2.p, (size_t)N * K * 2));
+    CK(cudaMalloc(&dy.p, (size_t)T * N * 4));
+    CK(cudaMemcpyAsync(dx.p, x, (size_t)T * K * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dw.p, w, (size_t)N * K * 2, cudaMemcpyHostToDevice, h->stream));
+    if (w2) CK(cudaMemcpyAsync(dw2.p, w2, (size_t)N * K * 2, cudaMemcpyHostToDevice, h->stream));
+    if (resid) CK(cudaMemcpyAsync(dy.p, resid, (size_t)T * N * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(launch_split_rows((const float *)dx.p, (int)K, (int)T, (int)K, nullptr, 0.f, h->pf_xs, h->pf_inv, nullptr,
+                         h->stream));
+    const bool tc = h->use_tc;
+    h->use_tc = impl == 0;
+    if (impl == 0) {
+        TcGemm g;
+        g.W = (const uint16_t *)dw.p, g.W2 = (const uint16_t *)dw2.p, g.N = (int)N, g.K = (int)K, g.xs = h->pf_xs;
+        g.T = (int)T, g.inv = h->pf_inv, g.epi = epi, g.y = (float *)dy.p, g.ldy = (int)N;
+        if (!tc_gemm_supported(g)) {
+            h->use_tc = tc;
+            return set_err(h, S2D_EINVAL, "the tensor-core GEMM does not take this shape");
+        }
+    }
+    rc = rows_linear(h, (const uint16_t *)dw.p, (const uint16_t *)dw2.p, (int)N, (int)K, (int)T, epi, (float *)dy.p,
+                     (int)N, (const float *)dy.p, (int)N);
+    h->use_tc = tc;
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(y, dy.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return check_device_error(h);
 }
 
 int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n, int64_t head_dim,

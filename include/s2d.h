@@ -275,6 +275,15 @@ int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *weig
                           int64_t in_dim, int64_t out_dim, float *out);
 /* MatmulBackend::rms_norm / rms_norm_heads (backend.rs:84-121);
  * head_dim == n gives the plain rms_norm. */
+/* MatmulBackend::linear (backend.rs:55-73) over T rows at once, the rows
+ * path's GEMM: y[t][n] = epi(sum_k x[t][k] * w[n][k]) for x [T][K] f32, w
+ * [N][K] f16 bits.  epi 0 stores, 1 adds resid [T][N], 2 / 3 the slow / fast
+ * SwiGLU with the up projection w2 [N][K].  impl 0: the tcgen05 tensor-core
+ * GEMM (S2D_EINVAL if it does not take the shape: K a multiple of 64); 1: cuBLAS
+ * and the combine pass.  T <= 512, K <= 16384, host buffers. */
+int32_t s2d_op_rows_linear_f16(S2dHandle *h, const float *x, int64_t T, int64_t K, const uint16_t *w,
+                               const uint16_t *w2, int64_t N, const float *resid, int32_t epi, int32_t impl,
+                               float *y);
 int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n,
                         int64_t head_dim, float eps, float *out);
 /* MatmulBackend::gqa_decode_attention (attention.rs:208-247): keys/values

@@ -89,6 +89,21 @@ def test_philox_matches_published_vectors():
 
 
 def test_batch_greedy_matches_oracle(gpu, cpu):
+    check_batch_greedy(gpu, cpu)
+
+
+def test_batch_greedy_on_tcgen05_gemm_matches_oracle(tiny_gguf, cpu, monkeypatch):
+    """The same run with the rows path's linears on the tcgen05 GEMM."""
+    from fish_s2pro_b200 import SlowArState
+    monkeypatch.setenv("S2D_TCGEMM", "1")
+    st = SlowArState.open(tiny_gguf, max_seq_len=256, max_batch=len(LENS))
+    try:
+        check_batch_greedy(st, cpu)
+    finally:
+        st.close()
+
+
+def check_batch_greedy(gpu, cpu):
     from fish_s2pro_b200 import SeededRng
     m = configs.C1.model
     frames = 12
