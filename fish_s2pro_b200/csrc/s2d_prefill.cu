@@ -405,6 +405,132 @@ cudaError_t launch_combine(int epi, const float *Y2, const float *Y2b, const flo
     return cudaGetLastError();
 }
 
+// Causal attention of one sequence's consecutive rows (the prefill case of
+// rows_attn_kernel: rows_per_seq = T, no state, one split), QB query rows per
+// block so that every staged K/V chunk serves all of them.  Grid (row
+// tile, kv head); warp w is query head kvh*rep + w for all QB rows.  Row r
+// of the tile sees positions 0 .. pos_const + m0 + r; the chunks past a
+// row's end are skipped for that row (warp-uniformly), so no fully masked
+// update happens.
+template <typename KV, int EPL, int QB>
+__global__ void __launch_bounds__(256) prefill_tile_attn_kernel(const RowsAttnArgs a) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int rep = blockDim.x >> 5;
+    const int m0 = blockIdx.x * QB, kvh = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = kvh * rep + warp;
+    const int hd = a.hd, rowb = hd * (int)sizeof(KV), pitch = rowb + 16;
+    const int nrows = min(QB, a.T - m0);
+    const int last_pos = min(a.pos_const + m0 + nrows - 1, a.max_seq - 1);
+    const int t1 = last_pos + 1;
+    float *qs = reinterpret_cast<float *>(sm + (size_t)2 * 2 * 32 * pitch) + (size_t)warp * QB * hd;
+    for (int r = 0; r < QB; ++r)
+        for (int i = lane; i < hd; i += 32)
+            qs[r * hd + i] = r < nrows ? a.q[(size_t)(m0 + r) * a.H * hd + (size_t)h * hd + i] : 0.f;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + (size_t)kvh * a.max_seq * rowb;
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + (size_t)kvh * a.max_seq * rowb;
+    const int units = rowb / 16;
+    auto issue = [&](int c0, int stg) {
+        const int n = min(32, t1 - c0);
+        uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
+        for (int u = threadIdx.x; u < 2 * n * units; u += blockDim.x) {
+            const int which = u >= n * units, uu = which ? u - n * units : u;
+            const int r = uu / units, c = uu - r * units;
+            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + (size_t)(c0 + r) * rowb + c * 16);
+        }
+        cp_async_commit();
+    };
+    float mrun[QB], l[QB], acc[QB][EPL];
+#pragma unroll
+    for (int r = 0; r < QB; ++r) {
+        mrun[r] = -INFINITY, l[r] = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[r][e] = 0.f;
+    }
+    issue(0, 0);
+    for (int c0 = 0, it = 0; c0 < t1; c0 += 32, ++it) {
+        const int stg = it & 1;
+        if (c0 + 32 < t1) {
+            issue(c0 + 32, stg ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();  // this chunk (and, on the first pass, qs) visible to every warp
+        const int n = min(32, t1 - c0);
+        const uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
+        // scores of this lane's position against the QB queries
+        float sc[QB];
+#pragma unroll
+        for (int r = 0; r < QB; ++r) sc[r] = 0.f;
+        if (lane < n) {
+            const KV *krow = reinterpret_cast<const KV *>(kt + lane * pitch);
+            for (int i = 0; i < hd; i += 4) {
+                float k4[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) k4[e] = float(krow[i + e]);
+#pragma unroll
+                for (int r = 0; r < QB; ++r) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qs + r * hd + i);
+                    sc[r] = fmaf(q4.x, k4[0], fmaf(q4.y, k4[1], fmaf(q4.z, k4[2], fmaf(q4.w, k4[3], sc[r]))));
+                }
+            }
+        }
+        float p[QB];
+#pragma unroll
+        for (int r = 0; r < QB; ++r) {
+            const int pos = a.pos_const + m0 + r;  // row r sees positions <= pos
+            p[r] = 0.f;
+            if (r >= nrows || c0 > pos) continue;  // uniform over the warp
+            const bool ok = lane < n && c0 + lane <= pos;
+            const float s = ok ? sc[r] * a.scale : -INFINITY;
+            const float mn = fmaxf(mrun[r], warp_max(s));  // finite: position c0 <= pos is valid
+            const float corr = expf(mrun[r] - mn);
+            p[r] = ok ? expf(s - mn) : 0.f;
+            l[r] = fmaf(l[r], corr, warp_sum(p[r]));
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[r][e] *= corr;
+            mrun[r] = mn;
+        }
+        for (int jj = 0; jj < n; ++jj) {
+            float vf[EPL];
+            load_v<KV, EPL>(reinterpret_cast<const KV *>(vt + jj * pitch) + lane * EPL, vf);
+#pragma unroll
+            for (int r = 0; r < QB; ++r) {
+                const float pj = __shfl_sync(0xffffffffu, p[r], jj);
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[r][e] = fmaf(pj, vf[e], acc[r][e]);
+            }
+        }
+        if (c0 + 32 < t1) __syncthreads();  // readers done before the stage is refilled
+    }
+#pragma unroll
+    for (int r = 0; r < QB; ++r) {
+        if (r >= nrows) break;
+        float *o = a.out + (size_t)(m0 + r) * a.H * hd + (size_t)h * hd + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] = acc[r][e] / l[r];
+    }
+}
+
+template <typename KV, int EPL>
+static cudaError_t prefill_tile_launch(const RowsAttnArgs &a, cudaStream_t s) {
+    constexpr int QB = 8;
+    const int rep = a.H / a.Hkv;
+    const int pitch = a.hd * (int)sizeof(KV) + 16;
+    const size_t smem = (size_t)2 * 2 * 32 * pitch + (size_t)rep * QB * a.hd * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_tile_attn_kernel<KV, EPL, QB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        if (e) return e;
+        configured = true;
+    }
+    if (smem > 160 * 1024) return cudaErrorInvalidValue;
+    prefill_tile_attn_kernel<KV, EPL, QB><<<dim3((a.T + QB - 1) / QB, a.Hkv), rep * 32, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
 template <typename KV, int EPL, int NST>
 static cudaError_t rows_attn_launch(const RowsAttnArgs &a, cudaStream_t s) {
     const int rep = a.H / a.Hkv;
@@ -427,6 +553,9 @@ cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStrea
     if (a.Hkv <= 0 || a.H % a.Hkv || a.H / a.Hkv > 8 || (a.hd != 64 && a.hd != 128) || a.rows_per_seq <= 0 ||
         a.S <= 0 || a.S > 65535 || a.T > 0x7fffffff || a.max_seq <= 0 || (a.S > 1 && (!a.part || !a.counters)))
         return cudaErrorInvalidValue;
+    // one sequence's consecutive rows (prompt chunks): query rows tiled per block
+    if (a.rows_per_seq >= a.T && !a.st && a.S == 1 && a.T >= 16 && kv_half)
+        return a.hd == 64 ? prefill_tile_launch<__half, 2>(a, s) : prefill_tile_launch<__half, 4>(a, s);
     if (kv_half) return a.hd == 64 ? rows_attn_launch<__half, 2, 2>(a, s) : rows_attn_launch<__half, 4, 2>(a, s);
     return a.hd == 64 ? rows_attn_launch<float, 2, 1>(a, s) : rows_attn_launch<float, 4, 1>(a, s);
 }
