@@ -143,7 +143,11 @@ WORKLOADS = {"C1": C1, "C2": C2, "C3": C3, "C4": C4, "C5": C5}
 # 2 GB on the device), small enough for full ncu captures of C2's kernels.
 C2S = Workload(s2pro(seed=1, slow_layers=4, fast_layers=1), prompt_len=64, frames=4,
                prompt_seed=1, im_end_id=S2PRO_IM_END)
-PROFILING = {"C2S": C2S}
+# Profiling case of the batched step: C4's shapes and batch with 4 Slow-AR and
+# 1 Fast-AR layers (about 3 GB on the device with the 64 caches).
+C4S = Workload(s2pro(seed=3, slow_layers=4, fast_layers=1), prompt_len=1024, frames=4, prompt_seed=3,
+               im_end_id=S2PRO_IM_END, batch=64, prompt_len_min=128)
+PROFILING = {"C2S": C2S, "C4S": C4S}
 
 
 def weight_bytes_per_frame(m: ModelConfig) -> dict:

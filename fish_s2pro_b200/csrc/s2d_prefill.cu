@@ -225,9 +225,7 @@ __device__ __forceinline__ void load_v(const KV *p, float *o) {
 }
 
 template <typename KV, int EPL, int NST>
-__global__ void __launch_bounds__(256) rows_attn_kernel(const RowsAttnArgs a) {
-    extern __shared__ __align__(16) uint8_t sm[];
-    __shared__ int s_last;
+__device__ __forceinline__ void rows_attn_body(const RowsAttnArgs &a, uint8_t *sm, int &s_last) {
     const int rep = blockDim.x >> 5;
     const int m = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -259,17 +257,23 @@ __global__ void __launch_bounds__(256) rows_attn_kernel(const RowsAttnArgs a) {
     float mrun = -INFINITY, l = 0.f, acc[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    if (t0 < t1) issue(t0, 0);
+    // NST-stage ring: chunks it .. it + NST - 2 are in flight while chunk it
+    // is scored (an empty group keeps the group count when no chunk is left)
+#pragma unroll
+    for (int i = 0; i < NST - 1; ++i) {
+        if (t0 + i * 32 < t1) issue(t0 + i * 32, i);
+        else cp_async_commit();
+    }
     for (int c0 = t0, it = 0; c0 < t1; c0 += 32, ++it) {
-        const int stg = NST == 2 ? (it & 1) : 0;
+        const int stg = it % NST;
         if (NST == 1) {
-            if (it > 0) issue(c0, 0);
+            issue(c0, 0);  // the previous chunk's readers are done (trailing barrier)
             cp_async_wait<0>();
-        } else if (c0 + 32 < t1) {
-            issue(c0 + 32, stg ^ 1);
-            cp_async_wait<1>();
         } else {
-            cp_async_wait<0>();
+            const int cn = c0 + (NST - 1) * 32;
+            if (cn < t1) issue(cn, (it + NST - 1) % NST);
+            else cp_async_commit();
+            cp_async_wait<NST - 1>();
         }
         __syncthreads();  // this chunk (and, on the first pass, qs) visible to every warp
         const int n = min(32, t1 - c0);
@@ -290,7 +294,7 @@ __global__ void __launch_bounds__(256) rows_attn_kernel(const RowsAttnArgs a) {
             for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj, vf[e], acc[e]);
         }
         mrun = mn;
-        if (NST == 1 || c0 + 32 < t1) __syncthreads();  // readers done before the stage is refilled
+        __syncthreads();  // readers done before the stage is refilled
     }
     if (a.S == 1) {
         float *o = a.out + (size_t)m * a.H * hd + (size_t)h * hd + lane * EPL;
@@ -404,6 +408,24 @@ cudaError_t launch_combine(int epi, const float *Y2, const float *Y2b, const flo
     }
     return cudaGetLastError();
 }
+
+template <typename KV, int EPL, int NST>
+__global__ void __launch_bounds__(256) rows_attn_kernel(const RowsAttnArgs a) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int s_last;
+    rows_attn_body<KV, EPL, NST>(a, sm, s_last);
+}
+
+// The batched decode step's rows (one per sequence, positions from the
+// sequences' states): the same body under its own name, so that profiles
+// tell it from the prompt-chunk tails.
+template <typename KV, int EPL, int NST>
+__global__ void __launch_bounds__(256) decode_rows_attn_kernel(const RowsAttnArgs a) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int s_last;
+    rows_attn_body<KV, EPL, NST>(a, sm, s_last);
+}
+
 
 // Causal attention of one sequence's consecutive rows (the prefill case of
 // rows_attn_kernel: rows_per_seq = T, no state, one split), QB query rows per
@@ -540,11 +562,17 @@ static cudaError_t rows_attn_launch(const RowsAttnArgs &a, cudaStream_t s) {
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(rows_attn_kernel<KV, EPL, NST>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        if (!e)
+            e = cudaFuncSetAttribute(decode_rows_attn_kernel<KV, EPL, NST>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
         if (e) return e;
         configured = true;
     }
     if (smem > 96 * 1024) return cudaErrorInvalidValue;
-    rows_attn_kernel<KV, EPL, NST><<<dim3(a.T, a.Hkv, a.S), rep * 32, smem, s>>>(a);
+    if (a.st && a.st_pos)
+        decode_rows_attn_kernel<KV, EPL, NST><<<dim3(a.T, a.Hkv, a.S), rep * 32, smem, s>>>(a);
+    else
+        rows_attn_kernel<KV, EPL, NST><<<dim3(a.T, a.Hkv, a.S), rep * 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -556,6 +584,10 @@ cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStrea
     // one sequence's consecutive rows (prompt chunks): query rows tiled per block
     if (a.rows_per_seq >= a.T && !a.st && a.S == 1 && a.T >= 16 && kv_half)
         return a.hd == 64 ? prefill_tile_launch<__half, 2>(a, s) : prefill_tile_launch<__half, 4>(a, s);
+    // decode rows (one or two per sequence): a deeper ring keeps more of the
+    // block's staging in flight
+    if (kv_half && a.rows_per_seq <= 2 && a.decode_stages == 4)
+        return a.hd == 64 ? rows_attn_launch<__half, 2, 4>(a, s) : rows_attn_launch<__half, 4, 4>(a, s);
     if (kv_half) return a.hd == 64 ? rows_attn_launch<__half, 2, 2>(a, s) : rows_attn_launch<__half, 4, 2>(a, s);
     return a.hd == 64 ? rows_attn_launch<float, 2, 1>(a, s) : rows_attn_launch<float, 4, 1>(a, s);
 }

@@ -54,6 +54,7 @@ struct RowsAttnArgs {
     int S;               // splits of each row's positions (1: no merge)
     float *part;         // S > 1: [T][H][S][hd + 2]
     int32_t *counters;   // S > 1: [T][Hkv], zero between launches (left zero)
+    int decode_stages;   // 4: a 4-stage K/V ring for rows of 1-2 per sequence (else 2)
 };
 cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
 

@@ -141,6 +141,7 @@ struct S2dHandle {
     int l2_lead = 0;                    // engine L2 prefetch lead in slots (S2D_L2_LEAD)
     int engine_att_splits = 0;          // cap on the Slow-AR attention splits (S2D_ATT_SPLITS; 0: none)
     int attn_blocks_per_sm = 16;        // batched step: rows-attention blocks per SM (S2D_BATCH_ATT_BLOCKS)
+    int attn_stages = 2;                // batched step: rows-attention K/V ring stages, 2 or 4 (S2D_BATCH_ATT_STAGES)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
@@ -1313,7 +1314,7 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.max_seq = rp.max_seq, t.out = h->pf_att, t.T = T, t.rows_per_seq = rp.rps, t.st = rp.st;
         t.st_pos = rp.st_pos, t.pos_const = rp.pos_const, t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd;
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
-        t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters;
+        t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters, t.decode_stages = h->attn_stages;
         CK(launch_rows_attention(t, !is_fast, h->stream));
         mark(h, PC_ATTN);
         // wo + residual, then the ffn_norm split
@@ -1717,6 +1718,7 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         if (const char *sp = getenv("S2D_ATT_SPLITS")) h->engine_att_splits = std::max(0, atoi(sp));
         if (const char *tc = getenv("S2D_TCGEMM")) h->use_tc = tc[0] == '1';
         if (const char *ab = getenv("S2D_BATCH_ATT_BLOCKS")) h->attn_blocks_per_sm = std::max(1, std::min(64, atoi(ab)));
+        if (const char *st = getenv("S2D_BATCH_ATT_STAGES")) h->attn_stages = atoi(st) == 2 ? 2 : 4;
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
