@@ -584,6 +584,7 @@ cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStrea
     // one sequence's consecutive rows (prompt chunks): query rows tiled per block
     if (a.rows_per_seq >= a.T && !a.st && a.S == 1 && a.T >= 16 && kv_half)
         return a.hd == 64 ? prefill_tile_launch<__half, 2>(a, s) : prefill_tile_launch<__half, 4>(a, s);
+    if (a.decode_mma && decode_mma_supported(a, kv_half)) return launch_decode_mma_attention(a, s);
     // decode rows (one or two per sequence): a deeper ring keeps more of the
     // block's staging in flight
     if (kv_half && a.rows_per_seq <= 2 && a.decode_stages == 4)

@@ -54,8 +54,15 @@ struct RowsAttnArgs {
     int S;               // splits of each row's positions (1: no merge)
     float *part;         // S > 1: [T][H][S][hd + 2]
     int32_t *counters;   // S > 1: [T][Hkv], zero between launches (left zero)
-    int decode_stages;   // 4: a 4-stage K/V ring for rows of 1-2 per sequence (else 2)
+    int decode_stages;   // K/V ring stages of the decode kernels (CUDA cores: 2 or 4; MMA: 2 or 3)
+    int decode_mma;      // batched step rows (one per sequence, f16 cache): the tensor-core kernel
+    int decode_warps;    // its warps per block, 2 or 4
 };
 cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
+// The batched step's attention on the tensor cores (s2d_decode_attn.cu):
+// rows of one position per sequence (st and st_pos set), f16 caches, head
+// dim 64 or 128, up to 8 query heads per kv head.
+bool decode_mma_supported(const RowsAttnArgs &a, bool kv_half);
+cudaError_t launch_decode_mma_attention(const RowsAttnArgs &a, cudaStream_t s);
 
 }  // namespace s2d

@@ -142,6 +142,10 @@ struct S2dHandle {
     int engine_att_splits = 0;          // cap on the Slow-AR attention splits (S2D_ATT_SPLITS; 0: none)
     int attn_blocks_per_sm = 16;        // batched step: rows-attention blocks per SM (S2D_BATCH_ATT_BLOCKS)
     int attn_stages = 2;                // batched step: rows-attention K/V ring stages, 2 or 4 (S2D_BATCH_ATT_STAGES)
+    int attn_mma = 1;                   // batched step: tensor-core attention (S2D_DECODE_MMA)
+    int attn_mma_warps = 4;             // its warps per block, 2 or 4 (S2D_DECODE_WARPS)
+    int attn_mma_stages = 2;            // its K/V ring stages per warp, 2 or 3 (S2D_DECODE_STAGES)
+    int attn_mma_blocks_per_sm = 2;     // its blocks per SM when choosing splits (S2D_DECODE_BLOCKS)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
@@ -1315,6 +1319,9 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.st_pos = rp.st_pos, t.pos_const = rp.pos_const, t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd;
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters, t.decode_stages = h->attn_stages;
+        if (h->attn_mma && rp.st && rp.st_pos && rp.rps == 1) {
+            t.decode_mma = 1, t.decode_warps = h->attn_mma_warps, t.decode_stages = h->attn_mma_stages;
+        }
         CK(launch_rows_attention(t, !is_fast, h->stream));
         mark(h, PC_ATTN);
         // wo + residual, then the ffn_norm split
@@ -1501,7 +1508,8 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
 // Attention splits of the batched Slow-AR step: enough blocks for ~8 per SM.
 int batch_splits(const S2dHandle *h, int B) {
     const int blocks = B * h->slow.Hkv;
-    return std::max(1, std::min(h->ra_smax, (h->attn_blocks_per_sm * std::max(h->num_sms, 1) + blocks - 1) / blocks));
+    const int per_sm = h->attn_mma ? h->attn_mma_blocks_per_sm : h->attn_blocks_per_sm;
+    return std::max(1, std::min(h->ra_smax, (per_sm * std::max(h->num_sms, 1) + blocks - 1) / blocks));
 }
 
 // One frame of B sequences (the loop body of generate_codes,
@@ -1719,6 +1727,10 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         if (const char *tc = getenv("S2D_TCGEMM")) h->use_tc = tc[0] == '1';
         if (const char *ab = getenv("S2D_BATCH_ATT_BLOCKS")) h->attn_blocks_per_sm = std::max(1, std::min(64, atoi(ab)));
         if (const char *st = getenv("S2D_BATCH_ATT_STAGES")) h->attn_stages = atoi(st) == 2 ? 2 : 4;
+        if (const char *v = getenv("S2D_DECODE_MMA")) h->attn_mma = atoi(v) != 0;
+        if (const char *v = getenv("S2D_DECODE_WARPS")) h->attn_mma_warps = atoi(v) == 2 ? 2 : 4;
+        if (const char *v = getenv("S2D_DECODE_STAGES")) h->attn_mma_stages = atoi(v) == 3 ? 3 : 2;
+        if (const char *v = getenv("S2D_DECODE_BLOCKS")) h->attn_mma_blocks_per_sm = std::max(1, std::min(64, atoi(v)));
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -2385,6 +2397,52 @@ int32_t s2d_op_rows_linear_f16(S2dHandle *h, const float *x, int64_t T, int64_t 
     CK(cudaMemcpyAsync(y, dy.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost, h->stream));
     CK(cudaStreamSynchronize(h->stream));
     return check_device_error(h);
+}
+
+int32_t s2d_op_batch_attention(S2dHandle *h, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                               int64_t B, int64_t H, int64_t Hkv, int64_t head_dim, int64_t max_seq,
+                               const int32_t *n_past, const int32_t *done, int32_t splits, int32_t impl, float *out) {
+    if (!h) return S2D_EINVAL;
+    if (!q || !kcache || !vcache || !n_past || !out || B <= 0 || B > 4096 || Hkv <= 0 || H % Hkv ||
+        H / Hkv > 8 || (head_dim != 64 && head_dim != 128) || max_seq <= 0 || max_seq > (1 << 20) || splits < 0 ||
+        splits > 64 || impl < 0 || impl > 1)
+        return set_err(h, S2D_EINVAL, "s2d_op_batch_attention: bad arguments");
+    for (int64_t b = 0; b < B; ++b)
+        if (n_past[b] < 0 || n_past[b] >= max_seq)
+            return set_err(h, S2D_EINVAL, "s2d_op_batch_attention: n_past out of range");
+    CK(cudaSetDevice(h->device));
+    const size_t per_seq = (size_t)Hkv * max_seq * head_dim, nq = (size_t)B * H * head_dim;
+    const int S = splits ? splits : std::max(1, std::min(16, (int)((h->attn_mma_blocks_per_sm * h->num_sms +
+                                                                    B * Hkv - 1) / (B * Hkv))));
+    std::vector<DevState> st((size_t)B);
+    for (int64_t b = 0; b < B; ++b) st[b] = DevState{}, st[b].n_past = n_past[b], st[b].done = done ? done[b] : 0;
+    DevBuf dq, dk, dv, dout, dst, part, cnt;
+    CK(cudaMalloc(&dq.p, nq * 4));
+    CK(cudaMalloc(&dk.p, (size_t)B * per_seq * 2));
+    CK(cudaMalloc(&dv.p, (size_t)B * per_seq * 2));
+    CK(cudaMalloc(&dout.p, nq * 4));
+    CK(cudaMalloc(&dst.p, (size_t)B * sizeof(DevState)));
+    CK(cudaMalloc(&part.p, nq / head_dim * S * (head_dim + 2) * 4));
+    CK(cudaMalloc(&cnt.p, (size_t)B * Hkv * 4));
+    CK(cudaMemsetAsync(cnt.p, 0, (size_t)B * Hkv * 4, h->stream));
+    CK(cudaMemsetAsync(dout.p, 0, nq * 4, h->stream));
+    CK(cudaMemcpyAsync(dq.p, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dk.p, kcache, (size_t)B * per_seq * 2, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dv.p, vcache, (size_t)B * per_seq * 2, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dst.p, st.data(), (size_t)B * sizeof(DevState), cudaMemcpyHostToDevice, h->stream));
+    RowsAttnArgs t{};
+    t.q = (const float *)dq.p, t.kcache = dk.p, t.vcache = dv.p, t.kv_seq_stride = per_seq, t.max_seq = (int)max_seq;
+    t.out = (float *)dout.p, t.T = (int)B, t.rows_per_seq = 1, t.st = (const DevState *)dst.p, t.st_pos = 1;
+    t.pos_const = 0, t.H = (int)H, t.Hkv = (int)Hkv, t.hd = (int)head_dim;
+    t.scale = 1.0f / sqrtf((float)head_dim), t.S = S, t.part = (float *)part.p, t.counters = (int32_t *)cnt.p;
+    t.decode_stages = impl == 0 ? h->attn_mma_stages : h->attn_stages;
+    t.decode_mma = impl == 0, t.decode_warps = h->attn_mma_warps;
+    if (impl == 0 && !decode_mma_supported(t, true))
+        return set_err(h, S2D_EINVAL, "the tensor-core attention does not take these arguments");
+    CK(launch_rows_attention(t, true, h->stream));
+    CK(cudaMemcpyAsync(out, dout.p, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return S2D_OK;
 }
 
 int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n, int64_t head_dim,

@@ -273,6 +273,19 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
  * (GGUF little-endian bits), i.e. matvec_f16_streaming (tensor.rs:220-264). */
 int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *weight_f16,
                           int64_t in_dim, int64_t out_dim, float *out);
+/* gqa_decode_attention + softmax_in_place (attention.rs:208-309) for B
+ * sequences at once, the batched Slow-AR step's attention: q [B][H][head_dim]
+ * f32; kcache / vcache [B][Hkv][max_seq][head_dim] f16 bits; sequence b's
+ * row sits at position n_past[b] and attends over positions 0..n_past[b]
+ * (done[b] != 0, when done is given, skips the sequence and leaves its out
+ * rows zero).  splits: position splits per (sequence, kv head), 0 for the
+ * runtime's choice.  impl 0: the tensor-core kernel; 1: the CUDA-core rows
+ * kernel.  head_dim 64 or 128, H / Hkv <= 8, host buffers; out
+ * [B][H][head_dim]. */
+int32_t s2d_op_batch_attention(S2dHandle *h, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                               int64_t B, int64_t H, int64_t Hkv, int64_t head_dim, int64_t max_seq,
+                               const int32_t *n_past, const int32_t *done, int32_t splits, int32_t impl,
+                               float *out);
 /* MatmulBackend::rms_norm / rms_norm_heads (backend.rs:84-121);
  * head_dim == n gives the plain rms_norm. */
 /* MatmulBackend::linear (backend.rs:55-73) over T rows at once, the rows
