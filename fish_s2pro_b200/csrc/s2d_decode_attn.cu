@@ -3,9 +3,12 @@
 //
 // One query row per sequence attends over that sequence's cached positions
 // (gqa_decode_attention + softmax_in_place, attention.rs:208-309, once per
-// sequence).  Grid (sequence, kv head, split); a block's warps share the
-// split's positions, warp w taking the 32-position chunks w, w + NW, ...
-// of it, each through its own cp.async ring in shared memory.
+// sequence).  A block takes one (sequence, kv head, split); its warps share
+// the split's positions, warp w taking the KC-position chunks w, w + NW, ...
+// of it, each through its own cp.async ring in shared memory.  Blocks are
+// numbered kv head fastest, then split, then sequence rank, where rank
+// follows an optional row order (longest context first, so the long blocks
+// start in the first wave and the short ones fill the tail).
 //
 // One warp serves the whole query group of its kv head (rep <= 8 heads) with
 // m16n8k16 f16 MMAs:
@@ -19,11 +22,14 @@
 // element near 2^14 (the power is taken out of the scores exactly), so the
 // softmax runs in base 2 with exp2f.
 //
-// The block merges its warps' (max, sum, weighted V) states in shared memory;
+// The block merges its warps' (max, sum, weighted V) states in shared memory
+// (over the drained rings);
 // with S > 1 splits it writes the merged state as a partial and the last
 // block of the (sequence, kv head) to arrive merges the S partials.
 #include <cuda_fp16.h>
 #include <math.h>
+
+#include <algorithm>
 
 #include "s2d_common.cuh"
 #include "s2d_prefill.cuh"
@@ -31,8 +37,6 @@
 namespace s2d {
 
 namespace {
-
-constexpr int kChunk = 32;  // positions per staged chunk
 
 __device__ __forceinline__ void cp_async16_zfill(void *dst, const void *src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
@@ -73,26 +77,30 @@ __device__ __forceinline__ void split_half2(float x, float y, uint32_t &hi, uint
     lo = pack_half2(x - hf.x, y - hf.y);
 }
 
-template <int HD, int NST>
+template <int HD, int NST, int KC>
 __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs a) {
     constexpr int KS = HD / 16;         // k-steps of the score MMA
     constexpr int NO = HD / 8;          // n-tiles of the output
+    constexpr int NP = KC / 8;          // n-tiles of the scores
     constexpr int UNITS = HD * 2 / 16;  // 16-byte units per cached row
     constexpr int PITCH = HD * 2 + 16;  // staged row pitch: conflict-free ldmatrix rows
-    constexpr int STAGE = 2 * kChunk * PITCH;
+    constexpr int STAGE = 2 * KC * PITCH;
+    static_assert(KC == 16 || KC == 32, "chunk of 16 or 32 positions");
+    static_assert((KC * UNITS) % 32 == 0, "whole copy rounds per lane");
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ int s_last;
     const int nw = blockDim.x >> 5;
     const int rep = a.H / a.Hkv;
-    const int m = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z;
+    const int kvh = blockIdx.x % a.Hkv, rest = blockIdx.x / a.Hkv, sp = rest % a.S, rank = rest / a.S;
+    const int m = a.row_order ? a.row_order[rank] : rank;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     if (a.st[m].done) return;  // every split of the row returns: no counter use
     const int pos = a.pos_const + a.st[m].n_past;
     const int visible = max(1, min(pos + 1, a.max_seq));
-    const int nch = (visible + kChunk - 1) / kChunk, cps = (nch + a.S - 1) / a.S;
-    const int t0 = min(visible, sp * cps * kChunk), t1 = min(visible, t0 + cps * kChunk);
-    const int nck = (t1 - t0 + kChunk - 1) / kChunk;
+    const int nch = (visible + KC - 1) / KC, cps = (nch + a.S - 1) / a.S;
+    const int t0 = min(visible, sp * cps * KC), t1 = min(visible, t0 + cps * KC);
+    const int nck = (t1 - t0 + KC - 1) / KC;
     const int mine = nck > warp ? (nck - warp + nw - 1) / nw : 0;
 
     const size_t so = (size_t)m * a.kv_seq_stride * 2 + (size_t)kvh * a.max_seq * (HD * 2);
@@ -100,10 +108,10 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
     const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
     uint8_t *ring = sm + (size_t)warp * NST * STAGE;
     auto issue = [&](int j, int stg) {
-        const int c0 = t0 + (warp + nw * j) * kChunk, n = min(kChunk, t1 - c0);
-        uint8_t *kt = ring + (size_t)stg * STAGE, *vt = kt + kChunk * PITCH;
+        const int c0 = t0 + (warp + nw * j) * KC, n = min(KC, t1 - c0);
+        uint8_t *kt = ring + (size_t)stg * STAGE, *vt = kt + KC * PITCH;
 #pragma unroll
-        for (int i = 0; i < UNITS; ++i) {
+        for (int i = 0; i < KC * UNITS / 32; ++i) {
             const int u = lane + 32 * i, r = u / UNITS, c = u - r * UNITS;
             const size_t src = (size_t)(c0 + (r < n ? r : 0)) * (HD * 2) + c * 16;
             cp_async16_zfill(kt + r * PITCH + c * 16, kb + src, r < n);
@@ -157,15 +165,15 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
         else commit_group();
         wait_group<NST - 1>();
         __syncwarp();
-        const uint8_t *kt = ring + (size_t)(j % NST) * STAGE, *vt = kt + kChunk * PITCH;
-        const int n = min(kChunk, t1 - (t0 + (warp + nw * j) * kChunk));
-        float s[4][4];
+        const uint8_t *kt = ring + (size_t)(j % NST) * STAGE, *vt = kt + KC * PITCH;
+        const int n = min(KC, t1 - (t0 + (warp + nw * j) * KC));
+        float s[NP][4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) s[p][0] = s[p][1] = s[p][2] = s[p][3] = 0.f;
+        for (int p = 0; p < NP; ++p) s[p][0] = s[p][1] = s[p][2] = s[p][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < HD / 32; ++kk) {
 #pragma unroll
-            for (int p = 0; p < 4; ++p) {
+            for (int p = 0; p < NP; ++p) {
                 uint32_t b[4];
                 ldsm_x4(b, kt + (p * 8 + (lane & 7)) * PITCH + (kk * 32 + (lane >> 3) * 8) * 2);
                 mma_16816(s[p], qa[2 * kk], b[0], b[1]);
@@ -173,9 +181,9 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
             }
         }
         // head g's scores of positions 8p + 2t + e: rows g (hi) + 8 + g (lo)
-        float sc[4][2], mx = -INFINITY;
+        float sc[NP][2], mx = -INFINITY;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
+        for (int p = 0; p < NP; ++p) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const float v = (s[p][e] + s[p][2 + e]) * qdown;
@@ -189,9 +197,9 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
         const float corr = exp2f(mrun - mnew);
         mrun = mnew;
         float psum = 0.f;
-        uint32_t pa[2][4];
+        uint32_t pa[KC / 16][4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
+        for (int p = 0; p < NP; ++p) {
             const float p0 = exp2f(sc[p][0] - mnew), p1 = exp2f(sc[p][1] - mnew);
             psum += p0 + p1;
             // k-step p / 2: regs 0 / 1 = positions 0..7 hi / lo, regs 2 / 3 = 8..15
@@ -204,7 +212,7 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
             for (int e = 0; e < 4; ++e) o[jn][e] *= corr;
         }
 #pragma unroll
-        for (int k2 = 0; k2 < 2; ++k2) {
+        for (int k2 = 0; k2 < KC / 16; ++k2) {
 #pragma unroll
             for (int nd = 0; nd < HD / 16; ++nd) {
                 uint32_t b[4];
@@ -217,9 +225,10 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
         __syncwarp();  // every lane's reads of this stage are done before it is refilled
     }
     wait_group<0>();
+    __syncthreads();  // every ring drained: the merge area reuses them
 
     // merge the warps: [warp][head][2 + HD] (max, sum, weighted V) in shared memory
-    float *ms = reinterpret_cast<float *>(sm + (size_t)nw * NST * STAGE);
+    float *ms = reinterpret_cast<float *>(sm);
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
     if (g < rep) {
@@ -281,21 +290,23 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
     if (threadIdx.x == 0) a.counters[(size_t)m * a.Hkv + kvh] = 0;
 }
 
-template <int HD, int NST>
+template <int HD, int NST, int KC>
 cudaError_t decode_mma_launch(const RowsAttnArgs &a, int warps, cudaStream_t s) {
     constexpr int PITCH = HD * 2 + 16;
     const int rep = a.H / a.Hkv;
-    const size_t smem = (size_t)warps * NST * 2 * kChunk * PITCH + (size_t)warps * rep * (HD + 2) * sizeof(float);
+    const size_t smem = std::max((size_t)warps * NST * 2 * KC * PITCH, (size_t)warps * rep * (HD + 2) * sizeof(float));
+    const int64_t blocks = (int64_t)a.T * a.Hkv * a.S;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
     // the opt-in limit is 227 KB per block, less the kernel's static 16 bytes
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     static size_t configured = 0;
     if (smem > configured) {
-        cudaError_t e = cudaFuncSetAttribute(decode_mma_attn_kernel<HD, NST>,
+        cudaError_t e = cudaFuncSetAttribute(decode_mma_attn_kernel<HD, NST, KC>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e) return e;
         configured = smem;
     }
-    decode_mma_attn_kernel<HD, NST><<<dim3(a.T, a.Hkv, a.S), warps * 32, smem, s>>>(a);
+    decode_mma_attn_kernel<HD, NST, KC><<<(unsigned)blocks, warps * 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -313,9 +324,14 @@ cudaError_t launch_decode_mma_attention(const RowsAttnArgs &a, cudaStream_t s) {
     const int warps = a.decode_warps == 2 ? 2 : 4, nst = a.decode_stages == 3 ? 3 : 2;
     if (a.S <= 0 || a.S > 65535 || a.max_seq <= 0 || (a.S > 1 && (!a.part || !a.counters)))
         return cudaErrorInvalidValue;
+    if (a.decode_chunk == 32) {
+        if (a.hd == 64)
+            return nst == 3 ? decode_mma_launch<64, 3, 32>(a, warps, s) : decode_mma_launch<64, 2, 32>(a, warps, s);
+        return nst == 3 ? decode_mma_launch<128, 3, 32>(a, warps, s) : decode_mma_launch<128, 2, 32>(a, warps, s);
+    }
     if (a.hd == 64)
-        return nst == 3 ? decode_mma_launch<64, 3>(a, warps, s) : decode_mma_launch<64, 2>(a, warps, s);
-    return nst == 3 ? decode_mma_launch<128, 3>(a, warps, s) : decode_mma_launch<128, 2>(a, warps, s);
+        return nst == 3 ? decode_mma_launch<64, 3, 16>(a, warps, s) : decode_mma_launch<64, 2, 16>(a, warps, s);
+    return nst == 3 ? decode_mma_launch<128, 3, 16>(a, warps, s) : decode_mma_launch<128, 2, 16>(a, warps, s);
 }
 
 }  // namespace s2d

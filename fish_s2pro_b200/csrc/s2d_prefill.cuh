@@ -57,6 +57,8 @@ struct RowsAttnArgs {
     int decode_stages;   // K/V ring stages of the decode kernels (CUDA cores: 2 or 4; MMA: 2 or 3)
     int decode_mma;      // batched step rows (one per sequence, f16 cache): the tensor-core kernel
     int decode_warps;    // its warps per block, 2 or 4
+    int decode_chunk;    // its positions per staged chunk, 16 or 32
+    const int32_t *row_order;  // its block order: row of each rank (longest context first), or nullptr
 };
 cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
 // The batched step's attention on the tensor cores (s2d_decode_attn.cu):

@@ -146,6 +146,8 @@ struct S2dHandle {
     int attn_mma_warps = 4;             // its warps per block, 2 or 4 (S2D_DECODE_WARPS)
     int attn_mma_stages = 2;            // its K/V ring stages per warp, 2 or 3 (S2D_DECODE_STAGES)
     int attn_mma_blocks_per_sm = 2;     // its blocks per SM when choosing splits (S2D_DECODE_BLOCKS)
+    int attn_mma_chunk = 16;            // its positions per staged chunk, 16 or 32 (S2D_DECODE_CHUNK)
+    int attn_mma_order = 1;             // its blocks longest context first (S2D_DECODE_ORDER)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
@@ -175,6 +177,7 @@ struct S2dHandle {
     size_t codes_b_cap = 0;
     float *ra_part = nullptr;             // rows attention split partials
     int32_t *ra_counters = nullptr;
+    int32_t *batch_order = nullptr;       // [max_batch]: sequences by prompt length, longest first
     int ra_rows = 0, ra_smax = 0;
     cudaGraphExec_t batch_exec = nullptr;
     // s2d_profile_batch: events recorded after each launch, tagged with the
@@ -1216,6 +1219,7 @@ int32_t rows_linear(S2dHandle *h, const uint16_t *W, const uint16_t *W2, int N, 
 struct RowsPlan {
     int T = 0, rps = 1, pos_const = 0, st_pos = 0, S = 1;
     const DevState *st = nullptr;
+    const int32_t *order = nullptr;  // one row per sequence: the attention's block order
     void *kv = nullptr;
     size_t kv_seq_stride = 0;
     int max_seq = 0;
@@ -1321,6 +1325,7 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters, t.decode_stages = h->attn_stages;
         if (h->attn_mma && rp.st && rp.st_pos && rp.rps == 1) {
             t.decode_mma = 1, t.decode_warps = h->attn_mma_warps, t.decode_stages = h->attn_mma_stages;
+            t.decode_chunk = h->attn_mma_chunk, t.row_order = rp.order;
         }
         CK(launch_rows_attention(t, !is_fast, h->stream));
         mark(h, PC_ATTN);
@@ -1489,6 +1494,10 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
         CK(cudaMalloc(&h->ra_part, (size_t)h->ra_rows * H * h->ra_smax * (hd + 2) * sizeof(float)));
         CK(cudaMalloc(&h->ra_counters, (size_t)h->ra_rows * Hkv * sizeof(int32_t)));
         CK(cudaMemset(h->ra_counters, 0, (size_t)h->ra_rows * Hkv * sizeof(int32_t)));
+        CK(cudaMalloc(&h->batch_order, B * sizeof(int32_t)));
+        std::vector<int32_t> ident(B);
+        for (size_t i = 0; i < B; ++i) ident[i] = (int32_t)i;
+        CK(cudaMemcpy(h->batch_order, ident.data(), B * sizeof(int32_t), cudaMemcpyHostToDevice));
     }
     const size_t need = B * K * std::max<uint32_t>(max_new, 1);
     if (need > h->codes_b_cap) {
@@ -1578,6 +1587,7 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     // Slow-AR step: one row per sequence at its own position
     RowsPlan rp;
     rp.T = B, rp.rps = 1, rp.pos_const = 0, rp.st = h->st_b, rp.st_pos = 1, rp.S = batch_splits(h, B);
+    rp.order = h->attn_mma_order ? h->batch_order : nullptr;
     rp.kv = h->kv_slow, rp.kv_seq_stride = h->kv_slow_seq, rp.max_seq = h->cfg.max_seq;
     if ((rc = rows_layers(h, false, h->bx, d, rp))) return rc;
     // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
@@ -1612,7 +1622,7 @@ void free_handle(S2dHandle *h) {
     if (h->shard_arena) cudaFree(h->shard_arena);
     for (void *p : {(void *)h->st_b, (void *)h->bx, (void *)h->fx, (void *)h->hidden_b, (void *)h->logits_b,
                     (void *)h->logits_fast_b, (void *)h->kv_fast_b, (void *)h->frame_codes_b, (void *)h->codes_b,
-                    (void *)h->ra_part, (void *)h->ra_counters})
+                    (void *)h->ra_part, (void *)h->ra_counters, (void *)h->batch_order})
         if (p) cudaFree(p);
     void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
                     h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
@@ -1731,6 +1741,8 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         if (const char *v = getenv("S2D_DECODE_WARPS")) h->attn_mma_warps = atoi(v) == 2 ? 2 : 4;
         if (const char *v = getenv("S2D_DECODE_STAGES")) h->attn_mma_stages = atoi(v) == 3 ? 3 : 2;
         if (const char *v = getenv("S2D_DECODE_BLOCKS")) h->attn_mma_blocks_per_sm = std::max(1, std::min(64, atoi(v)));
+        if (const char *v = getenv("S2D_DECODE_CHUNK")) h->attn_mma_chunk = atoi(v) == 32 ? 32 : 16;
+        if (const char *v = getenv("S2D_DECODE_ORDER")) h->attn_mma_order = atoi(v) != 0;
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -2067,6 +2079,13 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
     }
     h->n_past = 0;  // sequence 0's cache now holds batch sequence 0
     const uint32_t prefill_kernels = h->launches - launches0;
+    // the batched attention's block order: longest context first (every
+    // sequence advances one position per frame, so the order holds)
+    std::vector<int32_t> order((size_t)n_seq);
+    for (int i = 0; i < n_seq; ++i) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) { return cols[x] > cols[y]; });
+    CK(cudaMemcpyAsync(h->batch_order, order.data(), order.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                       h->stream));
     CK(cudaEventRecord(h->ev1, h->stream));
 
     // frames: one captured graph advances every sequence by one frame
@@ -2436,7 +2455,14 @@ int32_t s2d_op_batch_attention(S2dHandle *h, const float *q, const uint16_t *kca
     t.pos_const = 0, t.H = (int)H, t.Hkv = (int)Hkv, t.hd = (int)head_dim;
     t.scale = 1.0f / sqrtf((float)head_dim), t.S = S, t.part = (float *)part.p, t.counters = (int32_t *)cnt.p;
     t.decode_stages = impl == 0 ? h->attn_mma_stages : h->attn_stages;
-    t.decode_mma = impl == 0, t.decode_warps = h->attn_mma_warps;
+    t.decode_mma = impl == 0, t.decode_warps = h->attn_mma_warps, t.decode_chunk = h->attn_mma_chunk;
+    std::vector<int32_t> order((size_t)B);
+    for (int64_t b = 0; b < B; ++b) order[b] = (int32_t)b;
+    std::stable_sort(order.begin(), order.end(), [&](int32_t x, int32_t y) { return n_past[x] > n_past[y]; });
+    DevBuf dorder;
+    CK(cudaMalloc(&dorder.p, (size_t)B * sizeof(int32_t)));
+    CK(cudaMemcpyAsync(dorder.p, order.data(), (size_t)B * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
+    t.row_order = (const int32_t *)dorder.p;
     if (impl == 0 && !decode_mma_supported(t, true))
         return set_err(h, S2D_EINVAL, "the tensor-core attention does not take these arguments");
     CK(launch_rows_attention(t, true, h->stream));

@@ -131,3 +131,24 @@ def test_batch_attention_rejects_bad_arguments(st):
         v.view(np.uint16).ctypes.data_as(_P(ctypes.c_uint16)), 2, 8, 2, 64, 32,
         npast.ctypes.data_as(_P(ctypes.c_int32)), None, 0, 0, out.ctypes.data_as(_P(ctypes.c_float)))
     assert rc != 0
+
+
+@pytest.mark.parametrize("env", [
+    {"S2D_DECODE_CHUNK": "32"},
+    {"S2D_DECODE_CHUNK": "32", "S2D_DECODE_STAGES": "3"},
+    {"S2D_DECODE_WARPS": "2", "S2D_DECODE_STAGES": "3"},
+])
+def test_batch_attention_kernel_variants(tiny_gguf, monkeypatch, env):
+    """The chunk / ring / warp variants (selected when a state opens)."""
+    from fish_s2pro_b200 import SlowArState
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    s = SlowArState.open(tiny_gguf, max_seq_len=64)
+    try:
+        for B, H, Hkv, hd, max_seq, pos in (CASES[1], CASES[2], CASES[4]):
+            q, k, v = case(B, H, Hkv, hd, max_seq, 5)
+            want = reference(q, k, v, pos)
+            got = run(s, q, k, v, pos, impl=0)
+            assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < TOL
+    finally:
+        s.close()
