@@ -805,6 +805,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
     __shared__ SampleShared sh;
     __shared__ float rv[32];
     __shared__ int ri[32], rj[32];
+    __shared__ int sel_hist[256];
+    __shared__ unsigned long long sel_keys[kSampleSelMax], sel_prefix, sel_fkey;
+    __shared__ int sel_need, sel_level, sel_count, sel_rank;
     grid_dep_launch();
     grid_dep_wait();
     const uint32_t sq = a.batched ? blockIdx.x : 0u, rseq = a.rng_seq + sq;
@@ -898,44 +901,141 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const SampleArgs
     __syncthreads();
 
     if (sh.general) {
-        // bitonic sort of (value desc, id asc) keys
-        int np2 = 2;
-        while (np2 < n) np2 <<= 1;
-        for (int r = tid; r < np2; r += kSampleThreads) {
-            if (r < n) {
-                const float v = cval(r);
-                skeys[r] = ((unsigned long long)(~f2ord(v)) << 32) | cid(r);
-            } else {
-                skeys[r] = ~0ull;
+        const int nkeep = (int)min(k_eff, (int64_t)sh.nfin);  // the top-k items that are finite
+        const bool select = k_eff <= kSampleSelMax;
+        if (tid == 0) sh.force_pos = 0x7fffffff, sh.force_v = -INFINITY, sh.fin_below = 0;
+        if (select) {
+            // Only the first nkeep entries of the sorted list are read (the
+            // -inf entries behind them only when nkeep == nfin): radix-select
+            // the nkeep smallest (value desc, id asc) keys, 8 bits a level,
+            // then place each by its rank among them.
+            unsigned long long kr[kSampleMax / kSampleThreads];
+#pragma unroll
+            for (int i = 0; i < kSampleMax / kSampleThreads; ++i) {
+                const int r = tid + i * kSampleThreads;
+                kr[i] = r < n ? ((unsigned long long)(~f2ord(cval(r))) << 32) | cid(r) : ~0ull;
             }
-        }
-        __syncthreads();
-        for (int k = 2; k <= np2; k <<= 1) {
-            for (int j = k >> 1; j > 0; j >>= 1) {
-                for (int i = tid; i < np2; i += kSampleThreads) {
-                    const int ixj = i ^ j;
-                    if (ixj > i) {
-                        const unsigned long long x = skeys[i], y = skeys[ixj];
-                        const bool up = (i & k) == 0;
-                        if ((x > y) == up) skeys[i] = y, skeys[ixj] = x;
+            if (tid == 0) sel_prefix = 0ull, sel_need = nkeep, sel_level = 0, sel_count = 0, sel_fkey = ~0ull, sel_rank = 0;
+            __syncthreads();
+            for (int lev = 1; lev <= 8 && nkeep > 0; ++lev) {
+                const int shift = 64 - 8 * lev;
+                if (tid < 256) sel_hist[tid] = 0;
+                __syncthreads();
+                const unsigned long long pre = sel_prefix;
+#pragma unroll
+                for (int i = 0; i < kSampleMax / kSampleThreads; ++i)
+                    if (lev == 1 || (kr[i] >> (shift + 8)) == pre) atomicAdd(&sel_hist[(kr[i] >> shift) & 255u], 1);
+                __syncthreads();
+                if (warp == 0) {
+                    int c[8], tot = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) c[j] = sel_hist[lane * 8 + j], tot += c[j];
+                    int incl = tot;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += y;
+                    }
+                    const int need = sel_need;
+                    int b = incl - tot;
+                    if (b < need && need <= incl) {
+                        int d = 0;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            if (b + c[j] >= need) {
+                                d = j;
+                                break;
+                            }
+                            b += c[j];
+                        }
+                        // the need-th key lies in bin lane * 8 + d: every key of a
+                        // lower bin is kept, and the whole bin once it holds no more
+                        sel_prefix = (pre << 8) | (unsigned long long)(lane * 8 + d);
+                        sel_need = need - b;
+                        if (c[d] == need - b) sel_level = lev;
                     }
                 }
                 __syncthreads();
+                if (sel_level) break;
             }
-        }
-        // Position of the force id in the reference's sorted list: among the
-        // sorted finite entries if its logit is finite, otherwise among the
-        // -inf entries, which follow in id order (sampling.rs:146-168).
-        if (tid == 0) sh.force_pos = 0x7fffffff, sh.force_v = -INFINITY, sh.fin_below = 0;
-        __syncthreads();
-        if (force >= 0 && force < a.vocab_full) {
-            for (int r = tid; r < sh.nfin; r += kSampleThreads) {
-                if ((uint32_t)(skeys[r] & 0xffffffffu) == (uint32_t)force) {
-                    sh.force_pos = r;
-                    const uint32_t ord = ~(uint32_t)(skeys[r] >> 32);
-                    sh.force_v = __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
+            if (nkeep > 0) {
+                const int shift = 64 - 8 * sel_level;
+                const unsigned long long pre = sel_prefix;
+#pragma unroll
+                for (int i = 0; i < kSampleMax / kSampleThreads; ++i)
+                    if ((shift == 64 ? 0ull : kr[i] >> shift) <= pre) {
+                        const int pos = atomicAdd(&sel_count, 1);
+                        if (pos < kSampleSelMax) sel_keys[pos] = kr[i];
+                    }
+            }
+            __syncthreads();
+            if (tid < nkeep) {
+                const unsigned long long key = sel_keys[tid];
+                int rank = 0;
+                for (int j = 0; j < nkeep; ++j) rank += sel_keys[j] < key;
+                skeys[rank] = key;
+            }
+            // Position of a finite force id among the sorted entries: the
+            // number of keys below its own.
+            if (force >= 0 && force < a.vocab_full) {
+#pragma unroll
+                for (int i = 0; i < kSampleMax / kSampleThreads; ++i) {
+                    const int r = tid + i * kSampleThreads;
+                    if (r < n && (int64_t)cid(r) == force && cval(r) > -INFINITY) sel_fkey = kr[i], sh.force_v = cval(r);
                 }
             }
+            __syncthreads();
+            const unsigned long long fk = sel_fkey;
+            if (fk != ~0ull) {
+                int less = 0;
+#pragma unroll
+                for (int i = 0; i < kSampleMax / kSampleThreads; ++i) less += kr[i] < fk;
+                if (less) atomicAdd(&sel_rank, less);
+            }
+            __syncthreads();
+            if (tid == 0 && fk != ~0ull) sh.force_pos = sel_rank;
+            __syncthreads();
+        } else {
+            // bitonic sort of (value desc, id asc) keys
+            int np2 = 2;
+            while (np2 < n) np2 <<= 1;
+            for (int r = tid; r < np2; r += kSampleThreads) {
+                if (r < n) {
+                    const float v = cval(r);
+                    skeys[r] = ((unsigned long long)(~f2ord(v)) << 32) | cid(r);
+                } else {
+                    skeys[r] = ~0ull;
+                }
+            }
+            __syncthreads();
+            for (int k = 2; k <= np2; k <<= 1) {
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    for (int i = tid; i < np2; i += kSampleThreads) {
+                        const int ixj = i ^ j;
+                        if (ixj > i) {
+                            const unsigned long long x = skeys[i], y = skeys[ixj];
+                            const bool up = (i & k) == 0;
+                            if ((x > y) == up) skeys[i] = y, skeys[ixj] = x;
+                        }
+                    }
+                    __syncthreads();
+                }
+            }
+            // Position of the force id in the reference's sorted list: among the
+            // sorted finite entries if its logit is finite (sampling.rs:146-168).
+            if (force >= 0 && force < a.vocab_full) {
+                for (int r = tid; r < sh.nfin; r += kSampleThreads) {
+                    if ((uint32_t)(skeys[r] & 0xffffffffu) == (uint32_t)force) {
+                        sh.force_pos = r;
+                        const uint32_t ord = ~(uint32_t)(skeys[r] >> 32);
+                        sh.force_v = __uint_as_float((ord & 0x80000000u) ? (ord & 0x7fffffffu) : ~ord);
+                    }
+                }
+            }
+            __syncthreads();
+        }
+        // otherwise among the -inf entries, which follow in id order
+        if (force >= 0 && force < a.vocab_full) {
             int below = 0;
             for (int r = tid; r < n; r += kSampleThreads)
                 below += (cval(r) > -INFINITY) && ((int64_t)cid(r) < force);

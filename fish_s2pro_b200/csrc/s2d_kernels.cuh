@@ -316,6 +316,8 @@ __host__ __device__ __forceinline__ int attn_tile_bytes(int rows, int hd, int kv
 
 constexpr int kSampleMax = 8192;
 constexpr int kSampleThreads = 1024;
+// top-k up to this size takes the sampler's radix-select path instead of a full sort
+constexpr int kSampleSelMax = 256;
 constexpr int kGemvThreads = 256;
 
 // Host launchers (s2d_kernels.cu). All enqueue on `stream`; pdl enables

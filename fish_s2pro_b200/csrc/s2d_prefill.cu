@@ -86,49 +86,141 @@ __device__ void split_row_tail(float *row, float ss, int t, int T, int K, const 
 // One block per row t of x [T][ldx]: optional RMSNorm (gain w), then the
 // scaled hi/lo split into xs rows t and T + t ([2T][K] f16); inv[t] undoes
 // the scaling.  With w, the normalised row is also written to xn (if set).
+// With v4 (K and ldx multiples of 4, x 16-byte aligned) the row arrives in
+// one round of float4 loads, up to kRowRounds per thread issued together.
+constexpr int kRowRounds = 4;  // float4s per thread: rows of up to 16,384 values in one round
 __global__ void __launch_bounds__(kSplitThreads) split_rows_kernel(const float *x, int ldx, int T, int K,
                                                                    const float *w, float eps, __half *xs,
-                                                                   float *inv, float *xn) {
+                                                                   float *inv, float *xn, bool v4) {
     extern __shared__ float row[];  // [K]
     __shared__ float red[kSplitThreads / 32];
     const int t = blockIdx.x;
     const float *src = x + (size_t)t * ldx;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        const float v = src[i];
-        row[i] = v;
-        ss = fmaf(v, v, ss);
+    if (v4) {
+        const int K4 = K >> 2;
+        float4 buf[kRowRounds];
+#pragma unroll
+        for (int j = 0; j < kRowRounds; ++j) {
+            const int i4 = threadIdx.x + j * blockDim.x;
+            if (i4 < K4) buf[j] = reinterpret_cast<const float4 *>(src)[i4];
+        }
+#pragma unroll
+        for (int j = 0; j < kRowRounds; ++j) {
+            const int i4 = threadIdx.x + j * blockDim.x;
+            if (i4 < K4) {
+                reinterpret_cast<float4 *>(row)[i4] = buf[j];
+                ss = fmaf(buf[j].x, buf[j].x, ss);
+                ss = fmaf(buf[j].y, buf[j].y, ss);
+                ss = fmaf(buf[j].z, buf[j].z, ss);
+                ss = fmaf(buf[j].w, buf[j].w, ss);
+            }
+        }
+        for (int i = 4 * (threadIdx.x + kRowRounds * blockDim.x); i < K; i += 4 * blockDim.x) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float v = src[i + e];
+                row[i + e] = v;
+                ss = fmaf(v, v, ss);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float v = src[i];
+            row[i] = v;
+            ss = fmaf(v, v, ss);
+        }
     }
     split_row_tail(row, ss, t, T, K, w, eps, xs, inv, xn, red);
 }
 
+// (top + bottom) * s, then the epilogue: the residual r, or SwiGLU with the
+// up projection's halves ut + ub
 template <int EPI>
-__device__ __forceinline__ float combine_one(const float *Y2, const float *Y2b, float s, size_t top, size_t bot,
-                                             const float *resid) {
-    const float v = __fadd_rn(Y2[top], Y2[bot]) * s;
+__device__ __forceinline__ float combine_vals(float top, float bot, float ut, float ub, float s, float r) {
+    const float v = __fadd_rn(top, bot) * s;
     if (EPI == PF_STORE) return v;
-    if (EPI == PF_RESID) return __fadd_rn(*resid, v);
-    const float u = __fadd_rn(Y2b[top], Y2b[bot]) * s;
+    if (EPI == PF_RESID) return __fadd_rn(r, v);
+    const float u = __fadd_rn(ut, ub) * s;
     if (EPI == PF_SWIGLU_SLOW) {
         const float sig = 1.0f / (1.0f + expf(-v));
         return __fmul_rn(__fmul_rn(v, sig), u);
     }
     return __fmul_rn(v / (1.0f + expf(-v)), u);
 }
+template <int EPI>
+__device__ __forceinline__ float combine_one(const float *Y2, const float *Y2b, float s, size_t top, size_t bot,
+                                             const float *resid) {
+    const bool up = EPI == PF_SWIGLU_SLOW || EPI == PF_SWIGLU_FAST;
+    return combine_vals<EPI>(Y2[top], Y2[bot], up ? Y2b[top] : 0.f, up ? Y2b[bot] : 0.f, s,
+                             EPI == PF_RESID ? *resid : 0.f);
+}
 
 // combine_kernel then split_rows_kernel on the same row, in one pass: one
 // block per row t; y (optional) receives the combined row, the split goes to
-// xs / inv (inv[t] is read before it is replaced).
+// xs / inv (inv[t] is read before it is replaced).  With v4 (N, ldy, ldr
+// multiples of 4, the buffers 16-byte aligned) every operand of the row
+// arrives in one round of float4 loads.
 template <int EPI>
 __global__ void __launch_bounds__(kSplitThreads) combine_split_kernel(const float *Y2, const float *Y2b, float *inv,
                                                                       int T, int N, float *y, int ldy,
                                                                       const float *resid, int ldr, const float *w,
-                                                                      float eps, __half *xs) {
+                                                                      float eps, __half *xs, bool v4) {
     extern __shared__ float row[];  // [N]
     __shared__ float red[kSplitThreads / 32];
     const int t = blockIdx.x;
     const float s = inv[t];
     float ss = 0.f;
+    constexpr bool up = EPI == PF_SWIGLU_SLOW || EPI == PF_SWIGLU_FAST;
+    constexpr int RR = up ? 3 : kRowRounds;  // four operands per element: 3 rounds stay in registers
+    if (v4) {
+        const int N4 = N >> 2;
+        const float4 *yt = reinterpret_cast<const float4 *>(Y2 + (size_t)t * N);
+        const float4 *yb = reinterpret_cast<const float4 *>(Y2 + ((size_t)T + t) * N);
+        const float4 *ut = reinterpret_cast<const float4 *>((up ? Y2b : Y2) + (size_t)t * N);
+        const float4 *ub = reinterpret_cast<const float4 *>((up ? Y2b : Y2) + ((size_t)T + t) * N);
+        const float4 *rr = reinterpret_cast<const float4 *>(resid + (size_t)t * ldr);
+        float4 A[RR], B[RR], C[RR], D[RR], R[RR];
+#pragma unroll
+        for (int j = 0; j < RR; ++j) {
+            const int i4 = threadIdx.x + j * blockDim.x;
+            if (i4 < N4) {
+                A[j] = yt[i4], B[j] = yb[i4];
+                if (up) C[j] = ut[i4], D[j] = ub[i4];
+                if (EPI == PF_RESID) R[j] = rr[i4];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < RR; ++j) {
+            const int i4 = threadIdx.x + j * blockDim.x;
+            if (i4 < N4) {
+                const float4 c = up ? C[j] : A[j], d = up ? D[j] : A[j], r = EPI == PF_RESID ? R[j] : A[j];
+                float4 o;
+                o.x = combine_vals<EPI>(A[j].x, B[j].x, c.x, d.x, s, r.x);
+                o.y = combine_vals<EPI>(A[j].y, B[j].y, c.y, d.y, s, r.y);
+                o.z = combine_vals<EPI>(A[j].z, B[j].z, c.z, d.z, s, r.z);
+                o.w = combine_vals<EPI>(A[j].w, B[j].w, c.w, d.w, s, r.w);
+                reinterpret_cast<float4 *>(row)[i4] = o;
+                if (y) reinterpret_cast<float4 *>(y + (size_t)t * ldy)[i4] = o;
+                ss = fmaf(o.x, o.x, ss);
+                ss = fmaf(o.y, o.y, ss);
+                ss = fmaf(o.z, o.z, ss);
+                ss = fmaf(o.w, o.w, ss);
+            }
+        }
+        for (int n = 4 * (threadIdx.x + RR * blockDim.x); n < N; n += 4 * blockDim.x) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float v = combine_one<EPI>(Y2, Y2b, s, (size_t)t * N + n + e, ((size_t)T + t) * N + n + e,
+                                                 resid + (size_t)t * ldr + n + e);
+                row[n + e] = v;
+                if (y) y[(size_t)t * ldy + n + e] = v;
+                ss = fmaf(v, v, ss);
+            }
+        }
+        split_row_tail(row, ss, t, T, N, w, eps, xs, inv, nullptr, red);
+        return;
+    }
     for (int n = threadIdx.x; n < N; n += blockDim.x) {
         const float v = combine_one<EPI>(Y2, Y2b, s, (size_t)t * N + n, ((size_t)T + t) * N + n,
                                          resid + (size_t)t * ldr + n);
@@ -347,7 +439,8 @@ cudaError_t launch_split_rows(const float *x, int ldx, int T, int K, const float
         configured = true;
     }
     if (smem > 64 * 1024) return cudaErrorInvalidValue;
-    split_rows_kernel<<<T, kSplitThreads, smem, s>>>(x, ldx, T, K, norm_w, eps, xs, inv, xn);
+    const bool v4 = K % 4 == 0 && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    split_rows_kernel<<<T, kSplitThreads, smem, s>>>(x, ldx, T, K, norm_w, eps, xs, inv, xn, v4);
     return cudaGetLastError();
 }
 
@@ -369,20 +462,24 @@ cudaError_t launch_combine_split(int epi, const float *Y2, const float *Y2b, flo
         configured = true;
     }
     const float *r = resid ? resid : Y2;
+    auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool v4 = N % 4 == 0 && a16(Y2) && (!Y2b || a16(Y2b)) && (!y || (ldy % 4 == 0 && a16(y))) &&
+                    (epi != PF_RESID || (ldr % 4 == 0 && a16(resid))) &&
+                    (!(epi == PF_SWIGLU_SLOW || epi == PF_SWIGLU_FAST) || Y2b);
     switch (epi) {
     case PF_STORE:
-        combine_split_kernel<PF_STORE><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs);
+        combine_split_kernel<PF_STORE><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs, v4);
         break;
     case PF_RESID:
-        combine_split_kernel<PF_RESID><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs);
+        combine_split_kernel<PF_RESID><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w, eps, xs, v4);
         break;
     case PF_SWIGLU_SLOW:
         combine_split_kernel<PF_SWIGLU_SLOW><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w,
-                                                                            eps, xs);
+                                                                            eps, xs, v4);
         break;
     case PF_SWIGLU_FAST:
         combine_split_kernel<PF_SWIGLU_FAST><<<T, kSplitThreads, smem, s>>>(Y2, Y2b, inv, T, N, y, ldy, r, ldr, norm_w,
-                                                                            eps, xs);
+                                                                            eps, xs, v4);
         break;
     default: return cudaErrorInvalidValue;
     }

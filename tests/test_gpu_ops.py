@@ -92,6 +92,8 @@ SAMPLER_CASES = [
     (1.0, 1.0, 0),
     (1.3, 0.95, 200),
     (0.5, 0.3, 3),
+    (0.9, 0.99, 256),  # the largest top-k of the radix-select path
+    (0.9, 1.0, 257),   # the smallest top-k of the full sort
 ]
 
 
