@@ -400,12 +400,16 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
     const int pos = a.pos_const + (a.st_b && a.st_pos ? a.st_b[seq].n_past : (a.pos_dev ? *a.pos_dev : 0)) + j;
     const int hd = a.hd;
     const float *row = a.qkv + (size_t)m * a.ld_qkv;
+    const float *row_lo = a.qkv_lo ? a.qkv_lo + (size_t)m * a.ld_qkv : nullptr;
+    const float s_lo = a.qkv_lo ? a.inv[m] : 1.0f;
+    // element i of the row: the stored value, or the combined GEMM halves
+    auto fetch = [&](int i) { return row_lo ? __fadd_rn(row[i], row_lo[i]) * s_lo : row[i]; };
     const bool is_q = head < a.H;
     const int h = is_q ? head : head - a.H;
-    const float *src = is_q ? row + h * hd : row + (a.H + h) * hd;
+    const int src = is_q ? h * hd : (a.H + h) * hd;
     float v[EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) v[e] = src[lane * EPL + e];
+    for (int e = 0; e < EPL; ++e) v[e] = fetch(src + lane * EPL + e);
     const float *nw = is_q ? a.q_norm : a.k_norm;
     if (nw) {
         float ss = 0.f;
@@ -439,11 +443,11 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
     const size_t so = (size_t)seq * a.kv_seq_stride;
     KV *kc = reinterpret_cast<KV *>(a.kcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
     KV *vc = reinterpret_cast<KV *>(a.vcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
-    const float *vsrc = row + (a.H + a.Hkv + h) * hd + lane * EPL;
+    const int vsrc = (a.H + a.Hkv + h) * hd + lane * EPL;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
         kc[e] = to_kv<KV>(v[e]);
-        vc[e] = to_kv<KV>(vsrc[e]);
+        vc[e] = to_kv<KV>(fetch(vsrc + e));
     }
 }
 

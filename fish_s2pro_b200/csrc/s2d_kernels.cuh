@@ -43,6 +43,10 @@ struct GemvArgs {
 struct RopeArgs {
     const float *qkv;    // [M][ld_qkv]: Q | K | V
     int ld_qkv;
+    // With qkv_lo: row m is (qkv[m] + qkv_lo[m]) * inv[m], the two halves of
+    // a rows-path GEMM over the stacked hi / lo rows (the store combine).
+    const float *qkv_lo;
+    const float *inv;
     float *q_out;        // [M][H*hd]
     void *kcache, *vcache; // layer base, [Hkv][max_seq][hd] (half or float)
     int max_seq;

@@ -1186,10 +1186,19 @@ void mark(S2dHandle *h, int cat) {
     h->marks->emplace_back(cat, e);
 }
 
+// Whether rows_linear takes the tcgen05 GEMM for an N x K weight over T rows.
+bool tc_gemm_supported_rows(const S2dHandle *h, int N, int K, int T) {
+    TcGemm g;
+    g.W = reinterpret_cast<const uint16_t *>(16), g.N = N, g.K = K, g.xs = h->pf_xs, g.T = T, g.inv = h->pf_inv;
+    g.y = h->pf_y2, g.ldy = N;
+    return tc_gemm_supported(g);
+}
+
 // y = epilogue(W . x) over the T rows split into pf_xs / pf_inv: the tcgen05
 // GEMM with the epilogue fused when it takes the shape, else cuBLAS over the
 // stacked rows followed by the combine pass.  W2 is the up projection of the
 // SwiGLU forms.
+
 int32_t rows_linear(S2dHandle *h, const uint16_t *W, const uint16_t *W2, int N, int K, int T, int epi, float *y,
                     int ldy, const float *resid, int ldr) {
     TcGemm g;
@@ -1303,11 +1312,20 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
             h->launches += 1;
         }
         presplit = false;
-        if ((rc = rows_linear(h, L.wqkv, nullptr, qo, d, T, PF_STORE, h->pf_qkv, qo, nullptr, 0))) return rc;
+        // On cuBLAS, RoPE reads the GEMM's stacked hi / lo rows itself (the
+        // store combine folded into its loads); the tcgen05 epilogue combines.
+        const bool qkv_fold = !(h->use_tc && tc_gemm_supported_rows(h, qo, d, T));
+        if (qkv_fold) {
+            if ((rc = prefill_gemm(h, L.wqkv, qo, d, T, h->pf_y2))) return rc;
+            mark(h, PC_GEMM);
+        } else if ((rc = rows_linear(h, L.wqkv, nullptr, qo, d, T, PF_STORE, h->pf_qkv, qo, nullptr, 0))) {
+            return rc;
+        }
         // QK-norm (Slow-AR) + RoPE + KV write for every row
         uint8_t *base = reinterpret_cast<uint8_t *>(rp.kv) + (size_t)l * layer_bytes;
         RopeArgs r{};
         r.qkv = h->pf_qkv, r.ld_qkv = qo, r.q_out = h->pf_q;
+        if (qkv_fold) r.qkv = h->pf_y2, r.qkv_lo = h->pf_y2 + (size_t)T * qo, r.inv = h->pf_inv;
         r.kcache = base, r.vcache = base + layer_bytes / 2, r.max_seq = rp.max_seq;
         if (!is_fast) r.q_norm = L.q_norm, r.k_norm = L.k_norm;
         r.rope_denom = is_fast ? h->rope_fast : h->rope_slow;
