@@ -290,6 +290,177 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
     if (threadIdx.x == 0) a.counters[(size_t)m * a.Hkv + kvh] = 0;
 }
 
+// One staged chunk of KC positions for one warp's 16 MMA rows: scores
+// against the chunk's K rows (positions at or past kmax, a per-row limit,
+// masked), the base-2 online softmax of the running (mrun, lrun), and the
+// P . V accumulation into o.  Rows g and 8 + g hold the f16 hi / lo halves of
+// the same query, as in the decode kernel above.
+template <int HD, int KC>
+__device__ __forceinline__ void mma_chunk(const uint8_t *kt, const uint8_t *vt, const uint32_t (&qa)[HD / 16][4],
+                                          float qdown, int kmax, int lane, float &mrun, float &lrun,
+                                          float (&o)[HD / 8][4]) {
+    constexpr int NP = KC / 8, NO = HD / 8, PITCH = HD * 2 + 16;
+    const int t = lane & 3;
+    float s[NP][4];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) s[p][0] = s[p][1] = s[p][2] = s[p][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 32; ++kk) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            uint32_t b[4];
+            ldsm_x4(b, kt + (p * 8 + (lane & 7)) * PITCH + (kk * 32 + (lane >> 3) * 8) * 2);
+            mma_16816(s[p], qa[2 * kk], b[0], b[1]);
+            mma_16816(s[p], qa[2 * kk + 1], b[2], b[3]);
+        }
+    }
+    float sc[NP][2], mx = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const float v = (s[p][e] + s[p][2 + e]) * qdown;
+            sc[p][e] = p * 8 + 2 * t + e < kmax ? v : -INFINITY;
+            mx = fmaxf(mx, sc[p][e]);
+        }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(mrun, mx);
+    // a row with every position of the chunk masked keeps its state
+    const float corr = mnew == -INFINITY ? 1.f : exp2f(mrun - mnew);
+    float psum = 0.f;
+    uint32_t pa[KC / 16][4];
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        const float p0 = mnew == -INFINITY ? 0.f : exp2f(sc[p][0] - mnew);
+        const float p1 = mnew == -INFINITY ? 0.f : exp2f(sc[p][1] - mnew);
+        psum += p0 + p1;
+        split_half2(p0, p1, pa[p >> 1][(p & 1) * 2], pa[p >> 1][(p & 1) * 2 + 1]);
+    }
+    mrun = mnew;
+    lrun = fmaf(lrun, corr, psum);
+#pragma unroll
+    for (int jn = 0; jn < NO; ++jn) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[jn][e] *= corr;
+    }
+#pragma unroll
+    for (int k2 = 0; k2 < KC / 16; ++k2) {
+#pragma unroll
+        for (int nd = 0; nd < HD / 16; ++nd) {
+            uint32_t b[4];
+            ldsm_x4_trans(b, vt + (16 * k2 + (lane & 7) + ((lane >> 3) & 1) * 8) * PITCH +
+                                 (nd * 16 + (lane >> 4) * 8) * 2);
+            mma_16816(o[2 * nd], pa[k2], b[0], b[1]);
+            mma_16816(o[2 * nd + 1], pa[k2], b[2], b[3]);
+        }
+    }
+}
+
+// Causal attention of one prompt chunk (T consecutive rows of one sequence
+// at positions pos_const + m; the prefill case of the rows attention,
+// forward_prefill_sequence, slow_ar.rs:579-593) on the tensor cores.  Grid
+// (query tile, kv head); the 8 warps of a block take 8 / rep tokens each, so
+// a warp's 8 MMA rows are its tokens' rep query heads (f16 hi; rows 8 + r the
+// lo halves).  The block stages 32-position K/V chunks in a two-stage cp.async
+// ring shared by its warps, up to its last token's position; a warp scores a
+// chunk only while it holds one of its tokens' visible positions, and each
+// row masks the positions past its own.  Tiles run last first (the longest
+// causal ranges start in the first wave).
+template <int HD>
+__global__ void __launch_bounds__(256, 2) prefill_mma_attn_kernel(const RowsAttnArgs a) {
+    constexpr int KC = 32, KS = HD / 16, NO = HD / 8, UNITS = HD * 2 / 16, PITCH = HD * 2 + 16;
+    constexpr int STAGE = 2 * KC * PITCH;
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int nw = blockDim.x >> 5;
+    const int rep = a.H / a.Hkv, tpw = 8 / rep, qb = nw * tpw;
+    const int ntiles = (a.T + qb - 1) / qb;
+    const int tile = ntiles - 1 - (int)blockIdx.x, kvh = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int m0 = tile * qb, mlast = min(m0 + qb, a.T) - 1;
+    const int vis_end = min(a.pos_const + mlast + 1, a.max_seq);
+    const int wm0 = m0 + warp * tpw, wlast = min(wm0 + tpw, a.T) - 1;
+    const int wend = wlast >= wm0 ? min(a.pos_const + wlast + 1, a.max_seq) : 0;
+    const int mrow = wm0 + g / rep, h = kvh * rep + g % rep;
+    const bool row_ok = mrow < a.T;
+    const int prow = a.pos_const + mrow;
+
+    const size_t so = (size_t)kvh * a.max_seq * (HD * 2);
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + so;
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
+    const int nchunks = (vis_end + KC - 1) / KC;
+    auto issue = [&](int c, int stg) {
+        uint8_t *kt = sm + (size_t)stg * STAGE, *vt = kt + KC * PITCH;
+        for (int u = threadIdx.x; u < KC * UNITS; u += blockDim.x) {
+            const int r = u / UNITS, cc = u - r * UNITS, key = c * KC + r;
+            const bool valid = key < vis_end;
+            const size_t src = (size_t)(valid ? key : 0) * (HD * 2) + cc * 16;
+            cp_async16_zfill(kt + r * PITCH + cc * 16, kb + src, valid);
+            cp_async16_zfill(vt + r * PITCH + cc * 16, vb + src, valid);
+        }
+        commit_group();
+    };
+    if (nchunks > 0) issue(0, 0);
+
+    // Q fragments of row g (token mrow, head h), pre-scaled as in the decode kernel
+    uint32_t qa[KS][4];
+    float qv[KS][4];
+    float amax = 0.f;
+    const float qmul = a.scale * 1.4426950408889634f;  // log2(e)
+    {
+        const float *qrow = a.q + (size_t)(row_ok ? mrow : 0) * a.H * HD + (size_t)h * HD;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+            float2 v0 = make_float2(0.f, 0.f), v1 = v0;
+            if (row_ok) {
+                v0 = *reinterpret_cast<const float2 *>(qrow + 16 * k + 2 * t);
+                v1 = *reinterpret_cast<const float2 *>(qrow + 16 * k + 2 * t + 8);
+            }
+            qv[k][0] = v0.x * qmul, qv[k][1] = v0.y * qmul, qv[k][2] = v1.x * qmul, qv[k][3] = v1.y * qmul;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fabsf(qv[k][e]));
+        }
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    int ex = 0;
+    frexpf(amax, &ex);
+    const float qup = ldexpf(1.f, 14 - ex), qdown = ldexpf(1.f, ex - 14);
+#pragma unroll
+    for (int k = 0; k < KS; ++k) {
+        split_half2(qv[k][0] * qup, qv[k][1] * qup, qa[k][0], qa[k][1]);
+        split_half2(qv[k][2] * qup, qv[k][3] * qup, qa[k][2], qa[k][3]);
+    }
+    float o[NO][4];
+#pragma unroll
+    for (int j = 0; j < NO; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float mrun = -INFINITY, lrun = 0.f;
+
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + 1 < nchunks) issue(c + 1, (c + 1) & 1);
+        else commit_group();
+        wait_group<1>();
+        __syncthreads();  // chunk c visible to every warp
+        const int c0 = c * KC;
+        if (c0 < wend) {
+            const uint8_t *kt = sm + (size_t)(c & 1) * STAGE;
+            mma_chunk<HD, KC>(kt, kt + KC * PITCH, qa, qdown, row_ok ? prow + 1 - c0 : KC, lane, mrun, lrun, o);
+        }
+        __syncthreads();  // every warp's reads done before the stage is refilled
+    }
+    wait_group<0>();
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
+    lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
+    if (!row_ok) return;
+    const float inv_l = 1.f / lrun;
+    float *out = a.out + (size_t)mrow * a.H * HD + (size_t)h * HD;
+#pragma unroll
+    for (int jn = 0; jn < NO; ++jn)
+        *reinterpret_cast<float2 *>(out + jn * 8 + 2 * t) =
+            make_float2((o[jn][0] + o[jn][2]) * inv_l, (o[jn][1] + o[jn][3]) * inv_l);
+}
+
 template <int HD, int NST, int KC>
 cudaError_t decode_mma_launch(const RowsAttnArgs &a, int warps, cudaStream_t s) {
     constexpr int PITCH = HD * 2 + 16;
@@ -332,6 +503,36 @@ cudaError_t launch_decode_mma_attention(const RowsAttnArgs &a, cudaStream_t s) {
     if (a.hd == 64)
         return nst == 3 ? decode_mma_launch<64, 3, 16>(a, warps, s) : decode_mma_launch<64, 2, 16>(a, warps, s);
     return nst == 3 ? decode_mma_launch<128, 3, 16>(a, warps, s) : decode_mma_launch<128, 2, 16>(a, warps, s);
+}
+
+bool prefill_mma_supported(const RowsAttnArgs &a, bool kv_half) {
+    const int rep = a.Hkv > 0 ? a.H / a.Hkv : 0;
+    return kv_half && !a.st && a.S == 1 && a.rows_per_seq >= a.T && a.T >= 1 && (a.hd == 64 || a.hd == 128) &&
+           a.Hkv > 0 && a.H % a.Hkv == 0 && rep >= 1 && 8 % rep == 0 && a.q &&
+           (reinterpret_cast<uintptr_t>(a.q) & 7) == 0 && (reinterpret_cast<uintptr_t>(a.out) & 7) == 0 &&
+           (reinterpret_cast<uintptr_t>(a.kcache) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.vcache) & 15) == 0 &&
+           a.pos_const >= 0 && a.max_seq > 0;
+}
+
+cudaError_t launch_prefill_mma_attention(const RowsAttnArgs &a, cudaStream_t s) {
+    if (a.T <= 0) return cudaSuccess;
+    const int rep = a.H / a.Hkv, qb = 8 * (8 / rep);
+    const unsigned tiles = (unsigned)((a.T + qb - 1) / qb);
+    const size_t smem = (size_t)2 * 2 * 32 * (a.hd * 2 + 16);
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(prefill_mma_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             64 * 1024);
+        if (!e)
+            e = cudaFuncSetAttribute(prefill_mma_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     64 * 1024);
+        if (e) return e;
+        configured = true;
+    }
+    if (a.Hkv > 65535) return cudaErrorInvalidValue;
+    if (a.hd == 64) prefill_mma_attn_kernel<64><<<dim3(tiles, a.Hkv), 256, smem, s>>>(a);
+    else prefill_mma_attn_kernel<128><<<dim3(tiles, a.Hkv), 256, smem, s>>>(a);
+    return cudaGetLastError();
 }
 
 }  // namespace s2d

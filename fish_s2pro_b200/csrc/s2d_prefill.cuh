@@ -59,6 +59,7 @@ struct RowsAttnArgs {
     int decode_warps;    // its warps per block, 2 or 4
     int decode_chunk;    // its positions per staged chunk, 16 or 32
     const int32_t *row_order;  // its block order: row of each rank (longest context first), or nullptr
+    int prefill_mma;     // prompt chunks (one sequence's consecutive rows, f16 cache): the tensor-core kernel
 };
 cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
 // The batched step's attention on the tensor cores (s2d_decode_attn.cu):
@@ -66,5 +67,10 @@ cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStrea
 // dim 64 or 128, up to 8 query heads per kv head.
 bool decode_mma_supported(const RowsAttnArgs &a, bool kv_half);
 cudaError_t launch_decode_mma_attention(const RowsAttnArgs &a, cudaStream_t s);
+// A prompt chunk's causal attention on the tensor cores (s2d_decode_attn.cu):
+// one sequence's consecutive rows (rows_per_seq >= T, no st), S == 1, f16
+// caches, head dim 64 or 128, a GQA group of 1, 2, 4 or 8 heads.
+bool prefill_mma_supported(const RowsAttnArgs &a, bool kv_half);
+cudaError_t launch_prefill_mma_attention(const RowsAttnArgs &a, cudaStream_t s);
 
 }  // namespace s2d

@@ -148,6 +148,7 @@ struct S2dHandle {
     int attn_mma_blocks_per_sm = 2;     // its blocks per SM when choosing splits (S2D_DECODE_BLOCKS)
     int attn_mma_chunk = 16;            // its positions per staged chunk, 16 or 32 (S2D_DECODE_CHUNK)
     int attn_mma_order = 1;             // its blocks longest context first (S2D_DECODE_ORDER)
+    int prefill_mma = 1;                // prompt-chunk attention on the tensor cores (S2D_PREFILL_MMA)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
@@ -1341,6 +1342,7 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.st_pos = rp.st_pos, t.pos_const = rp.pos_const, t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd;
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters, t.decode_stages = h->attn_stages;
+        t.prefill_mma = h->prefill_mma;
         if (h->attn_mma && rp.st && rp.st_pos && rp.rps == 1) {
             t.decode_mma = 1, t.decode_warps = h->attn_mma_warps, t.decode_stages = h->attn_mma_stages;
             t.decode_chunk = h->attn_mma_chunk, t.row_order = rp.order;
@@ -1761,6 +1763,7 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         if (const char *v = getenv("S2D_DECODE_BLOCKS")) h->attn_mma_blocks_per_sm = std::max(1, std::min(64, atoi(v)));
         if (const char *v = getenv("S2D_DECODE_CHUNK")) h->attn_mma_chunk = atoi(v) == 32 ? 32 : 16;
         if (const char *v = getenv("S2D_DECODE_ORDER")) h->attn_mma_order = atoi(v) != 0;
+        if (const char *v = getenv("S2D_PREFILL_MMA")) h->prefill_mma = atoi(v) != 0;
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -2484,6 +2487,38 @@ int32_t s2d_op_batch_attention(S2dHandle *h, const float *q, const uint16_t *kca
     if (impl == 0 && !decode_mma_supported(t, true))
         return set_err(h, S2D_EINVAL, "the tensor-core attention does not take these arguments");
     CK(launch_rows_attention(t, true, h->stream));
+    CK(cudaMemcpyAsync(out, dout.p, nq * 4, cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return S2D_OK;
+}
+
+int32_t s2d_op_prefill_attention(S2dHandle *h, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                                 int64_t T, int64_t H, int64_t Hkv, int64_t head_dim, int64_t max_seq, int64_t pos0,
+                                 int32_t impl, float *out) {
+    if (!h) return S2D_EINVAL;
+    if (!q || !kcache || !vcache || !out || T <= 0 || T > 4096 || Hkv <= 0 || H % Hkv || H / Hkv > 8 ||
+        (head_dim != 64 && head_dim != 128) || max_seq <= 0 || max_seq > (1 << 20) || pos0 < 0 ||
+        pos0 + T > max_seq || impl < 0 || impl > 1)
+        return set_err(h, S2D_EINVAL, "s2d_op_prefill_attention: bad arguments");
+    CK(cudaSetDevice(h->device));
+    const size_t kvn = (size_t)Hkv * max_seq * head_dim, nq = (size_t)T * H * head_dim;
+    DevBuf dq, dk, dv, dout;
+    CK(cudaMalloc(&dq.p, nq * 4));
+    CK(cudaMalloc(&dk.p, kvn * 2));
+    CK(cudaMalloc(&dv.p, kvn * 2));
+    CK(cudaMalloc(&dout.p, nq * 4));
+    CK(cudaMemcpyAsync(dq.p, q, nq * 4, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dk.p, kcache, kvn * 2, cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemcpyAsync(dv.p, vcache, kvn * 2, cudaMemcpyHostToDevice, h->stream));
+    RowsAttnArgs t{};
+    t.q = (const float *)dq.p, t.kcache = dk.p, t.vcache = dv.p, t.kv_seq_stride = 0, t.max_seq = (int)max_seq;
+    t.out = (float *)dout.p, t.T = (int)T, t.rows_per_seq = (int)T, t.st = nullptr, t.st_pos = 0;
+    t.pos_const = (int)pos0, t.H = (int)H, t.Hkv = (int)Hkv, t.hd = (int)head_dim;
+    t.scale = 1.0f / sqrtf((float)head_dim), t.S = 1, t.decode_stages = 2, t.prefill_mma = impl == 0;
+    if (impl == 0 && !prefill_mma_supported(t, true))
+        return set_err(h, S2D_EINVAL, "the tensor-core prefill attention does not take these arguments");
+    if (impl == 0) CK(launch_prefill_mma_attention(t, h->stream));
+    else CK(launch_rows_attention(t, true, h->stream));
     CK(cudaMemcpyAsync(out, dout.p, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     CK(cudaStreamSynchronize(h->stream));
     return S2D_OK;

@@ -129,6 +129,9 @@ SIGNATURES = {
     "s2d_op_rows_linear_f16": (ctypes.c_int32, [ctypes.c_void_p, _f32p, ctypes.c_int64, ctypes.c_int64,
                                                 _u16p, _u16p, ctypes.c_int64, _f32p, ctypes.c_int32,
                                                 ctypes.c_int32, _f32p]),
+    "s2d_op_prefill_attention": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _u16p, _u16p, ctypes.c_int64,
+                                                  ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                                  ctypes.c_int64, ctypes.c_int32, _f32p]),
     "s2d_op_batch_attention": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _u16p, _u16p, ctypes.c_int64,
                                                 ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                 _i32p, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p]),

@@ -273,6 +273,15 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
  * (GGUF little-endian bits), i.e. matvec_f16_streaming (tensor.rs:220-264). */
 int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *weight_f16,
                           int64_t in_dim, int64_t out_dim, float *out);
+/* The causal attention of forward_prefill_sequence (slow_ar.rs:579-593):
+ * T query rows of one sequence, row m at position pos0 + m attending over
+ * positions 0..pos0 + m of kcache / vcache [Hkv][max_seq][head_dim] (f16
+ * bits); q and out [T][H][head_dim] f32.  impl 0: the tensor-core kernel;
+ * 1: the CUDA-core kernels (tiled for T >= 16).  pos0 + T <= max_seq,
+ * T <= 4096, head_dim 64 or 128, H / Hkv <= 8, host buffers. */
+int32_t s2d_op_prefill_attention(S2dHandle *h, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                                 int64_t T, int64_t H, int64_t Hkv, int64_t head_dim, int64_t max_seq,
+                                 int64_t pos0, int32_t impl, float *out);
 /* gqa_decode_attention + softmax_in_place (attention.rs:208-309) for B
  * sequences at once, the batched Slow-AR step's attention: q [B][H][head_dim]
  * f32; kcache / vcache [B][Hkv][max_seq][head_dim] f16 bits; sequence b's

@@ -152,3 +152,56 @@ def test_batch_attention_kernel_variants(tiny_gguf, monkeypatch, env):
             assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < TOL
     finally:
         s.close()
+
+
+# ---- prompt-chunk (prefill) attention ---------------------------------------
+
+def run_prefill(st, q, k, v, pos0, impl):
+    import ctypes
+
+    from fish_s2pro_b200 import lib
+    from fish_s2pro_b200.s2d import _P
+    T, H, hd = q.shape
+    Hkv, max_seq = k.shape[0], k.shape[1]
+    out = np.zeros_like(q)
+    rc = lib().s2d_op_prefill_attention(
+        st.handle, q.ctypes.data_as(_P(ctypes.c_float)), k.view(np.uint16).ctypes.data_as(_P(ctypes.c_uint16)),
+        v.view(np.uint16).ctypes.data_as(_P(ctypes.c_uint16)), T, H, Hkv, hd, max_seq, pos0, impl,
+        out.ctypes.data_as(_P(ctypes.c_float)))
+    assert rc == 0, lib().s2d_last_error(st.handle)
+    return out
+
+
+def reference_prefill(q, k, v, pos0):
+    T, H, hd = q.shape
+    rep = H // k.shape[0]
+    out = np.zeros((T, H, hd))
+    for m in range(T):
+        n = pos0 + m + 1
+        for h in range(H):
+            s = k[h // rep, :n].astype(np.float64) @ q[m, h].astype(np.float64) / np.sqrt(hd)
+            p = np.exp(s - s.max())
+            out[m, h] = (p / p.sum()) @ v[h // rep, :n].astype(np.float64)
+    return out
+
+
+PREFILL_CASES = [  # T, H, Hkv, hd, max_seq, pos0
+    (16, 8, 2, 64, 64, 0),
+    (40, 32, 8, 128, 96, 0),
+    (37, 32, 8, 128, 200, 100),   # a later chunk, ragged tile
+    (64, 16, 2, 64, 700, 600),
+    (33, 8, 8, 128, 80, 7),       # one head per group (8 tokens per warp)
+    (48, 16, 8, 128, 90, 20),     # two heads per group
+]
+
+
+@pytest.mark.parametrize("T,H,Hkv,hd,max_seq,pos0", PREFILL_CASES)
+@pytest.mark.parametrize("impl", [0, 1])
+def test_prefill_attention_matches_float_reference(st, T, H, Hkv, hd, max_seq, pos0, impl):
+    rng = np.random.default_rng(T * 3 + H + hd + pos0)
+    q = (rng.standard_normal((T, H, hd)) * 2.0).astype(np.float32)
+    k = rng.standard_normal((Hkv, max_seq, hd)).astype(np.float16)
+    v = rng.standard_normal((Hkv, max_seq, hd)).astype(np.float16)
+    want = reference_prefill(q, k, v, pos0)
+    got = run_prefill(st, q, k, v, pos0, impl)
+    assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < TOL
