@@ -374,7 +374,7 @@ def run_ours(args, d: Dist):
     return line
 
 
-def run_batch(args, d: Dist, wl):
+def run_batch(args, d: Dist, wl, name=None):
     """Batched workload (C4): every rank generates for `wl.batch` independent
     prompts at once through s2d_generate_codes_batch; one step = one call
     (every sequence's prefill + `frames` frames of all sequences)."""
@@ -436,7 +436,7 @@ def run_batch(args, d: Dist, wl):
         "ms_per_step": round(wall / args.steps * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": f"synthetic (seeded random-init S2-Pro-shaped GGUF, {B} seeded prompts)",
-        "config": {"workload": f"{args.workload}: full-size f16 S2-Pro-shaped Dual-AR, {B} sequences, "
+        "config": {"workload": f"{name or args.workload}: full-size f16 S2-Pro-shaped Dual-AR, {B} sequences, "
                                f"prompt lengths {min(lens)}..{max(lens)} (uniform "
                                f"{wl.prompt_len_min}..{wl.prompt_len}), {frames} frames each, "
                                f"T {gp['temperature']} top-p {gp['top_p']} top-k {gp['top_k']}, "
@@ -516,7 +516,7 @@ def main():
         # C2 run also measures the batch-64 workload (C4) and nests its line
         if args.workload == "C2" and not args.tp and not args.no_batch64:
             try:
-                b = run_batch(args, d, configs.C4)
+                b = run_batch(args, d, configs.C4, name="C4")
                 line["batch64"] = {k: b[k] for k in ("metric", "value", "unit", "n_gpus", "ms_per_step",
                                                      "ms_per_frame_step", "prefill_ms", "e2e", "gpu_launches",
                                                      "roofline", "config", "clocks")}
