@@ -8,7 +8,7 @@ softmax weights to the MMAs as f16 hi + lo pairs (about 22 bits) with f32
 accumulation, so both kernels match the float64 result to ~1e-6 of
 max|out|; the bound below (2e-5) is far under what a fragment-layout,
 masking or merge error gives.  Cases cover head dims 64 / 128, GQA groups of
-1, 4 and 8 heads, context lengths from 1 to past 4,000 positions (partial
+1, 2, 4 and 8 heads, context lengths from 1 to past 4,000 positions (partial
 last chunks, more warps and splits than chunks), explicit split counts, and
 finished sequences.
 """
@@ -77,6 +77,7 @@ CASES = [  # B, H, Hkv, hd, max_seq, positions
     (4, 32, 8, 128, 1100, (1000, 33, 64, 1099)),
     (2, 8, 8, 128, 300, (299, 17)),
     (2, 16, 2, 64, 4200, (4199, 2500)),
+    (3, 8, 1, 128, 120, (119, 0, 64)),  # one kv head for 8 query heads
 ]
 
 
@@ -192,6 +193,7 @@ PREFILL_CASES = [  # T, H, Hkv, hd, max_seq, pos0
     (64, 16, 2, 64, 700, 600),
     (33, 8, 8, 128, 80, 7),       # one head per group (8 tokens per warp)
     (48, 16, 8, 128, 90, 20),     # two heads per group
+    (20, 8, 1, 64, 50, 30),       # eight heads per group (one token per warp)
 ]
 
 
