@@ -62,3 +62,22 @@ def test_workload_byte_model():
     assert b["lm_head"] == 20_976_640
     assert b["fast"] == 9 * (807_403_520 + 20_971_520)
     assert configs.kv_bytes_per_position(configs.C2.model) == 147_456
+
+
+def header_param_counts():
+    """Parameter count of every s2d_* declaration in include/s2d.h."""
+    text = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "s2d.h").read_text(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(s2d_\w+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+        p = " ".join(params.split())
+        out[name] = 0 if p in ("", "void") else p.count(",") + 1
+    return out
+
+
+def test_python_signatures_match_header_arity():
+    """Each ctypes binding passes as many arguments as the C declaration takes."""
+    from fish_s2pro_b200 import s2d
+    counts = header_param_counts()
+    assert sorted(counts) == sorted(s2d.SIGNATURES)
+    wrong = {n: (len(s2d.SIGNATURES[n][1]), c) for n, c in counts.items() if len(s2d.SIGNATURES[n][1]) != c}
+    assert not wrong, wrong
