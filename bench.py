@@ -27,9 +27,13 @@ One step = one generate_codes call (prefill + 256 frames).  Reported:
              MEASURED_PEAKS.json.  The Fast-AR pass program is listed beside it.
   cpu_baseline  the CPU oracle (port of the reference's algorithm) on a
              bounded sample of the same workload, rank 0, N = 1 only.
-Multi-GPU: every rank decodes its own utterance (independent replicas,
-weak scaling); the only collectives are the barrier and the max of the
-timings.
+Nested lines (N = 1): "q8_0" (C3) and "q4_k" (C5), the quantized batch-1
+configurations, timed over min(steps, 5) steps each (--no-quant skips them).
+Multi-GPU (torchrun, N > 1): the headline line is the Slow-AR tensor-parallel
+run (all ranks decode one utterance, heads and FFN columns sharded, NCCL
+allreduce per residual add; "scaling": "strong"); the independent-replica run
+(every rank decodes its own utterance, weak scaling, no data-path collective)
+is nested under "replicas".  --replicas makes the replica run the headline.
 """
 from __future__ import annotations
 
@@ -79,7 +83,11 @@ def parse():
                     help="skip the batch-64 (C4) measurement that the default C2 run adds to its line")
     ap.add_argument("--tp", action="store_true",
                     help="under torchrun: all ranks form one tensor-parallel Slow-AR decoding one "
-                         "utterance (strong scaling) instead of independent replicas")
+                         "utterance (strong scaling); the default under torchrun")
+    ap.add_argument("--replicas", action="store_true",
+                    help="under torchrun: independent replicas (weak scaling) as the headline line")
+    ap.add_argument("--no-quant", action="store_true",
+                    help="skip the nested C3 (Q8_0) and C5 (Q4_K) lines of the default N = 1 run")
     return ap.parse_args()
 
 
@@ -242,27 +250,34 @@ def oracle_frames(model_path, wl, frames: int, warmup: int, prompt_len: int, see
 # arms
 # ---------------------------------------------------------------------------
 
-def ensure_model(d: Dist, wl, model_dir) -> Path:
+def ensure_model(d, wl, model_dir, lib_path=None) -> Path:
+    """The workload's synthetic GGUF, written once per host (local rank 0)
+    with the writer at lib_path (default: the package's, see synth._load)."""
     from fish_s2pro_b200 import synth
-    if d.rank == 0 or d.local == 0:
-        path = synth.cached_gguf(wl.model, model_dir)
+    if d.local == 0:
+        synth.cached_gguf(wl.model, model_dir, lib_path)
     d.barrier()
-    path = synth.cached_gguf(wl.model, model_dir)
-    return path
+    return synth.cached_gguf(wl.model, model_dir, lib_path)
 
 
-def run_ours(args, d: Dist):
+def run_ours(args, d: Dist, wl_name=None, use_tp=False, steps=None, warmup=None, cpu_baseline=True):
+    """Batch-1 generation of workload wl_name (default args.workload): one
+    utterance per rank (replicas) or, with use_tp under torchrun, one
+    utterance over all ranks (Slow-AR tensor parallelism)."""
     from fish_s2pro_b200 import (FastArWeights, GenerateParams, PromptTensor, SeededRng,
                                  SlowArState, build, generate_codes)
     build.build_runtime()
-    wl = {**configs.WORKLOADS, **configs.PROFILING}[args.workload]
+    wl_name = wl_name or args.workload
+    wl = {**configs.WORKLOADS, **configs.PROFILING}[wl_name]
     if args.prompt_len:
         wl = configs.Workload(wl.model, args.prompt_len, wl.frames, wl.prompt_seed, wl.im_end_id)
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     frames = args.frames or wl.frames
     m = wl.model
     path = ensure_model(d, wl, args.model_dir)
     tp = None
-    if args.tp and d.world > 1:
+    if use_tp and d.world > 1:
         from fish_s2pro_b200 import nccl_unique_id
         tp = (d.world, d.rank, d.bcast_bytes(nccl_unique_id() if d.rank == 0 else None))
     st = SlowArState.open(path, max_seq_len=wl.prompt_len + frames + 8, device=d.local, tp=tp)
@@ -281,14 +296,14 @@ def run_ours(args, d: Dist):
     def one(seed):
         return generate_codes(st, gp["im_end_id"], spec, pt, params, fw, SeededRng(seed))
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         one(i)
     clocks = Clocks(d.local)
     d.barrier()
     device_sync()
     clocks.start()
     t0 = time.perf_counter()
-    results = [one(100 + i) for i in range(args.steps)]
+    results = [one(100 + i) for i in range(steps)]
     device_sync()
     t1 = time.perf_counter()
     d.barrier()
@@ -315,7 +330,7 @@ def run_ours(args, d: Dist):
                                    (2, "fast_pass", bpf["fast"] / passes)):
             ms = statistics.median(st.profile_engine(prog, trace=False)[0] for _ in range(7))
             kern[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6}
-    top = kern.get("slow_step", {"ms": float("nan"), "bytes": 0.0, "gbs": float("nan")})
+    top = kern.get("slow_step")
     p_avg = wl.prompt_len + frames / 2
     frame_bytes = sum(bpf.values()) + configs.kv_bytes_per_position(m) * p_avg
     # HBM bytes each GPU streams per second: a replica streams whole frames;
@@ -329,18 +344,19 @@ def run_ours(args, d: Dist):
         gpu_gbs = frame_bytes * value / d.world / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": d.world,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(wall / args.steps * 1e3, 2),
+        "steps": steps, "warmup": warmup,
+        "ms_per_step": round(wall / steps * 1e3, 2),
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": WTYPE[m.linear_type],
         "data": f"synthetic (seeded random-init S2-Pro-shaped GGUF, seeded {wl.prompt_len}-id prompt)",
-        "config": {"workload": f"{args.workload}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, "
+        "config": {"workload": f"{wl_name}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, "
                                f"{wl.prompt_len}-token prompt, greedy {frames} frames, batch 1",
-                   "global_batch": d.world, "seq_len": wl.prompt_len + frames,
+                   "global_batch": 1 if tp else d.world, "seq_len": wl.prompt_len + frames,
                    "parallelism": (f"tp{d.world} (Slow-AR heads and FFN columns sharded, NCCL "
                                    "allreduce after wo and w2; Fast-AR replicated)") if tp
                                   else f"replicas x{d.world} (independent utterances)",
-                   "l2": "inputs larger than L2 (each frame streams ~14.8 GB of weights)"},
+                   "l2": f"inputs larger than L2 (each frame streams {frame_bytes / 1e9:.2f} GB of "
+                         f"{WTYPE[m.linear_type]} weights and KV rows; L2 is 0.126 GB)"},
         "e2e": {"value": round(e2e, 2), "unit": UNIT,
                 "h2d_bytes_per_step": int(prompt.nbytes),
                 "d2h_bytes_per_step": int(m.num_codebooks * frames * 4 + 40)},
@@ -349,38 +365,47 @@ def run_ours(args, d: Dist):
         "frame_bytes": int(frame_bytes),
         "frame_gbs": round(gpu_gbs, 1),
         "frame_roofline_frac": round(gpu_gbs / pk["hbm_gbs"], 3),
-        "roofline": {"bound": "hbm", "kernel": "engine_kernel, Slow-AR step program (36 layers + masked LM head)",
-                     "achieved": round(top["gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(top["gbs"] / pk["hbm_gbs"], 3),
-                     "traffic": (int(top["bytes"] * ENGINE_TRAFFIC_RATIO)
-                                 if top["bytes"] and m.linear_type == configs.GGML_F16 else None),
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 4-layer "
-                                       "C2S Slow-AR step (1.019 x its algorithmic bytes), scaled to "
-                                       "this step's algorithmic bytes",
-                     "peak_source": pk["source"],
-                     "bytes_per_launch": int(top["bytes"]),
-                     "kernels": {k: {"us": round(v["ms"] * 1e3, 2), "gbs": round(v["gbs"], 1),
-                                     "bytes": int(v["bytes"])} for k, v in kern.items()}},
+        "roofline": ({"bound": "hbm", "kernel": f"engine_kernel, Slow-AR step program ({m.slow_layers} "
+                                                "layers + masked LM head)",
+                      "achieved": round(top["gbs"], 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                      "frac": round(top["gbs"] / pk["hbm_gbs"], 3),
+                      "traffic": (int(top["bytes"] * ENGINE_TRAFFIC_RATIO)
+                                  if m.linear_type == configs.GGML_F16 else None),
+                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 4-layer "
+                                        "C2S Slow-AR step (1.019 x its algorithmic bytes), scaled to "
+                                        "this step's algorithmic bytes",
+                      "peak_source": pk["source"],
+                      "bytes_per_launch": int(top["bytes"]),
+                      "kernels": {k: {"us": round(v["ms"] * 1e3, 2), "gbs": round(v["gbs"], 1),
+                                      "bytes": int(v["bytes"])} for k, v in kern.items()}}
+                     if top else
+                     {"bound": "hbm", "kernel": "whole frame on each rank (tensor-parallel Slow-AR: the "
+                                                "rank's weight and KV shard, replicated LM head and Fast-AR)",
+                      "achieved": round(gpu_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                      "frac": round(gpu_gbs / pk["hbm_gbs"], 3), "traffic": None,
+                      "peak_source": pk["source"]}),
         "clocks": ck,
     }
-    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+    if cpu_baseline and d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         spf, cores, _ = oracle_frames(path, wl, frames=2, warmup=0, prompt_len=16)
         line["cpu_baseline"] = {
             "value": round(1.0 / spf, 4), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": "2 decode frames after a 16-token prefill of the same C2 model, "
+            "sample": f"2 decode frames after a 16-token prefill of the same {wl_name} model, "
                       "reference-faithful CPU oracle (f32 re-expansion per step, Fast-AR "
                       "prefix recomputation, full-vocab LM head and sort)"}
     st.close()
     return line
 
 
-def run_batch(args, d: Dist, wl, name=None):
+def run_batch(args, d: Dist, wl, name=None, steps=None, warmup=None):
     """Batched workload (C4): every rank generates for `wl.batch` independent
     prompts at once through s2d_generate_codes_batch; one step = one call
     (every sequence's prefill + `frames` frames of all sequences)."""
     from fish_s2pro_b200 import (RNG_PHILOX, FastArWeights, GenerateParams, PromptTensor,
                                  SeededRng, SlowArState, build, generate_codes_batch)
     build.build_runtime()
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     frames = args.frames or wl.frames
     m = wl.model
     path = ensure_model(d, wl, args.model_dir)
@@ -398,14 +423,14 @@ def run_batch(args, d: Dist, wl, name=None):
         return generate_codes_batch(st, gp["im_end_id"], spec, pts, params, fw,
                                     [SeededRng(0) for _ in ps], rng_kind=RNG_PHILOX, philox_key=key)
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         one(i)
     clocks = Clocks(d.local)
     d.barrier()
     device_sync()
     clocks.start()
     t0 = time.perf_counter()
-    results = [one(100 + i) for i in range(args.steps)]
+    results = [one(100 + i) for i in range(steps)]
     device_sync()
     t1 = time.perf_counter()
     d.barrier()
@@ -425,18 +450,18 @@ def run_batch(args, d: Dist, wl, name=None):
     lens = [p.shape[1] for p in ps]
     # one batched frame step: the weights once, every sequence's KV rows
     step_bytes = bpf["slow"] + bpf["lm_head"] + bpf["fast"] + kv_pos * sum(n + frames / 2 for n in lens)
-    step_s = decode_s / (args.steps * frames) / 1.0
+    step_s = decode_s / (steps * frames)
     achieved = step_bytes / step_s / 1e9
     h2d = int(sum(p.nbytes for p in ps))
     breakdown = {} if args.no_kernel_profile else {
         k: round(v, 3) for k, v in st.profile_batch(B).items()}
     line = {
         "metric": METRIC_BATCH, "value": round(value, 1), "unit": UNIT, "n_gpus": d.world,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(wall / args.steps * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "steps": steps, "warmup": warmup,
+        "ms_per_step": round(wall / steps * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": WTYPE[m.linear_type],
         "data": f"synthetic (seeded random-init S2-Pro-shaped GGUF, {B} seeded prompts)",
-        "config": {"workload": f"{name or args.workload}: full-size f16 S2-Pro-shaped Dual-AR, {B} sequences, "
+        "config": {"workload": f"{name or args.workload}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, {B} sequences, "
                                f"prompt lengths {min(lens)}..{max(lens)} (uniform "
                                f"{wl.prompt_len_min}..{wl.prompt_len}), {frames} frames each, "
                                f"T {gp['temperature']} top-p {gp['top_p']} top-k {gp['top_k']}, "
@@ -468,7 +493,12 @@ def run_reference(args, d: Dist):
     wl = configs.WORKLOADS[args.workload]
     if d.rank != 0:
         return None
-    path = ensure_model(d, wl, args.model_dir)
+    # the model file comes from the oracle's build of the synthetic writer, so
+    # that this process maps only oracle/ libraries
+    synth_lib = ROOT / "oracle" / "libs2o_synth.so"
+    if not synth_lib.exists():
+        subprocess.run(["make", "-C", str(ROOT / "oracle")], check=True, capture_output=True)
+    path = ensure_model(d, wl, args.model_dir, lib_path=synth_lib)
     prompt_len = 16
     spf, cores, t_prefill = oracle_frames(path, wl, frames=max(args.steps, 1),
                                           warmup=args.warmup, prompt_len=prompt_len)
@@ -478,8 +508,9 @@ def run_reference(args, d: Dist):
         "warmup": args.warmup, "ms_per_step": round(spf * 1e3, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random-init S2-Pro-shaped GGUF)",
-        "config": {"workload": f"{args.workload}: full-size f16 S2-Pro-shaped Dual-AR, greedy, "
-                               f"batch 1 (CPU sample: {prompt_len}-token prompt)",
+        "config": {"workload": f"{args.workload}: full-size {WTYPE[wl.model.linear_type]} S2-Pro-shaped "
+                               f"Dual-AR, greedy, batch 1 (CPU sample: {prompt_len}-token prompt instead "
+                               f"of {wl.prompt_len}, one decode frame per step)",
                    "global_batch": 1, "seq_len": prompt_len + args.steps + args.warmup,
                    "parallelism": "host threads"},
         "impl": "reference",
@@ -492,11 +523,19 @@ def run_reference(args, d: Dist):
 
 
 class _Single:
+    """One process and no process group (the CPU reference arm)."""
+    world = 1
     rank = 0
     local = 0
 
     def barrier(self):
         pass
+
+    def max(self, v: float) -> float:
+        return v
+
+    def sum(self, v: float) -> float:
+        return v
 
 
 def main():
@@ -509,19 +548,38 @@ def main():
         print(json.dumps(line), flush=True)
         return 0
     d = Dist(args.gpus)
+    nested_keys = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "dtype",
+                   "scaling", "prefill_ms", "e2e", "gpu_launches", "roofline", "config", "clocks")
     try:
         wl = {**configs.WORKLOADS, **configs.PROFILING}[args.workload]
-        line = run_batch(args, d, wl) if wl.batch > 1 else run_ours(args, d)
+        use_tp = d.world > 1 and (args.tp or not args.replicas) and wl.batch == 1
+        line = run_batch(args, d, wl) if wl.batch > 1 else run_ours(args, d, use_tp=use_tp)
+        default_c2 = args.workload == "C2"
+        # under torchrun the tensor-parallel run heads the line; the replica
+        # run (the same workload, one utterance per rank) is nested beside it
+        if use_tp and default_c2:
+            r = run_ours(args, d, use_tp=False, cpu_baseline=False)
+            line["replicas"] = {k: r[k] for k in nested_keys if k in r}
         # the headline metric is frames/s at batch 1 and batch 64: the default
         # C2 run also measures the batch-64 workload (C4) and nests its line
-        if args.workload == "C2" and not args.tp and not args.no_batch64:
+        if default_c2 and not args.no_batch64:
             try:
-                b = run_batch(args, d, configs.C4, name="C4")
-                line["batch64"] = {k: b[k] for k in ("metric", "value", "unit", "n_gpus", "ms_per_step",
-                                                     "ms_per_frame_step", "prefill_ms", "e2e", "gpu_launches",
-                                                     "roofline", "config", "clocks")}
+                b = run_batch(args, d, configs.C4, name="C4", steps=min(args.steps, 10),
+                              warmup=min(args.warmup, 3))
+                line["batch64"] = {k: b[k] for k in nested_keys + ("ms_per_frame_step",) if k in b}
             except Exception as e:  # the batch-1 line stands on its own
                 line["batch64"] = {"metric": METRIC_BATCH, "error": repr(e)[:300]}
+        # the quantized batch-1 configurations, on one GPU, over a few steps
+        if default_c2 and d.world == 1 and not args.no_quant:
+            for key, name in (("q8_0", "C3"), ("q4_k", "C5")):
+                try:
+                    q = run_ours(args, d, wl_name=name, steps=min(args.steps, 5),
+                                 warmup=min(args.warmup, 3), cpu_baseline=False)
+                    line[key] = {k: q[k] for k in nested_keys if k in q}
+                    line[key]["parity"] = ("quantized parity is pinned to the oracle's restatement of "
+                                           "ggml's published block format only")
+                except Exception as e:
+                    line[key] = {"metric": METRIC, "error": repr(e)[:300]}
         if d.rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -8,6 +8,7 @@
 // caller's device buffers and whose split-K scratch (per-split softmax
 // partials and arrival counters) lives in a file-scope device array below.
 #include <cuda_runtime.h>
+#include <stdint.h>
 #include <stdio.h>
 
 #include <algorithm>
@@ -46,6 +47,14 @@ extern "C" int32_t s2d_op_gqa_decode_attention_noalloc(
         return fail(err, err_cap, S2D_EINVAL, "invalid GQA split or attention dims");
     if (hd % 64 || hd > 256 || H / Hkv > 16)
         return fail(err, err_cap, S2D_EINVAL, "unsupported head_dim or group size");
+    // The kernel reads each lane's head_dim/32 key and value elements as one
+    // float2 (head_dim 64) or float4s, and query and out as single floats.
+    const uintptr_t kv_align = hd == 64 ? 8 : 16;
+    if ((uintptr_t)keys % kv_align || (uintptr_t)values % kv_align || (uintptr_t)query % 4 ||
+        (uintptr_t)out % 4)
+        return fail(err, err_cap, S2D_EINVAL,
+                    "misaligned buffer: keys and values must be 16-byte aligned (8 at head_dim 64), "
+                    "query and out 4-byte aligned");
     // the same split count as s2d_op_gqa_decode_attention, so both give the same result
     const int S = std::max(1, std::min(16, T / 8));
     if ((int64_t)H * S * (hd + 2) > kNoAllocPartFloats || Hkv > kNoAllocCounters) {
@@ -65,6 +74,8 @@ extern "C" int32_t s2d_op_gqa_decode_attention_noalloc(
     {
         // Once per device, with that device current: the host-side name of a
         // __device__ array is not a device address, so look the address up.
+        // The address belongs to the device's primary context; a
+        // cudaDeviceReset ends that context and with it the cached address.
         std::lock_guard<std::mutex> lock(g_setup_mutex);
         if (!g_part_ptr[dev]) {
             void *p = nullptr, *c = nullptr;

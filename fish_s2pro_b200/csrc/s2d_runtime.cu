@@ -1379,8 +1379,9 @@ int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
     return rows_layers(h, false, h->pf_x, h->slow.d, rp);
 }
 
-int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t logits_mode,
-                  uint32_t im_end) {
+// The checks of SlowArState::eval on n_flat time-major ids (slow_ar.rs:456-474)
+// and of embed_slow_ar_time_major (slow_ar.rs:1071-1105, tensor.rs:177-185).
+int32_t check_eval_ids(S2dHandle *h, const int32_t *flat, int64_t n_flat) {
     const S2dGraphSpec &s = h->spec;
     const int64_t cd = s.num_codebooks + 1;
     if (n_flat <= 0 || n_flat % cd)
@@ -1391,7 +1392,6 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
         return set_err(h, S2D_ESTATE, "KV cache overflow: n_past=" + std::to_string(h->n_past) +
                                           " n_tokens=" + std::to_string(n) +
                                           " max_seq_len=" + std::to_string(h->cfg.max_seq));
-    // embed_slow_ar_time_major's id checks (slow_ar.rs:1071-1105, tensor.rs:177-185)
     for (int64_t t = 0; t < n; ++t) {
         const int32_t id = flat[t * cd];
         if (id < 0) return set_err(h, S2D_EINVAL, "semantic token id must be non-negative, got " + std::to_string(id));
@@ -1408,7 +1408,17 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
                                                   std::to_string(s.codebook_rows));
         }
     }
-    int32_t rc = ensure_tokens(h, (size_t)n_flat);
+    return S2D_OK;
+}
+
+int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t logits_mode,
+                  uint32_t im_end) {
+    const S2dGraphSpec &s = h->spec;
+    const int64_t cd = s.num_codebooks + 1;
+    int32_t rc = check_eval_ids(h, flat, n_flat);
+    if (rc) return rc;
+    const int64_t n = n_flat / cd;
+    rc = ensure_tokens(h, (size_t)n_flat);
     if (rc) return rc;
     CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
     if (n >= kPrefillMin) {
@@ -1456,6 +1466,40 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
     rc = check_device_error(h);
     if (rc) return rc;
     h->n_past += (int32_t)n;
+    return S2D_OK;
+}
+
+// One Slow-AR step (SlowArState::step, slow_ar.rs:444-454) on the persistent
+// engine: the step program that every generated frame runs, fed with the
+// caller's step input instead of the sampled one.  Leaves the post-norm
+// hidden in hidden_post and the allowed logits (semantic rows + im_end) in
+// h->logits, like slow_eval with S2D_LOGITS_ALLOWED.
+int32_t engine_step(S2dHandle *h, const int32_t *flat, int64_t n_flat, uint32_t im_end) {
+    const S2dGraphSpec &s = h->spec;
+    int32_t rc = check_eval_ids(h, flat, n_flat);
+    if (rc) return rc;
+    if ((rc = ensure_tokens(h, (size_t)n_flat))) return rc;
+    if (h->slow_prog.ops && h->slow_prog_im_end != im_end && h->frame_exec) {
+        // the captured frame graph points at the program about to be replaced
+        cudaGraphExecDestroy(h->frame_exec);
+        h->frame_exec = nullptr;
+    }
+    if ((rc = build_programs(h, im_end))) return rc;
+    CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
+    // the program reads the step's position from the device state
+    CK(launch_set_state(h->st, h->n_past, 0, 0, h->stream));
+    EmbedArgs ea{};
+    ea.tokens = h->tokens_dev, ea.emb = h->emb, ea.cb_emb = h->cb_emb, ea.d = s.hidden;
+    ea.K = s.num_codebooks, ea.cb_size = s.codebook_size, ea.vocab = s.vocab_size;
+    ea.cb_rows = s.codebook_rows, ea.sem_begin = (uint32_t)s.semantic_begin_id;
+    ea.sem_end = (uint32_t)s.semantic_end_id, ea.scale_on = 1;
+    ea.sem_scale = 1.0f / sqrtf((float)(s.num_codebooks + 1));
+    ea.out = h->x, ea.M = 1, ea.error = &h->st->error;
+    h->launches += 2;
+    CK(launch_embed(ea, h->stream, false));
+    CK(enqueue_engine(h, h->slow_prog));
+    if ((rc = check_device_error(h))) return rc;
+    h->n_past += 1;
     return S2D_OK;
 }
 
@@ -1839,6 +1883,14 @@ int32_t s2d_step(S2dHandle *h, int32_t seq, const int32_t *step_input, int64_t n
     if (n != h->spec.num_codebooks + 1)
         return set_err(h, S2D_EINVAL, "step token width mismatch: expected " +
                                           std::to_string(h->spec.num_codebooks + 1) + ", got " + std::to_string(n));
+    // Full-vocabulary logits need the per-op LM head; every other step runs
+    // the engine's step program, the one the generated frames run.
+    if (h->use_engine && logits_mode != S2D_LOGITS_FULL && seq == 0 && step_input) {
+        CK(cudaSetDevice(h->device));
+        int32_t rc = engine_step(h, step_input, n, im_end);
+        if (rc) return rc;
+        return copy_eval_outputs(h, out_hidden, out_logits, logits_mode, im_end);
+    }
     return s2d_prefill(h, seq, step_input, n, out_hidden, out_logits, logits_mode, im_end);
 }
 
@@ -2537,6 +2589,34 @@ int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, i
     CK(cudaMemcpyAsync(x.p, input, (size_t)n * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(w.p, weight, (size_t)head_dim * 4, cudaMemcpyHostToDevice, st));
     CK(launch_rms_norm_heads((const float *)x.p, (const float *)w.p, (float *)y.p, n, (int)head_dim, eps, st));
+    CK(cudaMemcpyAsync(out, y.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return S2D_OK;
+}
+
+int32_t s2d_op_rope_normal(S2dHandle *h, const float *values, int64_t n, int64_t head_dim, int64_t position,
+                           float rope_base, float *out) {
+    if (!values || !out || n <= 0 || head_dim <= 0 || n % head_dim || position < 0 || position > INT32_MAX)
+        return set_err(h, S2D_EINVAL, "bad arguments");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+        return set_err(h, S2D_EINVAL, "head_dim must be 64, 128 or 256");
+    cudaStream_t st = h ? h->stream : nullptr;
+    if (h) CK(cudaSetDevice(h->device));
+    // the denominators as the model's tables hold them (alloc_buffers)
+    std::vector<float> den((size_t)head_dim / 2);
+    for (int64_t p = 0; p < head_dim; p += 2) den[(size_t)p / 2] = powf(rope_base, (float)p / (float)head_dim);
+    DevBuf x, dn, y;
+    CK(cudaMalloc(&x.p, (size_t)n * 4));
+    CK(cudaMalloc(&dn.p, den.size() * 4));
+    CK(cudaMalloc(&y.p, (size_t)n * 4));
+    CK(cudaMemcpyAsync(x.p, values, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(dn.p, den.data(), den.size() * 4, cudaMemcpyHostToDevice, st));
+    // every head as a query head of rope_kv_kernel: no QK-norm, no KV write
+    RopeArgs a{};
+    a.qkv = (const float *)x.p, a.ld_qkv = (int)n, a.q_out = (float *)y.p;
+    a.rope_denom = (const float *)dn.p, a.pos_const = (int)position;
+    a.H = (int)(n / head_dim), a.Hkv = 0, a.hd = (int)head_dim, a.M = 1, a.max_seq = 1;
+    CK(launch_rope_kv(a, false, st, false));
     CK(cudaMemcpyAsync(out, y.p, (size_t)n * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return S2D_OK;

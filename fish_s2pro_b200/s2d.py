@@ -137,6 +137,8 @@ SIGNATURES = {
                                                 _i32p, _i32p, ctypes.c_int32, ctypes.c_int32, _f32p]),
     "s2d_op_rms_norm": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _f32p, ctypes.c_int64,
                                          ctypes.c_int64, ctypes.c_float, _f32p]),
+    "s2d_op_rope_normal": (ctypes.c_int32, [ctypes.c_void_p, _f32p, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_float, _f32p]),
     "s2d_op_gqa_decode_attention": (ctypes.c_int32, [ctypes.c_void_p, _f32p, _f32p, _f32p,
                                                      ctypes.c_int32, ctypes.c_int32,
                                                      ctypes.c_int32, ctypes.c_int32,
@@ -629,6 +631,16 @@ class CudaMatmulBackend:
             raise S2dError(-1, f"rms_norm length mismatch: input={x.size}, "
                                f"weight={np.asarray(weight).size}")
         return self.rms_norm_heads(x, weight, x.size, eps)
+
+    def apply_rope_normal(self, values, head_dim: int, position: int, base: float) -> np.ndarray:
+        """apply_rope_normal (attention.rs:172-206) over every head of values."""
+        x = np.ascontiguousarray(np.asarray(values, dtype=np.float32))
+        if x.size == 0 or x.size % head_dim:
+            raise S2dError(-1, f"rope input length {x.size} is not a multiple of head_dim {head_dim}")
+        out = np.empty_like(x)
+        self._check(lib().s2d_op_rope_normal(self._h(), _ptr(x, ctypes.c_float), x.size, head_dim,
+                                             position, base, _ptr(out, ctypes.c_float)))
+        return out
 
     def gqa_decode_attention(self, query, keys, values, head_count: int, head_count_kv: int,
                              head_dim: int, token_count: int, attn_scale: float) -> np.ndarray:

@@ -17,24 +17,31 @@ class _SynthConfig(ctypes.Structure):
                             ("weight_std", ctypes.c_float), ("seed", ctypes.c_uint64)]
 
 
-_lib = None
+_libs: dict = {}
 
 
-def _load():
-    global _lib
-    if _lib is None:
-        from . import build
-        path = build.build_synth()
-        _lib = ctypes.CDLL(str(path))
-        _lib.s2d_synth_write_gguf.argtypes = [ctypes.c_char_p, ctypes.POINTER(_SynthConfig),
-                                              ctypes.c_char_p, ctypes.c_size_t]
-        _lib.s2d_synth_write_gguf.restype = ctypes.c_int
-    return _lib
+def _load(lib_path: str | os.PathLike | None = None):
+    """The writer library: the package's libs2d_synth.so, or another build of
+    csrc/synth_gguf.c at `lib_path` (the CPU reference arm of bench.py uses
+    the oracle's build, so that its process maps no library of this
+    package)."""
+    key = str(lib_path) if lib_path else ""
+    if key not in _libs:
+        if lib_path is None:
+            from . import build
+            lib_path = build.build_synth()
+        lib = ctypes.CDLL(str(lib_path))
+        lib.s2d_synth_write_gguf.argtypes = [ctypes.c_char_p, ctypes.POINTER(_SynthConfig),
+                                             ctypes.c_char_p, ctypes.c_size_t]
+        lib.s2d_synth_write_gguf.restype = ctypes.c_int
+        _libs[key] = lib
+    return _libs[key]
 
 
-def write_gguf(path: str | os.PathLike, m: ModelConfig) -> Path:
+def write_gguf(path: str | os.PathLike, m: ModelConfig,
+               lib_path: str | os.PathLike | None = None) -> Path:
     """Write model `m` to `path` (overwritten).  Deterministic in m.seed."""
-    lib = _load()
+    lib = _load(lib_path)
     c = _SynthConfig(
         slow_layers=m.slow_layers, d=m.d, heads=m.heads, kv_heads=m.kv_heads,
         head_dim=m.head_dim, ffn=m.ffn, vocab=m.vocab, sem_begin=m.sem_begin, sem_end=m.sem_end,
@@ -66,16 +73,20 @@ def default_model_dir() -> Path:
     return Path("/tmp/s2d_models")
 
 
-def cached_gguf(m: ModelConfig, directory: str | os.PathLike | None = None) -> Path:
+def model_file_name(m: ModelConfig) -> str:
+    return (f"{m.name}-L{m.slow_layers}F{m.fast_layers}-t{m.linear_type}-s{m.seed}"
+            f"-d{m.d}-v{m.vocab}.gguf")
+
+
+def cached_gguf(m: ModelConfig, directory: str | os.PathLike | None = None,
+                lib_path: str | os.PathLike | None = None) -> Path:
     """Path of model `m` under `directory` (default: default_model_dir()),
-    written on first use."""
+    written on first use (with the writer at `lib_path`, see _load)."""
     d = Path(directory or default_model_dir())
     d.mkdir(parents=True, exist_ok=True)
-    name = (f"{m.name}-L{m.slow_layers}F{m.fast_layers}-t{m.linear_type}-s{m.seed}"
-            f"-d{m.d}-v{m.vocab}.gguf")
-    p = d / name
+    p = d / model_file_name(m)
     if not p.exists():
         tmp = p.with_suffix(f".tmp{os.getpid()}")
-        write_gguf(tmp, m)
+        write_gguf(tmp, m, lib_path)
         os.replace(tmp, p)
     return p

@@ -155,7 +155,10 @@ int32_t s2d_n_past(const S2dHandle *h, int32_t seq, int32_t *out);
 int32_t s2d_prefill(S2dHandle *h, int32_t seq, const int32_t *flat_tokens, int64_t n_flat,
                     float *out_hidden, float *out_logits, int32_t logits_mode,
                     uint32_t im_end_id);
-/* SlowArState::step (slow_ar.rs:444-454): exactly num_codebooks+1 ids. */
+/* SlowArState::step (slow_ar.rs:444-454): exactly num_codebooks+1 ids.
+ * With S2D_LOGITS_ALLOWED or S2D_LOGITS_NONE the step runs on the persistent
+ * decode engine (the step program every generated frame runs); with
+ * S2D_LOGITS_FULL on the per-op kernels, whose LM head covers the vocabulary. */
 int32_t s2d_step(S2dHandle *h, int32_t seq, const int32_t *step_input, int64_t n,
                  float *out_hidden, float *out_logits, int32_t logits_mode, uint32_t im_end_id);
 
@@ -308,6 +311,12 @@ int32_t s2d_op_rows_linear_f16(S2dHandle *h, const float *x, int64_t T, int64_t 
                                float *y);
 int32_t s2d_op_rms_norm(S2dHandle *h, const float *input, const float *weight, int64_t n,
                         int64_t head_dim, float eps, float *out);
+/* apply_rope_normal (attention.rs:172-206): rotate every head of values (n =
+ * heads * head_dim floats, head-major) by position, adjacent pairs (2i, 2i+1)
+ * at theta = position / rope_base^(2i/head_dim).  Runs the RoPE of the per-op
+ * and rows paths (rope_kv_kernel).  head_dim 64, 128 or 256; host buffers. */
+int32_t s2d_op_rope_normal(S2dHandle *h, const float *values, int64_t n, int64_t head_dim,
+                           int64_t position, float rope_base, float *out);
 /* MatmulBackend::gqa_decode_attention (attention.rs:208-247): keys/values
  * token-major [token_count][head_count_kv][head_dim]. */
 int32_t s2d_op_gqa_decode_attention(S2dHandle *h, const float *query, const float *keys,
@@ -321,17 +330,22 @@ int32_t s2d_op_gqa_decode_attention(S2dHandle *h, const float *query, const floa
  * gives this library a fixed memory budget owns every device allocation.
  * query (head_count*head_dim), keys and values (head-major
  * [head_count_kv][token_count][head_dim]) and out (head_count*head_dim) are
- * the caller's DEVICE buffers, f32.  The split-K scratch is a fixed device
+ * the caller's DEVICE buffers, f32; keys and values 16-byte aligned (8 bytes
+ * suffice at head_dim 64), query and out 4-byte aligned, else S2D_EINVAL
+ * before any device work.  The split-K scratch is a fixed device
  * array inside the library: 512 KiB of partials plus 64 counters, held by
  * every GPU that loads the library until the process exits.  Calls needing
  * more (head_count * splits * (head_dim+2) > 131072 floats, with
  * splits = clamp(token_count/8, 1, 16), or head_count_kv > 64) are rejected
  * with S2D_EINVAL.  The first call on a device looks the array's device
  * address up (cudaGetSymbolAddress) and should come before any stream capture
- * on that device.  All calls share the array, so calls that overlap on the
- * GPU race.  The call is enqueued on `stream` (a cudaStream_t; NULL = the
- * legacy default stream) and returns after that stream has finished it.
- * Errors are written into err. */
+ * on that device; the cached address lives as long as the device's primary
+ * context, so do not call this entry point after a cudaDeviceReset of that
+ * device in the same process.  All calls share the array, so calls that
+ * overlap on the GPU race: serialise them.  The call is synchronous: it is
+ * enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream) and
+ * returns only after that stream has finished it.  Errors are written into
+ * err. */
 int32_t s2d_op_gqa_decode_attention_noalloc(const float *query, const float *keys,
                                             const float *values, int32_t head_count,
                                             int32_t head_count_kv, int32_t head_dim,

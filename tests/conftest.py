@@ -14,12 +14,15 @@ def pytest_configure(config):
 
 
 @pytest.fixture(scope="session")
-def model_dir(tmp_path_factory):
-    d = os.environ.get("S2D_MODEL_CACHE")
-    if d:
-        Path(d).mkdir(parents=True, exist_ok=True)
-        return Path(d)
-    return tmp_path_factory.mktemp("models")
+def model_dir():
+    """Where the seeded synthetic model files live: $S2D_MODEL_CACHE, else
+    the shared cache of synth.default_model_dir() (RAM-backed when it has
+    room), so that the full-size models are written once per host and shared
+    with bench.py.  Files are written under a temporary name and renamed."""
+    from fish_s2pro_b200 import synth
+    d = synth.default_model_dir()
+    d.mkdir(parents=True, exist_ok=True)
+    return d
 
 
 @pytest.fixture(scope="session")

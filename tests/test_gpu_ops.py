@@ -50,6 +50,31 @@ def test_rms_norm_heads_matches_oracle(backend, n, hd):
     assert np.max(np.abs(got - want)) <= 4e-6 * np.max(np.abs(want))
 
 
+@pytest.mark.parametrize("heads,hd,pos,base", [(32, 128, 0, 1e6), (32, 128, 511, 1e6), (8, 128, 8191, 1e6),
+                                               (4, 64, 10, 1e4), (2, 256, 30000, 1e6)])
+def test_rope_normal_matches_oracle(backend, heads, hd, pos, base):
+    """apply_rope_normal (attention.rs:172-206) on the per-op/rows RoPE: the
+    rotation's sin and cos come from CUDA's sincosf where the reference calls
+    f32 sin_cos, so the tolerance is a few f32 ulps of the largest value."""
+    rng = np.random.default_rng(pos + heads)
+    x = rng.standard_normal(heads * hd).astype(F32)
+    got = backend.apply_rope_normal(x, hd, pos, base)
+    want = o.rope_normal(x, hd, pos, base)
+    assert rel_err(got, want) < 2e-6
+    # the rotation keeps every pair's length
+    a, b = got.reshape(-1, 2).astype(np.float64), x.reshape(-1, 2).astype(np.float64)
+    np.testing.assert_allclose(np.hypot(a[:, 0], a[:, 1]), np.hypot(b[:, 0], b[:, 1]), rtol=1e-5)
+
+
+def test_rope_normal_kat(backend):  # attention.rs:336-343 at head_dim 64
+    x = np.zeros(64, F32)
+    x[0], x[3] = 1.0, 1.0
+    got = backend.apply_rope_normal(x, 64, 1, 10_000.0)
+    want = o.rope_normal(x, 64, 1, 10_000.0)
+    np.testing.assert_allclose(got, want, atol=1e-6)
+    assert abs(got[0] - math.cos(1.0)) < 1e-6 and abs(got[1] - math.sin(1.0)) < 1e-6
+
+
 @pytest.mark.parametrize("H,Hkv,hd,T", [(4, 2, 64, 1), (32, 8, 128, 7), (32, 8, 128, 700),
                                        (8, 2, 64, 129), (16, 16, 128, 33)])
 def test_gqa_attention_matches_oracle(backend, H, Hkv, hd, T):
