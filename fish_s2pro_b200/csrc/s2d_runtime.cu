@@ -125,6 +125,12 @@ struct S2dHandle {
     // quantized models: one layer's linears dequantised to f16 for the
     // tensor-core rows path (wqkv, wo, w1, w3, w2)
     __half *qscratch[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    // Batched generation of a quantized model: every quantized linear expanded
+    // once to f16 (rounded to nearest), per layer, and fast_output; empty
+    // until the first batched call.
+    std::vector<LayerDev> slow_f16, fast_f16;
+    __half *fast_out_f16 = nullptr;
+    std::vector<__half *> f16_bufs;
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_act = nullptr;
     float *pf_inv = nullptr, *pf_y2 = nullptr, *pf_y2b = nullptr;
@@ -1266,6 +1272,46 @@ int32_t dequant_layer(S2dHandle *h, const ArShape &a, LayerDev *L) {
     return S2D_OK;
 }
 
+// The resident f16 expansion of every quantized linear (batched generation):
+// the rows path then streams f16 weights once per frame step instead of
+// dequantising each layer again.  Exact dequantisation, rounded to f16, as the
+// per-layer scratch of the quantized prefill.
+int32_t ensure_f16_linears(S2dHandle *h) {
+    auto expand = [&](int wq, const uint16_t *src, int64_t n, const uint16_t **dst) -> int32_t {
+        __half *p = nullptr;
+        CK(cudaMalloc(&p, (size_t)n * sizeof(__half)));
+        h->f16_bufs.push_back(p);
+        CK(launch_dequant_f16(wq, src, p, n, h->stream));
+        *dst = reinterpret_cast<const uint16_t *>(p);
+        return S2D_OK;
+    };
+    int32_t rc;
+    for (int fast = 0; fast < 2; ++fast) {
+        const ArShape &a = fast ? h->fast : h->slow;
+        std::vector<LayerDev> &src = fast ? h->fast_layers : h->slow_layers;
+        std::vector<LayerDev> &dst = fast ? h->fast_f16 : h->slow_f16;
+        if (!dst.empty()) continue;
+        std::vector<LayerDev> out = src;
+        for (LayerDev &L : out) {
+            if (L.wq == EW_F16) continue;
+            const int64_t n[5] = {(int64_t)a.qkv_out() * a.d, (int64_t)a.d * a.qs(), (int64_t)a.F * a.d,
+                                  (int64_t)a.F * a.d, (int64_t)a.d * a.F};
+            const uint16_t **w[5] = {&L.wqkv, &L.wo, &L.w1, &L.w3, &L.w2};
+            for (int i = 0; i < 5; ++i)
+                if ((rc = expand(L.wq, *w[i], n[i], w[i]))) return rc;
+            L.wq = EW_F16;
+            h->launches += 5;
+        }
+        dst = std::move(out);
+    }
+    if (h->fast_out_wq != EW_F16 && !h->fast_out_f16) {
+        const uint16_t *p = nullptr;
+        if ((rc = expand(h->fast_out_wq, h->fast_out, (int64_t)h->spec.codebook_size * h->spec.hidden, &p))) return rc;
+        h->fast_out_f16 = const_cast<__half *>(reinterpret_cast<const __half *>(p));
+    }
+    return S2D_OK;
+}
+
 int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPlan &rp) {
     const ArShape &a = is_fast ? h->fast : h->slow;
     const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F, T = rp.T;
@@ -1305,6 +1351,8 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
     bool presplit = false;  // pf_xs / pf_inv already hold this layer's attention-norm split
     for (int l = 0; l < a.L; ++l) {
         LayerDev L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
+        const std::vector<LayerDev> &x16 = is_fast ? h->fast_f16 : h->slow_f16;
+        if (L.wq != EW_F16 && !x16.empty()) L = x16[(size_t)l];  // the resident f16 expansion
         if (L.wq != EW_F16 && (rc = dequant_layer(h, a, &L))) return rc;
         // attention_norm + WQKV
         if (!presplit) {
@@ -1622,8 +1670,8 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
         CK(launch_split_rows(h->fx + (size_t)(M - 1) * d, 2 * d, B, d, h->fast_norm, f.eps, h->pf_xs, h->pf_inv,
                              nullptr, h->stream));
         mark(h, PC_SPLIT);
-        if ((rc = rows_linear(h, h->fast_out, nullptr, cb, d, B, PF_STORE, h->logits_fast_b, cb, nullptr, 0)))
-            return rc;
+        const uint16_t *fo = h->fast_out_wq == EW_F16 ? h->fast_out : reinterpret_cast<const uint16_t *>(h->fast_out_f16);
+        if ((rc = rows_linear(h, fo, nullptr, cb, d, B, PF_STORE, h->logits_fast_b, cb, nullptr, 0))) return rc;
         SampleArgs a{};
         a.logits = h->logits_fast_b, a.n = cb, a.n_contig = -1, a.vocab_full = cb;
         a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
@@ -1701,6 +1749,7 @@ void free_handle(S2dHandle *h) {
     for (void *p : {(void *)h->pf_x, (void *)h->pf_qkv, (void *)h->pf_q, (void *)h->pf_att, (void *)h->pf_act,
                     (void *)h->pf_inv, (void *)h->pf_y2, (void *)h->pf_y2b, (void *)h->pf_xs})
         if (p) cudaFree(p);
+    for (__half *p : h->f16_bufs) cudaFree(p);
     for (__half *p : h->qscratch)
         if (p) cudaFree(p);
     if (h->blas) cublasDestroy(h->blas);
@@ -2099,8 +2148,6 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
                                           "), max_batch = " + std::to_string(h->max_batch));
     if (rng_kind != S2D_RNG_SEEDED && rng_kind != S2D_RNG_PHILOX) return set_err(h, S2D_EINVAL, "unknown rng_kind");
     if (rows != s.num_codebooks + 1) return set_err(h, S2D_EINVAL, "prompt rows must be num_codebooks+1");
-    if (s.linear_type != 1) return set_err(h, S2D_EINVAL, "batched generation needs f16 linear weights");
-    if (h->fast_out_wq != EW_F16) return set_err(h, S2D_EINVAL, "batched generation needs an f16 fast_output");
     for (int i = 0; i < n_seq; ++i) {
         if (!prompts[i]) return set_err(h, S2D_EINVAL, "prompt " + std::to_string(i) + " is NULL");
         if (cols[i] <= 0) return set_err(h, S2D_EINVAL, "expected at least one token in prompt " + std::to_string(i));
@@ -2110,6 +2157,8 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
     CK(cudaSetDevice(h->device));
     int32_t rc;
     if ((rc = ensure_batch(h, p->max_new_tokens))) return rc;
+    // quantized linears: GEMMs over their resident f16 expansion
+    if ((s.linear_type != 1 || h->fast_out_wq != EW_F16) && (rc = ensure_f16_linears(h))) return rc;
     const size_t codes_stride = (size_t)K * std::max<uint32_t>(p->max_new_tokens, 1);
     CK(cudaMemsetAsync(h->codes_b, 0, (size_t)n_seq * codes_stride * sizeof(int32_t), h->stream));
     GenKey k;

@@ -198,8 +198,10 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
  * codebook-major and compacted to out_n_frames[i] frames; rng_states[i] is
  * advanced in place.  With S2D_RNG_SEEDED sequence i produces the codes of
  * s2d_generate_codes on prompt i with state rng_states[i] (up to rounding
- * of the batched GEMMs).  Needs n_seq <= max_batch (S2dConfig), f16 linears,
- * and cols[i] + max_new_tokens <= max_seq.  Resets the single-sequence
+ * of the batched GEMMs).  Needs n_seq <= max_batch (S2dConfig) and
+ * cols[i] + max_new_tokens <= max_seq.  Q8_0 / Q4_K linears run as GEMMs over
+ * an f16 expansion (exact dequantisation rounded to f16) that the first
+ * batched call builds and the handle keeps.  Resets the single-sequence
  * state (n_past = 0): sequence 0's cache is reused.  profile (may be NULL)
  * counts frames over all sequences. */
 int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *const *prompts,

@@ -79,7 +79,8 @@ class Pair:
         from fish_s2pro_b200 import SlowArState, synth
         self.m, self.tol = MODELS[key]
         self.path = synth.cached_gguf(self.m, model_dir)
-        self.gpu = SlowArState.open(self.path, max_seq_len=MAX_SEQ)
+        # the layer-shape variants also decode batches of 2 sequences
+        self.gpu = SlowArState.open(self.path, max_seq_len=MAX_SEQ, max_batch=2 if key.endswith("S") else 1)
         self.cpu = o.OracleModel(str(self.path), max_seq_len=MAX_SEQ, mode=0)
 
     def close(self):
@@ -195,7 +196,39 @@ def check_dequant(p, key):
     assert seen == len(names)
 
 
-CHECKS = {"steps": check_steps, "fast": check_fast, "generation": check_generation, "dequant": check_dequant}
+def _replay(p, key, pr, codes):
+    """The oracle's greedy choices along a GPU trajectory (margin rule)."""
+    m = p.m
+    p.cpu.reset()
+    h, lg = p.cpu.eval(pr.T.reshape(-1).astype(np.int32), allowed_only=True, im_end_id=IM_END)
+    for f in range(codes.shape[1]):
+        assert greedy_consistent(int(codes[0, f]), lg[m.sem_begin:m.sem_end + 1], p.tol), (key, f)
+        for k in range(1, m.num_codebooks):
+            cl = p.cpu.fast_prefix_logits(h, codes[:k, f].tolist())
+            assert greedy_consistent(int(codes[k, f]), cl, p.tol), (key, f, k)
+        h, lg = p.cpu.eval([m.sem_begin + int(codes[0, f])] + codes[:, f].tolist(), allowed_only=True,
+                           im_end_id=IM_END)
+
+
+def check_batch(p, key, frames=3):
+    """Batched greedy generation of two sequences (the rows path's GEMMs over
+    the resident f16 expansion of the quantized linears), each replayed on
+    the oracle."""
+    from fish_s2pro_b200 import (FastArWeights, GenerateParams, PromptTensor, SeededRng,
+                                 generate_codes_batch)
+    m = p.m
+    prs = [prompt(m, 11, 21), prompt(m, 8, 22)]
+    res = generate_codes_batch(p.gpu, IM_END, p.gpu.graph_spec(),
+                               [PromptTensor(x.shape[0], x.shape[1], x.reshape(-1)) for x in prs],
+                               GenerateParams(frames, 0.0, 1.0, 0, 2 * frames + 2), FastArWeights.from_state(p.gpu),
+                               [SeededRng(0), SeededRng(1)])
+    for pr, r in zip(prs, res):
+        assert r.n_frames == frames
+        _replay(p, key, pr, r.codes.reshape(m.num_codebooks, frames))
+
+
+CHECKS = {"steps": check_steps, "fast": check_fast, "generation": check_generation, "dequant": check_dequant,
+          "batch": check_batch}
 
 
 # one test function per model, so that each model file is uploaded once
@@ -216,11 +249,11 @@ def test_c5_full_depth(pairs, check):
     CHECKS[check](pairs("C5"), "C5")
 
 
-@pytest.mark.parametrize("check", ["steps", "fast", "generation", "dequant"])
+@pytest.mark.parametrize("check", ["steps", "fast", "generation", "dequant", "batch"])
 def test_c3_layer_shapes(pairs, check):
     CHECKS[check](pairs("C3S"), "C3S")
 
 
-@pytest.mark.parametrize("check", ["steps", "fast", "generation", "dequant"])
+@pytest.mark.parametrize("check", ["steps", "fast", "generation", "dequant", "batch"])
 def test_c5_layer_shapes(pairs, check):
     CHECKS[check](pairs("C5S"), "C5S")
