@@ -419,6 +419,21 @@ __device__ __forceinline__ ulonglong2 ll_load2(const uint64_t *p) {
     asm volatile("ld.relaxed.gpu.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
     return v;
 }
+// System-scope forms for the tensor-parallel exchange: the words are written
+// by other GPUs (over NVLink) into this GPU's exchange buffer.
+__device__ __forceinline__ void ll_store_sys(uint64_t *p, float v, uint32_t tag) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(ll_word(v, tag)) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load_sys(const uint64_t *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ ulonglong2 ll_load2_sys(const uint64_t *p) {
+    ulonglong2 v;
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0,%1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ bool ll_fresh(unsigned long long w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 __device__ __forceinline__ float ll_value(unsigned long long w) { return __uint_as_float((uint32_t)w); }
 
@@ -427,7 +442,7 @@ __device__ __forceinline__ float ll_value(unsigned long long w) { return __uint_
 // every load at once and later passes re-read only the stale ones.  Bounded:
 // on timeout kErrEngineWait is flagged; when another CTA has flagged an
 // error the wait gives up; either way it returns false.
-template <int N, class Addr>
+template <bool SYS = false, int N, class Addr>
 __device__ __forceinline__ bool ll_wait(unsigned long long (&w)[N], Addr addr, uint32_t tag, int32_t *err) {
     for (uint32_t spin = 0;; ++spin) {
         bool all = true;
@@ -436,7 +451,7 @@ __device__ __forceinline__ bool ll_wait(unsigned long long (&w)[N], Addr addr, u
             const uint64_t *p = addr(i);
             if (p && !ll_fresh(w[i], tag)) {
                 all = false;
-                w[i] = ll_load(p);
+                w[i] = SYS ? ll_load_sys(p) : ll_load(p);
             }
         }
         if (all) return true;
@@ -447,7 +462,7 @@ __device__ __forceinline__ bool ll_wait(unsigned long long (&w)[N], Addr addr, u
         }
     }
 }
-template <int N, class Addr>
+template <bool SYS = false, int N, class Addr>
 __device__ __forceinline__ bool ll_wait2(ulonglong2 (&w)[N], Addr addr, uint32_t tag, int32_t *err) {
     for (uint32_t spin = 0;; ++spin) {
         bool all = true;
@@ -456,7 +471,7 @@ __device__ __forceinline__ bool ll_wait2(ulonglong2 (&w)[N], Addr addr, uint32_t
             const uint64_t *p = addr(i);
             if (p && !(ll_fresh(w[i].x, tag) && ll_fresh(w[i].y, tag))) {
                 all = false;
-                w[i] = ll_load2(p);
+                w[i] = SYS ? ll_load2_sys(p) : ll_load2(p);
             }
         }
         if (all) return true;
@@ -468,13 +483,28 @@ __device__ __forceinline__ bool ll_wait2(ulonglong2 (&w)[N], Addr addr, uint32_t
     }
 }
 
-// One input value of an op: a float written before the launch (src < 0) or
-// an LL word of op src.
+// One input value of an op: a float written before the launch (src < 0), an
+// LL word of op src, or (nsum > 1) the sum in rank order of nsum ranks' LL
+// words of op src, rstride words apart.
 __device__ __forceinline__ bool read_input(const void *base, size_t idx, int src, uint32_t epoch, float &v,
-                                           int32_t *err) {
+                                           int32_t *err, int nsum = 1, long long rstride = 0) {
     if (src < 0) {
         v = __ldcg(reinterpret_cast<const float *>(base) + idx);
         return true;
+    }
+    if (nsum > 1) {
+        const uint64_t *p = reinterpret_cast<const uint64_t *>(base) + idx;
+        unsigned long long w[kEngineMaxPeers];
+#pragma unroll
+        for (int r = 0; r < kEngineMaxPeers; ++r) w[r] = 0ull;
+        const bool ok =
+            ll_wait<true>(w, [&](int r) { return r < nsum ? p + r * rstride : nullptr; }, engine_tag(epoch, src), err);
+        float t = ll_value(w[0]);
+#pragma unroll
+        for (int r = 1; r < kEngineMaxPeers; ++r)
+            if (r < nsum) t = __fadd_rn(t, ll_value(w[r]));
+        v = t;
+        return ok;
     }
     const uint64_t *p = reinterpret_cast<const uint64_t *>(base) + idx;
     unsigned long long w[1] = {0ull};
@@ -515,6 +545,36 @@ __device__ bool stage_x(const EngineOp &op, float *xs, ConsumerShared &cs, int32
                     ss[m] = fmaf(v[b].y, v[b].y, ss[m]);
                     ss[m] = fmaf(v[b].z, v[b].z, ss[m]);
                     ss[m] = fmaf(v[b].w, v[b].w, ss[m]);
+                }
+            }
+        } else if (op.x_nsum > 1) {
+            // tensor parallelism: the sum in rank order of every rank's
+            // partial sums; nb chunks of the n rows in flight per thread
+            const uint32_t tag = engine_tag(cs.epoch, op.x_src);
+            const uint64_t *src = reinterpret_cast<const uint64_t *>(op.x) + (size_t)m * op.ldx;
+            const int n = op.x_nsum, nb = kEngineMaxPeers / n;
+            const long long rs = op.x_rstride;
+            for (int c0 = tid; c0 < (K >> 1); c0 += nb * T) {
+                ulonglong2 v[kEngineMaxPeers];
+#pragma unroll
+                for (int i = 0; i < kEngineMaxPeers; ++i) v[i] = make_ulonglong2(0ull, 0ull);
+                ok = ll_wait2<true>(v,
+                                    [&](int i) {
+                                        const int b = i / n, r = i - b * n, c = c0 + b * T;
+                                        return b < nb && c < (K >> 1) ? src + r * rs + 2 * c : nullptr;
+                                    },
+                                    tag, err) && ok;
+                for (int b = 0; b < nb; ++b) {
+                    const int c = c0 + b * T;
+                    if (c >= (K >> 1)) break;
+                    float f0 = ll_value(v[b * n].x), f1 = ll_value(v[b * n].y);
+                    for (int r = 1; r < n; ++r) {
+                        f0 = __fadd_rn(f0, ll_value(v[b * n + r].x));
+                        f1 = __fadd_rn(f1, ll_value(v[b * n + r].y));
+                    }
+                    reinterpret_cast<float2 *>(dst)[c] = make_float2(f0, f1);
+                    ss[m] = fmaf(f0, f0, ss[m]);
+                    ss[m] = fmaf(f1, f1, ss[m]);
                 }
             }
         } else {
@@ -730,6 +790,8 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, int opi, u
     const GemvTiling T(op, a.slot_bytes);
     const SliceGeom sg = T.sg;
     const int K = T.K, epi = op.epi, ldy = op.ldy, ldr = op.ldr, resid_src = op.resid_src;
+    const int r_nsum = op.r_nsum, n_peer = op.n_peer;
+    const long long r_rstride = op.r_rstride;
     const bool y_ll = op.y_ll != 0;
     void *y = op.y;
     const void *resid = op.resid;
@@ -815,7 +877,8 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, int opi, u
                     out = g1;
                 } else if (epi == EPI_RESID) {
                     float r;
-                    ok = read_input(resid, (size_t)m * ldr + row, resid_src, epoch, r, a.error) && ok;
+                    ok = read_input(resid, (size_t)m * ldr + row, resid_src, epoch, r, a.error, r_nsum, r_rstride) &&
+                         ok;
                     out = __fadd_rn(r, g1);
                 } else if (epi == EPI_SWIGLU_SLOW) {
                     const float sig = 1.0f / (1.0f + expf(-g1));
@@ -823,8 +886,14 @@ __device__ bool consume_gemv(const EngineArgs &a, const EngineOp &op, int opi, u
                 } else {
                     out = __fmul_rn(g1 / (1.0f + expf(-g1)), g3);
                 }
-                if (y_ll) ll_store(reinterpret_cast<uint64_t *>(y) + (size_t)m * ldy + row, out, out_tag);
-                else reinterpret_cast<float *>(y)[(size_t)m * ldy + row] = out;
+                if (n_peer > 0) {
+                    // tensor parallelism: this rank's partial sum into every rank's exchange buffer
+                    for (int q = 0; q < n_peer; ++q) ll_store_sys(op.y_peer[q] + (size_t)m * ldy + row, out, out_tag);
+                } else if (y_ll) {
+                    ll_store(reinterpret_cast<uint64_t *>(y) + (size_t)m * ldy + row, out, out_tag);
+                } else {
+                    reinterpret_cast<float *>(y)[(size_t)m * ldy + row] = out;
+                }
             }
         }
     }

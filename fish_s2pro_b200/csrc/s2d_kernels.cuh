@@ -158,6 +158,8 @@ struct SampleArgs {
 
 enum EngineOpKind { OP_GEMV = 0, OP_ATTN = 1 };
 
+constexpr int kEngineMaxPeers = 8;  // tensor-parallel ranks of one engine program
+
 // One step of the engine's program.  A GEMV op reads its input vector(s) and
 // writes its outputs like gemv_kernel (GemvArgs fields); an ATTN op fuses
 // rope_kv_kernel and attn_kernel (RopeArgs / AttnArgs fields).
@@ -202,6 +204,15 @@ struct EngineOp {
     // Wt + tr0 * K * mats + s * R * kt * mats and holds [mat][R][kw].
     const uint16_t *Wt;
     int wt;              // EngineWeight of W (and W2)
+    // Tensor parallelism (every field 0 on one GPU).  An input of x_nsum > 1
+    // rows is the sum, in rank order, of x_nsum rank rows of LL words
+    // x_rstride words apart (each rank's partial sums of the same op); the
+    // residual likewise with r_nsum / r_rstride.  With n_peer > 0 every
+    // output word also goes to y_peer[q] + m * ldy + row for each rank q (this
+    // rank's row of each rank's exchange buffer, the peers' over NVLink).
+    int x_nsum, r_nsum, n_peer;
+    long long x_rstride, r_rstride;
+    uint64_t *y_peer[kEngineMaxPeers];
 };
 
 __host__ __device__ __forceinline__ uint32_t engine_tag(uint32_t epoch, int op) {

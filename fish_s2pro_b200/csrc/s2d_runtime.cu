@@ -131,6 +131,11 @@ struct S2dHandle {
     std::vector<LayerDev> slow_f16, fast_f16;
     __half *fast_out_f16 = nullptr;
     std::vector<__half *> f16_bufs;
+    // tensor parallelism on the engine (setup_exchange): this rank's exchange
+    // buffer and every rank's, mapped here (xchg_peer[tp_rank] == xchg)
+    uint64_t *xchg = nullptr;
+    uint64_t *xchg_peer[kEngineMaxPeers] = {};
+    size_t xchg_words = 0;
     int pf_cap = 0;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_act = nullptr;
     float *pf_inv = nullptr, *pf_y2 = nullptr, *pf_y2b = nullptr;
@@ -568,6 +573,7 @@ struct NcclApi {
     ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                                cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
     bool ok = false;
@@ -582,9 +588,11 @@ const NcclApi &nccl() {
         a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(lib, "ncclGetUniqueId"));
         a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(lib, "ncclCommInitRank"));
         a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(lib, "ncclAllReduce"));
+        a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(lib, "ncclAllGather"));
         a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(lib, "ncclCommDestroy"));
         a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(lib, "ncclGetErrorString"));
-        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+        a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy &&
+               a.error_string;
         return a;
     }();
     return api;
@@ -597,6 +605,45 @@ cudaError_t tp_allreduce(S2dHandle *h, float *x, size_t n) {
     if (h->tp <= 1) return cudaSuccess;
     const ncclResult_t r = nccl().all_reduce(x, x, n, ncclFloat32, ncclSum, h->comm, h->stream);
     return r == ncclSuccess ? cudaSuccess : cudaErrorUnknown;
+}
+
+// The residual exchange of tensor parallelism inside the persistent engine.
+// Each rank's exchange buffer holds, for every wo and w2 op of the Slow-AR
+// step program (2 per layer), one row of d LL words per rank: [op][rank][d].
+// Every rank maps every other rank's buffer (CUDA IPC handles, gathered over
+// NCCL), so that its engine writes its partial sums straight into the peers'
+// buffers over NVLink with plain stores, and every rank sums the rows of an
+// op in rank order: the ranks see bit-identical residuals.  Plain peer
+// stores and local loads only: no bulk or tensor copies touch peer memory.
+int32_t setup_exchange(S2dHandle *h) {
+    if (h->tp <= 1 || h->tp > kEngineMaxPeers) return S2D_OK;
+    const size_t words = (size_t)2 * h->slow.L * h->tp * h->spec.hidden;
+    CK(cudaMalloc(&h->xchg, words * sizeof(uint64_t)));
+    CK(cudaMemset(h->xchg, 0, words * sizeof(uint64_t)));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, h->xchg));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t *dbuf = nullptr;
+    CK(cudaMalloc(&dbuf, hb * (size_t)h->tp));
+    CK(cudaMemcpy(dbuf + hb * (size_t)h->tp_rank, &mine, hb, cudaMemcpyHostToDevice));
+    const ncclResult_t nr = nccl().all_gather(dbuf + hb * (size_t)h->tp_rank, dbuf, hb, ncclUint8, h->comm, h->stream);
+    std::vector<cudaIpcMemHandle_t> all((size_t)h->tp);
+    cudaError_t e = nr == ncclSuccess ? cudaStreamSynchronize(h->stream) : cudaErrorUnknown;
+    if (!e) e = cudaMemcpy(all.data(), dbuf, hb * (size_t)h->tp, cudaMemcpyDeviceToHost);
+    cudaFree(dbuf);
+    if (nr != ncclSuccess) return set_err(h, S2D_ECUDA, std::string("ncclAllGather: ") + nccl().error_string(nr));
+    CK(e);
+    for (int q = 0; q < h->tp; ++q) {
+        if (q == h->tp_rank) {
+            h->xchg_peer[q] = h->xchg;
+            continue;
+        }
+        void *p = nullptr;
+        CK(cudaIpcOpenMemHandle(&p, all[(size_t)q], cudaIpcMemLazyEnablePeerAccess));
+        h->xchg_peer[q] = static_cast<uint64_t *>(p);
+    }
+    h->xchg_words = words;
+    return S2D_OK;
 }
 
 int32_t alloc_buffers(S2dHandle *h) {
@@ -913,7 +960,24 @@ void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, cons
     const ArShape &a = is_fast ? h->fast : h->slow;
     const LayerDev &L = is_fast ? h->fast_layers[(size_t)l] : h->slow_layers[(size_t)l];
     const int d = a.d;
-    const void *x = *x_src < 0 ? static_cast<const void *>(x_in) : static_cast<const void *>(h->ll_x);
+    // Tensor parallelism (Slow-AR): wo and w2 leave partial sums over this
+    // rank's heads / FFN columns, written into every rank's exchange buffer
+    // (setup_exchange: region 2l for wo, 2l + 1 for w2); their readers sum the
+    // ranks' rows in rank order.  Rank 0's partials carry the residual.
+    const bool xt = !is_fast && h->tp > 1 && h->xchg;
+    const int n = h->tp;
+    const long long region = (long long)n * M * d;
+    const void *x = *x_src < 0 ? static_cast<const void *>(x_in)
+                    : xt       ? static_cast<const void *>(h->xchg + (size_t)(2 * l - 1) * region)
+                               : static_cast<const void *>(h->ll_x);
+    const int x_nsum = xt && *x_src >= 0 ? n : 1;
+    auto summed = [&](EngineOp &o, int nsum) {  // o's input: the sum of nsum rank rows
+        o.x_nsum = nsum, o.x_rstride = (long long)M * d;
+    };
+    auto to_peers = [&](EngineOp &o, int e) {  // o's outputs: exchange region e of every rank
+        o.n_peer = n;
+        for (int q = 0; q < n; ++q) o.y_peer[q] = h->xchg_peer[q] + (size_t)e * region + (size_t)h->tp_rank * M * d;
+    };
     const int i_qkv = (int)ops.size();
     ops.push_back(gemv_op(M, EPI_STORE, L.wqkv, nullptr, x, d, *x_src, L.attn_norm, a.eps, h->ll_qkv, a.qkv_out(), 1,
                           nullptr, -1, d, a.qkv_out(), L.wq));
@@ -935,15 +999,28 @@ void layer_ops(S2dHandle *h, bool is_fast, int l, const float *x_in, int M, cons
     t.att_out = h->ll_att, t.part = h->ll_part;
     const int i_att = (int)ops.size();
     ops.push_back(t);
+    if (xt) summed(ops[(size_t)i_qkv], x_nsum);
     const int i_wo = (int)ops.size();
-    ops.push_back(gemv_op(M, EPI_RESID, L.wo, nullptr, h->ll_att, a.qs(), i_att, nullptr, 0.f, h->ll_x, d, 1, x,
+    const int resid_epi = xt && h->tp_rank != 0 ? EPI_STORE : EPI_RESID;
+    ops.push_back(gemv_op(M, resid_epi, L.wo, nullptr, h->ll_att, a.qs(), i_att, nullptr, 0.f, h->ll_x, d, 1, x,
                           *x_src, a.qs(), d, L.wq));
+    if (xt) {
+        ops.back().r_nsum = x_nsum, ops.back().r_rstride = (long long)M * d;
+        to_peers(ops.back(), 2 * l);
+    }
+    const void *x_att = xt ? static_cast<const void *>(h->xchg + (size_t)(2 * l) * region)
+                           : static_cast<const void *>(h->ll_x);
     const int i_w13 = (int)ops.size();
-    ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, h->ll_x, d, i_wo, L.ffn_norm,
+    ops.push_back(gemv_op(M, is_fast ? EPI_SWIGLU_FAST : EPI_SWIGLU_SLOW, L.w1, L.w3, x_att, d, i_wo, L.ffn_norm,
                           a.eps, h->ll_act, a.F, 1, nullptr, -1, d, a.F, L.wq));
+    if (xt) summed(ops.back(), n);
     *x_src = (int)ops.size();
-    ops.push_back(gemv_op(M, EPI_RESID, L.w2, nullptr, h->ll_act, a.F, i_w13, nullptr, 0.f, h->ll_x, d, 1, h->ll_x,
+    ops.push_back(gemv_op(M, resid_epi, L.w2, nullptr, h->ll_act, a.F, i_w13, nullptr, 0.f, h->ll_x, d, 1, x_att,
                           i_wo, a.F, d, L.wq));
+    if (xt) {
+        ops.back().r_nsum = n, ops.back().r_rstride = (long long)M * d;
+        to_peers(ops.back(), 2 * l + 1);
+    }
 }
 
 // The weights of a GEMV op in the engine's slot order (engine_relayout),
@@ -1028,8 +1105,14 @@ int32_t build_programs(S2dHandle *h, uint32_t im_end) {
         const int nsem = s.semantic_end_id - s.semantic_begin_id + 1;
         const bool extra = (int64_t)im_end < s.vocab_size &&
                            ((int)im_end < s.semantic_begin_id || (int)im_end > s.semantic_end_id);
-        EngineOp head = gemv_op(1, EPI_STORE, h->emb, nullptr, h->ll_x, d, x_src, h->norm, h->slow.eps, h->logits,
+        // the final residual: LL words of the last w2, or on a tensor-parallel
+        // handle the ranks' rows of its exchange region
+        const bool xt = h->tp > 1 && h->xchg;
+        const void *xf = xt ? static_cast<const void *>(h->xchg + (size_t)(2 * h->slow.L - 1) * h->tp * d)
+                            : static_cast<const void *>(h->ll_x);
+        EngineOp head = gemv_op(1, EPI_STORE, h->emb, nullptr, xf, d, x_src, h->norm, h->slow.eps, h->logits,
                                 s.vocab_size, 0, nullptr, -1, d, nsem + (extra ? 1 : 0));
+        if (xt) head.x_nsum = h->tp, head.x_rstride = d;
         head.row_base = s.semantic_begin_id, head.n_contig = nsem;
         head.extra_row = extra ? (int)im_end : s.semantic_begin_id;
         head.x_out = h->hidden_post;
@@ -1730,6 +1813,9 @@ void free_handle(S2dHandle *h) {
     if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
     h->frame_exec = nullptr, h->batch_exec = nullptr;
     if (h->stream) cudaStreamSynchronize(h->stream);
+    for (int q = 0; q < kEngineMaxPeers; ++q)
+        if (h->xchg_peer[q] && h->xchg_peer[q] != h->xchg) cudaIpcCloseMemHandle(h->xchg_peer[q]);
+    if (h->xchg) cudaFree(h->xchg);
     if (h->comm) nccl().comm_destroy(h->comm);
     if (h->shard_arena) cudaFree(h->shard_arena);
     for (void *p : {(void *)h->st_b, (void *)h->bx, (void *)h->fx, (void *)h->hidden_b, (void *)h->logits_b,
@@ -1839,12 +1925,16 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         }
     }
     if ((rc = alloc_buffers(h))) return report(h, rc);
+    if (h->tp > 1 && (rc = setup_exchange(h))) return report(h, rc);
     {
         int coop = 0;
         cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, h->device);
         cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, h->device);
         const char *env = getenv("S2D_ENGINE");
-        h->use_engine = coop && h->tp == 1 && engine_supported(h) && !(env && env[0] == '0');
+        // a tensor-parallel handle runs the engine when the ranks' exchange
+        // buffers are mapped (setup_exchange); otherwise the per-op kernels
+        // with NCCL allreduces
+        h->use_engine = coop && (h->tp == 1 || h->xchg) && engine_supported(h) && !(env && env[0] == '0');
         if (const char *lead = getenv("S2D_L2_LEAD")) h->l2_lead = std::max(0, std::min(64, atoi(lead)));
         if (const char *sp = getenv("S2D_ATT_SPLITS")) h->engine_att_splits = std::max(0, atoi(sp));
         if (const char *tc = getenv("S2D_TCGEMM")) h->use_tc = tc[0] == '1';

@@ -178,10 +178,12 @@ def test_batch_rejects_bad_arguments(gpu, tiny_gguf, model_dir):
     gp2 = dict(gp, max_new_tokens=250)
     with pytest.raises(S2dError):
         run_batch(gpu, prompts(), gp2, [SeededRng(0) for _ in LENS])  # exceeds max_seq
+    # a quantized model decodes in batches too (over the f16 expansion of its
+    # linears; parity in tests/test_gpu_full_configs.py)
     q = synth.cached_gguf(configs.tiny(seed=7, linear_type=configs.GGML_Q8_0), model_dir)
     st = SlowArState.open(q, max_seq_len=128, max_batch=2)
     try:
-        with pytest.raises(S2dError):
-            run_batch(st, prompts()[:2], gp, [SeededRng(0), SeededRng(1)])
+        res = run_batch(st, prompts()[:2], dict(gp, min_tokens_before_end=10), [SeededRng(0), SeededRng(1)])
+        assert [r.n_frames for r in res] == [4, 4]
     finally:
         st.close()
