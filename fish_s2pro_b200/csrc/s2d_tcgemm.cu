@@ -6,8 +6,10 @@
 // range of K.  Per K block of 64 values (one 128-byte swizzle row):
 //   TMA: W tile [128][64] (and W2 for SwiGLU), hi tile [NT][64], lo tile [NT][64]
 //        (128-byte swizzle, K-major) into a ring of stages;
-//   MMA (one thread): 4 K-steps of 16, hi and lo into the same accumulator,
-//        so that the TMEM accumulator holds W.(hi + lo) = W.x in f32;
+//   MMA (one thread): 4 K-steps of 16; the hi and lo tiles sit back to back
+//        in the stage, so one MMA of N = 2 NT multiplies both (accumulator
+//        columns [0, NT) W.hi, [NT, 2 NT) W.lo) and the epilogue adds the
+//        two halves, W.(hi + lo) = W.x in f32;
 //   tcgen05.commit frees the stage when its MMAs have read it.
 // The epilogue warps (TMEM lanes 0..127, one output row per thread) read the
 // accumulator 32 columns at a time and apply inv[t], the residual or SwiGLU.
@@ -119,6 +121,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+// 32 columns of the hi half plus the matching 32 of the lo half (off columns
+// later): this lane's W.hi + W.lo for 32 tokens.
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int off, float (&v)[32]) {
+    float lo[32];
+    tmem_ld32(taddr, v);
+    tmem_ld32(taddr + (uint32_t)off, lo);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += lo[j];
+}
+
 // Every thread of every CTA of the cluster (not .aligned: the producer and
 // MMA lanes arrive apart from the rest of their warps).
 __device__ __forceinline__ void cluster_sync_all() {
@@ -159,7 +171,8 @@ struct TcCfg {
     static constexpr int B = NT * 128;        // hi or lo tile bytes
     static constexpr int STAGE = A * (DUAL ? 2 : 1) + 2 * B;
     static constexpr int ST = kTcStageBudget / STAGE < kTcMaxStages ? kTcStageBudget / STAGE : kTcMaxStages;
-    static constexpr int COLS = NT * (DUAL ? 2 : 1) <= 32 ? 32 : NT * (DUAL ? 2 : 1);  // a power of two here
+    // accumulator columns per matrix: the stacked hi and lo rows (2 NT)
+    static constexpr int COLS = 2 * NT * (DUAL ? 2 : 1);  // a power of two here
     static constexpr int RP = NT + 4;  // split-K partial tile row pitch (floats): conflict-free float4s
     static constexpr int RED = kTcRows * RP * 4 * (DUAL ? 2 : 1);  // split-K partial tile bytes
     static constexpr size_t SMEM = (size_t)ST * STAGE + 1024;
@@ -225,7 +238,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             (void)mb_wait(&full[i % C::ST], (i / C::ST) & 1, abort_v, false);
     } else if (warp == 5 && lane == 0) {
         // MMA issuer
-        constexpr uint32_t idesc = idesc_f16_f32(kTcRows, NT);
+        // the hi and lo tiles are adjacent in the stage: one MMA of N = 2 NT
+        // multiplies both (accumulator columns [0, NT) hi, [NT, 2 NT) lo)
+        constexpr uint32_t idesc = idesc_f16_f32(kTcRows, 2 * NT);
         for (int i = 0; i < nit; ++i) {
             const int s = i % C::ST;
             if (!mb_wait(&full[s], (i / C::ST) & 1, abort_v)) {
@@ -234,17 +249,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             tc_fence_after();
             const uint64_t da = desc_k_sw128(su32(stage_a(s))), dhi = desc_k_sw128(su32(stage_hi(s)));
-            const uint64_t dlo = desc_k_sw128(su32(stage_lo(s)));
             const uint64_t da2 = DUAL ? desc_k_sw128(su32(stage_a2(s))) : 0ull;
 #pragma unroll
             for (int k = 0; k < kTcKBlock / 16; ++k) {
                 const uint64_t kk = (uint64_t)(2 * k);  // 32 bytes per K-step of 16 f16
                 umma_f16(tmem, da + kk, dhi + kk, idesc, (i | k) != 0);
-                umma_f16(tmem, da + kk, dlo + kk, idesc, 1u);
-                if (DUAL) {
-                    umma_f16(tmem + NT, da2 + kk, dhi + kk, idesc, (i | k) != 0);
-                    umma_f16(tmem + NT, da2 + kk, dlo + kk, idesc, 1u);
-                }
+                if (DUAL) umma_f16(tmem + 2 * NT, da2 + kk, dhi + kk, idesc, (i | k) != 0);
             }
             umma_commit(&empty[s]);
         }
@@ -269,8 +279,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
             for (int c = 0; c < NT / 32; ++c) {
                 float v[32], u[32];
-                tmem_ld32(lane_addr + c * 32, v);
-                if (DUAL) tmem_ld32(lane_addr + NT + c * 32, u);
+                tmem_ld_sum(lane_addr + c * 32, NT, v);
+                if (DUAL) tmem_ld_sum(lane_addr + 2 * NT + c * 32, NT, u);
                 if (n < a.N) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -297,8 +307,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int c = 0; c < NT / 32; ++c) {
                 float v[32], u[32];
                 if (have) {
-                    tmem_ld32(lane_addr + c * 32, v);
-                    if (DUAL) tmem_ld32(lane_addr + NT + c * 32, u);
+                    tmem_ld_sum(lane_addr + c * 32, NT, v);
+                    if (DUAL) tmem_ld_sum(lane_addr + 2 * NT + c * 32, NT, u);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = 0.f, u[j] = 0.f;
