@@ -103,17 +103,18 @@ __global__ void __launch_bounds__(128) decode_mma_attn_kernel(const RowsAttnArgs
     const int nck = (t1 - t0 + KC - 1) / KC;
     const int mine = nck > warp ? (nck - warp + nw - 1) / nw : 0;
 
-    const size_t so = (size_t)m * a.kv_seq_stride * 2 + (size_t)kvh * a.max_seq * (HD * 2);
-    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + so;
-    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache);
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache);
     uint8_t *ring = sm + (size_t)warp * NST * STAGE;
     auto issue = [&](int j, int stg) {
         const int c0 = t0 + (warp + nw * j) * KC, n = min(KC, t1 - c0);
         uint8_t *kt = ring + (size_t)stg * STAGE, *vt = kt + KC * PITCH;
+        // the chunk's rows are consecutive in one page (chunks start at multiples of KC)
+        const size_t cb = kv_row(a.kv_pages, a.kv_seq_stride, a.max_seq, m, kvh, c0, HD) * 2;
 #pragma unroll
         for (int i = 0; i < KC * UNITS / 32; ++i) {
             const int u = lane + 32 * i, r = u / UNITS, c = u - r * UNITS;
-            const size_t src = (size_t)(c0 + (r < n ? r : 0)) * (HD * 2) + c * 16;
+            const size_t src = cb + (size_t)(r < n ? r : 0) * (HD * 2) + c * 16;
             cp_async16_zfill(kt + r * PITCH + c * 16, kb + src, r < n);
             cp_async16_zfill(vt + r * PITCH + c * 16, vb + src, r < n);
         }
@@ -386,16 +387,16 @@ __global__ void __launch_bounds__(256, 2) prefill_mma_attn_kernel(const RowsAttn
     const bool row_ok = mrow < a.T;
     const int prow = a.pos_const + mrow;
 
-    const size_t so = (size_t)kvh * a.max_seq * (HD * 2);
-    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + so;
-    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache);
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache);
     const int nchunks = (vis_end + KC - 1) / KC;
     auto issue = [&](int c, int stg) {
         uint8_t *kt = sm + (size_t)stg * STAGE, *vt = kt + KC * PITCH;
+        const size_t cb = kv_row(a.kv_pages, 0, a.max_seq, 0, kvh, c * KC, HD) * 2;  // one sequence
         for (int u = threadIdx.x; u < KC * UNITS; u += blockDim.x) {
             const int r = u / UNITS, cc = u - r * UNITS, key = c * KC + r;
             const bool valid = key < vis_end;
-            const size_t src = (size_t)(valid ? key : 0) * (HD * 2) + cc * 16;
+            const size_t src = cb + (size_t)(valid ? r : 0) * (HD * 2) + cc * 16;
             cp_async16_zfill(kt + r * PITCH + cc * 16, kb + src, valid);
             cp_async16_zfill(vt + r * PITCH + cc * 16, vb + src, valid);
         }

@@ -440,9 +440,9 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(const RopeArgs a) {
         if (lane == 0 && a.error) atomicExch(a.error, 1);
         return;
     }
-    const size_t so = (size_t)seq * a.kv_seq_stride;
-    KV *kc = reinterpret_cast<KV *>(a.kcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
-    KV *vc = reinterpret_cast<KV *>(a.vcache) + so + ((size_t)h * a.max_seq + pos) * hd + lane * EPL;
+    const size_t ro = kv_row(a.kv_pages, a.kv_seq_stride, a.max_seq, seq, h, pos, hd);
+    KV *kc = reinterpret_cast<KV *>(a.kcache) + ro + lane * EPL;
+    KV *vc = reinterpret_cast<KV *>(a.vcache) + ro + lane * EPL;
     const int vsrc = (a.H + a.Hkv + h) * hd + lane * EPL;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {

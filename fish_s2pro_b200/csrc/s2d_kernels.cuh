@@ -40,6 +40,30 @@ struct GemvArgs {
     int wq;              // weight format: 0 f16 rows, 1 ggml Q8_0, 2 ggml Q4_K (EngineWeight)
 };
 
+// Paged KV caches of the batched path.  A page holds kKvPage consecutive
+// positions of one sequence for every layer: [layer][K | V][kv head]
+// [kKvPage][hd]; pages[seq * per_seq + t / kKvPage] is the page of position t
+// of sequence seq.  Paged kernels get the layer's K (and V) base inside page
+// 0, so every row is base + page * page_elems + (kvh * kKvPage + t % kKvPage)
+// * hd.  The rows kernels stage K/V chunks of 16 or 32 positions that start at
+// multiples of the chunk, so a chunk never spans two pages.
+constexpr int kKvPage = 64;
+struct KvPages {
+    const int32_t *pages;  // nullptr: contiguous caches
+    int per_seq;           // page-table entries per sequence
+    size_t page_elems;     // elements (f16 or f32) of one page
+};
+// Element offset of position t's row of kv head kvh of sequence seq from the
+// layer's K (or V) base: paged, or contiguous sequences of seq_stride
+// elements with [kv head][max_seq][hd] layer caches.
+__host__ __device__ __forceinline__ size_t kv_row(const KvPages &p, size_t seq_stride, int max_seq, int seq,
+                                                  int kvh, int t, int hd) {
+    if (p.pages)
+        return (size_t)p.pages[(size_t)seq * p.per_seq + t / kKvPage] * p.page_elems +
+               ((size_t)kvh * kKvPage + t % kKvPage) * hd;
+    return (size_t)seq * seq_stride + ((size_t)kvh * max_seq + t) * hd;
+}
+
 struct RopeArgs {
     const float *qkv;    // [M][ld_qkv]: Q | K | V
     int ld_qkv;
@@ -67,6 +91,7 @@ struct RopeArgs {
     const DevState *st_b;
     int st_pos;
     size_t kv_seq_stride;
+    KvPages kv_pages;    // paged caches (kv_pages.pages set): kv_seq_stride unused
 };
 
 struct AttnArgs {

@@ -332,17 +332,18 @@ __device__ __forceinline__ void rows_attn_body(const RowsAttnArgs &a, uint8_t *s
     float *qs = reinterpret_cast<float *>(sm + (size_t)NST * 2 * 32 * pitch) + warp * hd;
     const float *qrow = a.q + (size_t)m * a.H * hd + (size_t)h * hd;
     for (int i = lane; i < hd; i += 32) qs[i] = qrow[i];
-    const size_t so = (size_t)seq * a.kv_seq_stride * sizeof(KV) + (size_t)kvh * a.max_seq * rowb;
-    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + so;
-    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + so;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache);
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache);
     const int units = rowb / 16;
     auto issue = [&](int c0, int stg) {
         const int n = min(32, t1 - c0);
         uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
+        // the chunk's rows are consecutive in one page (chunks start at multiples of 32)
+        const size_t cb = kv_row(a.kv_pages, a.kv_seq_stride, a.max_seq, seq, kvh, c0, hd) * sizeof(KV);
         for (int u = threadIdx.x; u < 2 * n * units; u += blockDim.x) {
             const int which = u >= n * units, uu = which ? u - n * units : u;
             const int r = uu / units, c = uu - r * units;
-            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + (size_t)(c0 + r) * rowb + c * 16);
+            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + cb + (size_t)r * rowb + c * 16);
         }
         cp_async_commit();
     };
@@ -546,16 +547,17 @@ __global__ void __launch_bounds__(256) prefill_tile_attn_kernel(const RowsAttnAr
     for (int r = 0; r < QB; ++r)
         for (int i = lane; i < hd; i += 32)
             qs[r * hd + i] = r < nrows ? a.q[(size_t)(m0 + r) * a.H * hd + (size_t)h * hd + i] : 0.f;
-    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache) + (size_t)kvh * a.max_seq * rowb;
-    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache) + (size_t)kvh * a.max_seq * rowb;
+    const uint8_t *kb = reinterpret_cast<const uint8_t *>(a.kcache);
+    const uint8_t *vb = reinterpret_cast<const uint8_t *>(a.vcache);
     const int units = rowb / 16;
     auto issue = [&](int c0, int stg) {
         const int n = min(32, t1 - c0);
         uint8_t *kt = sm + (size_t)stg * 2 * 32 * pitch, *vt = kt + 32 * pitch;
+        const size_t cb = kv_row(a.kv_pages, 0, a.max_seq, 0, kvh, c0, hd) * sizeof(KV);  // one sequence
         for (int u = threadIdx.x; u < 2 * n * units; u += blockDim.x) {
             const int which = u >= n * units, uu = which ? u - n * units : u;
             const int r = uu / units, c = uu - r * units;
-            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + (size_t)(c0 + r) * rowb + c * 16);
+            cp_async16((which ? vt : kt) + r * pitch + c * 16, (which ? vb : kb) + cb + (size_t)r * rowb + c * 16);
         }
         cp_async_commit();
     };

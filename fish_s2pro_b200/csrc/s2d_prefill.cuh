@@ -44,6 +44,7 @@ struct RowsAttnArgs {
     const void *kcache, *vcache;
     size_t kv_seq_stride;
     int max_seq;
+    KvPages kv_pages;    // paged caches (kv_pages.pages set; see kv_row): kv_seq_stride unused
     float *out;
     int T, rows_per_seq;
     const DevState *st;

@@ -172,11 +172,17 @@ struct S2dHandle {
     ncclComm_t comm = nullptr;
     uint8_t *shard_arena = nullptr;
     S2dTpShard shard{};
-    // batched generation (s2d_generate_codes_batch): kv_slow holds max_batch
-    // sequences of kv_slow_seq elements each (sequence 0 is the one of the
-    // single-sequence calls)
+    // batched generation (s2d_generate_codes_batch): the Slow-AR caches of
+    // its sequences live in a pool of kKvPage-position pages (KvPages), with
+    // a page table of kv_per_seq entries per sequence; kv_slow holds only the
+    // single-sequence calls' cache
     int max_batch = 1;
     size_t kv_slow_seq = 0;
+    __half *kv_pool = nullptr;
+    int32_t *kv_page_table = nullptr;  // [max_batch][kv_per_seq] page ids (device)
+    int kv_per_seq = 0;
+    size_t kv_page_elems = 0;
+    const int32_t *pf_pages = nullptr;  // set while a batched sequence is prefilled: its page-table row
     DevState *st_b = nullptr;             // [max_batch]
     float *bx = nullptr;                  // [max_batch][d] Slow-AR residual rows
     float *fx = nullptr;                  // [max_batch][2][d] Fast-AR rows of a pass
@@ -678,7 +684,7 @@ int32_t alloc_buffers(S2dHandle *h) {
         CK(cudaMemcpy(h->rope_cs_fast, tf.data(), tf.size() * sizeof(float2), cudaMemcpyHostToDevice));
     }
     h->kv_slow_seq = (size_t)a.L * 2 * a.Hkv * maxseq * a.hd;
-    const size_t kv_slow = h->kv_slow_seq * (size_t)h->max_batch;
+    const size_t kv_slow = h->kv_slow_seq;
     CK(cudaMalloc(&h->kv_slow, kv_slow * sizeof(__half)));
     CK(cudaMemset(h->kv_slow, 0, kv_slow * sizeof(__half)));
     const size_t kv_fast = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
@@ -1322,6 +1328,7 @@ struct RowsPlan {
     void *kv = nullptr;
     size_t kv_seq_stride = 0;
     int max_seq = 0;
+    KvPages pages{};  // paged caches (pages.pages set): kv is the pool, kv_seq_stride unused
 };
 
 // Every layer of the Slow-AR (is_fast false) or the Fast-AR over T rows of
@@ -1399,7 +1406,9 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
     const ArShape &a = is_fast ? h->fast : h->slow;
     const int d = a.d, qo = a.qkv_out(), qs = a.qs(), F = a.F, T = rp.T;
     const size_t kvb = is_fast ? sizeof(float) : sizeof(__half);
-    const size_t layer_bytes = (size_t)2 * a.Hkv * rp.max_seq * a.hd * kvb;
+    // a layer's K and V: contiguous [Hkv][max_seq][hd] each, or (paged) the
+    // layer's slice of page 0 of the pool, [Hkv][kKvPage][hd] each
+    const size_t layer_bytes = (size_t)2 * a.Hkv * (rp.pages.pages ? kKvPage : rp.max_seq) * a.hd * kvb;
     // tensor parallel (Slow-AR rows in one block of d floats each): rank 0
     // adds the residual, the others store their partial sums; summed in place
     const bool part = !is_fast && h->tp > 1;
@@ -1464,11 +1473,13 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         r.eps = a.eps, r.pos_dev = nullptr, r.pos_const = rp.pos_const;
         r.H = a.H, r.Hkv = a.Hkv, r.hd = a.hd, r.M = T, r.done = nullptr, r.error = &h->st->error;
         r.rows_per_seq = rp.rps, r.st_b = rp.st, r.st_pos = rp.st_pos, r.kv_seq_stride = rp.kv_seq_stride;
+        r.kv_pages = rp.pages;
         CK(launch_rope_kv(r, !is_fast, h->stream, false));
         mark(h, PC_ROPE);
         // GQA attention of every row over its sequence's cache
         RowsAttnArgs t{};
         t.q = h->pf_q, t.kcache = r.kcache, t.vcache = r.vcache, t.kv_seq_stride = rp.kv_seq_stride;
+        t.kv_pages = rp.pages;
         t.max_seq = rp.max_seq, t.out = h->pf_att, t.T = T, t.rows_per_seq = rp.rps, t.st = rp.st;
         t.st_pos = rp.st_pos, t.pos_const = rp.pos_const, t.H = a.H, t.Hkv = a.Hkv, t.hd = a.hd;
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
@@ -1507,6 +1518,10 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
 int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
     RowsPlan rp;
     rp.T = T, rp.rps = T, rp.pos_const = pos0, rp.kv = h->kv_slow, rp.max_seq = h->cfg.max_seq;
+    if (h->pf_pages) {  // a batched sequence: its pages of the pool
+        rp.kv = h->kv_pool;
+        rp.pages = KvPages{h->pf_pages, h->kv_per_seq, h->kv_page_elems};
+    }
     return rows_layers(h, false, h->pf_x, h->slow.d, rp);
 }
 
@@ -1552,7 +1567,8 @@ int32_t slow_eval(S2dHandle *h, const int32_t *flat, int64_t n_flat, int32_t log
     rc = ensure_tokens(h, (size_t)n_flat);
     if (rc) return rc;
     CK(cudaMemcpyAsync(h->tokens_dev, flat, (size_t)n_flat * sizeof(int32_t), cudaMemcpyHostToDevice, h->stream));
-    if (n >= kPrefillMin) {
+    // a batched sequence's prompt always takes the rows path (its cache is paged)
+    if (n >= kPrefillMin || h->pf_pages) {
         if ((rc = ensure_prefill(h))) return rc;
         for (int64_t c0 = 0; c0 < n; c0 += h->pf_cap) {
             const int T = (int)std::min<int64_t>(h->pf_cap, n - c0);
@@ -1668,6 +1684,27 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
     if (!h->st_b) {
         const size_t nsem = (size_t)(s.semantic_end_id - s.semantic_begin_id + 1);
         const size_t kvf = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
+        // The Slow-AR caches of the batch: a pool of kKvPage-position pages
+        // ([layer][K | V][kv head][kKvPage][hd] f16 each) and a page table.
+        // The pages are dealt out in a seeded random order, so that no
+        // sequence's cache is contiguous; a continuous-batching host would
+        // hand pages out and take them back per sequence instead.
+        h->kv_per_seq = (h->cfg.max_seq + kKvPage - 1) / kKvPage;
+        h->kv_page_elems = (size_t)a.L * 2 * a.Hkv * kKvPage * a.hd;
+        const size_t n_pages = B * (size_t)h->kv_per_seq;
+        CK(cudaMalloc(&h->kv_pool, n_pages * h->kv_page_elems * sizeof(__half)));
+        CK(cudaMemset(h->kv_pool, 0, n_pages * h->kv_page_elems * sizeof(__half)));
+        std::vector<int32_t> table(n_pages);
+        for (size_t i = 0; i < n_pages; ++i) table[i] = (int32_t)i;
+        uint64_t x = 0x9e3779b97f4a7c15ull;  // splitmix64 stream for a Fisher-Yates shuffle
+        for (size_t i = n_pages; i > 1; --i) {
+            x += 0x9e3779b97f4a7c15ull;
+            uint64_t z = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+            z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+            std::swap(table[i - 1], table[(z ^ (z >> 31)) % i]);
+        }
+        CK(cudaMalloc(&h->kv_page_table, n_pages * sizeof(int32_t)));
+        CK(cudaMemcpy(h->kv_page_table, table.data(), n_pages * sizeof(int32_t), cudaMemcpyHostToDevice));
         CK(cudaMalloc(&h->st_b, B * sizeof(DevState)));
         CK(cudaMemset(h->st_b, 0, B * sizeof(DevState)));
         CK(cudaMalloc(&h->bx, B * d * sizeof(float)));
@@ -1783,7 +1820,8 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     RowsPlan rp;
     rp.T = B, rp.rps = 1, rp.pos_const = 0, rp.st = h->st_b, rp.st_pos = 1, rp.S = batch_splits(h, B);
     rp.order = h->attn_mma_order ? h->batch_order : nullptr;
-    rp.kv = h->kv_slow, rp.kv_seq_stride = h->kv_slow_seq, rp.max_seq = h->cfg.max_seq;
+    rp.kv = h->kv_pool, rp.max_seq = h->cfg.max_seq;
+    rp.pages = KvPages{h->kv_page_table, h->kv_per_seq, h->kv_page_elems};
     if ((rc = rows_layers(h, false, h->bx, d, rp))) return rc;
     // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
     CK(launch_split_rows(h->bx, d, B, d, h->norm, h->slow.eps, h->pf_xs, h->pf_inv, h->hidden_b, h->stream));
@@ -1822,7 +1860,7 @@ void free_handle(S2dHandle *h) {
                     (void *)h->logits_fast_b, (void *)h->kv_fast_b, (void *)h->frame_codes_b, (void *)h->codes_b,
                     (void *)h->ra_part, (void *)h->ra_counters, (void *)h->batch_order})
         if (p) cudaFree(p);
-    void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast,
+    void *bufs[] = {h->arena, h->norm_arena, h->rope_slow, h->rope_fast, h->kv_slow, h->kv_fast, h->kv_pool, h->kv_page_table,
                     h->x, h->qkv, h->q, h->att, h->act, h->fast_x, h->hidden_post, h->logits,
                     h->logits_fast, h->part, h->counters, h->st, h->tokens_dev, h->frame_codes,
                     h->codes_out, h->tok_out, h->code_override, h->engine_epoch, h->slow_prog.ops,
@@ -2259,23 +2297,21 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
     // into its own KV cache
     CK(cudaEventRecord(h->ev0, h->stream));
     const uint32_t launches0 = h->launches;
-    __half *kv0 = h->kv_slow;
     for (int i = 0; i < n_seq; ++i) {
         std::vector<int32_t> flat((size_t)rows * cols[i]);
         for (int t = 0; t < cols[i]; ++t)
             for (int r = 0; r < rows; ++r) {
                 const uint32_t v = prompts[i][(size_t)r * cols[i] + t];
                 if (v > 0x7fffffffu) {
-                    h->kv_slow = kv0;
                     h->n_past = 0;
                     return set_err(h, S2D_EINVAL, "prompt token id does not fit i32");
                 }
                 flat[(size_t)t * rows + r] = (int32_t)v;
             }
-        h->kv_slow = kv0 + (size_t)i * h->kv_slow_seq;
+        h->pf_pages = h->kv_page_table + (size_t)i * h->kv_per_seq;  // sequence i's pages
         h->n_past = 0;
         rc = slow_eval(h, flat.data(), (int64_t)flat.size(), S2D_LOGITS_ALLOWED, p->im_end_id);
-        h->kv_slow = kv0;
+        h->pf_pages = nullptr;
         if (rc) {
             h->n_past = 0;
             return rc;
@@ -2289,7 +2325,7 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
                            cudaMemcpyDeviceToDevice, h->stream));
         h->launches += 2;
     }
-    h->n_past = 0;  // sequence 0's cache now holds batch sequence 0
+    h->n_past = 0;  // the single-sequence state is reset
     const uint32_t prefill_kernels = h->launches - launches0;
     // the batched attention's block order: longest context first (every
     // sequence advances one position per frame, so the order holds)
