@@ -352,8 +352,9 @@ def run_ours(args, d: Dist, wl_name=None, use_tp=False, steps=None, warmup=None,
         "config": {"workload": f"{wl_name}: full-size {WTYPE[m.linear_type]} S2-Pro-shaped Dual-AR, "
                                f"{wl.prompt_len}-token prompt, greedy {frames} frames, batch 1",
                    "global_batch": 1 if tp else d.world, "seq_len": wl.prompt_len + frames,
-                   "parallelism": (f"tp{d.world} (Slow-AR heads and FFN columns sharded, NCCL "
-                                   "allreduce after wo and w2; Fast-AR replicated)") if tp
+                   "parallelism": (f"tp{d.world} (Slow-AR heads and FFN columns sharded; the wo "
+                                   "and w2 partial sums exchanged inside the persistent engine "
+                                   "over NVLink peer stores; Fast-AR replicated)") if tp
                                   else f"replicas x{d.world} (independent utterances)",
                    "l2": f"inputs larger than L2 (each frame streams {frame_bytes / 1e9:.2f} GB of "
                          f"{WTYPE[m.linear_type]} weights and KV rows; L2 is 0.126 GB)"},
