@@ -23,6 +23,7 @@
 
 #include "s2d_common.cuh"
 #include "s2d_kernels.cuh"
+#include "s2d_sample.cuh"
 
 namespace s2d {
 
@@ -94,6 +95,17 @@ __device__ __forceinline__ void bulk_copy(void *dst, const void *src, uint32_t b
 
 __device__ __forceinline__ void consumers_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kEngineConsumerWarps * 32) : "memory");
+}
+// consumers_sync that also returns whether any consumer thread passed true.
+__device__ __forceinline__ bool consumers_sync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kEngineConsumerWarps * 32)
+        : "memory");
+    return r != 0;
 }
 
 __device__ __forceinline__ void group_sync(int id, int threads) {
@@ -227,6 +239,7 @@ __device__ void attn_slot(const EngineOp &op, const AttnPlan &pl, int j, SlotCop
 
 // Walks this CTA's ring slots in program order: the weight slots of GEMV
 // ops and the cache-row slots of ATTN ops.
+template <bool FRAME>
 struct SlotIter {
     int i = -1, t = 0, s = 0;  // op, tile (ATTN: slot), slice of the next slot
     bool attn = false;
@@ -262,10 +275,12 @@ struct SlotIter {
             if (++i >= a.n_ops) return -1;
             const EngineOp &op = a.ops[i];
             t = s = 0;
-            attn = op.kind != OP_GEMV;
+            attn = FRAME ? op.kind == OP_ATTN : op.kind != OP_GEMV;
             if (attn) {
                 plan.init(op, a.slot_bytes);
                 ntiles = plan.slots();
+            } else if (FRAME && op.kind != OP_GEMV) {  // SAMPLE, ATTN_CTX: no slots
+                ntiles = 0;
             } else {
                 const GemvTiling T(op, a.slot_bytes);
                 r0 = T.r0, n = T.n, ntiles = T.ntiles, mats = T.mats, K = T.K, sg = T.sg, wt = T.wt;
@@ -280,13 +295,14 @@ __device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+template <bool FRAME>
 __device__ void producer(const EngineArgs &a, uint64_t *full, uint64_t *empty, uint8_t *ring) {
     const int NS = a.nslots;
     uint32_t g = 0;   // slots issued
     uint32_t pf = 0;  // slots the prefetch cursor has passed
     int slot = 0;
     uint32_t phase = 0;
-    SlotIter cur, ahead;
+    SlotIter<FRAME> cur, ahead;
     AttnPlan cur_plan, ahead_plan;
     SlotCopies c, pc;
     for (;;) {
@@ -931,6 +947,14 @@ struct RopeNorm {
 #pragma unroll
         for (int e = 0; e < EPL; e += 2) cs[e / 2] = rope_row[(lane * EPL + e) >> 1];
     }
+    // the same from global memory; gains may be null (no QK-norm)
+    __device__ __forceinline__ void load_global(const float *gains, const float2 *rope_row) {
+        const int lane = threadIdx.x & 31;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) g[e] = gains ? __ldg(gains + lane * EPL + e) : 1.f;
+#pragma unroll
+        for (int e = 0; e < EPL; e += 2) cs[e / 2] = __ldg(rope_row + ((lane * EPL + e) >> 1));
+    }
     // QK-norm (when `norm`) + RoPE of one head held as EPL values per lane
     __device__ __forceinline__ void apply(float *v, bool norm, float eps, int hd) const {
         if (norm) {
@@ -1210,6 +1234,151 @@ __device__ bool consume_attn(const EngineArgs &a, const EngineOp &op, int opi, u
     return ok;
 }
 
+// An ATTN op over an LL context (EngineOp::ctx_n > 0).  Group gid of the CTA
+// takes item (KV head kvh, token m) like consume_attn with one split: its
+// warps rebuild the visible K / V rows [0, pos] from the words of the ops
+// that produced them (QK-norm and RoPE of K as when those rows were cached),
+// then warp wr scores query head kvh * rep + wr, lane j owning position j,
+// with consume_attn's arithmetic.  Group area: q [rep][hd], K [ctx_n][hd],
+// V [ctx_n][hd].
+template <int EPL>
+__device__ __forceinline__ bool consume_attn_ctx(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch,
+                                              uint8_t *area) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hd = op.hd, rep = op.H / op.Hkv, gpc = kEngineConsumerWarps / rep;
+    const int gid = warp / rep, wr = warp % rep;
+    if (gid >= gpc) return true;
+    const int item = gid * gridDim.x + blockIdx.x;
+    if (item >= op.M * op.Hkv) return true;
+    const int kvh = item % op.Hkv, m = item / op.Hkv, h = kvh * rep + wr;
+    const int pos = op.pos_const + m, np = pos + 1;  // np <= ctx_n <= 32 (host-checked)
+    float *qsm = reinterpret_cast<float *>(area + (size_t)gid * attn_ctx_group_bytes(rep, hd, op.ctx_n));
+    float *ks = qsm + rep * hd, *vs = ks + (size_t)op.ctx_n * hd;
+    bool ok = true;
+    for (int j = wr; j < np; j += rep) {
+        const uint64_t *kp = op.ctx_qkv[j] + (size_t)(op.H + kvh) * hd + lane * EPL;
+        const uint64_t *vp = kp + (size_t)op.Hkv * hd;
+        unsigned long long w[2 * EPL];
+#pragma unroll
+        for (int e = 0; e < 2 * EPL; ++e) w[e] = 0ull;
+        ok = ll_wait(w, [&](int e) { return e < EPL ? kp + e : vp + (e - EPL); }, engine_tag(epoch, op.ctx_src[j]),
+                     a.error) && ok;
+        float kf[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) kf[e] = ll_value(w[e]), vs[(size_t)j * hd + lane * EPL + e] = ll_value(w[EPL + e]);
+        RopeNorm<EPL> rn;
+        rn.load_global(op.k_norm, op.rope_cs + (size_t)j * (hd >> 1));
+        rn.apply(kf, op.k_norm != nullptr, op.eps, hd);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) ks[(size_t)j * hd + lane * EPL + e] = kf[e];
+    }
+    {
+        const uint64_t *qp = op.qkv + (size_t)m * op.ld_qkv + (size_t)h * hd + lane * EPL;
+        unsigned long long w[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) w[e] = 0ull;
+        ok = ll_wait(w, [&](int e) { return qp + e; }, engine_tag(epoch, op.qkv_src), a.error) && ok;
+        float q[EPL];
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) q[e] = ll_value(w[e]);
+        RopeNorm<EPL> rn;
+        rn.load_global(op.q_norm, op.rope_cs + (size_t)pos * (hd >> 1));
+        rn.apply(q, op.q_norm != nullptr, op.eps, hd);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) qsm[wr * hd + lane * EPL + e] = q[e];
+    }
+    group_sync(2 + gid, rep * 32);  // the group's K / V rows and queries are complete
+    float sc = -INFINITY;
+    if (lane < np) {
+        const uint8_t *krow = reinterpret_cast<const uint8_t *>(ks + (size_t)lane * hd);
+        const float4 *q4 = reinterpret_cast<const float4 *>(qsm + wr * hd);
+        const int ng = hd / 4;  // a power of two
+        float d0 = 0.f, d1 = 0.f;
+        for (int i = 0; i < ng; i += 2) {
+            const int i0 = (i + lane) & (ng - 1), i1 = (i + 1 + lane) & (ng - 1);
+            const float4 k0 = kv_load4<float>(krow, i0), k1 = kv_load4<float>(krow, i1);
+            const float4 a0 = q4[i0], a1 = q4[i1];
+            d0 = fmaf(a0.x, k0.x, d0);
+            d0 = fmaf(a0.y, k0.y, d0);
+            d0 = fmaf(a0.z, k0.z, d0);
+            d0 = fmaf(a0.w, k0.w, d0);
+            d1 = fmaf(a1.x, k1.x, d1);
+            d1 = fmaf(a1.y, k1.y, d1);
+            d1 = fmaf(a1.z, k1.z, d1);
+            d1 = fmaf(a1.w, k1.w, d1);
+        }
+        sc = (d0 + d1) * op.scale;
+    }
+    const float mn = warp_max(sc);
+    const float p = lane < np ? expf(sc - mn) : 0.f;
+    const float l = warp_sum(p);
+    float acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int j = 0; j < np; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        const float *vr = vs + (size_t)j * hd + lane * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pj, vr[e], acc[e]);
+    }
+    uint64_t *outp = op.att_out + (size_t)m * op.H * hd + (size_t)h * hd + lane * EPL;
+    const uint32_t out_tag = engine_tag(epoch, opi);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) ll_store(outp + e, acc[e] / l, out_tag);
+    return ok;
+}
+
+// A SAMPLE op: CTA sample_cta stages the logits, runs the device sampler
+// (sample_block, the 256 consumer threads) and writes the sampled code's
+// Fast-AR embedding row as the next pass's input words.  Area layout:
+// engine_sample_bytes.
+__device__ __forceinline__ bool run_sample(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch,
+                                        uint8_t *area) {
+    if ((int)blockIdx.x != op.sample_cta) return true;
+    constexpr int T = kEngineConsumerWarps * 32;
+    constexpr int B = 8;  // word pairs in flight per thread
+    const int tid = threadIdx.x, n = op.K;
+    float *lg = reinterpret_cast<float *>(area);
+    unsigned long long *keys = reinterpret_cast<unsigned long long *>(area + attn_round(n * 4));
+    float *probs = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(keys) + (size_t)engine_sample_pow2(n) * 8);
+    SampleScratch *scr =
+        reinterpret_cast<SampleScratch *>(reinterpret_cast<uint8_t *>(probs) + attn_round((n + 1) * 4));
+    const uint32_t tag = engine_tag(epoch, op.x_src);
+    const uint64_t *src = reinterpret_cast<const uint64_t *>(op.x);
+    bool ok = true;
+    for (int c0 = tid; c0 < (n >> 1); c0 += B * T) {
+        ulonglong2 v[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) v[b] = make_ulonglong2(0ull, 0ull);
+        ok = ll_wait2(v, [&](int b) { return c0 + b * T < (n >> 1) ? src + 2 * (c0 + b * T) : nullptr; }, tag,
+                      a.error) && ok;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int c = c0 + b * T;
+            if (c < (n >> 1)) lg[2 * c] = ll_value(v[b].x), lg[2 * c + 1] = ll_value(v[b].y);
+        }
+    }
+    if (consumers_sync_or(!ok)) return false;
+    const uint32_t token =
+        sample_block<T, kEngineSampleMax>(op.samp, 0, lg, keys, probs, *scr, [] { consumers_sync(); });
+    if (op.y) {
+        uint64_t *y = reinterpret_cast<uint64_t *>(op.y);
+        const uint16_t *row = op.samp.fast_emb + (size_t)token * op.N;
+        const uint32_t out_tag = engine_tag(epoch, opi);
+        for (int i = tid; i < op.N; i += T) ll_store(y + i, h2f(row[i]), out_tag);
+    }
+    return true;
+}
+
+// The ops that only whole-frame programs use (engine_kernel<true>).  Inlined:
+// with them as calls the frame kernel's program ran 2.8% slower (2.907
+// against 2.827 ms for C2's nine passes).
+__device__ __forceinline__ bool run_frame_op(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch,
+                                          uint8_t *area) {
+    if (op.kind == OP_SAMPLE) return run_sample(a, op, opi, epoch, area);
+    return op.hd == 64 ? consume_attn_ctx<2>(a, op, opi, epoch, area) : consume_attn_ctx<4>(a, op, opi, epoch, area);
+}
+
 // Not inlined: attention's register pressure stays out of the GEMV loops.
 template <typename KV>
 __device__ __noinline__ bool consume_attn_dispatch(const EngineArgs &a, const EngineOp &op, int opi, uint32_t epoch,
@@ -1224,6 +1393,7 @@ __device__ __noinline__ bool consume_attn_dispatch(const EngineArgs &a, const En
 
 }  // namespace
 
+template <bool FRAME>
 __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ ConsumerShared cs;
@@ -1249,7 +1419,7 @@ __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineA
     __syncthreads();
     if (a.done && *a.done) return;
     if (warp == kEngineConsumerWarps) {
-        if ((tid & 31) == 0) producer(a, full, empty, ring);
+        if ((tid & 31) == 0) producer<FRAME>(a, full, empty, ring);
         return;
     }
     const uint32_t epoch = cs.epoch;
@@ -1265,6 +1435,8 @@ __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineA
             float *xs = reinterpret_cast<float *>(area);
             ok = op.M == 2 ? run_gemv<2>(a, op, i, g, full, empty, ring, xs, cs, tr)
                            : run_gemv<1>(a, op, i, g, full, empty, ring, xs, cs, tr);
+        } else if (FRAME && op.kind != OP_ATTN) {
+            ok = run_frame_op(a, op, i, epoch, area);
         } else {
             // attention timeline (group 0 of the CTA): [1] inputs ready, [3] merge started
             unsigned long long *atr = a.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1)
@@ -1289,12 +1461,13 @@ __global__ void __launch_bounds__(kEngineThreads, 1) engine_kernel(const EngineA
     if (blockIdx.x == 0 && tid == 0) *reinterpret_cast<volatile uint32_t *>(a.epoch) = epoch + 1;
 }
 
-cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s) {
+cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s, bool frame) {
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(engine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kEngineSmemMax);
-        if (e) return e;
+        for (auto k : {engine_kernel<false>, engine_kernel<true>}) {
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kEngineSmemMax);
+            if (e) return e;
+        }
         configured = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -1307,7 +1480,7 @@ cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, engine_kernel, a);
+    return frame ? cudaLaunchKernelEx(&cfg, engine_kernel<true>, a) : cudaLaunchKernelEx(&cfg, engine_kernel<false>, a);
 }
 
 int engine_weight_format(int gtype) {

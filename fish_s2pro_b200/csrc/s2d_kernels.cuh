@@ -181,9 +181,11 @@ struct SampleArgs {
 
 // ---- persistent layer engine (s2d_engine.cu) -------------------------------
 
-enum EngineOpKind { OP_GEMV = 0, OP_ATTN = 1 };
+enum EngineOpKind { OP_GEMV = 0, OP_ATTN = 1, OP_SAMPLE = 2, OP_ATTN_CTX = 3 };
 
 constexpr int kEngineMaxPeers = 8;  // tensor-parallel ranks of one engine program
+constexpr int kEngineMaxCtx = 16;   // positions of an ATTN op over an LL context (ctx_n)
+constexpr int kEngineSampleMax = 4096;  // candidates of a SAMPLE op
 
 // One step of the engine's program.  A GEMV op reads its input vector(s) and
 // writes its outputs like gemv_kernel (GemvArgs fields); an ATTN op fuses
@@ -194,7 +196,8 @@ constexpr int kEngineMaxPeers = 8;  // tensor-parallel ranks of one engine progr
 // single 64-bit store.  The tag of op i's outputs in a launch with epoch e is
 // engine_tag(e, i); a reader polls the words it needs until they carry the
 // producer's tag, so no grid-wide barrier separates the ops.  Inputs written
-// before the launch are plain floats (src index -1).
+// before the launch are plain floats (src index -1).  A SAMPLE op runs the
+// device sampler on one CTA (see the SAMPLE fields).
 struct EngineOp {
     int kind, epi, M;
     // GEMV
@@ -238,12 +241,29 @@ struct EngineOp {
     int x_nsum, r_nsum, n_peer;
     long long x_rstride, r_rstride;
     uint64_t *y_peer[kEngineMaxPeers];
+    // ATTN_CTX: attention over an LL context of ctx_n <= kEngineMaxCtx
+    // positions (ATTN fields otherwise): position j's Q | K | V row is the
+    // [ld_qkv] LL words ctx_qkv[j] written by op ctx_src[j], the op's own
+    // tokens included; K is normed and rotated here, and no cache and no
+    // ring slot is used.  Token m attends to positions [0, pos_const + m].
+    // SAMPLE and ATTN_CTX ops run only in the frame variant of the engine
+    // kernel (launch_engine's `frame`).
+    int ctx_n;
+    const uint64_t *ctx_qkv[kEngineMaxCtx];
+    int ctx_src[kEngineMaxCtx];
+    // SAMPLE: CTA sample_cta polls the K <= kEngineSampleMax logits (LL words
+    // x of op x_src), draws a token with the device sampler under samp (its
+    // logits / fast_x_next fields unused) and writes row `token` of
+    // samp.fast_emb, N = d values, as LL words to y (when y is not null).
+    int sample_cta;
+    SampleArgs samp;
 };
 
+// The tag of op `op`'s outputs in the launch of epoch `epoch` (op < 1024).
 __host__ __device__ __forceinline__ uint32_t engine_tag(uint32_t epoch, int op) {
-    return (epoch << 8) | (uint32_t)op;
+    return (epoch << 10) | (uint32_t)op;
 }
-constexpr int kEngineMaxOps = 255;
+constexpr int kEngineMaxOps = 1023;
 
 struct EngineArgs {
     const EngineOp *ops;
@@ -321,7 +341,8 @@ constexpr int kErrEngineWeights = 16;  // a weight-ring wait ran out
 constexpr int kErrEngineWait = 17;     // a wait for another op's outputs ran out
 constexpr int kErrEngineAlign = 18;    // the shared-memory ring is not 128-byte aligned
 
-cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s);
+// frame: the kernel variant that also runs SAMPLE and ATTN_CTX ops.
+cudaError_t launch_engine(const EngineArgs &a, int grid, size_t smem, cudaStream_t s, bool frame = false);
 
 // Copies a linear's weights into the engine's slot order for a `grid`-CTA
 // launch with ring slots of slot_bytes.  W and W2 are GGUF tensors of ggml
@@ -348,6 +369,22 @@ __host__ __device__ __forceinline__ int attn_group_bytes(int rep, int hd, int kv
     return attn_round(rep * hd * 4 + 4 * hd * kvb);
 }
 __host__ __device__ __forceinline__ int attn_side_bytes(int hd) { return 16 * hd; }
+// Shared area of one group of an ATTN op over an LL context: the rep query
+// rows, then ctx K rows and ctx V rows, f32.
+__host__ __device__ __forceinline__ int attn_ctx_group_bytes(int rep, int hd, int ctx) {
+    return attn_round((rep + 2 * ctx) * hd * 4);
+}
+// Shared area of a SAMPLE op over n candidates: the logits [n] f32, the sort
+// keys [next power of two >= n] u64, the probabilities [n + 1] f32, then
+// scratch_bytes of SampleScratch.
+__host__ __device__ __forceinline__ int engine_sample_pow2(int n) {
+    int p = 2;
+    while (p < n) p <<= 1;
+    return p;
+}
+__host__ __device__ __forceinline__ int engine_sample_bytes(int n, int scratch_bytes) {
+    return attn_round(n * 4) + engine_sample_pow2(n) * 8 + attn_round((n + 1) * 4) + scratch_bytes;
+}
 __host__ __device__ __forceinline__ int attn_slot_rows(int hd, int kvb, int slot_bytes) {
     const int p = (slot_bytes - attn_side_bytes(hd) - 256) / (2 * hd * kvb);
     return p > 32 ? 32 : p;

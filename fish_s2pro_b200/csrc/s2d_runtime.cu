@@ -25,6 +25,7 @@
 #include "../../include/s2d.h"
 #include "s2d_gguf.h"
 #include "s2d_kernels.cuh"
+#include "s2d_sample.cuh"
 #include "s2d_prefill.cuh"
 #include "s2d_tcgemm.cuh"
 
@@ -61,6 +62,7 @@ struct ArShape {
 struct EngineProgram {
     EngineOp *ops = nullptr;
     int n_ops = 0;
+    bool frame = false;  // has SAMPLE / ATTN_CTX ops: the frame kernel variant
     int nslots = 0, area_bytes = 0;
     size_t smem = 0;
 };
@@ -145,6 +147,15 @@ struct S2dHandle {
     uint64_t *ll_x = nullptr, *ll_qkv = nullptr, *ll_att = nullptr, *ll_act = nullptr, *ll_part = nullptr;
     float2 *rope_cs_slow = nullptr, *rope_cs_fast = nullptr;  // [positions][hd / 2] (cos, sin)
     std::vector<EngineProgram> fast_progs;  // index = codebook being produced (1..K-1)
+    // A frame's whole Fast-AR in one engine launch (build_fast_frame): every
+    // pass, its head and its sampler; S2D_FAST_FRAME=0 keeps one launch per
+    // pass.  Its passes keep their WQKV words for the later passes'
+    // attention (fr_qkv [pass][layer][2][qkv_out]) and exchange the logits
+    // (fr_logits) and the next input rows (fr_x [codebook][d]) as LL words.
+    EngineProgram fast_frame_prog;
+    GenKey fast_frame_key;
+    bool fast_frame = true;
+    uint64_t *fr_qkv = nullptr, *fr_logits = nullptr, *fr_x = nullptr;
     // engine weight copies in slot order, keyed by (W, W2, N, K, n_contig, row_base, extra_row)
     std::map<std::tuple<const uint16_t *, const uint16_t *, int, int, int, int, int>, uint16_t *> tiled;
     size_t tiled_bytes = 0;
@@ -721,6 +732,17 @@ int32_t alloc_buffers(S2dHandle *h) {
             CK(cudaMalloc(bufs[i], ns[i] * sizeof(uint64_t)));
             CK(cudaMemset(*bufs[i], 0, ns[i] * sizeof(uint64_t)));
         }
+        {
+            const int K = std::max(s.num_codebooks, 1);
+            const size_t nq = (size_t)std::max(K - 1, 1) * f.L * 2 * f.qkv_out();
+            const size_t nl = (size_t)std::max(s.codebook_size, 2), nxr = (size_t)K * f.d;
+            uint64_t **fb[] = {&h->fr_qkv, &h->fr_logits, &h->fr_x};
+            const size_t fn[] = {nq, nl, nxr};
+            for (int i = 0; i < 3; ++i) {
+                CK(cudaMalloc(fb[i], fn[i] * sizeof(uint64_t)));
+                CK(cudaMemset(*fb[i], 0, fn[i] * sizeof(uint64_t)));
+            }
+        }
         const uint32_t one = 1;
         CK(cudaMalloc(&h->engine_epoch, sizeof(uint32_t)));
         CK(cudaMemcpy(h->engine_epoch, &one, sizeof(uint32_t), cudaMemcpyHostToDevice));
@@ -1062,6 +1084,17 @@ int32_t upload_program(S2dHandle *h, const std::vector<EngineOp> &ops_in, Engine
             ab = std::max(ab, o.M * o.K * 4);
             const int32_t rc = tiled_weights(h, o);
             if (rc) return rc;
+        } else if (o.kind == OP_SAMPLE) {
+            if (o.K < 2 || o.K % 2 || o.K > kEngineSampleMax || o.samp.n != o.K || o.sample_cta < 0 ||
+                o.sample_cta >= h->num_sms)
+                return set_err(h, S2D_EINVAL, "engine: unsupported sample op");
+            ab = std::max(ab, engine_sample_bytes(o.K, (int)sizeof(SampleScratch)));
+        } else if (o.kind == OP_ATTN_CTX) {
+            if (o.ctx_n > kEngineMaxCtx || o.pos_const + o.M > o.ctx_n || (o.hd != 64 && o.hd != 128) ||
+                o.H % o.Hkv || (o.H / o.Hkv) > kEngineConsumerWarps)
+                return set_err(h, S2D_EINVAL, "engine: unsupported context attention op");
+            const int rep = o.H / o.Hkv;
+            ab = std::max(ab, (kEngineConsumerWarps / rep) * attn_ctx_group_bytes(rep, o.hd, o.ctx_n));
         } else {
             if (o.M > 2) return set_err(h, S2D_EINVAL, "engine: attention over more than 2 tokens");
             const int kvb = o.kv_half ? 2 : 4;
@@ -1077,6 +1110,8 @@ int32_t upload_program(S2dHandle *h, const std::vector<EngineOp> &ops_in, Engine
     CK(cudaMalloc(&p->ops, ops.size() * sizeof(EngineOp)));
     CK(cudaMemcpy(p->ops, ops.data(), ops.size() * sizeof(EngineOp), cudaMemcpyHostToDevice));
     p->n_ops = (int)ops.size();
+    p->frame = false;
+    for (const EngineOp &o : ops) p->frame |= o.kind == OP_SAMPLE || o.kind == OP_ATTN_CTX;
     p->area_bytes = ab;
     p->nslots = ns;
     p->smem = (size_t)kEngineBarrierBytes + (size_t)ab + (size_t)ns * h->slot_bytes;
@@ -1130,13 +1165,82 @@ int32_t build_programs(S2dHandle *h, uint32_t im_end) {
     return S2D_OK;
 }
 
+// The Fast-AR of one frame as a single engine program (the loop of
+// generate_codebooks_for_semantic, fast_ar.rs:440-470): for each codebook
+// k = 1..K-1 the pass's layers (pass 1 over positions 0 and 1, pass k > 1
+// over position k), the head (fast_ar.rs:429-435) and a SAMPLE op on CTA 0
+// (sample_token, sampling.rs:121-241) that writes code k and the next
+// pass's input row fast_emb[code k].  Attention reads the earlier positions
+// from the WQKV words of the passes that produced them (ctx_qkv), so no KV
+// cache and no launch boundary sits between the passes.  The sampling
+// parameters are part of the program: rebuilt when the key changes.
+int32_t build_fast_frame(S2dHandle *h, const GenKey &k) {
+    const S2dGraphSpec &s = h->spec;
+    const ArShape &f = h->fast;
+    const int d = s.hidden, K = s.num_codebooks, L = f.L, q_out = f.qkv_out();
+    if (!h->fast_frame || K < 2 || K > kEngineMaxCtx || (f.hd != 64 && f.hd != 128) ||
+        s.codebook_size > kEngineSampleMax || s.codebook_size % 2 ||
+        (size_t)(K - 1) * (5 * L + 2) > (size_t)kEngineMaxOps) {
+        if (h->fast_frame_prog.ops) cudaFree(h->fast_frame_prog.ops);
+        h->fast_frame_prog = EngineProgram{};
+        return S2D_OK;  // one launch per pass
+    }
+    if (h->fast_frame_prog.ops && h->fast_frame_key == k) return S2D_OK;
+    std::vector<EngineOp> ops;
+    std::vector<std::vector<int>> qkv_op((size_t)K, std::vector<int>((size_t)L, -1));
+    auto qbuf = [&](int pass, int l) { return h->fr_qkv + ((size_t)(pass - 1) * L + l) * 2 * q_out; };
+    int prev_sample = -1;
+    for (int cbk = 1; cbk < K; ++cbk) {
+        const int p0 = cbk == 1 ? 0 : cbk, M = cbk == 1 ? 2 : 1;
+        int x_src = -1;
+        for (int l = 0; l < L; ++l) {
+            const size_t base = ops.size();
+            layer_ops(h, true, l, h->fast_x + (size_t)p0 * d, M, nullptr, p0, ops, &x_src);
+            EngineOp &q = ops[base], &at = ops[base + 1], &wo = ops[base + 2];
+            q.y = qbuf(cbk, l);
+            at.qkv = qbuf(cbk, l);
+            if (l == 0 && cbk > 1) {  // the previous sample op's input row
+                q.x = h->fr_x + (size_t)cbk * d, q.x_src = prev_sample;
+                wo.resid = q.x, wo.resid_src = prev_sample;
+            }
+            qkv_op[(size_t)cbk][(size_t)l] = (int)base;
+            at.kind = OP_ATTN_CTX, at.ctx_n = p0 + M;
+            for (int j = 0; j < p0 + M; ++j) {
+                const int pass = j <= 1 ? 1 : j, row = j <= 1 ? j : 0;
+                at.ctx_qkv[j] = qbuf(pass, l) + (size_t)row * q_out;
+                at.ctx_src[j] = qkv_op[(size_t)pass][(size_t)l];
+            }
+        }
+        const int i_head = (int)ops.size();
+        ops.push_back(gemv_op(1, EPI_STORE, h->fast_out, nullptr, h->ll_x + (size_t)(M - 1) * d, d, x_src,
+                              h->fast_norm, h->fast.eps, h->fr_logits, s.codebook_size, 1, nullptr, -1, d,
+                              s.codebook_size, h->fast_out_wq));
+        EngineOp sm{};
+        sm.kind = OP_SAMPLE, sm.M = 1, sm.x = h->fr_logits, sm.x_src = i_head, sm.K = s.codebook_size, sm.N = d;
+        sm.y = cbk + 1 < K ? static_cast<void *>(h->fr_x + (size_t)(cbk + 1) * d) : nullptr;
+        sm.sample_cta = 0;
+        SampleArgs &a = sm.samp;
+        a.logits = nullptr, a.n = s.codebook_size, a.n_contig = -1, a.vocab_full = s.codebook_size;
+        a.temperature = k.temperature, a.top_p = k.top_p, a.top_k = k.top_k, a.force_id = -1;
+        a.mode = SAMPLE_FAST, a.max_new = (int)k.max_new, a.st = h->st, a.rng = &h->st->rng;
+        a.cb_index = cbk, a.frame_codes = h->frame_codes, a.codes_out = h->codes_out;
+        a.fast_emb = h->fast_emb, a.fast_x_next = nullptr, a.d = d, a.out_token = h->tok_out;
+        prev_sample = (int)ops.size();
+        ops.push_back(sm);
+    }
+    int32_t rc = upload_program(h, ops, &h->fast_frame_prog);
+    if (rc) return rc;
+    h->fast_frame_key = k;
+    return S2D_OK;
+}
+
 cudaError_t enqueue_engine(S2dHandle *h, const EngineProgram &p) {
     EngineArgs a{};
     a.ops = p.ops, a.n_ops = p.n_ops, a.nslots = p.nslots, a.slot_bytes = h->slot_bytes;
     a.area_bytes = p.area_bytes, a.epoch = h->engine_epoch, a.done = &h->st->done, a.error = &h->st->error;
     a.l2_lead = h->l2_lead;
     h->launches += 1;
-    return launch_engine(a, h->num_sms, p.smem, h->stream);
+    return launch_engine(a, h->num_sms, p.smem, h->stream, p.frame);
 }
 
 // One frame with the persistent engine: 9 Fast-AR pass programs and one
@@ -1153,7 +1257,10 @@ cudaError_t enqueue_frame_engine(S2dHandle *h, const GenKey &k) {
     fi.sem_begin = (uint32_t)s.semantic_begin_id, fi.sem_end = (uint32_t)s.semantic_end_id;
     h->launches += 1;
     if ((e = launch_fast_init(fi, h->stream, false))) return e;
-    for (int cbk = 1; cbk < K; ++cbk) {
+    if (h->fast_frame_prog.ops) {
+        if ((e = enqueue_engine(h, h->fast_frame_prog))) return e;
+    }
+    for (int cbk = 1; cbk < K && !h->fast_frame_prog.ops; ++cbk) {
         if ((e = enqueue_engine(h, h->fast_progs[(size_t)cbk]))) return e;
         SampleArgs a{};
         a.logits = h->logits_fast, a.n = s.codebook_size, a.n_contig = -1, a.vocab_full = s.codebook_size;
@@ -1869,6 +1976,9 @@ void free_handle(S2dHandle *h) {
         if (p) cudaFree(p);
     for (EngineProgram &p : h->fast_progs)
         if (p.ops) cudaFree(p.ops);
+    if (h->fast_frame_prog.ops) cudaFree(h->fast_frame_prog.ops);
+    for (void *p : {(void *)h->fr_qkv, (void *)h->fr_logits, (void *)h->fr_x})
+        if (p) cudaFree(p);
     for (auto &kv : h->tiled) cudaFree(kv.second);
     for (void *p : {(void *)h->pf_x, (void *)h->pf_qkv, (void *)h->pf_q, (void *)h->pf_att, (void *)h->pf_act,
                     (void *)h->pf_inv, (void *)h->pf_y2, (void *)h->pf_y2b, (void *)h->pf_xs})
@@ -1974,6 +2084,7 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         // with NCCL allreduces
         h->use_engine = coop && (h->tp == 1 || h->xchg) && engine_supported(h) && !(env && env[0] == '0');
         if (const char *lead = getenv("S2D_L2_LEAD")) h->l2_lead = std::max(0, std::min(64, atoi(lead)));
+        if (const char *ff = getenv("S2D_FAST_FRAME")) h->fast_frame = ff[0] != '0';
         if (const char *sp = getenv("S2D_ATT_SPLITS")) h->engine_att_splits = std::max(0, atoi(sp));
         if (const char *tc = getenv("S2D_TCGEMM")) h->use_tc = tc[0] == '1';
         if (const char *ab = getenv("S2D_BATCH_ATT_BLOCKS")) h->attn_blocks_per_sm = std::max(1, std::min(64, atoi(ab)));
@@ -2201,6 +2312,7 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
     // frames (generate.rs:165-211): one captured graph per frame
     if (!h->frame_exec || !(h->frame_key == k)) {
         if (h->use_engine && (rc = build_programs(h, k.im_end))) return rc;
+        if (h->use_engine && (rc = build_fast_frame(h, k))) return rc;
         if (h->frame_exec) cudaGraphExecDestroy(h->frame_exec);
         h->frame_exec = nullptr;
         cudaGraph_t graph = nullptr;
@@ -2549,8 +2661,10 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
     CK(cudaSetDevice(h->device));
     int32_t rc = build_programs(h, h->slow_prog.ops ? h->slow_prog_im_end : 0xffffffffu);
     if (rc) return rc;
-    if (program < 0 || program >= (int)h->fast_progs.size()) return set_err(h, S2D_EINVAL, "no such program");
-    const EngineProgram &p = program == 0 ? h->slow_prog : h->fast_progs[(size_t)program];
+    if (program < -1 || program >= (int)h->fast_progs.size()) return set_err(h, S2D_EINVAL, "no such program");
+    const EngineProgram &p = program == -1  ? h->fast_frame_prog
+                             : program == 0 ? h->slow_prog
+                                            : h->fast_progs[(size_t)program];
     if (!p.ops) return set_err(h, S2D_EINVAL, "no such program");
     *n_ops = p.n_ops;
     unsigned long long *dtr = nullptr;
@@ -2566,7 +2680,7 @@ int32_t s2d_profile_engine(S2dHandle *h, int32_t program, uint64_t *trace, int64
     a.l2_lead = h->l2_lead;
     a.trace = dtr;
     cudaError_t e = cudaEventRecord(h->ev0, h->stream);
-    if (!e) e = launch_engine(a, h->num_sms, p.smem, h->stream);
+    if (!e) e = launch_engine(a, h->num_sms, p.smem, h->stream, p.frame);
     if (!e) e = cudaEventRecord(h->ev1, h->stream);
     if (!e) e = cudaEventSynchronize(h->ev1);
     float t = 0.f;
