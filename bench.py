@@ -330,6 +330,11 @@ def run_ours(args, d: Dist, wl_name=None, use_tp=False, steps=None, warmup=None,
                                    (2, "fast_pass", bpf["fast"] / passes)):
             ms = statistics.median(st.profile_engine(prog, trace=False)[0] for _ in range(7))
             kern[name] = {"ms": ms, "bytes": nbytes, "gbs": nbytes / ms / 1e6}
+        try:  # the frame's whole Fast-AR in one launch (all passes, heads and samplers)
+            ms = statistics.median(st.profile_engine(-1, trace=False)[0] for _ in range(7))
+            kern["fast_frame"] = {"ms": ms, "bytes": bpf["fast"], "gbs": bpf["fast"] / ms / 1e6}
+        except RuntimeError:
+            pass
     top = kern.get("slow_step")
     p_avg = wl.prompt_len + frames / 2
     frame_bytes = sum(bpf.values()) + configs.kv_bytes_per_position(m) * p_avg

@@ -383,7 +383,9 @@ class SlowArState:
         return float(ms.value), float(nb.value)
 
     def profile_engine(self, program: int = 0, trace: bool = True, per_cta: bool = False):
-        """Run one persistent-engine program once (s2d_profile_engine).
+        """Run one persistent-engine program once (s2d_profile_engine):
+        0 the Slow-AR step, k >= 1 Fast-AR pass k, -1 the frame's whole
+        Fast-AR.
         Returns (ms, trace) with trace shaped [2 CTAs][n_ops][4] in ns; with
         per_cta, (ms, trace, finish) where finish is [n_ops][CTAs] in ns."""
         n = ctypes.c_int32()

@@ -260,7 +260,10 @@ int32_t s2d_profile_kernel(S2dHandle *h, int32_t kernel, int32_t iters, double *
 /* Runs one program of the persistent decode engine once, outside any graph,
  * on the handle's current state (call after s2d_generate_codes): program 0 is
  * the Slow-AR step (all layers + LM head), program k >= 1 the Fast-AR pass
- * that produces codebook k.  *ms: its CUDA-event duration.  If trace is not
+ * that produces codebook k, program -1 the whole Fast-AR of a frame (every
+ * pass, head and sampler in one launch; built by the first
+ * s2d_generate_codes, absent with S2D_FAST_FRAME=0).  *ms: its CUDA-event
+ * duration.  If trace is not
  * NULL it receives n_ops*(8+G) timestamps (ns, %globaltimer), G = the SM
  * count: first for CTA 0 then the last CTA, per op: op started, input staged,
  * op finished, producer done issuing the op's weights; then per op, every
