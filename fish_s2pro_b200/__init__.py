@@ -3,7 +3,8 @@
 The product is libs2d.so (C ABI: include/s2d.h).  This package holds its
 sources (csrc/), the in-tree build (build.py), the Python mirror of the
 reference's `rust-pure` interface (s2d.py), the workload configurations
-(configs.py) and the seeded synthetic GGUF writer (synth.py).
+(configs.py), the seeded synthetic GGUF writer (synth.py) and the
+continuous-batching scheduler over the s2d_serve_* calls (serve.py).
 """
 from .s2d import (  # noqa: F401
     LOGITS_ALLOWED,
@@ -33,3 +34,4 @@ from .s2d import (  # noqa: F401
     sample_token,
     transpose_to_time_major,
 )
+from .serve import ServeSession, TtsScheduler  # noqa: F401,E402

@@ -216,6 +216,18 @@ struct S2dHandle {
     GenKey batch_key;
     int batch_n = 0, batch_rng_kind = -1;
     uint64_t batch_philox = 0;
+    // Continuous batching (s2d_serve_*): every slot of the batched frame is
+    // either free, running or finished; admission hands a sequence the pool
+    // pages its prompt and generation need (serve_free lists the pages no
+    // slot holds) and writes them into the slot's page-table row.
+    bool serving = false;
+    GenKey serve_key;
+    int serve_rng_kind = 0;
+    uint64_t serve_philox = 0;
+    std::vector<int32_t> serve_cols;  // per slot: prompt columns, -1 when free
+    std::vector<std::vector<int32_t>> serve_pages;
+    std::vector<int32_t> serve_free;
+    std::vector<int32_t> pool_order;  // the pool's pages in dealing order
     uint32_t batch_kernels = 0;
 };
 
@@ -1792,13 +1804,15 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
         const size_t nsem = (size_t)(s.semantic_end_id - s.semantic_begin_id + 1);
         const size_t kvf = (size_t)f.L * 2 * f.Hkv * f.ctx * f.hd;
         // The Slow-AR caches of the batch: a pool of kKvPage-position pages
-        // ([layer][K | V][kv head][kKvPage][hd] f16 each) and a page table.
-        // The pages are dealt out in a seeded random order, so that no
-        // sequence's cache is contiguous; a continuous-batching host would
-        // hand pages out and take them back per sequence instead.
+        // ([layer][K | V][kv head][kKvPage][hd] f16 each) and a page table
+        // of kv_per_seq entries per slot.  Pages are dealt out per call
+        // (deal_pages) or per admitted request (s2d_serve_admit) in a seeded
+        // random order of the pool (pool_order), so that no sequence's cache
+        // is contiguous.
         h->kv_per_seq = (h->cfg.max_seq + kKvPage - 1) / kKvPage;
         h->kv_page_elems = (size_t)a.L * 2 * a.Hkv * kKvPage * a.hd;
-        const size_t n_pages = B * (size_t)h->kv_per_seq;
+        const size_t n_rows = B * (size_t)h->kv_per_seq;  // page-table entries
+        const size_t n_pages = h->cfg.kv_pages > 0 ? (size_t)h->cfg.kv_pages : n_rows;
         CK(cudaMalloc(&h->kv_pool, n_pages * h->kv_page_elems * sizeof(__half)));
         CK(cudaMemset(h->kv_pool, 0, n_pages * h->kv_page_elems * sizeof(__half)));
         std::vector<int32_t> table(n_pages);
@@ -1810,8 +1824,9 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
             z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
             std::swap(table[i - 1], table[(z ^ (z >> 31)) % i]);
         }
-        CK(cudaMalloc(&h->kv_page_table, n_pages * sizeof(int32_t)));
-        CK(cudaMemcpy(h->kv_page_table, table.data(), n_pages * sizeof(int32_t), cudaMemcpyHostToDevice));
+        CK(cudaMalloc(&h->kv_page_table, n_rows * sizeof(int32_t)));
+        CK(cudaMemset(h->kv_page_table, 0, n_rows * sizeof(int32_t)));
+        h->pool_order = table;
         CK(cudaMalloc(&h->st_b, B * sizeof(DevState)));
         CK(cudaMemset(h->st_b, 0, B * sizeof(DevState)));
         CK(cudaMalloc(&h->bx, B * d * sizeof(float)));
@@ -2020,7 +2035,7 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
     }
     S2dHandle *h = new (std::nothrow) S2dHandle();
     if (!h) return report(nullptr, S2D_ENOMEM);
-    h->cfg = cfg ? *cfg : S2dConfig{0, 4096, 1, 0};
+    h->cfg = cfg ? *cfg : S2dConfig{0, 4096, 1, 0, 0};
     if (h->cfg.max_seq <= 0) {
         h->err = "max_seq_len must be non-zero";
         return report(h, S2D_EINVAL);
@@ -2374,6 +2389,69 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
     return S2D_OK;
 }
 
+namespace {
+
+// Prefill of batch slot i (generate.rs:126-162 for one sequence): the
+// prompt (rows x cols, row-major, transposed to time-major here) into the
+// slot's pages of the pool, then the first semantic sample into the slot's
+// DevState with RNG state `rng`; the post-norm hidden goes to the slot's row
+// of hidden_b.  The single-sequence state is reset afterwards.
+int32_t batch_admit_seq(S2dHandle *h, int i, const uint32_t *prompt, int rows, int cols, const GenKey &k,
+                        uint64_t rng, int rng_kind, uint64_t philox_key) {
+    const S2dGraphSpec &s = h->spec;
+    std::vector<int32_t> flat((size_t)rows * cols);
+    for (int t = 0; t < cols; ++t)
+        for (int r = 0; r < rows; ++r) {
+            const uint32_t v = prompt[(size_t)r * cols + t];
+            if (v > 0x7fffffffu) return set_err(h, S2D_EINVAL, "prompt token id does not fit i32");
+            flat[(size_t)t * rows + r] = (int32_t)v;
+        }
+    h->pf_pages = h->kv_page_table + (size_t)i * h->kv_per_seq;  // slot i's pages
+    h->n_past = 0;
+    int32_t rc = slow_eval(h, flat.data(), (int64_t)flat.size(), S2D_LOGITS_ALLOWED, k.im_end);
+    h->pf_pages = nullptr;
+    const int32_t n_past = h->n_past;
+    h->n_past = 0;  // the single-sequence state is reset
+    if (rc) return rc;
+    CK(launch_set_state(h->st_b + i, n_past, cols, rng, h->stream));
+    SampleArgs first = slow_sample_args(h, SAMPLE_SLOW_FIRST, k);
+    first.st = h->st_b + i, first.rng = &h->st_b[i].rng, first.out_token = nullptr;
+    first.rng_kind = rng_kind, first.philox_key = philox_key, first.rng_seq = (uint32_t)i;
+    CK(launch_sample(first, h->stream, false));
+    CK(cudaMemcpyAsync(h->hidden_b + (size_t)i * s.hidden, h->hidden_post, (size_t)s.hidden * sizeof(float),
+                       cudaMemcpyDeviceToDevice, h->stream));
+    h->launches += 2;
+    return S2D_OK;
+}
+
+// The captured frame of n_seq batch slots for key k (re-captured when any of
+// the key, the slot count or the RNG changes).
+int32_t ensure_batch_graph(S2dHandle *h, const GenKey &k, int n_seq, int rng_kind, uint64_t philox_key) {
+    if (h->batch_exec && h->batch_key == k && h->batch_n == n_seq && h->batch_rng_kind == rng_kind &&
+        h->batch_philox == philox_key)
+        return S2D_OK;
+    if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
+    h->batch_exec = nullptr;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    const uint32_t l0 = h->launches;
+    const int32_t rc = enqueue_frame_batch(h, k, n_seq, rng_kind, philox_key);
+    h->batch_kernels = h->launches - l0;
+    cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
+    if (rc || e2) {
+        if (graph) cudaGraphDestroy(graph);
+        if (rc) return rc;
+        return set_err(h, S2D_ECUDA, std::string("batch frame capture: ") + cudaGetErrorString(e2));
+    }
+    cudaError_t e = cudaGraphInstantiateWithFlags(&h->batch_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e) return set_err(h, S2D_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    h->batch_key = k, h->batch_n = n_seq, h->batch_rng_kind = rng_kind, h->batch_philox = philox_key;
+    return S2D_OK;
+}
+
+}  // namespace
+
 int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *const *prompts,
                                  const int32_t *cols, int32_t rows, const S2dGenParams *p, int32_t rng_kind,
                                  uint64_t philox_key, uint64_t *rng_states, int32_t *out_codes,
@@ -2409,35 +2487,27 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
     // into its own KV cache
     CK(cudaEventRecord(h->ev0, h->stream));
     const uint32_t launches0 = h->launches;
-    for (int i = 0; i < n_seq; ++i) {
-        std::vector<int32_t> flat((size_t)rows * cols[i]);
-        for (int t = 0; t < cols[i]; ++t)
-            for (int r = 0; r < rows; ++r) {
-                const uint32_t v = prompts[i][(size_t)r * cols[i] + t];
-                if (v > 0x7fffffffu) {
-                    h->n_past = 0;
-                    return set_err(h, S2D_EINVAL, "prompt token id does not fit i32");
-                }
-                flat[(size_t)t * rows + r] = (int32_t)v;
-            }
-        h->pf_pages = h->kv_page_table + (size_t)i * h->kv_per_seq;  // sequence i's pages
-        h->n_past = 0;
-        rc = slow_eval(h, flat.data(), (int64_t)flat.size(), S2D_LOGITS_ALLOWED, p->im_end_id);
-        h->pf_pages = nullptr;
-        if (rc) {
-            h->n_past = 0;
-            return rc;
+    h->serving = false;  // any serving slots are dropped
+    {
+        // each sequence gets the pages of positions [0, cols + max_new), in
+        // the pool's dealing order
+        std::vector<int32_t> table((size_t)n_seq * h->kv_per_seq);
+        size_t next = 0;
+        for (int i = 0; i < n_seq; ++i) {
+            const size_t need = ((size_t)cols[i] + p->max_new_tokens + kKvPage - 1) / kKvPage;
+            if (next + need > h->pool_order.size())
+                return set_err(h, S2D_EFULL, "the KV pool has " + std::to_string(h->pool_order.size()) +
+                                                 " pages; the batch needs more");
+            for (int j = 0; j < h->kv_per_seq; ++j)
+                table[(size_t)i * h->kv_per_seq + j] = h->pool_order[next + std::min((size_t)j, need - 1)];
+            next += need;
         }
-        CK(launch_set_state(h->st_b + i, h->n_past, cols[i], rng_states[i], h->stream));
-        SampleArgs first = slow_sample_args(h, SAMPLE_SLOW_FIRST, k);
-        first.st = h->st_b + i, first.rng = &h->st_b[i].rng, first.out_token = nullptr;
-        first.rng_kind = rng_kind, first.philox_key = philox_key, first.rng_seq = (uint32_t)i;
-        CK(launch_sample(first, h->stream, false));
-        CK(cudaMemcpyAsync(h->hidden_b + (size_t)i * s.hidden, h->hidden_post, (size_t)s.hidden * sizeof(float),
-                           cudaMemcpyDeviceToDevice, h->stream));
-        h->launches += 2;
+        CK(cudaMemcpyAsync(h->kv_page_table, table.data(), table.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                           h->stream));
     }
-    h->n_past = 0;  // the single-sequence state is reset
+    for (int i = 0; i < n_seq; ++i)
+        if ((rc = batch_admit_seq(h, i, prompts[i], rows, cols[i], k, rng_states[i], rng_kind, philox_key)))
+            return rc;
     const uint32_t prefill_kernels = h->launches - launches0;
     // the batched attention's block order: longest context first (every
     // sequence advances one position per frame, so the order holds)
@@ -2449,26 +2519,7 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
     CK(cudaEventRecord(h->ev1, h->stream));
 
     // frames: one captured graph advances every sequence by one frame
-    if (!h->batch_exec || !(h->batch_key == k) || h->batch_n != n_seq || h->batch_rng_kind != rng_kind ||
-        h->batch_philox != philox_key) {
-        if (h->batch_exec) cudaGraphExecDestroy(h->batch_exec);
-        h->batch_exec = nullptr;
-        cudaGraph_t graph = nullptr;
-        CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-        const uint32_t l0 = h->launches;
-        rc = enqueue_frame_batch(h, k, n_seq, rng_kind, philox_key);
-        h->batch_kernels = h->launches - l0;
-        cudaError_t e2 = cudaStreamEndCapture(h->stream, &graph);
-        if (rc || e2) {
-            if (graph) cudaGraphDestroy(graph);
-            if (rc) return rc;
-            return set_err(h, S2D_ECUDA, std::string("batch frame capture: ") + cudaGetErrorString(e2));
-        }
-        cudaError_t e = cudaGraphInstantiateWithFlags(&h->batch_exec, graph, 0);
-        cudaGraphDestroy(graph);
-        if (e) return set_err(h, S2D_ECUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
-        h->batch_key = k, h->batch_n = n_seq, h->batch_rng_kind = rng_kind, h->batch_philox = philox_key;
-    }
+    if ((rc = ensure_batch_graph(h, k, n_seq, rng_kind, philox_key))) return rc;
     const uint32_t poll = 8;
     std::vector<DevState> st((size_t)n_seq);
     uint32_t launched = 0;
@@ -2516,6 +2567,163 @@ int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *co
         profile->prefill_kernels = prefill_kernels;
         profile->frame_launches = launched;
     }
+    return S2D_OK;
+}
+
+// ---- continuous batching ---------------------------------------------------
+
+namespace {
+
+// The batched attention's block order over the session's slots: running
+// slots by descending prompt length (their contexts grow in step), then the
+// others.
+int32_t serve_order(S2dHandle *h) {
+    const int B = h->max_batch;
+    std::vector<int32_t> order((size_t)B);
+    for (int i = 0; i < B; ++i) order[(size_t)i] = i;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int32_t x, int32_t y) { return h->serve_cols[(size_t)x] > h->serve_cols[(size_t)y]; });
+    CK(cudaMemcpyAsync(h->batch_order, order.data(), order.size() * sizeof(int32_t), cudaMemcpyHostToDevice,
+                       h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    return S2D_OK;
+}
+
+}  // namespace
+
+int32_t s2d_serve_begin(S2dHandle *h, const S2dGenParams *p, int32_t rng_kind, uint64_t philox_key) {
+    if (!h) return S2D_EINVAL;
+    if (!p) return set_err(h, S2D_EINVAL, "s2d_serve_begin: NULL params");
+    if (rng_kind != S2D_RNG_SEEDED && rng_kind != S2D_RNG_PHILOX) return set_err(h, S2D_EINVAL, "unknown rng_kind");
+    if (p->max_new_tokens == 0) return set_err(h, S2D_EINVAL, "max_new_tokens must be positive");
+    const int B = h->max_batch;
+    if (B > kBatchMaxSeq)
+        return set_err(h, S2D_EINVAL, "max_batch must be at most " + std::to_string(kBatchMaxSeq) + " for serving");
+    if ((int64_t)p->max_new_tokens >= h->cfg.max_seq) return set_err(h, S2D_EINVAL, "max_new_tokens exceeds max_seq");
+    CK(cudaSetDevice(h->device));
+    const S2dGraphSpec &s = h->spec;
+    int32_t rc;
+    if ((rc = ensure_batch(h, p->max_new_tokens))) return rc;
+    if ((s.linear_type != 1 || h->fast_out_wq != EW_F16) && (rc = ensure_f16_linears(h))) return rc;
+    GenKey k;
+    k.max_new = p->max_new_tokens, k.min_tokens = p->min_tokens_before_end, k.im_end = p->im_end_id;
+    k.temperature = p->temperature, k.top_p = p->top_p, k.top_k = p->top_k;
+    // every slot free: a finished DevState, so that every kernel skips it
+    std::vector<DevState> st((size_t)B);
+    for (DevState &x : st) x = DevState{}, x.done = 1;
+    CK(cudaMemcpyAsync(h->st_b, st.data(), st.size() * sizeof(DevState), cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemsetAsync(h->codes_b, 0, (size_t)B * s.num_codebooks * p->max_new_tokens * sizeof(int32_t),
+                       h->stream));
+    h->serve_key = k, h->serve_rng_kind = rng_kind, h->serve_philox = philox_key;
+    h->serve_cols.assign((size_t)B, -1);
+    h->serve_pages.assign((size_t)B, {});
+    h->serve_free = h->pool_order;  // the pool's pages, in the dealing (shuffled) order
+    h->serving = true;
+    if ((rc = ensure_batch_graph(h, k, B, rng_kind, philox_key))) return rc;
+    if ((rc = serve_order(h))) return rc;
+    return check_device_error(h);
+}
+
+int32_t s2d_serve_admit(S2dHandle *h, int32_t slot, const uint32_t *prompt, int32_t rows, int32_t cols,
+                        uint64_t rng_state) {
+    if (!h) return S2D_EINVAL;
+    if (!h->serving) return set_err(h, S2D_ESTATE, "s2d_serve_admit needs s2d_serve_begin first");
+    if (!prompt) return set_err(h, S2D_EINVAL, "s2d_serve_admit: NULL prompt");
+    if (slot < 0 || slot >= h->max_batch) return set_err(h, S2D_EINVAL, "slot out of range");
+    if (h->serve_cols[(size_t)slot] >= 0) return set_err(h, S2D_ESTATE, "slot is not free");
+    if (rows != h->spec.num_codebooks + 1) return set_err(h, S2D_EINVAL, "prompt rows must be num_codebooks+1");
+    if (cols <= 0) return set_err(h, S2D_EINVAL, "expected at least one prompt token");
+    const GenKey &k = h->serve_key;
+    if ((int64_t)cols + (int64_t)k.max_new > h->cfg.max_seq)
+        return set_err(h, S2D_ESTATE, "prompt + max_new_tokens exceeds max_seq");
+    // the pages of positions [0, cols + max_new): the prompt, then one per frame
+    const size_t need = ((size_t)cols + k.max_new + kKvPage - 1) / kKvPage;
+    if (need > h->serve_free.size())
+        return set_err(h, S2D_EFULL, "not enough free KV pages: " + std::to_string(need) + " needed, " +
+                                         std::to_string(h->serve_free.size()) + " free");
+    CK(cudaSetDevice(h->device));
+    std::vector<int32_t> row((size_t)h->kv_per_seq);
+    std::vector<int32_t> pages(h->serve_free.begin(), h->serve_free.begin() + (ptrdiff_t)need);
+    for (size_t j = 0; j < row.size(); ++j) row[j] = pages[std::min(j, need - 1)];  // unused entries: never read
+    CK(cudaMemcpyAsync(h->kv_page_table + (size_t)slot * h->kv_per_seq, row.data(), row.size() * sizeof(int32_t),
+                       cudaMemcpyHostToDevice, h->stream));
+    const size_t codes_stride = (size_t)h->spec.num_codebooks * k.max_new;
+    CK(cudaMemsetAsync(h->codes_b + (size_t)slot * codes_stride, 0, codes_stride * sizeof(int32_t), h->stream));
+    int32_t rc = batch_admit_seq(h, slot, prompt, rows, cols, k, rng_state, h->serve_rng_kind, h->serve_philox);
+    if (rc) {
+        // leave the slot free and finished again
+        DevState x{};
+        x.done = 1;
+        cudaMemcpyAsync(h->st_b + slot, &x, sizeof(DevState), cudaMemcpyHostToDevice, h->stream);
+        cudaStreamSynchronize(h->stream);
+        return rc;
+    }
+    h->serve_free.erase(h->serve_free.begin(), h->serve_free.begin() + (ptrdiff_t)need);
+    h->serve_pages[(size_t)slot] = std::move(pages);
+    h->serve_cols[(size_t)slot] = cols;
+    if ((rc = serve_order(h))) return rc;
+    return check_device_error(h);
+}
+
+int32_t s2d_serve_step(S2dHandle *h, int32_t n_frames, int32_t *slot_status, uint32_t *slot_frames) {
+    if (!h) return S2D_EINVAL;
+    if (!h->serving) return set_err(h, S2D_ESTATE, "s2d_serve_step needs s2d_serve_begin first");
+    if (n_frames < 0) return set_err(h, S2D_EINVAL, "n_frames must not be negative");
+    CK(cudaSetDevice(h->device));
+    const int B = h->max_batch;
+    std::vector<DevState> st((size_t)B);
+    bool running = false;
+    for (int i = 0; i < B; ++i) running |= h->serve_cols[(size_t)i] >= 0;
+    if (running)
+        for (int32_t f = 0; f < n_frames; ++f) CK(cudaGraphLaunch(h->batch_exec, h->stream));
+    CK(cudaMemcpyAsync(st.data(), h->st_b, st.size() * sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    int32_t rc;
+    if ((rc = check_device_error(h))) return rc;
+    for (int i = 0; i < B; ++i) {
+        const DevState &x = st[(size_t)i];
+        if (x.error)
+            return set_err(h, S2D_EDEVICE, "slot " + std::to_string(i) + ": device error flag " + std::to_string(x.error));
+        const bool busy = h->serve_cols[(size_t)i] >= 0;
+        if (slot_status) slot_status[i] = !busy ? S2D_SLOT_FREE : x.done ? S2D_SLOT_FINISHED : S2D_SLOT_RUNNING;
+        if (slot_frames) slot_frames[i] = busy ? (uint32_t)x.step_index : 0u;
+    }
+    return S2D_OK;
+}
+
+int32_t s2d_serve_collect(S2dHandle *h, int32_t slot, int32_t *out_codes, uint32_t *out_n_frames,
+                          uint64_t *rng_state) {
+    if (!h) return S2D_EINVAL;
+    if (!h->serving) return set_err(h, S2D_ESTATE, "s2d_serve_collect needs s2d_serve_begin first");
+    if (!out_codes || !out_n_frames) return set_err(h, S2D_EINVAL, "s2d_serve_collect: NULL argument");
+    if (slot < 0 || slot >= h->max_batch) return set_err(h, S2D_EINVAL, "slot out of range");
+    if (h->serve_cols[(size_t)slot] < 0) return set_err(h, S2D_ESTATE, "slot holds no request");
+    CK(cudaSetDevice(h->device));
+    const int K = h->spec.num_codebooks;
+    const uint32_t max_new = h->serve_key.max_new;
+    DevState x{};
+    std::vector<int32_t> codes((size_t)K * max_new);
+    CK(cudaMemcpyAsync(&x, h->st_b + slot, sizeof(DevState), cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaMemcpyAsync(codes.data(), h->codes_b + (size_t)slot * codes.size(), codes.size() * sizeof(int32_t),
+                       cudaMemcpyDeviceToHost, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+    if (!x.done) return set_err(h, S2D_ESTATE, "slot " + std::to_string(slot) + " has not finished");
+    // compact_codes (generate.rs:346-390)
+    const uint32_t frames = (uint32_t)x.step_index;
+    for (int cb = 0; cb < K; ++cb)
+        for (uint32_t t = 0; t < frames; ++t) out_codes[(size_t)cb * frames + t] = codes[(size_t)cb * max_new + t];
+    *out_n_frames = frames;
+    if (rng_state) *rng_state = x.rng;
+    std::vector<int32_t> &pg = h->serve_pages[(size_t)slot];
+    h->serve_free.insert(h->serve_free.end(), pg.begin(), pg.end());
+    pg.clear();
+    h->serve_cols[(size_t)slot] = -1;
+    return serve_order(h);
+}
+
+int32_t s2d_serve_free_pages(const S2dHandle *h, int32_t *out) {
+    if (!h || !out) return S2D_EINVAL;
+    *out = h->serving ? (int32_t)h->serve_free.size() : 0;
     return S2D_OK;
 }
 

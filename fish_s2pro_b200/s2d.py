@@ -40,7 +40,7 @@ class S2dError(RuntimeError):
 
 class _Config(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("max_seq", ctypes.c_int32),
-                ("max_batch", ctypes.c_int32), ("flags", ctypes.c_int32)]
+                ("max_batch", ctypes.c_int32), ("flags", ctypes.c_int32), ("kv_pages", ctypes.c_int32)]
 
 
 _SPEC_INTS1 = ["slow_layers", "hidden", "ffn", "heads", "kv_heads", "head_dim", "context_length",
@@ -113,6 +113,12 @@ SIGNATURES = {
                                                   _P(ctypes.c_void_p), _i32p, ctypes.c_int32,
                                                   _P(_GenParams), ctypes.c_int32, ctypes.c_uint64,
                                                   _u64p, _i32p, _u32p, _P(_Profile)]),
+    "s2d_serve_begin": (ctypes.c_int32, [ctypes.c_void_p, _P(_GenParams), ctypes.c_int32, ctypes.c_uint64]),
+    "s2d_serve_admit": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _u32p, ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.c_uint64]),
+    "s2d_serve_step": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _i32p, _u32p]),
+    "s2d_serve_collect": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _i32p, _u32p, _u64p]),
+    "s2d_serve_free_pages": (ctypes.c_int32, [ctypes.c_void_p, _i32p]),
     "s2d_philox4x32_10": (ctypes.c_int32, [_u32p, _u32p, _u32p]),
     "s2d_profile_batch": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_int32, _P(ctypes.c_double),
                                            ctypes.c_int32]),
@@ -291,16 +297,17 @@ class SlowArState:
 
     @classmethod
     def open(cls, transformer_path, max_seq_len: int = 32768, device: int = 0,
-             max_batch: int = 1, tp: Optional[tuple] = None) -> "SlowArState":
-        """max_batch: sequences of generate_codes_batch (each with its own KV
-        cache of max_seq_len positions).  tp: (tp_size, tp_rank, nccl_id) to
+             max_batch: int = 1, tp: Optional[tuple] = None, kv_pages: int = 0) -> "SlowArState":
+        """max_batch: sequences of generate_codes_batch or serving slots;
+        kv_pages: pages of 64 positions in their shared KV pool (0: room for
+        max_batch sequences of max_seq_len positions).  tp: (tp_size, tp_rank, nccl_id) to
         open one rank of a tensor-parallel Slow-AR (collective over the
         ranks; nccl_id from nccl_unique_id() on one rank)."""
         if max_seq_len <= 0:
             raise S2dError(-1, "max_seq_len must be non-zero")
         h = ctypes.c_void_p()
         err = ctypes.create_string_buffer(1024)
-        cfg = _Config(device=device, max_seq=max_seq_len, max_batch=max_batch, flags=0)
+        cfg = _Config(device=device, max_seq=max_seq_len, max_batch=max_batch, flags=0, kv_pages=kv_pages)
         if tp is not None and tp[0] > 1:
             size, rank, nid = tp
             rc = lib().s2d_open_tp(str(transformer_path).encode(), ctypes.byref(cfg), size, rank,
@@ -310,7 +317,9 @@ class SlowArState:
                                 err, len(err))
         if rc != 0:
             raise S2dError(rc, err.value.decode(errors="replace"))
-        return cls(h, str(transformer_path))
+        st = cls(h, str(transformer_path))
+        st.max_batch = max(1, int(max_batch))
+        return st
 
     def close(self) -> None:
         if self._h:

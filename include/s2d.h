@@ -31,6 +31,7 @@ extern "C" {
 #define S2D_ENOMEM (-4)   /* device or host allocation failed         */
 #define S2D_ESTATE (-5)   /* KV cache overflow or call out of order   */
 #define S2D_EDEVICE (-6)  /* a kernel reported an error flag           */
+#define S2D_EFULL (-7)    /* serving: no free slot or KV pages; collect first */
 
 typedef struct S2dHandle S2dHandle;
 
@@ -42,6 +43,11 @@ typedef struct S2dConfig {
     int32_t max_batch;    /* sequences of s2d_generate_codes_batch (<= 0: 1); each
                              holds its own Slow-AR KV cache of max_seq positions   */
     int32_t flags;        /* reserved, 0                                             */
+    int32_t kv_pages;     /* pages of 64 positions in the batched KV pool (every
+                             layer's K and V of one sequence's 64 positions);
+                             <= 0: max_batch * ceil(max_seq / 64), room for every
+                             sequence at max_seq.  Batched calls give each
+                             sequence the pages of its prompt + max_new_tokens. */
 } S2dConfig;
 
 /* DualArGraphSpec (registry.rs:30-42, 216-231), shape-parametric. */
@@ -202,12 +208,53 @@ int32_t s2d_generate_codes(S2dHandle *h, const uint32_t *prompt, int32_t rows, i
  * cols[i] + max_new_tokens <= max_seq.  Q8_0 / Q4_K linears run as GEMMs over
  * an f16 expansion (exact dequantisation rounded to f16) that the first
  * batched call builds and the handle keeps.  Resets the single-sequence
- * state (n_past = 0): sequence 0's cache is reused.  profile (may be NULL)
- * counts frames over all sequences. */
+ * state (n_past = 0): sequence 0's cache is reused.  Ends a serving session
+ * (s2d_serve_begin) on the handle.  profile (may be NULL) counts frames over
+ * all sequences. */
 int32_t s2d_generate_codes_batch(S2dHandle *h, int32_t n_seq, const uint32_t *const *prompts,
                                  const int32_t *cols, int32_t rows, const S2dGenParams *params,
                                  int32_t rng_kind, uint64_t philox_key, uint64_t *rng_states,
                                  int32_t *out_codes, uint32_t *out_n_frames, S2dProfile *profile);
+
+/* ---- continuous batching (serving) -----------------------------------------
+ * The server-side form of generate_codes.  The reference serves one /v1/tts
+ * request at a time under a lock (tts_handler, server.rs:89-120, over
+ * InferenceEngine::synthesize_wav, engine.rs:255-287, whose pipeline calls
+ * generate_codes, pipeline.rs:174-182).  Here a session holds max_batch
+ * slots (S2dConfig) that advance together, one captured batched frame per
+ * frame; requests join and leave between frames:
+ *   s2d_serve_begin   opens the session with one set of generation params
+ *                     and RNG kind, every slot free;
+ *   s2d_serve_admit   prefills one request (prompt rows x cols, row-major,
+ *                     rows = num_codebooks + 1) into a free slot and samples
+ *                     its first semantic token.  The request takes the KV
+ *                     pages of positions [0, cols + max_new_tokens) from
+ *                     the handle's pool (ceil(.../64) pages of 64
+ *                     positions); S2D_EFULL when too few are free;
+ *   s2d_serve_step    runs n_frames frames; slot_status[i] (may be NULL)
+ *                     receives S2D_SLOT_*, slot_frames[i] the frames slot i
+ *                     has produced;
+ *   s2d_serve_collect copies a finished slot's codes (codebook-major,
+ *                     compacted to *out_n_frames frames, like
+ *                     s2d_generate_codes; out_codes holds num_codebooks *
+ *                     max_new_tokens) and its final RNG state, and frees the
+ *                     slot and its pages.
+ * With S2D_RNG_SEEDED a request's codes do not depend on which slot it runs
+ * in, on its neighbours or on when it was admitted (each row of the batched
+ * frame is computed alone); with S2D_RNG_PHILOX its draws are keyed by the
+ * slot index.  Every call is synchronous; no counterpart in the reference
+ * beyond the loop it batches. */
+#define S2D_SLOT_FREE 0
+#define S2D_SLOT_RUNNING 1
+#define S2D_SLOT_FINISHED 2
+int32_t s2d_serve_begin(S2dHandle *h, const S2dGenParams *params, int32_t rng_kind, uint64_t philox_key);
+int32_t s2d_serve_admit(S2dHandle *h, int32_t slot, const uint32_t *prompt, int32_t rows, int32_t cols,
+                        uint64_t rng_state);
+int32_t s2d_serve_step(S2dHandle *h, int32_t n_frames, int32_t *slot_status, uint32_t *slot_frames);
+int32_t s2d_serve_collect(S2dHandle *h, int32_t slot, int32_t *out_codes, uint32_t *out_n_frames,
+                          uint64_t *rng_state);
+/* KV pages of the pool that no serving slot holds (0 outside a session). */
+int32_t s2d_serve_free_pages(const S2dHandle *h, int32_t *out);
 
 /* Device time of one batched frame by kernel category: the frame of the
  * last s2d_generate_codes_batch call (its first n_seq sequences), replayed

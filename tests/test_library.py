@@ -34,7 +34,7 @@ def test_struct_layouts_match_header():
     fields = re.findall(r"\b(\w+)\s*[,;]", re.sub(r"/\*.*?\*/", "", spec, flags=re.S))
     assert [f for f, _ in s2d._Spec._fields_] == [f for f in fields if f not in ("int32_t", "float")]
     assert ctypes.sizeof(s2d._GenParams) == 24
-    assert ctypes.sizeof(s2d._Config) == 16
+    assert ctypes.sizeof(s2d._Config) == 20
 
 
 def test_open_reports_missing_file_without_crashing(tmp_path):
