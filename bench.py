@@ -86,6 +86,8 @@ def parse():
                          "utterance (strong scaling); the default under torchrun")
     ap.add_argument("--replicas", action="store_true",
                     help="under torchrun: independent replicas (weak scaling) as the headline line")
+    ap.add_argument("--no-serving", action="store_true",
+                    help="skip the nested continuous-batching line of the default run")
     ap.add_argument("--no-quant", action="store_true",
                     help="skip the nested C3 (Q8_0) and C5 (Q4_K) lines of the default N = 1 run")
     return ap.parse_args()
@@ -403,6 +405,73 @@ def run_ours(args, d: Dist, wl_name=None, use_tp=False, steps=None, warmup=None,
     return line
 
 
+def run_serving(args, d: Dist, wl, n_req=128, frames=64, slots=64, kv_pages=640):
+    """Continuous batching (TtsScheduler over s2d_serve_*) on the C4 model:
+    n_req requests with C4's prompt lengths (uniform 128..1024) arrive at
+    once and share `slots` slots of the batched frame; each generates
+    `frames` frames (T 0.8, top-p 0.9, top-k 30, per-request SeededRng).  The
+    KV pool holds kv_pages pages of 64 positions, fewer than slots requests
+    of the longest prompt need, so admission also waits for pages.  The timed
+    region is the whole run: every admission prefill, every frame, every
+    collection (host copies included).  Each rank serves its own requests."""
+    from fish_s2pro_b200 import GenerateParams, PromptTensor, SeededRng, SlowArState, TtsScheduler, build
+    build.build_runtime()
+    m = wl.model
+    path = ensure_model(d, wl, args.model_dir)
+    st = SlowArState.open(path, max_seq_len=wl.prompt_len + frames + 8, device=d.local, max_batch=slots,
+                          kv_pages=kv_pages)
+    gp = wl.gen_params(greedy=False)
+    params = GenerateParams(frames, gp["temperature"], gp["top_p"], gp["top_k"], 2 * frames + 2)
+    reqs = []
+    for j in range((n_req + slots - 1) // slots):
+        ps = configs.Workload(m, wl.prompt_len, frames, wl.prompt_seed + 1000 * d.rank + j, wl.im_end_id,
+                              batch=slots, prompt_len_min=wl.prompt_len_min).batch_prompts()
+        reqs += [PromptTensor(p.shape[0], p.shape[1], p.reshape(-1)) for p in ps]
+    reqs = reqs[:n_req]
+
+    def serve(rs):
+        sch = TtsScheduler(st, gp["im_end_id"], params, frames_per_step=4)
+        for i, r in enumerate(rs):
+            sch.submit(r, SeededRng(7 + i))
+        return sch, sch.run()
+
+    serve(reqs[:8])  # capture the frame graph
+    clocks = Clocks(d.local)
+    d.barrier()
+    device_sync()
+    clocks.start()
+    t0 = time.perf_counter()
+    sch, out = serve(reqs)
+    device_sync()
+    t1 = time.perf_counter()
+    d.barrier()
+    ck = clocks.stop()
+    wall = d.max(t1 - t0)
+    my_frames = sum(r.result.n_frames for r in out.values())
+    frames_total = d.sum(my_frames)
+    lat = sorted(r.latency_s for r in out.values())
+    line = {
+        "metric": METRIC_BATCH, "value": round(frames_total / wall, 1), "unit": UNIT, "n_gpus": d.world,
+        "steps": 1, "warmup": 1, "ms_per_step": round(wall * 1e3, 2), "dtype": WTYPE[m.linear_type],
+        "scaling": "weak",
+        "requests_per_s": round(d.sum(len(out)) / wall, 2),
+        "latency_s": {"mean": round(statistics.mean(lat), 3), "p50": round(lat[len(lat) // 2], 3),
+                      "p95": round(lat[min(len(lat) - 1, int(0.95 * len(lat)))], 3)},
+        "queue_s_mean": round(statistics.mean(r.queue_s for r in out.values()), 3),
+        "e2e": {"value": round(frames_total / wall, 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(sum(r.data.nbytes for r in reqs)),
+                "d2h_bytes_per_step": int(my_frames * m.num_codebooks * 4)},
+        "config": {"workload": f"serving: continuous batching on the C4 model, {n_req} requests arriving at "
+                               f"once (prompts {wl.prompt_len_min}..{wl.prompt_len} tokens), {frames} frames each, "
+                               f"{slots} slots, KV pool of {kv_pages} pages of 64 positions, T 0.8 / top-p 0.9 / "
+                               "top-k 30, per-request SeededRng; prefills, frames and collection all timed",
+                   "global_batch": slots * d.world, "parallelism": f"replicas x{d.world}"},
+        "clocks": ck,
+    }
+    st.close()
+    return line
+
+
 def run_batch(args, d: Dist, wl, name=None, steps=None, warmup=None):
     """Batched workload (C4): every rank generates for `wl.batch` independent
     prompts at once through s2d_generate_codes_batch; one step = one call
@@ -575,6 +644,12 @@ def main():
                 line["batch64"] = {k: b[k] for k in nested_keys + ("ms_per_frame_step",) if k in b}
             except Exception as e:  # the batch-1 line stands on its own
                 line["batch64"] = {"metric": METRIC_BATCH, "error": repr(e)[:300]}
+        # continuous batching on the batch-64 model (requests joining and leaving)
+        if default_c2 and not args.no_serving:
+            try:
+                line["serving"] = run_serving(args, d, configs.C4)
+            except Exception as e:
+                line["serving"] = {"metric": METRIC_BATCH, "error": repr(e)[:300]}
         # the quantized batch-1 configurations, on one GPU, over a few steps
         if default_c2 and d.world == 1 and not args.no_quant:
             for key, name in (("q8_0", "C3"), ("q4_k", "C5")):
