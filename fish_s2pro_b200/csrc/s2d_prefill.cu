@@ -681,6 +681,7 @@ cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStrea
         a.S <= 0 || a.S > 65535 || a.T > 0x7fffffff || a.max_seq <= 0 || (a.S > 1 && (!a.part || !a.counters)))
         return cudaErrorInvalidValue;
     // one sequence's consecutive rows (prompt chunks): query rows tiled per block
+    if (a.prefill_tc && a.T >= 16 && prefill_tc_supported(a, kv_half)) return launch_prefill_tc_attention(a, s);
     if (a.prefill_mma && a.T >= 16 && prefill_mma_supported(a, kv_half)) return launch_prefill_mma_attention(a, s);
     if (a.rows_per_seq >= a.T && !a.st && a.S == 1 && a.T >= 16 && kv_half)
         return a.hd == 64 ? prefill_tile_launch<__half, 2>(a, s) : prefill_tile_launch<__half, 4>(a, s);

@@ -61,8 +61,16 @@ struct RowsAttnArgs {
     int decode_chunk;    // its positions per staged chunk, 16 or 32
     const int32_t *row_order;  // its block order: row of each rank (longest context first), or nullptr
     int prefill_mma;     // prompt chunks (one sequence's consecutive rows, f16 cache): the tensor-core kernel
+    int prefill_tc;      // prompt chunks at head dim 128: the tcgen05 kernel (s2d_tc_attn.cu)
+    size_t k_rows, v_rows;  // rows of hd f16 from kcache / vcache to the end of their buffer (0: unknown)
+    int32_t *error;      // set when a bounded wait of the tcgen05 kernel gives up
 };
 cudaError_t launch_rows_attention(const RowsAttnArgs &a, bool kv_half, cudaStream_t s);
+// A prompt chunk's causal attention on tcgen05 (s2d_tc_attn.cu): one
+// sequence's consecutive rows, S == 1, f16 caches (contiguous or paged, with
+// k_rows / v_rows set), head dim 128, 128 % (H / Hkv) == 0.
+bool prefill_tc_supported(const RowsAttnArgs &a, bool kv_half);
+cudaError_t launch_prefill_tc_attention(const RowsAttnArgs &a, cudaStream_t s);
 // The batched step's attention on the tensor cores (s2d_decode_attn.cu):
 // rows of one position per sequence (st and st_pos set), f16 caches, head
 // dim 64 or 128, up to 8 query heads per kv head.

@@ -171,6 +171,7 @@ struct S2dHandle {
     int attn_mma_chunk = 16;            // its positions per staged chunk, 16 or 32 (S2D_DECODE_CHUNK)
     int attn_mma_order = 1;             // its blocks longest context first (S2D_DECODE_ORDER)
     int prefill_mma = 1;                // prompt-chunk attention on the tensor cores (S2D_PREFILL_MMA)
+    int prefill_tc = 1;                 // ... on tcgen05 at head dim 128 (S2D_PREFILL_TC)
     EngineProgram slow_prog;
     uint32_t slow_prog_im_end = 0xffffffffu;
     // Slow-AR tensor parallelism (s2d_open_tp): this rank's shard of every
@@ -228,6 +229,7 @@ struct S2dHandle {
     std::vector<std::vector<int32_t>> serve_pages;
     std::vector<int32_t> serve_free;
     std::vector<int32_t> pool_order;  // the pool's pages in dealing order
+    size_t kv_pool_pages = 0;
     uint32_t batch_kernels = 0;
 };
 
@@ -1448,6 +1450,7 @@ struct RowsPlan {
     size_t kv_seq_stride = 0;
     int max_seq = 0;
     KvPages pages{};  // paged caches (pages.pages set): kv is the pool, kv_seq_stride unused
+    size_t kv_bytes = 0;  // bytes of the buffer kv points into (the tcgemm attention's bounds)
 };
 
 // Every layer of the Slow-AR (is_fast false) or the Fast-AR over T rows of
@@ -1604,6 +1607,12 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
         t.scale = 1.0f / sqrtf((float)a.hd);  // SlowArLayerShape::attn_scale (slow_ar.rs:59-61)
         t.S = rp.S, t.part = h->ra_part, t.counters = h->ra_counters, t.decode_stages = h->attn_stages;
         t.prefill_mma = h->prefill_mma;
+        t.prefill_tc = h->prefill_tc && !is_fast && rp.kv_bytes > 0;
+        if (t.prefill_tc) {
+            const size_t kb = base - reinterpret_cast<uint8_t *>(rp.kv), rowb = (size_t)a.hd * 2;
+            t.k_rows = (rp.kv_bytes - kb) / rowb, t.v_rows = (rp.kv_bytes - kb - layer_bytes / 2) / rowb;
+        }
+        t.error = &h->st->error;
         if (h->attn_mma && rp.st && rp.st_pos && rp.rps == 1) {
             t.decode_mma = 1, t.decode_warps = h->attn_mma_warps, t.decode_stages = h->attn_mma_stages;
             t.decode_chunk = h->attn_mma_chunk, t.row_order = rp.order;
@@ -1637,8 +1646,9 @@ int32_t rows_layers(S2dHandle *h, bool is_fast, float *x, int ldx, const RowsPla
 int32_t prefill_layers(S2dHandle *h, int T, int pos0) {
     RowsPlan rp;
     rp.T = T, rp.rps = T, rp.pos_const = pos0, rp.kv = h->kv_slow, rp.max_seq = h->cfg.max_seq;
+    rp.kv_bytes = h->kv_slow_seq * sizeof(__half);
     if (h->pf_pages) {  // a batched sequence: its pages of the pool
-        rp.kv = h->kv_pool;
+        rp.kv = h->kv_pool, rp.kv_bytes = h->kv_pool_pages * h->kv_page_elems * sizeof(__half);
         rp.pages = KvPages{h->pf_pages, h->kv_per_seq, h->kv_page_elems};
     }
     return rows_layers(h, false, h->pf_x, h->slow.d, rp);
@@ -1813,6 +1823,7 @@ int32_t ensure_batch(S2dHandle *h, uint32_t max_new) {
         h->kv_page_elems = (size_t)a.L * 2 * a.Hkv * kKvPage * a.hd;
         const size_t n_rows = B * (size_t)h->kv_per_seq;  // page-table entries
         const size_t n_pages = h->cfg.kv_pages > 0 ? (size_t)h->cfg.kv_pages : n_rows;
+        h->kv_pool_pages = n_pages;
         CK(cudaMalloc(&h->kv_pool, n_pages * h->kv_page_elems * sizeof(__half)));
         CK(cudaMemset(h->kv_pool, 0, n_pages * h->kv_page_elems * sizeof(__half)));
         std::vector<int32_t> table(n_pages);
@@ -1943,6 +1954,7 @@ int32_t enqueue_frame_batch(S2dHandle *h, const GenKey &k, int B, int rng_kind, 
     rp.T = B, rp.rps = 1, rp.pos_const = 0, rp.st = h->st_b, rp.st_pos = 1, rp.S = batch_splits(h, B);
     rp.order = h->attn_mma_order ? h->batch_order : nullptr;
     rp.kv = h->kv_pool, rp.max_seq = h->cfg.max_seq;
+    rp.kv_bytes = h->kv_pool_pages * h->kv_page_elems * sizeof(__half);
     rp.pages = KvPages{h->kv_page_table, h->kv_per_seq, h->kv_page_elems};
     if ((rc = rows_layers(h, false, h->bx, d, rp))) return rc;
     // final norm (post-norm hidden for the next frame's Fast-AR) + masked LM head
@@ -2111,6 +2123,7 @@ int32_t open_handle(const char *path, const S2dConfig *cfg, int32_t tp_size, int
         if (const char *v = getenv("S2D_DECODE_CHUNK")) h->attn_mma_chunk = atoi(v) == 32 ? 32 : 16;
         if (const char *v = getenv("S2D_DECODE_ORDER")) h->attn_mma_order = atoi(v) != 0;
         if (const char *v = getenv("S2D_PREFILL_MMA")) h->prefill_mma = atoi(v) != 0;
+        if (const char *v = getenv("S2D_PREFILL_TC")) h->prefill_tc = atoi(v) != 0;
         if (const char *kb = getenv("S2D_SLOT_KB")) {
             const int v = atoi(kb);
             if (v >= 4 && v <= 96) h->slot_bytes = v * 1024;
@@ -3047,7 +3060,7 @@ int32_t s2d_op_prefill_attention(S2dHandle *h, const float *q, const uint16_t *k
     if (!h) return S2D_EINVAL;
     if (!q || !kcache || !vcache || !out || T <= 0 || T > 4096 || Hkv <= 0 || H % Hkv || H / Hkv > 8 ||
         (head_dim != 64 && head_dim != 128) || max_seq <= 0 || max_seq > (1 << 20) || pos0 < 0 ||
-        pos0 + T > max_seq || impl < 0 || impl > 1)
+        pos0 + T > max_seq || impl < 0 || impl > 2)
         return set_err(h, S2D_EINVAL, "s2d_op_prefill_attention: bad arguments");
     CK(cudaSetDevice(h->device));
     const size_t kvn = (size_t)Hkv * max_seq * head_dim, nq = (size_t)T * H * head_dim;
@@ -3064,10 +3077,18 @@ int32_t s2d_op_prefill_attention(S2dHandle *h, const float *q, const uint16_t *k
     t.out = (float *)dout.p, t.T = (int)T, t.rows_per_seq = (int)T, t.st = nullptr, t.st_pos = 0;
     t.pos_const = (int)pos0, t.H = (int)H, t.Hkv = (int)Hkv, t.hd = (int)head_dim;
     t.scale = 1.0f / sqrtf((float)head_dim), t.S = 1, t.decode_stages = 2, t.prefill_mma = impl == 0;
+    t.k_rows = t.v_rows = (size_t)Hkv * max_seq, t.error = &h->st->error;
     if (impl == 0 && !prefill_mma_supported(t, true))
         return set_err(h, S2D_EINVAL, "the tensor-core prefill attention does not take these arguments");
+    if (impl == 2 && !prefill_tc_supported(t, true))
+        return set_err(h, S2D_EINVAL, "the tcgen05 prefill attention does not take these arguments");
     if (impl == 0) CK(launch_prefill_mma_attention(t, h->stream));
+    else if (impl == 2) CK(launch_prefill_tc_attention(t, h->stream));
     else CK(launch_rows_attention(t, true, h->stream));
+    if (impl == 2) {
+        int32_t rc = check_device_error(h);
+        if (rc) return rc;
+    }
     CK(cudaMemcpyAsync(out, dout.p, nq * 4, cudaMemcpyDeviceToHost, h->stream));
     CK(cudaStreamSynchronize(h->stream));
     return S2D_OK;

@@ -332,7 +332,8 @@ int32_t s2d_op_linear_f16(S2dHandle *h, const float *input, const uint16_t *weig
  * T query rows of one sequence, row m at position pos0 + m attending over
  * positions 0..pos0 + m of kcache / vcache [Hkv][max_seq][head_dim] (f16
  * bits); q and out [T][H][head_dim] f32.  impl 0: the tensor-core kernel;
- * 1: the CUDA-core kernels (tiled for T >= 16).  pos0 + T <= max_seq,
+ * 1: the CUDA-core kernels (tiled for T >= 16); 2: the tcgen05 kernel
+ * (TMEM accumulators, head_dim 128 only).  pos0 + T <= max_seq,
  * T <= 4096, head_dim 64 or 128, H / Hkv <= 8, host buffers. */
 int32_t s2d_op_prefill_attention(S2dHandle *h, const float *q, const uint16_t *kcache, const uint16_t *vcache,
                                  int64_t T, int64_t H, int64_t Hkv, int64_t head_dim, int64_t max_seq,

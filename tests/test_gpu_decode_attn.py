@@ -11,6 +11,12 @@ masking or merge error gives.  Cases cover head dims 64 / 128, GQA groups of
 1, 2, 4 and 8 heads, context lengths from 1 to past 4,000 positions (partial
 last chunks, more warps and splits than chunks), explicit split counts, and
 finished sequences.
+
+The prompt-chunk attention (s2d_op_prefill_attention, the attention of
+forward_prefill_sequence, slow_ar.rs:579-593) is checked the same way for its
+three kernels: impl 0 the mma.sync tensor-core kernel, 1 the CUDA-core
+kernels, 2 the tcgen05 kernel (TMEM accumulators, head dim 128), which also
+feeds q and the softmax weights as f16 hi + lo pairs.
 """
 import numpy as np
 import pytest
@@ -194,12 +200,18 @@ PREFILL_CASES = [  # T, H, Hkv, hd, max_seq, pos0
     (33, 8, 8, 128, 80, 7),       # one head per group (8 tokens per warp)
     (48, 16, 8, 128, 90, 20),     # two heads per group
     (20, 8, 1, 64, 50, 30),       # eight heads per group (one token per warp)
+    (256, 32, 8, 128, 1400, 1100),  # a long context: 22 position tiles of 64, 8 query tiles
+    (130, 32, 4, 128, 300, 150),  # eight heads per group: 16 tokens per tcgen05 tile, ragged
+    (16, 32, 32, 128, 40, 0),     # one head per group: 128 tokens per tcgen05 tile, one partial tile
 ]
 
 
+# impl 0: mma.sync tensor-core kernel, 1: CUDA cores, 2: tcgen05 (head dim 128 only)
 @pytest.mark.parametrize("T,H,Hkv,hd,max_seq,pos0", PREFILL_CASES)
-@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("impl", [0, 1, 2])
 def test_prefill_attention_matches_float_reference(st, T, H, Hkv, hd, max_seq, pos0, impl):
+    if impl == 2 and hd != 128:
+        pytest.skip("the tcgen05 kernel takes head dim 128")
     rng = np.random.default_rng(T * 3 + H + hd + pos0)
     q = (rng.standard_normal((T, H, hd)) * 2.0).astype(np.float32)
     k = rng.standard_normal((Hkv, max_seq, hd)).astype(np.float16)
