@@ -6,12 +6,12 @@
 // KV head, GQA with rep = H / Hkv query heads per KV head.
 //
 // One CTA takes 128 query rows of one KV head (128 / rep tokens x rep heads):
-// the M of every MMA.  Positions come in tiles of 64.  Two passes over the
-// tiles, so that the output accumulator never needs rescaling:
-//   pass 1: S = Q K^T (TMEM), and each row's running max and sum of
-//           exp2(s - max) in the softmax threads;
-//   pass 2: S = Q K^T again, P = exp2(s - max) / sum written to shared
-//           memory, O += P V in TMEM.
+// the M of every MMA.  Positions come in tiles of 64, in one pass: S = Q K^T
+// (TMEM), P = exp2(s - m) written to shared memory, O += P V (TMEM).  The
+// reference max m of a row moves only when a tile's max exceeds it by more
+// than 8 (base-2 units), so P stays below 2^8; then the softmax threads
+// rescale the row's O in TMEM (load, multiply, store) after the previous
+// P V has landed, which after the first tiles is rare.  O / sum at the end.
 // Q and P enter the MMAs as f16 hi + lo pairs (two MMAs accumulating into
 // the same TMEM tile), K and V are the cache's f16: about 22 bits of the
 // f32 operands with f32 accumulation, the precision of the CUDA-core path.
@@ -66,6 +66,18 @@ constexpr uint32_t kTaCols = 256;                      // TMEM: S0 [0, 64), S1 [
 // region of 128-byte rows.
 __device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+// 32 consecutive TMEM columns of this thread's lane, stored (warp-collective).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+        "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+        "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+        "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
@@ -93,6 +105,7 @@ struct TaShared {
     uint64_t kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2], p_full[2], p_empty[2], q_full, o_full;
     uint32_t tmem;
     int abort;
+    float xl[2][kTaRows];  // each row's sum of P over the two column halves
 };
 
 // The softmax threads' own barrier (warps 0-7).
@@ -135,12 +148,11 @@ __global__ void __launch_bounds__(kTaThreads, 1)
     const uint32_t tmem = sh.tmem;
 
     if (warp == kTaSoftmax / 32) {
-        // ---- loader: K tiles (pass 1), K and V tiles (pass 2) ----
+        // ---- loader: the K and V tiles of every position tile ----
         if (lane == 0) {
             int issued = 0;
-            for (int v = 0; v < 2 * J && !*abort_v; ++v) {
-                const int s = v % kStages, use = v / kStages, j = v % J;
-                const bool pass2 = v >= J;
+            for (int j = 0; j < J && !*abort_v; ++j) {
+                const int s = j % kStages, use = j / kStages;
                 if (use > 0 && !mb_wait(&sh.kv_empty[s], (use & 1) ^ 1, abort_v)) {
                     *abort_v = 1;
                     break;
@@ -152,19 +164,17 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                     row = a.kv_pages.pages[j] * (int)(a.kv_pages.page_elems / kTaHd) + kvh * kTaTile;
                 else
                     row = kvh * a.max_seq + j * kTaTile;
-                mb_expect_tx(&sh.kv_full[s], pass2 ? kStage : 2 * kKvHalf);
+                mb_expect_tx(&sh.kv_full[s], kStage);
                 uint8_t *st = smem + kOffKv + (size_t)s * kStage;
                 tma_load_2d(st, &mk, 0, row, &sh.kv_full[s]);
                 tma_load_2d(st + kKvHalf, &mk, 64, row, &sh.kv_full[s]);
-                if (pass2) {
-                    tma_load_2d(st + 2 * kKvHalf, &mv, 0, row, &sh.kv_full[s]);
-                    tma_load_2d(st + 3 * kKvHalf, &mv, 64, row, &sh.kv_full[s]);
-                }
+                tma_load_2d(st + 2 * kKvHalf, &mv, 0, row, &sh.kv_full[s]);
+                tma_load_2d(st + 3 * kKvHalf, &mv, 64, row, &sh.kv_full[s]);
                 ++issued;
             }
             // no copy may still be landing when the CTA leaves
-            for (int v = max(0, issued - kStages); v < issued; ++v)
-                (void)mb_wait(&sh.kv_full[v % kStages], (v / kStages) & 1, abort_v, false);
+            for (int j = max(0, issued - kStages); j < issued; ++j)
+                (void)mb_wait(&sh.kv_full[j % kStages], (j / kStages) & 1, abort_v, false);
         }
     } else if (warp == kTaSoftmax / 32 + 1) {
         // ---- MMA issuer ----
@@ -172,11 +182,11 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             constexpr uint32_t id_s = idesc_f16_f32(kTaRows, kTaTile);      // S: M 128, N 64, K-major
             constexpr uint32_t id_o = idesc_f16_f32_bmn(kTaRows, kTaHd);     // O: M 128, N 128, B MN-major
             const uint32_t q_hi = sbase, q_lo = sbase + 2 * kQHalf;
-            // S of use v (tile v % J) into S buffer v & 1: Q_hi K^T + Q_lo K^T,
-            // 8 K-steps of 16 over the head dim
-            auto issue_s = [&](int v) -> bool {
-                const int s = v % kStages, b = v & 1, buse = v >> 1;
-                if (!mb_wait(&sh.kv_full[s], (v / kStages) & 1, abort_v)) return false;
+            // S of tile j into S buffer j & 1: Q_hi K^T + Q_lo K^T, 8 K-steps
+            // of 16 over the head dim
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kStages, b = j & 1, buse = j >> 1;
+                if (!mb_wait(&sh.kv_full[s], (j / kStages) & 1, abort_v)) return false;
                 if (buse > 0 && !mb_wait(&sh.s_empty[b], (buse & 1) ^ 1, abort_v)) return false;
                 tc_fence_after();
                 const uint32_t kst = sbase + kOffKv + (uint32_t)s * kStage;
@@ -193,17 +203,12 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             };
             bool ok = mb_wait(&sh.q_full, 0, abort_v);
             tc_fence_after();
-            // pass 1: S only; its K stage is free once the MMAs have read it
-            for (int v = 0; v < J && ok; ++v) {
-                ok = issue_s(v);
-                if (ok) umma_commit(&sh.kv_empty[v % kStages]);
-            }
-            // pass 2: S of tile j + 1 goes out before P of tile j is waited
-            // for, so that the softmax of tile j overlaps the next S
-            if (ok) ok = issue_s(J);
+            // S of tile j + 1 goes out before P of tile j is waited for, so
+            // that the softmax of tile j overlaps the next S
+            if (ok) ok = issue_s(0);
             for (int j = 0; j < J && ok; ++j) {
-                if (j + 1 < J && !(ok = issue_s(J + j + 1))) break;
-                const int v = J + j, s = v % kStages, pb = j & 1, puse = j >> 1;
+                if (j + 1 < J && !(ok = issue_s(j + 1))) break;
+                const int s = j % kStages, pb = j & 1, puse = j >> 1;
                 if (!(ok = mb_wait(&sh.p_full[pb], puse & 1, abort_v))) break;
                 tc_fence_after();
                 // O += P_hi V + P_lo V: 4 K-steps of 16 positions
@@ -216,15 +221,16 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                     umma_f16(tmem + 128, desc_k_sw128(p_lo + (uint32_t)kk * 32u), dv, id_o, 1);
                 }
                 umma_commit(&sh.kv_empty[s]);
-                umma_commit(&sh.p_empty[pb]);
+                umma_commit(&sh.p_empty[pb]);  // also: O holds P V of tiles <= j
             }
             if (!ok) *abort_v = 1;
             umma_commit(&sh.o_full);  // completes once every MMA issued above has
         }
     } else {
         // ---- softmax and epilogue: warp w takes rows 32 (w % 4) + lane (its
-        // TMEM lane quarter) and column half ch = w / 4 of every S tile, the
-        // Q head-dim half ch and the O head-dim half ch ----
+        // TMEM lane quarter) and half ch = w / 4 of the P columns, of the Q
+        // head dim and of the O columns; both threads of a row read the
+        // row's whole S tile and so take the same decisions ----
         const int r = 32 * (warp & 3) + lane, ch = warp >> 2;
         const int m = m0 + r / rep, h = kvh * rep + r % rep;
         const bool valid = m < a.T;
@@ -236,10 +242,9 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             const float4 v = valid ? reinterpret_cast<const float4 *>(qrow)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         }
-        // row exchanges between the column halves go through P buffer 1 (free
-        // until pass 2 writes it, which every softmax thread does only after
-        // the barrier that closes the exchange)
-        float *xq = reinterpret_cast<float *>(smem + kOffP + 3 * kPMat), *xl = xq + 2 * kTaRows;
+        // the row's |q| max: the two halves meet in P buffer 1 (written only
+        // after Q is complete, which needs every thread past this point)
+        float *xq = reinterpret_cast<float *>(smem + kOffP + 3 * kPMat);
         xq[ch * kTaRows + r] = amax;
         softmax_sync();
         amax = fmaxf(xq[r], xq[kTaRows + r]) * qmul;
@@ -260,94 +265,101 @@ __global__ void __launch_bounds__(kTaThreads, 1)
         fence_proxy_async_smem();
         mb_arrive(&sh.q_full);
         const uint32_t lane_t = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-        float mrow = -INFINITY, lrow = 0.f;  // over this thread's columns; both halves after pass 1
+        // Online softmax in base 2 with a lazy rescale: mrow is the reference
+        // max of P = 2^(s - mrow); it moves (and O and lrow are rescaled)
+        // only when a tile's max exceeds it by more than 8, so P stays below
+        // 2^8 and O in TMEM is rarely touched.
+        float mrow = -INFINITY, lrow = 0.f;  // lrow: this thread's columns
         bool ok = true;
-        for (int v = 0; v < 2 * J; ++v) {
-            const int b = v & 1, use = v >> 1, j = v % J;
-            const bool pass2 = v >= J;
-            if (v == J) {
-                // both column halves' (max, sum) of each row
-                xq[ch * kTaRows + r] = mrow, xl[ch * kTaRows + r] = lrow;
-                softmax_sync();
-                const float m2 = xq[(ch ^ 1) * kTaRows + r], l2 = xl[(ch ^ 1) * kTaRows + r];
-                softmax_sync();  // every exchange read before P buffer 1 is written
-                const float mm = fmaxf(mrow, m2);
-                if (mm > -INFINITY) {
-                    lrow = (mrow > -INFINITY ? lrow * exp2f(mrow - mm) : 0.f) + (m2 > -INFINITY ? l2 * exp2f(m2 - mm) : 0.f);
-                    mrow = mm;
-                }
-            }
-            // after a failed wait the loop runs on without work, so that every
-            // softmax warp reaches the barrier between the passes
-            if (!ok) continue;
+        for (int j = 0; j < J; ++j) {
+            if (!ok) break;
+            const int b = j & 1, use = j >> 1;
             const bool got = mb_wait(&sh.s_full[b], use & 1, abort_v);
             if (!__all_sync(0xffffffffu, got)) {
                 ok = false;
-                continue;
+                break;
             }
             tc_fence_after();
-            float s[32];
-            tmem_ld32(lane_t + (uint32_t)(b * kTaTile + 32 * ch), s);  // warp-collective
+            float s0[32], s1[32];  // columns 0-31 and 32-63 of the S row
+            tmem_ld32(lane_t + (uint32_t)(b * kTaTile), s0);  // warp-collective
+            tmem_ld32(lane_t + (uint32_t)(b * kTaTile + 32), s1);
             tc_fence_before();
             mb_arrive(&sh.s_empty[b]);
-            const int t0 = j * kTaTile + 32 * ch, nvis = valid ? min(32, prow + 1 - t0) : 0;  // positions < nvis visible
-            if (!pass2) {
-                float mx = -INFINITY;
-                if (nvis >= 32) {  // the whole half visible: no per-position mask
+            const int nvis = valid ? min(kTaTile, prow + 1 - j * kTaTile) : 0;  // positions < nvis visible
+            const bool full = nvis >= kTaTile;
+            float mx = -INFINITY;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, s[i]);
-                    mx *= qdown;
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (i < nvis) mx = fmaxf(mx, s[i] * qdown);
-                }
-                if (mx > -INFINITY) {
-                    const float mnew = fmaxf(mrow, mx);
-                    float acc = 0.f;
-                    if (nvis >= 32) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) acc += exp2f(fmaf(s[i], qdown, -mnew));
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (i < nvis) acc += exp2f(fmaf(s[i], qdown, -mnew));
-                    }
-                    lrow = fmaf(lrow, exp2f(mrow - mnew), acc);
-                    mrow = mnew;
-                }
-                continue;
+            for (int i = 0; i < 32; ++i) {
+                if (full || i < nvis) mx = fmaxf(mx, s0[i]);
+                if (full || i + 32 < nvis) mx = fmaxf(mx, s1[i]);
             }
-            // pass 2: P = exp2(s - max) / sum into P buffer pb, row r, chunks 4 ch ..
+            mx *= qdown;
+            // P buffer pb is free once P V of tile j - 2 is done; with j >= 1
+            // the wait on tile j - 1's buffer also says O holds tiles < j
             const int pb = j & 1, puse = j >> 1;
             if (puse > 0) {
                 const bool free_ = mb_wait(&sh.p_empty[pb], (puse & 1) ^ 1, abort_v);
                 if (!__all_sync(0xffffffffu, free_)) {
                     ok = false;
-                    continue;
+                    break;
                 }
             }
-            const float inv_l = lrow > 0.f ? 1.f / lrow : 0.f;
+            // a new reference max for this row, and the factor for O and lrow
+            const bool up = mx > mrow + 8.f;
+            const float mnew = up ? mx : mrow;
+            const float corr = up && mrow > -INFINITY ? exp2f(mrow - mnew) : 1.f;
+            if (__any_sync(0xffffffffu, corr != 1.f)) {
+                // O (this thread's 64 columns) *= corr once P V of tile j - 1
+                // is done; the TMEM loads and stores are warp-collective
+                const int pj = j - 1, ppb = pj & 1, ppuse = pj >> 1;
+                const bool ready = mb_wait(&sh.p_empty[ppb], ppuse & 1, abort_v);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int q = 0; q < 2; ++q) {
+                    float o[32];
+                    const uint32_t ot = lane_t + 128u + (uint32_t)(64 * ch + 32 * q);
+                    tmem_ld32(ot, o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] *= corr;
+                    tmem_st32(ot, o);
+                }
+            }
+            lrow *= corr;
+            mrow = mnew;
+            // P = 2^(s - mrow) of this thread's 32 columns into P buffer pb
             const uint32_t p_hi = sbase + kOffP + (uint32_t)pb * 2 * kPMat;
-            const bool full = nvis >= 32;
+            float acc = 0.f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 float x[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const int i = 8 * c + e;
-                    x[e] = full || i < nvis ? exp2f(fmaf(s[i], qdown, -mrow)) * inv_l : 0.f;
+                    const int i = 32 * ch + 8 * c + e;
+                    const float sv = ch ? s1[8 * c + e] : s0[8 * c + e];  // constant indices: no local array
+                    x[e] = full || i < nvis ? exp2f(fmaf(sv, qdown, -mrow)) : 0.f;
+                    acc += x[e];
                 }
                 uint4 hi, lo;
                 split8(x, hi, lo);
                 st_shared16(p_hi + sw128(r, 4 * ch + c), hi);
                 st_shared16(p_hi + kPMat + sw128(r, 4 * ch + c), lo);
             }
+            lrow += acc;
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
             fence_proxy_async_smem();
             mb_arrive(&sh.p_full[pb]);
         }
         if (!ok) *abort_v = 1;
-        // epilogue: O row r, head-dim half ch, normalised already
+        // the row's sum over both column halves
+        sh.xl[ch][r] = lrow;
+        softmax_sync();
+        const float inv_l = valid ? 1.f / (sh.xl[0][r] + sh.xl[1][r]) : 0.f;
+        // epilogue: O row r, head-dim half ch
         const bool done = mb_wait(&sh.o_full, 0, abort_v, false);
         tc_fence_after();
         if (__all_sync(0xffffffffu, done && !*abort_v)) {  // warp-uniform: the loads are collective
@@ -359,7 +371,8 @@ __global__ void __launch_bounds__(kTaThreads, 1)
                 if (valid) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 4)
-                        *reinterpret_cast<float4 *>(out + 32 * c + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+                        *reinterpret_cast<float4 *>(out + 32 * c + e) =
+                            make_float4(o[e] * inv_l, o[e + 1] * inv_l, o[e + 2] * inv_l, o[e + 3] * inv_l);
                 }
             }
         }

@@ -219,3 +219,24 @@ def test_prefill_attention_matches_float_reference(st, T, H, Hkv, hd, max_seq, p
     want = reference_prefill(q, k, v, pos0)
     got = run_prefill(st, q, k, v, pos0, impl)
     assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < TOL
+
+
+@pytest.mark.parametrize("T,H,Hkv,max_seq,pos0", [(64, 32, 8, 200, 100), (130, 32, 4, 300, 150)])
+@pytest.mark.parametrize("impl", [0, 1, 2])
+def test_prefill_attention_rising_scores(st, T, H, Hkv, max_seq, pos0, impl):
+    """Key rows whose norm grows with the position: each row's max score
+    climbs by several base-2 units per 64-position tile (scores reach ~75),
+    so the tcgen05 kernel's online softmax moves its reference max and
+    rescales the accumulator in TMEM one to four times per row of the last
+    token; a key aligned with the last token's q sits mid-chunk on top."""
+    hd = 128
+    rng = np.random.default_rng(T + pos0)
+    q = (rng.standard_normal((T, H, hd)) * 2.0).astype(np.float32)
+    grow = (0.3 + 2.5 * np.arange(max_seq) / 64.0)[None, :, None]
+    k = (rng.standard_normal((Hkv, max_seq, hd)) * grow).astype(np.float16)
+    v = rng.standard_normal((Hkv, max_seq, hd)).astype(np.float16)
+    spike = pos0 + T // 2
+    k[:, spike] = (np.sign(q[T - 1, ::H // Hkv]) * 1.5).astype(np.float16)
+    want = reference_prefill(q, k, v, pos0)
+    got = run_prefill(st, q, k, v, pos0, impl)
+    assert np.max(np.abs(got - want)) / np.max(np.abs(want)) < TOL
