@@ -3,8 +3,9 @@
 The product is libs2d.so (C ABI: include/s2d.h).  This package holds its
 sources (csrc/), the in-tree build (build.py), the Python mirror of the
 reference's `rust-pure` interface (s2d.py), the workload configurations
-(configs.py), the seeded synthetic GGUF writer (synth.py) and the
-continuous-batching scheduler over the s2d_serve_* calls (serve.py).
+(configs.py), the seeded synthetic GGUF writers (synth.py, codec_synth.py),
+the continuous-batching scheduler over the s2d_serve_* calls (serve.py) and
+the codec decode from codes to PCM (codec.py, include/s2d_codec.h).
 """
 from .s2d import (  # noqa: F401
     LOGITS_ALLOWED,
@@ -35,3 +36,4 @@ from .s2d import (  # noqa: F401
     transpose_to_time_major,
 )
 from .serve import ServeSession, TtsScheduler  # noqa: F401,E402
+from .codec import CodecDecoder, CodecWaveformResult, pcm_to_wav  # noqa: F401,E402

@@ -21,7 +21,7 @@ LIB = PKG / "libs2d.so"
 SYNTH_LIB = PKG / "libs2d_synth.so"
 
 CUDA_SOURCES = ["s2d_kernels.cu", "s2d_engine.cu", "s2d_prefill.cu", "s2d_decode_attn.cu", "s2d_tcgemm.cu", "s2d_runtime.cu",
-                "s2d_gguf.cpp", "s2d_noalloc.cu", "s2d_tc_attn.cu"]
+                "s2d_gguf.cpp", "s2d_noalloc.cu", "s2d_tc_attn.cu", "s2d_codec.cu"]
 CUDA_HEADERS = ["s2d_common.cuh", "s2d_kernels.cuh", "s2d_sample.cuh", "s2d_prefill.cuh", "s2d_tcgemm.cuh", "s2d_tc_common.cuh",
                 "s2d_gguf.h"]
 CUDA_LIB = "/usr/local/cuda/lib64"
@@ -54,7 +54,7 @@ def _run(cmd: list[str]) -> None:
 
 
 def build_runtime(force: bool = False, verbose_ptxas: bool = False) -> Path:
-    deps = [CSRC / s for s in CUDA_SOURCES + CUDA_HEADERS] + [ROOT / "include" / "s2d.h"]
+    deps = [CSRC / s for s in CUDA_SOURCES + CUDA_HEADERS] + [ROOT / "include" / "s2d.h", ROOT / "include" / "s2d_codec.h"]
     if not force and not _stale(LIB, deps):
         return LIB
     cmd = [

@@ -1,0 +1,988 @@
+// s2d_codec.cu -- the codec decode on sm_100a: RVQ codes -> 44.1 kHz PCM
+// (crates/fish_s2_infer/src/codec.rs:1690 decode_waveform and what it calls).
+//
+// Activations are frame-major float rows in HBM ([frames][channels]); every
+// contraction is one f16 tensor-core GEMM with f32 accumulation:
+// * linears and transposed convolutions take float inputs, so their rows go
+//   in as power-of-two scaled f16 hi + lo pairs (launch_split_rows, about 22
+//   bits) stacked [2T][K], and an epilogue kernel adds the halves back;
+// * the causal convolutions round their padded input to f16 in the reference
+//   itself (codec.rs:2257-2259), so their im2col rows are exact in f16 and go
+//   in alone: one GEMM of K = taps x channels per convolution.
+// The transposed convolutions are one GEMM over all kernel taps ([T][k C]
+// per input frame) and a col2im pass that sums the overlapping taps in the
+// reference's frame order and adds the bias.  Snake, LayerNorm, GELU, RoPE,
+// the windowed attention and the output convolution are CUDA-core kernels.
+#include <cublas_v2.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "../../include/s2d.h"
+#include "../../include/s2d_codec.h"
+#include "s2d_gguf.h"
+#include "s2d_prefill.cuh"
+
+namespace s2d {
+namespace {
+
+// codec.rs:16-55
+constexpr int kHid = 1024, kProj = 8, kFfn = 3072, kHeads = 16, kHd = 64, kWin = 128, kLayers = 8;
+constexpr int kExp = 4096, kUpStages = 2, kUp = 2, kDw = 7, kEntry = 1536, kBlocks = 4, kBooks = 10;
+constexpr int kRates[kBlocks] = {8, 8, 4, 2};
+constexpr int kChan[kBlocks] = {768, 384, 192, 96};  // block_output_channels, codec.rs:2003-2012
+constexpr int kSemBook = 4096, kResBook = 1024;
+constexpr float kNormEps = 1e-5f, kLnEps = 1e-6f, kRopeBase = 10000.0f;
+constexpr int kSamplesPerLatent = 8 * 8 * 4 * 2;
+constexpr int kTailTile = 64;
+
+// ---------------------------------------------------------------- kernels --
+
+struct RvqArgs {
+    const __half *book[kBooks];   // [n][8]
+    const __half *oproj[kBooks];  // [1024][8]
+    const __half *obias[kBooks];  // [1024]
+    int size[kBooks];
+};
+
+// rvq_lookup_codes (codec.rs:2536): per frame and channel, for each codebook
+// in order, latents += (sum_j codebook[code][j] * out_proj[c][j]) + bias[c],
+// each sum left to right in f32 without fused multiply-adds, as the CPU
+// linear / add_bias / add do it: the result is bit-exact.
+__global__ void rvq_kernel(RvqArgs a, const int32_t *codes, int T, float *lat, int32_t *error) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < kHid; c += blockDim.x) {
+        float acc = 0.f;
+        for (int cb = 0; cb < kBooks; ++cb) {
+            const int code = codes[(size_t)cb * T + t];
+            if (code < 0 || code >= a.size[cb]) {
+                if (error) atomicCAS(error, 0, 1);
+                continue;
+            }
+            const __half *row = a.book[cb] + (size_t)code * kProj;
+            const __half *w = a.oproj[cb] + (size_t)c * kProj;
+            float p = 0.f;
+#pragma unroll
+            for (int j = 0; j < kProj; ++j) p = __fadd_rn(p, __fmul_rn(__half2float(row[j]), __half2float(w[j])));
+            p = __fadd_rn(p, __half2float(a.obias[cb][c]));
+            acc = __fadd_rn(acc, p);
+        }
+        lat[(size_t)t * kHid + c] = acc;
+    }
+}
+
+__device__ __forceinline__ float combine(const float *Y2, const float *inv, int T, int N, int t, int n) {
+    return (Y2[(size_t)t * N + n] + Y2[((size_t)T + t) * N + n]) * inv[t];
+}
+
+// The wqkv rows of the stacked GEMM combined, q and k rotated in place
+// (apply_rope_normal, attention.rs:172: adjacent pairs, theta = t / freq[i],
+// freq[i] = base^(2i / 64) computed on the host in f32).
+__global__ void qkv_rope_kernel(const float *Y2, const float *inv, int T, const float *freq, float *qkv) {
+    const int t = blockIdx.x;
+    constexpr int N = 3 * kHid;
+    for (int p = threadIdx.x; p < N / 2; p += blockDim.x) {
+        const int n = 2 * p;
+        float x0 = combine(Y2, inv, T, N, t, n), x1 = combine(Y2, inv, T, N, t, n + 1);
+        if (n < 2 * kHid) {
+            const float theta = (float)t / freq[(n % kHd) / 2];
+            float s, c;
+            sincosf(theta, &s, &c);
+            const float r0 = x0 * c - x1 * s, r1 = x0 * s + x1 * c;
+            x0 = r0, x1 = r1;
+        }
+        qkv[(size_t)t * N + n] = x0;
+        qkv[(size_t)t * N + n + 1] = x1;
+    }
+}
+
+// Query row t of head h over keys max(0, t + 1 - 128) .. t
+// (codec.rs:3270-3297 with gqa_decode_attention, attention.rs:208, and
+// softmax_in_place, attention.rs:296): one block of 128 threads, a thread per
+// visible position for the scores, two half-blocks over positions for P V.
+__global__ void __launch_bounds__(kWin) window_attn_kernel(const float *qkv, int T, float *out) {
+    const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    __shared__ float q[kHd], p[kWin], red[kWin / 32], part[2][kHd];
+    constexpr int N = 3 * kHid;
+    const int lo = max(0, t + 1 - kWin), n = t + 1 - lo;
+    if (tid < kHd) q[tid] = qkv[(size_t)t * N + h * kHd + tid];
+    __syncthreads();
+    float s = -INFINITY;
+    if (tid < n) {
+        const float4 *k = reinterpret_cast<const float4 *>(qkv + (size_t)(lo + tid) * N + kHid + h * kHd);
+        float acc = 0.f;
+#pragma unroll
+        for (int d = 0; d < kHd / 4; ++d) {
+            const float4 kv = k[d];
+            acc += q[4 * d] * kv.x + q[4 * d + 1] * kv.y + q[4 * d + 2] * kv.z + q[4 * d + 3] * kv.w;
+        }
+        s = acc * 0.125f;  // 1 / sqrt(64)
+    }
+    float m = s;
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    const float e = tid < n ? expf(s - m) : 0.f;
+    float sum = e;
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    sum = red[0] + red[1] + red[2] + red[3];
+    p[tid] = e / sum;
+    __syncthreads();
+    const int d = tid & (kHd - 1), half = tid >> 6;
+    float acc = 0.f;
+    for (int j = half; j < n; j += 2) acc += p[j] * qkv[(size_t)(lo + j) * N + 2 * kHid + h * kHd + d];
+    part[half][d] = acc;
+    __syncthreads();
+    if (tid < kHd) out[(size_t)t * kHid + h * kHd + tid] = part[0][tid] + part[1][tid];
+}
+
+enum CodecEpi { CE_STORE = 0, CE_GELU = 1, CE_SWIGLU = 2, CE_SCALE_RESID = 3 };
+
+// erf by Abramowitz & Stegun 7.1.26, the form codec.rs:3890 uses.
+__device__ __forceinline__ float erf_as(float v) {
+    const float sign = v < 0.f ? -1.f : 1.f, x = fabsf(v);
+    const float t = 1.f / (1.f + 0.3275911f * x);
+    const float poly = (((((1.061405429f * t - 1.453152027f) * t) + 1.421413741f) * t - 0.284496736f) * t +
+                        0.254829592f) * t;
+    return sign * (1.f - poly * expf(-x * x));
+}
+
+// y[t][n] from the stacked GEMM rows: v = combined + bias[n % nb]; STORE v,
+// GELU gelu_erf(v) (codec.rs:3886), SWIGLU silu(v) * u with u combined from
+// Y2b (codec.rs:3313-3317), SCALE_RESID r[t][n] + gamma[n] * v (y may alias r).
+__global__ void epilogue_kernel(int epi, const float *Y2, const float *Y2b, const float *inv, int T, int N,
+                                const float *bias, int nb, const float *gamma, const float *r, float *y) {
+    const size_t total = (size_t)T * N;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / N), n = (int)(i % N);
+        float v = combine(Y2, inv, T, N, t, n);
+        if (bias) v += bias[n % nb];
+        if (epi == CE_GELU) {
+            v = 0.5f * v * (1.f + erf_as(v * 0.70710678118654752f));
+        } else if (epi == CE_SWIGLU) {
+            const float u = combine(Y2b, inv, T, N, t, n);
+            v = v / (1.f + expf(-v)) * u;
+        } else if (epi == CE_SCALE_RESID) {
+            v = r[i] + gamma[n] * v;
+        }
+        y[i] = v;
+    }
+}
+
+// ConvNeXt front (codec.rs:3438-3458): depthwise causal conv (kernel 7) and
+// the affine LayerNorm of each frame, one block per frame.
+__global__ void __launch_bounds__(256) dwconv_ln_kernel(const float *x, int T, const float *w, const float *b,
+                                                        const float *lnw, const float *lnb, float *out) {
+    const int t = blockIdx.x;
+    constexpr int PER = kHid / 256;
+    __shared__ float red[8];
+    float h[PER];
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const int c = threadIdx.x + 256 * e;
+        float acc = b[c];
+#pragma unroll
+        for (int k = 0; k < kDw; ++k) {
+            const int src = t + k - (kDw - 1);
+            if (src >= 0) acc += x[(size_t)src * kHid + c] * w[c * kDw + k];
+        }
+        h[e] = acc;
+        s += acc;
+    }
+    auto block_sum = [&](float v) {
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float r = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r += red[i];
+        return r;
+    };
+    const float mean = block_sum(s) / kHid;
+    float v2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) v2 += (h[e] - mean) * (h[e] - mean);
+    const float scale = 1.f / sqrtf(block_sum(v2) / kHid + kLnEps);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        const int c = threadIdx.x + 256 * e;
+        out[(size_t)t * kHid + c] = (h[e] - mean) * scale * lnw[c] + lnb[c];
+    }
+}
+
+// snake (codec.rs:2162): x + sin(a x)^2 / a, with |a| < 1e-8 taken as 1e-8.
+__device__ __forceinline__ float snake(float x, float alpha) {
+    const float a = fabsf(alpha) < 1e-8f ? 1e-8f : alpha;
+    const float s = sinf(a * x);
+    return x + s * s / a;
+}
+
+// y[t][c] = snake(x[t][c] (+ bias[c])), float out (the transposed
+// convolution's input, which the reference does not round).
+__global__ void snake_kernel(const float *x, int T, int C, const float *bias, const float *alpha, float *y) {
+    const size_t total = (size_t)T * C;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c = (int)(i % C);
+        y[i] = snake(x[i] + (bias ? bias[c] : 0.f), alpha[c]);
+    }
+}
+
+// A causal convolution's padded input: P[pad + t][c] = f16(snake(x[t][c] +
+// bias[c])) (bias and snake optional), P[0 .. pad) = 0 (codec.rs:2247-2259).
+__global__ void pad_f16_kernel(const float *x, int T, int C, int pad, const float *bias, const float *alpha,
+                               __half *P) {
+    const size_t total = (size_t)(T + pad) * C;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = i / C;
+        const int c = (int)(i % C);
+        float v = 0.f;
+        if (row >= (size_t)pad) {
+            v = x[i - (size_t)pad * C] + (bias ? bias[c] : 0.f);
+            if (alpha) v = snake(v, alpha[c]);
+        }
+        P[i] = __float2half_rn(v);
+    }
+}
+
+// im2col of a stride-1 causal convolution: A[t][k C + c] = P[t + k d][c] for
+// the taps k < K, 16 bytes at a time (C * 2 is a multiple of 16).
+__global__ void im2col_kernel(const __half *P, int T, int C, int K, int d, __half *A) {
+    const int cv = C / 8;  // uint4 per row of P
+    const size_t total = (size_t)T * K * cv;
+    const uint4 *src = reinterpret_cast<const uint4 *>(P);
+    uint4 *dst = reinterpret_cast<uint4 *>(A);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = i / ((size_t)K * cv);
+        const int r = (int)(i % ((size_t)K * cv)), k = r / cv, j = r % cv;
+        dst[i] = src[(t + (size_t)k * d) * cv + j];
+    }
+}
+
+// causal_conv_transpose_1d (codec.rs:3505) from the GEMM over every tap:
+// Y2 holds [T][K C] (stacked hi / lo rows); output row u = f s + k sums the
+// taps that land on it in increasing f, then adds the bias; rows past T s are
+// not produced.
+__global__ void col2im_kernel(const float *Y2, const float *inv, int T, int K, int s, int C, const float *bias,
+                              float *y) {
+    const size_t total = (size_t)T * s * C;
+    const int N = K * C;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int u = (int)(i / C), c = (int)(i % C);
+        const int f_hi = min(u / s, T - 1);
+        int f_lo = u - (K - 1);
+        f_lo = f_lo <= 0 ? 0 : (f_lo + s - 1) / s;
+        float acc = 0.f;
+        for (int f = f_lo; f <= f_hi; ++f) acc += combine(Y2, inv, T, N, f, (u - f * s) * C + c);
+        y[i] = acc + bias[c];
+    }
+}
+
+// Residual unit output (codec.rs:2151): x += Z + bias.
+__global__ void resid_kernel(float *x, const float *Z, int T, int C, const float *bias) {
+    const size_t total = (size_t)T * C;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
+        x[i] += Z[i] + bias[i % C];
+}
+
+// Decoder tail (codec.rs:1978-1998): snake, the causal convolution 96 -> 1
+// (kernel 7, input rounded to f16) and tanh.  A block stages its 64 samples'
+// input rows (and the 6 before) in shared memory.
+__global__ void __launch_bounds__(kTailTile) tail_kernel(const float *x, int T, const float *alpha, const float *w,
+                                                         float bias, int C, int K, float *out) {
+    extern __shared__ float tile[];  // [(kTailTile + K - 1)][C]
+    const int t0 = blockIdx.x * kTailTile, rows = kTailTile + K - 1;
+    for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
+        const int r = i / C, c = i % C, src = t0 + r - (K - 1);
+        float v = 0.f;
+        if (src >= 0 && src < T) v = snake(x[(size_t)src * C + c], alpha[c]);
+        tile[i] = __half2float(__float2half_rn(v));
+    }
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t >= T) return;
+    float acc = bias;
+    for (int k = 0; k < K; ++k) {
+        const float *row = tile + (threadIdx.x + k) * C;
+        for (int c = 0; c < C; ++c) acc += row[c] * w[k * C + c];
+    }
+    out[t] = tanhf(acc);
+}
+
+unsigned grid_for(size_t n, int threads = 256) {
+    const size_t b = (n + threads - 1) / threads;
+    return (unsigned)(b < 148 * 16 ? (b ? b : 1) : 148 * 16);
+}
+
+float h2f_host(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31, exp = (h >> 10) & 0x1f, man = h & 0x3ff;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int e = -1;
+            uint32_t m = man;
+            do {
+                m <<= 1;
+                ++e;
+            } while (!(m & 0x400));
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((m & 0x3ff) << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- handle --
+
+struct CodecUnit {
+    const float *a0, *a1, *b0, *b1;
+    const __half *w0, *w1;  // [C][k0 C] (tap-major columns), [C][k1 C]
+    int k0, k1;
+};
+struct CodecBlock {
+    const float *alpha, *bt;
+    const __half *wt;  // [k C][C_in]: row (tap, out channel)
+    int kernel;
+    CodecUnit unit[3];
+};
+struct CodecLayer {
+    const __half *wqkv, *wo, *w1, *w3, *w2;
+    const float *an, *fn, *ga, *gf;
+};
+struct CodecUpStage {
+    const __half *wt, *pw1, *pw2;  // wt [2 x 1024][1024]
+    const float *bt, *dw, *dwb, *lnw, *lnb, *pw1b, *pw2b, *gamma;
+};
+
+}  // namespace s2d
+
+struct S2dCodec {
+    int device = 0;
+    std::string err;
+    cudaStream_t stream = nullptr;
+    cublasHandle_t blas = nullptr;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0;
+    s2d::RvqArgs rvq{};
+    s2d::CodecLayer layer[s2d::kLayers]{};
+    const float *post_norm = nullptr, *rope_freq = nullptr;
+    s2d::CodecUpStage up[s2d::kUpStages]{};
+    const __half *entry_w = nullptr;
+    const float *entry_b = nullptr;
+    s2d::CodecBlock block[s2d::kBlocks]{};
+    const float *tail_alpha = nullptr, *out_w = nullptr;
+    float out_b = 0.f;
+    // workspace, sized for `ws_frames` code frames
+    uint32_t ws_frames = 0;
+    uint8_t *ws = nullptr;
+    size_t ws_bytes = 0;
+    float *lat = nullptr, *x = nullptr, *x2 = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr;
+    float *Y2 = nullptr, *Y2b = nullptr, *inv = nullptr, *Z = nullptr;
+    __half *xs = nullptr, *P = nullptr, *A = nullptr;
+    int32_t *codes = nullptr, *error = nullptr;
+    float *samples = nullptr;
+};
+
+namespace s2d {
+namespace {
+
+int32_t cerr(S2dCodec *c, int32_t code, const std::string &m) {
+    if (c) c->err = m;
+    return code;
+}
+
+#define CCK(call)                                                                                    \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return cerr(c, S2D_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// ---- loading ---------------------------------------------------------------
+
+struct Loader {
+    S2dCodec *c;
+    const Gguf &g;
+    std::vector<uint8_t> host;  // staged arena
+    std::string err;
+    struct Fix {
+        size_t off;
+        const void **dst;
+    };
+    std::vector<Fix> fixes;
+
+    const GgufTensor *get(const std::string &name, std::vector<uint64_t> dims) {
+        const GgufTensor *t = g.tensor(name);
+        if (!t) {
+            if (err.empty()) err = "tensor not found: " + name;
+            return nullptr;
+        }
+        if (t->type != 1) {
+            if (err.empty()) err = "expected F16 tensor " + name;
+            return nullptr;
+        }
+        if (!dims.empty() && t->dims != dims) {
+            if (err.empty()) {
+                err = name + ": expected [";
+                for (size_t i = 0; i < dims.size(); ++i) err += (i ? ", " : "") + std::to_string(dims[i]);
+                err += "], got [";
+                for (size_t i = 0; i < t->dims.size(); ++i) err += (i ? ", " : "") + std::to_string(t->dims[i]);
+                err += "]";
+            }
+            return nullptr;
+        }
+        return t;
+    }
+    size_t alloc(size_t bytes) {
+        const size_t off = (host.size() + 255) & ~(size_t)255;
+        host.resize(off + bytes);
+        return off;
+    }
+    const uint16_t *src(const GgufTensor *t) { return reinterpret_cast<const uint16_t *>(t->data); }
+    // f16 tensor as stored
+    void f16(const GgufTensor *t, const __half **dst) {
+        if (!t) return;
+        const size_t off = alloc(t->elements * 2);
+        memcpy(host.data() + off, t->data, t->elements * 2);
+        fixes.push_back({off, reinterpret_cast<const void **>(dst)});
+    }
+    // f16 tensor as floats
+    void f32(const GgufTensor *t, const float **dst) {
+        if (!t) return;
+        const size_t off = alloc(t->elements * 4);
+        float *o = reinterpret_cast<float *>(host.data() + off);
+        const uint16_t *s = src(t);
+        for (uint64_t i = 0; i < t->elements; ++i) o[i] = h2f_host(s[i]);
+        fixes.push_back({off, reinterpret_cast<const void **>(dst)});
+    }
+    // causal conv weight ggml [k, in, out] (index tap + k (ic + in oc)) as
+    // [out][k in] with column tap * in + ic
+    void conv(const GgufTensor *t, int k, int in, int out, const __half **dst) {
+        if (!t) return;
+        const size_t off = alloc((size_t)k * in * out * 2);
+        uint16_t *o = reinterpret_cast<uint16_t *>(host.data() + off);
+        const uint16_t *s = src(t);
+        for (int oc = 0; oc < out; ++oc)
+            for (int ic = 0; ic < in; ++ic)
+                for (int tap = 0; tap < k; ++tap)
+                    o[(size_t)oc * k * in + (size_t)tap * in + ic] = s[tap + (size_t)k * (ic + (size_t)in * oc)];
+        fixes.push_back({off, reinterpret_cast<const void **>(dst)});
+    }
+    // transposed conv weight ggml [k, out, in] (index tap + k (oc + out ic))
+    // as [k out][in] with row tap * out + oc
+    void convt(const GgufTensor *t, int k, int out, int in, const __half **dst) {
+        if (!t) return;
+        const size_t off = alloc((size_t)k * in * out * 2);
+        uint16_t *o = reinterpret_cast<uint16_t *>(host.data() + off);
+        const uint16_t *s = src(t);
+        for (int ic = 0; ic < in; ++ic)
+            for (int oc = 0; oc < out; ++oc)
+                for (int tap = 0; tap < k; ++tap)
+                    o[((size_t)tap * out + oc) * in + ic] = s[tap + (size_t)k * (oc + (size_t)out * ic)];
+        fixes.push_back({off, reinterpret_cast<const void **>(dst)});
+    }
+    void floats(const std::vector<float> &v, const float **dst) {
+        const size_t off = alloc(v.size() * 4);
+        memcpy(host.data() + off, v.data(), v.size() * 4);
+        fixes.push_back({off, reinterpret_cast<const void **>(dst)});
+    }
+};
+
+int32_t load(S2dCodec *c, const Gguf &g) {
+    Loader L{c, g, {}, {}, {}};
+    using D = std::vector<uint64_t>;
+    const uint64_t H = kHid;
+    // quantizers (codec.rs:2356-2413: in_proj is read and checked there too)
+    for (int cb = 0; cb < kBooks; ++cb) {
+        const std::string p = cb == 0 ? "quantizer.semantic_quantizer.quantizers.0"
+                                      : "quantizer.quantizer.quantizers." + std::to_string(cb - 1);
+        const uint64_t n = cb == 0 ? kSemBook : kResBook;
+        L.get(p + ".in_proj.weight", D{1, H, kProj});
+        L.get(p + ".in_proj.bias", D{kProj});
+        L.f16(L.get(p + ".codebook.weight", D{kProj, n}), &c->rvq.book[cb]);
+        L.f16(L.get(p + ".out_proj.weight", D{1, kProj, H}), &c->rvq.oproj[cb]);
+        L.f16(L.get(p + ".out_proj.bias", D{H}), &c->rvq.obias[cb]);
+        c->rvq.size[cb] = (int)n;
+    }
+    // post module (codec.rs:502-540, 836-910)
+    for (int l = 0; l < kLayers; ++l) {
+        const std::string p = "quantizer.post_module.layers." + std::to_string(l);
+        CodecLayer &y = c->layer[l];
+        L.f16(L.get(p + ".attention.wqkv.weight", D{H, 3 * H}), &y.wqkv);
+        L.f16(L.get(p + ".attention.wo.weight", D{H, H}), &y.wo);
+        L.f32(L.get(p + ".attention_norm.weight", D{H}), &y.an);
+        L.f32(L.get(p + ".ffn_norm.weight", D{H}), &y.fn);
+        L.f16(L.get(p + ".feed_forward.w1.weight", D{H, kFfn}), &y.w1);
+        L.f16(L.get(p + ".feed_forward.w3.weight", D{H, kFfn}), &y.w3);
+        L.f16(L.get(p + ".feed_forward.w2.weight", D{kFfn, H}), &y.w2);
+        L.f32(L.get(p + ".attention_layer_scale.gamma", D{H}), &y.ga);
+        L.f32(L.get(p + ".ffn_layer_scale.gamma", D{H}), &y.gf);
+    }
+    L.f32(L.get("quantizer.post_module.norm.weight", D{H}), &c->post_norm);
+    std::vector<float> freq(kHd / 2);
+    for (int i = 0; i < kHd / 2; ++i) freq[i] = powf(kRopeBase, (float)(2 * i) / (float)kHd);
+    L.floats(freq, &c->rope_freq);
+    // upsample (codec.rs:736-820)
+    for (int s = 0; s < kUpStages; ++s) {
+        const std::string p = "quantizer.upsample." + std::to_string(s);
+        CodecUpStage &u = c->up[s];
+        L.convt(L.get(p + ".0.conv.weight", D{kUp, H, H}), kUp, kHid, kHid, &u.wt);
+        L.f32(L.get(p + ".0.conv.bias", D{H}), &u.bt);
+        L.f32(L.get(p + ".1.gamma", D{H}), &u.gamma);
+        // depthwise [7, 1, C] (index tap + 7 c) is already [c][tap]
+        L.f32(L.get(p + ".1.dwconv.conv.weight", D{kDw, 1, H}), &u.dw);
+        L.f32(L.get(p + ".1.dwconv.conv.bias", D{H}), &u.dwb);
+        L.f32(L.get(p + ".1.norm.weight", D{H}), &u.lnw);
+        L.f32(L.get(p + ".1.norm.bias", D{H}), &u.lnb);
+        L.f16(L.get(p + ".1.pwconv1.weight", D{H, kExp}), &u.pw1);
+        L.f32(L.get(p + ".1.pwconv1.bias", D{kExp}), &u.pw1b);
+        L.f16(L.get(p + ".1.pwconv2.weight", D{kExp, H}), &u.pw2);
+        L.f32(L.get(p + ".1.pwconv2.bias", D{H}), &u.pw2b);
+    }
+    // decoder (codec.rs:1626-1679; block shapes as the forward pass reads them)
+    L.conv(L.get("decoder.model.0.conv.weight", D{7, H, kEntry}), 7, kHid, kEntry, &c->entry_w);
+    L.f32(L.get("decoder.model.0.conv.bias", D{kEntry}), &c->entry_b);
+    int cin = kEntry;
+    for (int b = 0; b < kBlocks; ++b) {
+        const std::string p = "decoder.model." + std::to_string(b + 1);
+        const int C = kChan[b];
+        CodecBlock &k = c->block[b];
+        L.f32(L.get(p + ".block.0.alpha", D{1, (uint64_t)cin, 1}), &k.alpha);
+        const GgufTensor *wt = L.get(p + ".block.1.conv.weight", {});
+        if (wt && (wt->dims.size() != 3 || wt->dims[1] != (uint64_t)C || wt->dims[2] != (uint64_t)cin ||
+                   wt->dims[0] < 1 || wt->dims[0] > 64)) {
+            if (L.err.empty()) L.err = p + ".block.1.conv.weight: expected [k, " + std::to_string(C) + ", " +
+                                       std::to_string(cin) + "]";
+            wt = nullptr;
+        }
+        k.kernel = wt ? (int)wt->dims[0] : 0;
+        L.convt(wt, k.kernel, C, cin, &k.wt);
+        L.f32(L.get(p + ".block.1.conv.bias", D{(uint64_t)C}), &k.bt);
+        for (int u = 0; u < 3; ++u) {
+            const std::string q = p + ".block." + std::to_string(u + 2);
+            CodecUnit &n = k.unit[u];
+            L.f32(L.get(q + ".block.0.alpha", D{1, (uint64_t)C, 1}), &n.a0);
+            L.f32(L.get(q + ".block.2.alpha", D{1, (uint64_t)C, 1}), &n.a1);
+            for (int j = 0; j < 2; ++j) {
+                const GgufTensor *w = L.get(q + (j ? ".block.3.conv.weight" : ".block.1.conv.weight"), {});
+                if (w && (w->dims.size() != 3 || w->dims[1] != (uint64_t)C || w->dims[2] != (uint64_t)C ||
+                          w->dims[0] < 1 || w->dims[0] > 16)) {
+                    if (L.err.empty()) L.err = q + ": conv weight expected [k, C, C]";
+                    w = nullptr;
+                }
+                const int kk = w ? (int)w->dims[0] : 0;
+                (j ? n.k1 : n.k0) = kk;
+                L.conv(w, kk, C, C, j ? &n.w1 : &n.w0);
+            }
+            L.f32(L.get(q + ".block.1.conv.bias", D{(uint64_t)C}), &n.b0);
+            L.f32(L.get(q + ".block.3.conv.bias", D{(uint64_t)C}), &n.b1);
+        }
+        cin = C;
+    }
+    L.f32(L.get("decoder.model.5.alpha", D{1, 96, 1}), &c->tail_alpha);
+    const GgufTensor *ow = L.get("decoder.model.6.conv.weight", D{7, 96, 1});
+    if (ow) {  // [7, 96, 1]: index tap + 7 ic, kept as [tap][ic]
+        std::vector<float> w(7 * 96);
+        for (int tap = 0; tap < 7; ++tap)
+            for (int ic = 0; ic < 96; ++ic) w[tap * 96 + ic] = h2f_host(L.src(ow)[tap + 7 * ic]);
+        L.floats(w, &c->out_w);
+    }
+    if (const GgufTensor *ob = L.get("decoder.model.6.conv.bias", D{1})) c->out_b = h2f_host(L.src(ob)[0]);
+    if (!L.err.empty()) return cerr(c, S2D_EINVAL, "codec weights: " + L.err);
+
+    CCK(cudaMalloc(&c->arena, L.host.size()));
+    c->arena_bytes = L.host.size();
+    CCK(cudaMemcpy(c->arena, L.host.data(), L.host.size(), cudaMemcpyHostToDevice));
+    for (const auto &f : L.fixes) *f.dst = c->arena + f.off;
+    return S2D_OK;
+}
+
+// ---- workspace ---------------------------------------------------------------
+
+int32_t ensure_ws(S2dCodec *c, uint32_t frames) {
+    if (frames <= c->ws_frames) return S2D_OK;
+    const size_t T = frames, L = 4 * T;  // code frames, latent frames
+    // largest row counts x widths over the stages (floats unless noted)
+    size_t xf = std::max(L * kHid, (size_t)L * kEntry);
+    size_t yf = std::max(2 * T * 3 * (size_t)kHid, 2 * T * (size_t)kFfn);
+    yf = std::max(yf, 2 * L * (size_t)kExp);  // pwconv1 of the second stage: 2 x 4T rows of 4096
+    size_t pf = (L + 6) * (size_t)kHid, af = L * 7 * (size_t)kHid, xsf = 2 * L * (size_t)kExp;
+    size_t zf = L * (size_t)kEntry;
+    size_t rows = L, cin = kEntry;
+    for (int b = 0; b < kBlocks; ++b) {
+        const size_t C = kChan[b], K = c->block[b].kernel, out = rows * kRates[b];
+        yf = std::max(yf, 2 * rows * K * C);
+        xsf = std::max(xsf, 2 * rows * cin);
+        xf = std::max(xf, out * C);
+        for (int u = 0; u < 3; ++u) {
+            const int d = u == 0 ? 1 : u == 1 ? 3 : 9;
+            const size_t k0 = c->block[b].unit[u].k0, k1 = c->block[b].unit[u].k1;
+            pf = std::max(pf, (out + (k0 - 1) * d + k1) * C);
+            af = std::max(af, out * std::max(k0, k1) * C);
+        }
+        zf = std::max(zf, out * C);
+        rows = out, cin = C;
+    }
+    const size_t samples = rows;
+    struct Part {
+        void **p;
+        size_t bytes;
+    } parts[] = {
+        {(void **)&c->lat, T * kHid * 4},
+        {(void **)&c->x, xf * 4},
+        {(void **)&c->x2, xf * 4},
+        {(void **)&c->qkv, T * 3 * kHid * 4},
+        {(void **)&c->att, L * kHid * 4},
+        {(void **)&c->act, L * kExp * 4},
+        {(void **)&c->Y2, yf * 4},
+        {(void **)&c->Y2b, 2 * T * (size_t)kFfn * 4},
+        {(void **)&c->inv, std::max(2 * rows, (size_t)L) * 4},
+        {(void **)&c->Z, zf * 4},
+        {(void **)&c->xs, xsf * 2},
+        {(void **)&c->P, pf * 2},
+        {(void **)&c->A, af * 2},
+        {(void **)&c->codes, T * kBooks * 4},
+        {(void **)&c->samples, samples * 4},
+        {(void **)&c->error, 4},
+    };
+    size_t total = 0;
+    for (auto &p : parts) total += (p.bytes + 255) & ~(size_t)255;
+    if (c->ws) cudaFree(c->ws);
+    c->ws = nullptr, c->ws_frames = 0, c->ws_bytes = 0;
+    CCK(cudaMalloc(&c->ws, total));
+    size_t off = 0;
+    for (auto &p : parts) {
+        *p.p = c->ws + off;
+        off += (p.bytes + 255) & ~(size_t)255;
+    }
+    CCK(cudaMemset(c->error, 0, 4));
+    c->ws_frames = frames, c->ws_bytes = total;
+    return S2D_OK;
+}
+
+// ---- stages ------------------------------------------------------------------
+
+// C [M][N] = A [M][K] . W [N][K]^T, f16 in, f32 accumulate and out; long
+// row counts go in slices of 2^20 rows so that no operand passes 2^31 elements.
+int32_t gemm(S2dCodec *c, const __half *A, const __half *W, int M, int N, int K, float *Cm) {
+    const float one = 1.f, zero = 0.f;
+    constexpr int kSlice = 1 << 20;
+    for (int m0 = 0; m0 < M; m0 += kSlice) {
+        const int m = std::min(kSlice, M - m0);
+        const cublasStatus_t st =
+            cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, m, K, &one, W, CUDA_R_16F, K, A + (size_t)m0 * K,
+                         CUDA_R_16F, K, &zero, Cm + (size_t)m0 * N, CUDA_R_32F, N, CUBLAS_COMPUTE_32F,
+                         CUBLAS_GEMM_DEFAULT);
+        if (st != CUBLAS_STATUS_SUCCESS)
+            return cerr(c, S2D_ECUDA, "cublasGemmEx failed (" + std::to_string((int)st) + ")");
+    }
+    return S2D_OK;
+}
+
+// Y2 [2T][N] = the hi / lo split of x [T][K] (RMSNorm with norm_w first when
+// given) times W [N][K]^T.
+int32_t split_gemm(S2dCodec *c, const float *x, int T, int K, const float *norm_w, const __half *W, int N,
+                   float *Y2) {
+    CCK(launch_split_rows(x, K, T, K, norm_w, kNormEps, c->xs, c->inv, nullptr, c->stream));
+    return gemm(c, c->xs, W, 2 * T, N, K, Y2);
+}
+
+int32_t epilogue(S2dCodec *c, int epi, const float *Y2, const float *Y2b, int T, int N, const float *bias, int nb,
+                 const float *gamma, const float *r, float *y) {
+    epilogue_kernel<<<grid_for((size_t)T * N), 256, 0, c->stream>>>(epi, Y2, Y2b, c->inv, T, N, bias, nb, gamma, r, y);
+    CCK(cudaGetLastError());
+    return S2D_OK;
+}
+
+// forward_codec_post_module (codec.rs:986) on x [T][1024], in place; the final
+// RMSNorm lands in `out`.
+int32_t post_module(S2dCodec *c, float *x, int T, float *out) {
+    int32_t rc;
+    for (int l = 0; l < kLayers; ++l) {
+        const CodecLayer &y = c->layer[l];
+        if ((rc = split_gemm(c, x, T, kHid, y.an, y.wqkv, 3 * kHid, c->Y2))) return rc;
+        qkv_rope_kernel<<<T, 256, 0, c->stream>>>(c->Y2, c->inv, T, c->rope_freq, c->qkv);
+        window_attn_kernel<<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
+        CCK(cudaGetLastError());
+        if ((rc = split_gemm(c, c->att, T, kHid, nullptr, y.wo, kHid, c->Y2))) return rc;
+        if ((rc = epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T, kHid, nullptr, 1, y.ga, x, x))) return rc;
+        CCK(launch_split_rows(x, kHid, T, kHid, y.fn, kNormEps, c->xs, c->inv, nullptr, c->stream));
+        if ((rc = gemm(c, c->xs, y.w1, 2 * T, kFfn, kHid, c->Y2))) return rc;
+        if ((rc = gemm(c, c->xs, y.w3, 2 * T, kFfn, kHid, c->Y2b))) return rc;
+        if ((rc = epilogue(c, CE_SWIGLU, c->Y2, c->Y2b, T, kFfn, nullptr, 1, nullptr, nullptr, c->act))) return rc;
+        if ((rc = split_gemm(c, c->act, T, kFfn, nullptr, y.w2, kHid, c->Y2))) return rc;
+        if ((rc = epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T, kHid, nullptr, 1, y.gf, x, x))) return rc;
+    }
+    // the final RMSNorm: split_rows writes the normalised rows to `out`
+    CCK(launch_split_rows(x, kHid, T, kHid, c->post_norm, kNormEps, c->xs, c->inv, out, c->stream));
+    return S2D_OK;
+}
+
+// One upsample stage (codec.rs:3338): x [T][1024] -> y [2T][1024].
+int32_t upsample_stage(S2dCodec *c, const CodecUpStage &u, const float *x, int T, float *y) {
+    int32_t rc;
+    const int T2 = 2 * T;
+    // transposed conv, kernel 2 = stride: output row 2f + k is GEMM row f's
+    // columns [k 1024, (k + 1) 1024), so [T][2048] is already [2T][1024]
+    if ((rc = split_gemm(c, x, T, kHid, nullptr, u.wt, kUp * kHid, c->Y2))) return rc;
+    if ((rc = epilogue(c, CE_STORE, c->Y2, nullptr, T, kUp * kHid, u.bt, kHid, nullptr, nullptr, y))) return rc;
+    // ConvNeXt block (codec.rs:3438)
+    dwconv_ln_kernel<<<T2, 256, 0, c->stream>>>(y, T2, u.dw, u.dwb, u.lnw, u.lnb, c->att);
+    CCK(cudaGetLastError());
+    if ((rc = split_gemm(c, c->att, T2, kHid, nullptr, u.pw1, kExp, c->Y2))) return rc;
+    if ((rc = epilogue(c, CE_GELU, c->Y2, nullptr, T2, kExp, u.pw1b, kExp, nullptr, nullptr, c->act))) return rc;
+    if ((rc = split_gemm(c, c->act, T2, kExp, nullptr, u.pw2, kHid, c->Y2))) return rc;
+    return epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T2, kHid, u.pw2b, kHid, u.gamma, y, y);
+}
+
+// A stride-1 causal convolution (codec.rs:2212) of x [T][C] (+ bias, snake
+// first when alpha is set) into Z [T][N]: pad + round, im2col, one GEMM.
+int32_t causal_conv(S2dCodec *c, const float *x, int T, int C, const float *bias, const float *alpha,
+                    const __half *W, int K, int d, int N, float *Z) {
+    const int pad = (K - 1) * d;
+    pad_f16_kernel<<<grid_for((size_t)(T + pad) * C), 256, 0, c->stream>>>(x, T, C, pad, bias, alpha, c->P);
+    CCK(cudaGetLastError());
+    const __half *A = c->P;
+    if (K > 1) {
+        im2col_kernel<<<grid_for((size_t)T * K * C / 8), 256, 0, c->stream>>>(c->P, T, C, K, d, c->A);
+        CCK(cudaGetLastError());
+        A = c->A;
+    }
+    return gemm(c, A, W, T, N, K * C, Z);
+}
+
+// forward_codec_decoder (codec.rs:1941): hidden [L][1024] -> samples [512 L].
+int32_t decoder(S2dCodec *c, const float *hidden, int L, float *samples) {
+    int32_t rc;
+    // entry conv 1024 -> 1536; its bias is added by the first block's snake
+    if ((rc = causal_conv(c, hidden, L, kHid, nullptr, nullptr, c->entry_w, 7, 1, kEntry, c->Z))) return rc;
+    const float *in = c->Z, *in_bias = c->entry_b;
+    int rows = L, cin = kEntry;
+    float *x = c->x;
+    for (int b = 0; b < kBlocks; ++b) {
+        const CodecBlock &k = c->block[b];
+        const int C = kChan[b], s = kRates[b], out = rows * s;
+        // snake, then the transposed conv over every tap and col2im
+        snake_kernel<<<grid_for((size_t)rows * cin), 256, 0, c->stream>>>(in, rows, cin, in_bias, k.alpha, c->x2);
+        CCK(cudaGetLastError());
+        if ((rc = split_gemm(c, c->x2, rows, cin, nullptr, k.wt, k.kernel * C, c->Y2))) return rc;
+        col2im_kernel<<<grid_for((size_t)out * C), 256, 0, c->stream>>>(c->Y2, c->inv, rows, k.kernel, s, C, k.bt, x);
+        CCK(cudaGetLastError());
+        // residual units, dilations 1, 3, 9 (codec.rs:2040-2042)
+        for (int u = 0; u < 3; ++u) {
+            const CodecUnit &n = k.unit[u];
+            const int d = u == 0 ? 1 : u == 1 ? 3 : 9;
+            if ((rc = causal_conv(c, x, out, C, nullptr, n.a0, n.w0, n.k0, d, C, c->Z))) return rc;
+            if ((rc = causal_conv(c, c->Z, out, C, n.b0, n.a1, n.w1, n.k1, 1, C, c->x2))) return rc;
+            resid_kernel<<<grid_for((size_t)out * C), 256, 0, c->stream>>>(x, c->x2, out, C, n.b1);
+            CCK(cudaGetLastError());
+        }
+        in = x, in_bias = nullptr, rows = out, cin = C;
+    }
+    const size_t smem = (size_t)(kTailTile + 6) * 96 * sizeof(float);
+    tail_kernel<<<(rows + kTailTile - 1) / kTailTile, kTailTile, smem, c->stream>>>(x, rows, c->tail_alpha, c->out_w,
+                                                                                     c->out_b, 96, 7, samples);
+    CCK(cudaGetLastError());
+    return S2D_OK;
+}
+
+// RVQ lookup, post module, upsample and decoder on device codes.
+int32_t decode_device(S2dCodec *c, const int32_t *codes_dev, int T, float *samples) {
+    int32_t rc;
+    rvq_kernel<<<T, 256, 0, c->stream>>>(c->rvq, codes_dev, T, c->lat, c->error);
+    CCK(cudaGetLastError());
+    if ((rc = post_module(c, c->lat, T, c->x))) return rc;
+    if ((rc = upsample_stage(c, c->up[0], c->x, T, c->x2))) return rc;
+    if ((rc = upsample_stage(c, c->up[1], c->x2, 2 * T, c->Z))) return rc;
+    // the entry conv reads hidden (Z) into its padded f16 rows before its GEMM overwrites Z
+    return decoder(c, c->Z, 4 * T, samples);
+}
+
+int32_t check_codes(S2dCodec *c, const int32_t *codes, uint32_t ncb, uint32_t n) {
+    if (!codes) return cerr(c, S2D_EINVAL, "codes is null");
+    if (ncb != kBooks) return cerr(c, S2D_EINVAL, "codec codebook count mismatch: expected 10, got " + std::to_string(ncb));
+    if (n == 0) return cerr(c, S2D_EINVAL, "codec transformer requires at least one frame");
+    for (uint32_t cb = 0; cb < ncb; ++cb)
+        for (uint32_t f = 0; f < n; ++f) {
+            const int32_t v = codes[(size_t)cb * n + f];
+            if (v < 0) return cerr(c, S2D_EINVAL, "codec code must be non-negative, got " + std::to_string(v));
+            if (v >= c->rvq.size[cb])
+                return cerr(c, S2D_EINVAL, "embedding index " + std::to_string(v) + " out of range for codebook " +
+                                               std::to_string(cb));
+        }
+    return S2D_OK;
+}
+
+int32_t sync_and_check(S2dCodec *c) {
+    CCK(cudaStreamSynchronize(c->stream));
+    int32_t flag = 0;
+    CCK(cudaMemcpy(&flag, c->error, 4, cudaMemcpyDeviceToHost));
+    if (flag) {
+        CCK(cudaMemset(c->error, 0, 4));
+        return cerr(c, S2D_EDEVICE, "a codec code was out of range for its codebook");
+    }
+    return S2D_OK;
+}
+
+}  // namespace
+}  // namespace s2d
+
+using namespace s2d;
+
+extern "C" {
+
+int32_t s2d_codec_open(const char *gguf_path, int32_t device, S2dCodec **out) {
+    if (!out || !gguf_path) return S2D_EINVAL;
+    *out = nullptr;
+    S2dCodec *c = new S2dCodec();
+    c->device = device;
+    Gguf g;
+    std::string e;
+    int32_t rc = S2D_OK;
+    std::string arch;
+    if (!g.open(gguf_path, &e)) {
+        rc = cerr(c, S2D_EIO, e);
+    } else if (!g.meta_str("general.architecture", &arch, &e) || arch != "fish-speech-codec") {
+        rc = cerr(c, S2D_EINVAL, "expected fish-speech-codec codec GGUF, got " + (arch.empty() ? e : arch));
+    } else if (cudaSetDevice(device) != cudaSuccess) {
+        rc = cerr(c, S2D_ECUDA, "cudaSetDevice failed");
+    } else if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        rc = cerr(c, S2D_ECUDA, "cudaStreamCreate failed");
+    } else if (cublasCreate(&c->blas) != CUBLAS_STATUS_SUCCESS ||
+               cublasSetStream(c->blas, c->stream) != CUBLAS_STATUS_SUCCESS) {
+        rc = cerr(c, S2D_ECUDA, "cublasCreate failed");
+    } else {
+        rc = load(c, g);
+    }
+    *out = c;  // also on failure, so that the caller can read the message
+    return rc;
+}
+
+void s2d_codec_close(S2dCodec *c) {
+    if (!c) return;
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->ws) cudaFree(c->ws);
+    if (c->arena) cudaFree(c->arena);
+    if (c->blas) cublasDestroy(c->blas);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+const char *s2d_codec_last_error(const S2dCodec *c) { return c ? c->err.c_str() : "null codec"; }
+
+int32_t s2d_codec_decode_waveform(S2dCodec *c, const int32_t *codes, uint32_t num_codebooks, uint32_t n_frames,
+                                  float *samples, size_t capacity, size_t *num_samples, uint32_t *latent_frames) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    int32_t rc;
+    if ((rc = check_codes(c, codes, num_codebooks, n_frames))) return rc;
+    const size_t n = (size_t)n_frames * 4 * kSamplesPerLatent;
+    if (!samples || capacity < n) return cerr(c, S2D_EINVAL, "samples buffer holds " + std::to_string(capacity) +
+                                                                 " floats, the decode needs " + std::to_string(n));
+    if ((rc = ensure_ws(c, n_frames))) return rc;
+    CCK(cudaMemcpyAsync(c->codes, codes, (size_t)kBooks * n_frames * 4, cudaMemcpyHostToDevice, c->stream));
+    if ((rc = decode_device(c, c->codes, (int)n_frames, c->samples))) return rc;
+    CCK(cudaMemcpyAsync(samples, c->samples, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = sync_and_check(c))) return rc;
+    if (num_samples) *num_samples = n;
+    if (latent_frames) *latent_frames = 4 * n_frames;
+    return S2D_OK;
+}
+
+int32_t s2d_codec_decode_waveform_device(S2dCodec *c, const int32_t *codes_dev, uint32_t num_codebooks,
+                                         uint32_t n_frames, float *samples_dev, void *stream) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    if (!codes_dev || !samples_dev) return cerr(c, S2D_EINVAL, "null device buffer");
+    if (num_codebooks != kBooks) return cerr(c, S2D_EINVAL, "codec codebook count mismatch");
+    if (n_frames == 0) return cerr(c, S2D_EINVAL, "codec transformer requires at least one frame");
+    int32_t rc;
+    if ((rc = ensure_ws(c, n_frames))) return rc;
+    cudaStream_t own = c->stream;
+    if (stream) {
+        c->stream = (cudaStream_t)stream;
+        cublasSetStream(c->blas, c->stream);
+    }
+    rc = decode_device(c, codes_dev, (int)n_frames, samples_dev);
+    if (stream) {
+        c->stream = own;
+        cublasSetStream(c->blas, own);
+    }
+    return rc;
+}
+
+int32_t s2d_codec_sync(S2dCodec *c) {
+    if (!c || !c->stream) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    CCK(cudaDeviceSynchronize());
+    return sync_and_check(c);
+}
+
+int32_t s2d_codec_rvq_lookup(S2dCodec *c, const int32_t *codes, uint32_t num_codebooks, uint32_t n_frames,
+                             float *latents) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    int32_t rc;
+    if ((rc = check_codes(c, codes, num_codebooks, n_frames))) return rc;
+    if (!latents) return cerr(c, S2D_EINVAL, "latents is null");
+    if ((rc = ensure_ws(c, n_frames))) return rc;
+    CCK(cudaMemcpyAsync(c->codes, codes, (size_t)kBooks * n_frames * 4, cudaMemcpyHostToDevice, c->stream));
+    rvq_kernel<<<n_frames, 256, 0, c->stream>>>(c->rvq, c->codes, (int)n_frames, c->lat, c->error);
+    CCK(cudaGetLastError());
+    CCK(cudaMemcpyAsync(latents, c->lat, (size_t)n_frames * kHid * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+int32_t s2d_codec_decode_latents(S2dCodec *c, const float *latents, uint32_t n_frames, float *hidden) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    if (!latents || !hidden) return cerr(c, S2D_EINVAL, "null buffer");
+    if (n_frames == 0) return cerr(c, S2D_EINVAL, "codec transformer requires at least one frame");
+    int32_t rc;
+    if ((rc = ensure_ws(c, n_frames))) return rc;
+    const int T = (int)n_frames;
+    CCK(cudaMemcpyAsync(c->lat, latents, (size_t)T * kHid * 4, cudaMemcpyHostToDevice, c->stream));
+    if ((rc = post_module(c, c->lat, T, c->x))) return rc;
+    if ((rc = upsample_stage(c, c->up[0], c->x, T, c->x2))) return rc;
+    if ((rc = upsample_stage(c, c->up[1], c->x2, 2 * T, c->Z))) return rc;
+    CCK(cudaMemcpyAsync(hidden, c->Z, (size_t)4 * T * kHid * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+int32_t s2d_codec_decoder(S2dCodec *c, const float *hidden, uint32_t n_frames, uint32_t hidden_dim, float *samples) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    if (!hidden || !samples) return cerr(c, S2D_EINVAL, "null buffer");
+    if (hidden_dim != kHid)
+        return cerr(c, S2D_EINVAL, "decoder expects latent dim 1024, got " + std::to_string(hidden_dim));
+    if (n_frames == 0) return cerr(c, S2D_EINVAL, "decoder needs at least one frame");
+    int32_t rc;
+    if ((rc = ensure_ws(c, (n_frames + 3) / 4))) return rc;
+    const int L = (int)n_frames;
+    CCK(cudaMemcpyAsync(c->x2, hidden, (size_t)L * kHid * 4, cudaMemcpyHostToDevice, c->stream));
+    if ((rc = decoder(c, c->x2, L, c->samples))) return rc;
+    CCK(cudaMemcpyAsync(samples, c->samples, (size_t)L * kSamplesPerLatent * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+int32_t s2d_codec_memory(const S2dCodec *c, size_t *weight_bytes, size_t *workspace_bytes) {
+    if (!c) return S2D_EINVAL;
+    if (weight_bytes) *weight_bytes = c->arena_bytes;
+    if (workspace_bytes) *workspace_bytes = c->ws_bytes;
+    return S2D_OK;
+}
+
+}  // extern "C"

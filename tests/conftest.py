@@ -29,3 +29,16 @@ def model_dir():
 def tiny_gguf(model_dir):
     from fish_s2pro_b200 import configs, synth
     return synth.cached_gguf(configs.C1.model, model_dir)
+
+
+@pytest.fixture(scope="session")
+def codec_gguf(model_dir):
+    """The seeded synthetic codec file (decode tensors of the real shapes)."""
+    from fish_s2pro_b200 import codec_synth
+    return codec_synth.cached_codec_gguf(model_dir)
+
+
+@pytest.fixture(scope="session")
+def codec_oracle_weights(codec_gguf):
+    from oracle import codec_oracle
+    return codec_oracle.CodecWeights(codec_gguf)
