@@ -88,6 +88,10 @@ def parse():
                     help="under torchrun: independent replicas (weak scaling) as the headline line")
     ap.add_argument("--no-serving", action="store_true",
                     help="skip the nested continuous-batching line of the default run")
+    ap.add_argument("--no-codec", action="store_true",
+                    help="skip the nested codec-decode line (codes -> PCM) of the default run")
+    ap.add_argument("--codec-only", action="store_true",
+                    help="measure only the codec decode line (profiling)")
     ap.add_argument("--no-quant", action="store_true",
                     help="skip the nested C3 (Q8_0) and C5 (Q4_K) lines of the default N = 1 run")
     return ap.parse_args()
@@ -207,8 +211,8 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 # ---------------------------------------------------------------------------
@@ -472,6 +476,126 @@ def run_serving(args, d: Dist, wl, n_req=128, frames=64, slots=64, kv_pages=640)
     return line
 
 
+def codec_flops_per_frame() -> float:
+    """Algorithmic FLOPs of one code frame's decode (2 per multiply-add of
+    every contraction, each counted once): post module, upsample, decoder
+    (codec.rs:986, 2302, 1941).  The attention is counted at the full
+    128-frame window."""
+    H, F, E = 1024, 3072, 4096
+    post = 8 * 2 * (H * 3 * H + H * H + 2 * H * F + F * H) + 8 * 2 * 2 * 128 * H
+    up = 2 * (H * 2 * H) + 2 * 2 * (2 * H * E) + 2 * (2 * H * (2 * H)) + 2 * 4 * (2 * H * E)
+    dec = 2 * 4 * 7 * H * 1536
+    rows, cin = 4, 1536
+    for r, c in zip((8, 8, 4, 2), (768, 384, 192, 96)):
+        dec += 2 * rows * cin * 2 * r * c          # transposed conv, kernel 2 x stride
+        rows *= r
+        dec += 3 * 2 * rows * (7 * c * c + c * c)  # three residual units
+        cin = c
+    dec += 2 * rows * 7 * 96
+    return float(post + up + dec)
+
+
+def run_codec(args, d: Dist, frames=512, steps=None, warmup=None):
+    """The codec decode (codes -> 44.1 kHz PCM, CodecDecoder over
+    include/s2d_codec.h) of `frames` code frames (2,048 samples each) on a
+    synthetic codec of the real shapes.  One step = one decode; `value`
+    times it on device codes with CUDA events (s2d_codec_decode_waveform_device),
+    `e2e` through decode_waveform with host codes in and host samples out.
+    Each rank decodes its own codes (replicas)."""
+    import torch
+    from fish_s2pro_b200 import CodecDecoder, build, codec_synth
+    from fish_s2pro_b200.codec import codec_lib
+    build.build_runtime()
+    steps = max(10, min(args.steps, 30)) if steps is None else steps
+    warmup = max(3, min(args.warmup, 3)) if warmup is None else warmup
+    if d.local == 0:  # one writer per host; the others find the file after the barrier
+        codec_synth.cached_codec_gguf(args.model_dir)
+    d.barrier()
+    path = codec_synth.cached_codec_gguf(args.model_dir)
+    c = CodecDecoder.open(path, device=d.local)
+    rng = np.random.default_rng(1234 + d.rank)
+    codes = np.concatenate([rng.integers(0, 4096, frames), rng.integers(0, 1024, 9 * frames)]).astype(np.int32)
+    codes_dev = torch.from_numpy(codes).to(f"cuda:{d.local}")
+    out = torch.empty(frames * 2048, dtype=torch.float32, device=f"cuda:{d.local}")
+    # a stream of our own (not the legacy default stream, whose handle 0
+    # would select the codec's internal stream): the decode and the events share it
+    stream = torch.cuda.Stream(device=d.local)
+    device_sync()
+    lib = codec_lib()
+
+    def step():
+        rc = lib.s2d_codec_decode_waveform_device(c.handle, codes_dev.data_ptr(), 10, frames, out.data_ptr(),
+                                                  stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(lib.s2d_codec_last_error(c.handle).decode())
+
+    for _ in range(warmup):
+        step()
+    device_sync()
+    clocks = Clocks(d.local)
+    d.barrier()
+    device_sync()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    device_sync()
+    d.barrier()
+    ck = clocks.stop()
+    ms = d.max(e0.elapsed_time(e1) / steps)
+    if lib.s2d_codec_sync(c.handle) != 0:
+        raise RuntimeError(lib.s2d_codec_last_error(c.handle).decode())
+    # end to end through the public call: codes from the host, samples back
+    c.decode_waveform(codes, 10, frames)
+    device_sync()
+    d.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        w = c.decode_waveform(codes, 10, frames)
+    t1 = time.perf_counter()
+    d.barrier()
+    e2e_s = d.max((t1 - t0) / steps)
+    samples = frames * 2048
+    flops = codec_flops_per_frame() * frames
+    pk = peaks()
+    line = {
+        "metric": "codec_samples_per_s", "value": round(d.sum(samples) / (ms / 1e3)), "unit": "samples/s",
+        "n_gpus": d.world, "steps": steps, "warmup": warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "scaling": "weak", "dtype": "f16 tensor-core GEMMs, f32 accumulation",
+        "realtime_factor": round(d.sum(samples) / (ms / 1e3) / 44100.0, 1),
+        "e2e": {"value": round(d.sum(samples) / e2e_s), "unit": "samples/s", "h2d_bytes_per_step": int(codes.nbytes),
+                "d2h_bytes_per_step": int(w.samples.nbytes)},
+        "roofline": {"bound": "tensor", "achieved": round(flops / (ms / 1e3) / 1e12, 1), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(flops / (ms / 1e3) / 1e12 / pk["bf16_tflops"], 3),
+                     "traffic": None,
+                     "note": f"whole decode: {flops / 1e12:.2f} TFLOP of contractions per step over the step's "
+                             f"device time, of {pk['source']} dense bf16 peak"},
+        "config": {"workload": f"codec decode of {frames} code frames ({samples} samples, "
+                               f"{samples / 44100:.1f} s of 44.1 kHz audio) on a seeded synthetic codec of the "
+                               "s2-pro shapes; workspace > L2 (no flush needed)",
+                   "parallelism": f"replicas x{d.world}"},
+        "clocks": ck,
+    }
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        # the float64 numpy oracle on one code frame, all host threads (BLAS)
+        from oracle import codec_oracle as co
+        w64 = co.CodecWeights(path)
+        one = codes.reshape(10, frames)[:, :1].reshape(-1)
+        co.decode_waveform(one, 10, 1, w64)  # converts the weights once
+        t0 = time.perf_counter()
+        n_cpu = 2
+        for _ in range(n_cpu):
+            co.decode_waveform(one, 10, 1, w64)
+        dt = (time.perf_counter() - t0) / n_cpu
+        line["cpu_baseline"] = {"value": round(2048 / dt, 1), "unit": "samples/s", "cores": os.cpu_count(),
+                                "kind": "port", "sample": "one code frame (2,048 samples) through the float64 "
+                                                          "numpy codec oracle, twice"}
+    c.close()
+    return line
+
+
 def run_batch(args, d: Dist, wl, name=None, steps=None, warmup=None):
     """Batched workload (C4): every rank generates for `wl.batch` independent
     prompts at once through s2d_generate_codes_batch; one step = one call
@@ -623,6 +747,14 @@ def main():
         print(json.dumps(line), flush=True)
         return 0
     d = Dist(args.gpus)
+    if args.codec_only:
+        try:
+            line = run_codec(args, d)
+            if d.rank == 0:
+                print(json.dumps(line), flush=True)
+        finally:
+            d.close()
+        return 0
     nested_keys = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "dtype",
                    "scaling", "prefill_ms", "e2e", "gpu_launches", "roofline", "config", "clocks")
     try:
@@ -650,6 +782,12 @@ def main():
                 line["serving"] = run_serving(args, d, configs.C4)
             except Exception as e:
                 line["serving"] = {"metric": METRIC_BATCH, "error": repr(e)[:300]}
+        # the codec decode after the token loop (codes -> PCM)
+        if default_c2 and not args.no_codec:
+            try:
+                line["codec"] = run_codec(args, d)
+            except Exception as e:
+                line["codec"] = {"metric": "codec_samples_per_s", "error": repr(e)[:300]}
         # the quantized batch-1 configurations, on one GPU, over a few steps
         if default_c2 and d.world == 1 and not args.no_quant:
             for key, name in (("q8_0", "C3"), ("q4_k", "C5")):

@@ -40,7 +40,7 @@ constexpr int kChan[kBlocks] = {768, 384, 192, 96};  // block_output_channels, c
 constexpr int kSemBook = 4096, kResBook = 1024;
 constexpr float kNormEps = 1e-5f, kLnEps = 1e-6f, kRopeBase = 10000.0f;
 constexpr int kSamplesPerLatent = 8 * 8 * 4 * 2;
-constexpr int kTailTile = 64;
+constexpr int kTailTile = 128;
 
 // ---------------------------------------------------------------- kernels --
 
@@ -229,93 +229,212 @@ __device__ __forceinline__ float snake(float x, float alpha) {
     return x + s * s / a;
 }
 
-// y[t][c] = snake(x[t][c] (+ bias[c])), float out (the transposed
-// convolution's input, which the reference does not round).
-__global__ void snake_kernel(const float *x, int T, int C, const float *bias, const float *alpha, float *y) {
-    const size_t total = (size_t)T * C;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int c = (int)(i % C);
-        y[i] = snake(x[i] + (bias ? bias[c] : 0.f), alpha[c]);
+// f16 of four floats, stored as 8 bytes.
+__device__ __forceinline__ void st_half4(__half *dst, float a, float b, float c, float d) {
+    __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&lo);
+    u.y = *reinterpret_cast<uint32_t *>(&hi);
+    *reinterpret_cast<uint2 *>(dst) = u;
+}
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+
+// A causal convolution's padded input from a float map: P[pad + t][c] =
+// f16(snake(x[t][c] + bias[c])) with bias and snake optional, P[0 .. pad) = 0
+// (codec.rs:2247-2259).  Four channels per thread (C % 4 == 0).
+__global__ void pad_f16_kernel(const float *x, int T, int C, int pad, const float *bias, const float *alpha,
+                               __half *P) {
+    const int C4 = C / 4;
+    const long long total = (long long)(T + pad) * C4;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / C4;
+        const int c = (int)(i - row * C4) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row >= pad) {
+            v = ld4(x + (row - pad) * C + c);
+            if (bias) {
+                const float4 b = ld4(bias + c);
+                v.x += b.x, v.y += b.y, v.z += b.z, v.w += b.w;
+            }
+            if (alpha) {
+                const float4 a = ld4(alpha + c);
+                v = make_float4(snake(v.x, a.x), snake(v.y, a.y), snake(v.z, a.z), snake(v.w, a.w));
+            }
+        }
+        st_half4(P + row * C + c, v.x, v.y, v.z, v.w);
     }
 }
 
-// A causal convolution's padded input: P[pad + t][c] = f16(snake(x[t][c] +
-// bias[c])) (bias and snake optional), P[0 .. pad) = 0 (codec.rs:2247-2259).
-__global__ void pad_f16_kernel(const float *x, int T, int C, int pad, const float *bias, const float *alpha,
-                               __half *P) {
-    const size_t total = (size_t)(T + pad) * C;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t row = i / C;
-        const int c = (int)(i % C);
-        float v = 0.f;
-        if (row >= (size_t)pad) {
-            v = x[i - (size_t)pad * C] + (bias ? bias[c] : 0.f);
-            if (alpha) v = snake(v, alpha[c]);
+// The last two steps of a residual unit and the first of the next
+// (codec.rs:2085-2160): x += Z + bias (the unit's output, written back), and
+// the next unit's padded conv input P[pad + t] = f16(snake(x, alpha)),
+// P[0 .. pad) = 0.
+__global__ void resid_pad_kernel(float *x, const float *Z, const float *bias, int T, int C, const float *alpha,
+                                 int pad, __half *P) {
+    const int C4 = C / 4;
+    const long long total = (long long)(T + pad) * C4;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / C4;
+        const int c = (int)(i - row * C4) * 4;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row >= pad) {
+            float *xr = x + (row - pad) * C + c;
+            float4 v = ld4(xr);
+            const float4 z = ld4(Z + (row - pad) * C + c), b = ld4(bias + c), a = ld4(alpha + c);
+            v.x += z.x + b.x, v.y += z.y + b.y, v.z += z.z + b.z, v.w += z.w + b.w;
+            *reinterpret_cast<float4 *>(xr) = v;
+            s = make_float4(snake(v.x, a.x), snake(v.y, a.y), snake(v.z, a.z), snake(v.w, a.w));
         }
-        P[i] = __float2half_rn(v);
+        st_half4(P + row * C + c, s.x, s.y, s.z, s.w);
+    }
+}
+
+// A transposed convolution's input row, split for the tensor cores: v =
+// x[t] (+ Z[t] + zb: the previous residual unit's output) (+ bias), s =
+// snake(v), then the power-of-two scaled hi / lo halves into xs rows t and
+// T + t and inv[t] (the scaling of launch_split_rows).  One warp per row,
+// NI float2 per lane (C = 64 NI).
+template <int NI>
+__global__ void __launch_bounds__(256) snake_split_kernel(const float *x, const float *Z, const float *zb,
+                                                          const float *bias, const float *alpha, int T,
+                                                          __half *xs, float *inv) {
+    constexpr int C = 64 * NI;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= T) return;
+    float2 v[NI];
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < NI; ++j) {
+        const int c = 64 * j + 2 * lane;
+        float2 a = *reinterpret_cast<const float2 *>(x + (size_t)t * C + c);
+        if (Z) {
+            const float2 z = *reinterpret_cast<const float2 *>(Z + (size_t)t * C + c);
+            const float2 b = *reinterpret_cast<const float2 *>(zb + c);
+            a.x += z.x + b.x, a.y += z.y + b.y;
+        }
+        if (bias) {
+            const float2 b = *reinterpret_cast<const float2 *>(bias + c);
+            a.x += b.x, a.y += b.y;
+        }
+        const float2 al = *reinterpret_cast<const float2 *>(alpha + c);
+        v[j] = make_float2(snake(a.x, al.x), snake(a.y, al.y));
+        mx = fmaxf(mx, fmaxf(fabsf(v[j].x), fabsf(v[j].y)));
+    }
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // a power of two p with mx * p in [2^13, 2^14); 1 for an all-zero row
+    float p = 1.f;
+    if (mx > 0.f && isfinite(mx)) {
+        int e;
+        frexpf(mx, &e);
+        p = ldexpf(1.f, 14 - e);
+    }
+    if (lane == 0) inv[t] = 1.f / p;
+    __half *hi = xs + (size_t)t * C, *lo = xs + ((size_t)T + t) * C;
+#pragma unroll
+    for (int j = 0; j < NI; ++j) {
+        const int c = 64 * j + 2 * lane;
+        const float a = v[j].x * p, b = v[j].y * p;
+        const __half2 h = __floats2half2_rn(a, b);
+        const float2 hf = __half22float2(h);
+        *reinterpret_cast<__half2 *>(hi + c) = h;
+        *reinterpret_cast<__half2 *>(lo + c) = __floats2half2_rn(a - hf.x, b - hf.y);
     }
 }
 
 // im2col of a stride-1 causal convolution: A[t][k C + c] = P[t + k d][c] for
 // the taps k < K, 16 bytes at a time (C * 2 is a multiple of 16).
 __global__ void im2col_kernel(const __half *P, int T, int C, int K, int d, __half *A) {
-    const int cv = C / 8;  // uint4 per row of P
-    const size_t total = (size_t)T * K * cv;
+    const int cv = C / 8, row = K * cv;  // uint4 per row of P / of A
+    const long long total = (long long)T * row;
     const uint4 *src = reinterpret_cast<const uint4 *>(P);
     uint4 *dst = reinterpret_cast<uint4 *>(A);
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const size_t t = i / ((size_t)K * cv);
-        const int r = (int)(i % ((size_t)K * cv)), k = r / cv, j = r % cv;
-        dst[i] = src[(t + (size_t)k * d) * cv + j];
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i / row;
+        const int r = (int)(i - t * row), k = r / cv, j = r - k * cv;
+        dst[i] = src[(t + (long long)k * d) * cv + j];
     }
 }
 
-// causal_conv_transpose_1d (codec.rs:3505) from the GEMM over every tap:
-// Y2 holds [T][K C] (stacked hi / lo rows); output row u = f s + k sums the
-// taps that land on it in increasing f, then adds the bias; rows past T s are
-// not produced.
-__global__ void col2im_kernel(const float *Y2, const float *inv, int T, int K, int s, int C, const float *bias,
-                              float *y) {
-    const size_t total = (size_t)T * s * C;
-    const int N = K * C;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int u = (int)(i / C), c = (int)(i % C);
+// causal_conv_transpose_1d (codec.rs:3505) from the GEMM over every tap, and
+// the first residual unit's padded conv input: Y2 holds [T][K C] (stacked hi
+// / lo rows); output row u = f s + k sums the taps that land on it in
+// increasing f, then adds the bias (rows past T s are not produced) -> x;
+// P[pad + u] = f16(snake(x, alpha)), P[0 .. pad) = 0.  Four channels per
+// thread.
+__global__ void col2im_pad_kernel(const float *Y2, const float *inv, int T, int K, int s, int C, const float *bias,
+                                  float *x, const float *alpha, int pad, __half *P) {
+    const int C4 = C / 4, N = K * C;
+    const long long rows = (long long)T * s, total = (rows + pad) * C4;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long prow = i / C4;
+        const int c = (int)(i - prow * C4) * 4;
+        if (prow < pad) {
+            st_half4(P + prow * C + c, 0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        const int u = (int)(prow - pad);
         const int f_hi = min(u / s, T - 1);
         int f_lo = u - (K - 1);
         f_lo = f_lo <= 0 ? 0 : (f_lo + s - 1) / s;
-        float acc = 0.f;
-        for (int f = f_lo; f <= f_hi; ++f) acc += combine(Y2, inv, T, N, f, (u - f * s) * C + c);
-        y[i] = acc + bias[c];
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int f = f_lo; f <= f_hi; ++f) {
+            const size_t col = (size_t)(u - f * s) * C + c;
+            const float4 a = ld4(Y2 + (size_t)f * N + col), b = ld4(Y2 + ((size_t)T + f) * N + col);
+            const float w = inv[f];
+            acc.x += (a.x + b.x) * w, acc.y += (a.y + b.y) * w, acc.z += (a.z + b.z) * w, acc.w += (a.w + b.w) * w;
+        }
+        const float4 bb = ld4(bias + c), al = ld4(alpha + c);
+        acc.x += bb.x, acc.y += bb.y, acc.z += bb.z, acc.w += bb.w;
+        *reinterpret_cast<float4 *>(x + (size_t)u * C + c) = acc;
+        st_half4(P + prow * C + c, snake(acc.x, al.x), snake(acc.y, al.y), snake(acc.z, al.z), snake(acc.w, al.w));
     }
 }
 
-// Residual unit output (codec.rs:2151): x += Z + bias.
-__global__ void resid_kernel(float *x, const float *Z, int T, int C, const float *bias) {
-    const size_t total = (size_t)T * C;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
-        x[i] += Z[i] + bias[i % C];
-}
-
-// Decoder tail (codec.rs:1978-1998): snake, the causal convolution 96 -> 1
-// (kernel 7, input rounded to f16) and tanh.  A block stages its 64 samples'
-// input rows (and the 6 before) in shared memory.
-__global__ void __launch_bounds__(kTailTile) tail_kernel(const float *x, int T, const float *alpha, const float *w,
-                                                         float bias, int C, int K, float *out) {
-    extern __shared__ float tile[];  // [(kTailTile + K - 1)][C]
-    const int t0 = blockIdx.x * kTailTile, rows = kTailTile + K - 1;
-    for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
-        const int r = i / C, c = i % C, src = t0 + r - (K - 1);
-        float v = 0.f;
-        if (src >= 0 && src < T) v = snake(x[(size_t)src * C + c], alpha[c]);
-        tile[i] = __half2float(__float2half_rn(v));
+// Decoder tail (codec.rs:1978-1998) after the last residual unit: v = x + Z +
+// zb (that unit's output), snake, the causal convolution 96 -> 1 (kernel 7,
+// input rounded to f16) and tanh.  A block of 128 threads stages its 128
+// samples' input rows (and the 6 before) in shared memory as f16 (the
+// rounding the reference applies), rows padded to an odd number of words so
+// that a warp's threads read different banks, and the weights as floats.
+constexpr int kTailC = 96, kTailK = 7, kTailLd = kTailC + 2;  // halves per staged row
+__global__ void __launch_bounds__(kTailTile) tail_kernel(const float *x, const float *Z, const float *zb, int T,
+                                                         const float *alpha, const float *w, float bias, float *out) {
+    __shared__ __half tile[(kTailTile + kTailK - 1) * kTailLd];
+    __shared__ float ws[kTailK * kTailC];
+    const int t0 = blockIdx.x * kTailTile;
+    for (int i = threadIdx.x; i < kTailK * kTailC; i += kTailTile) ws[i] = w[i];
+    constexpr int C4 = kTailC / 4, rows = kTailTile + kTailK - 1;
+    for (int i = threadIdx.x; i < rows * C4; i += kTailTile) {
+        const int r = i / C4, c = (i - r * C4) * 4, src = t0 + r - (kTailK - 1);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (src >= 0 && src < T) {
+            const size_t o = (size_t)src * kTailC + c;
+            const float4 a = ld4(x + o), z = ld4(Z + o), b = ld4(zb + c), al = ld4(alpha + c);
+            v = make_float4(snake(a.x + z.x + b.x, al.x), snake(a.y + z.y + b.y, al.y), snake(a.z + z.z + b.z, al.z),
+                            snake(a.w + z.w + b.w, al.w));
+        }
+        __half2 *dst = reinterpret_cast<__half2 *>(tile + r * kTailLd + c);
+        dst[0] = __floats2half2_rn(v.x, v.y);
+        dst[1] = __floats2half2_rn(v.z, v.w);
     }
     __syncthreads();
     const int t = t0 + threadIdx.x;
     if (t >= T) return;
     float acc = bias;
-    for (int k = 0; k < K; ++k) {
-        const float *row = tile + (threadIdx.x + k) * C;
-        for (int c = 0; c < C; ++c) acc += row[c] * w[k * C + c];
+    for (int k = 0; k < kTailK; ++k) {
+        const __half2 *row = reinterpret_cast<const __half2 *>(tile + (threadIdx.x + k) * kTailLd);
+        const float *wk = ws + k * kTailC;
+#pragma unroll 8
+        for (int c = 0; c < kTailC / 2; ++c) {
+            const float2 v = __half22float2(row[c]);
+            acc += v.x * wk[2 * c] + v.y * wk[2 * c + 1];
+        }
     }
     out[t] = tanhf(acc);
 }
@@ -754,13 +873,9 @@ int32_t upsample_stage(S2dCodec *c, const CodecUpStage &u, const float *x, int T
     return epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T2, kHid, u.pw2b, kHid, u.gamma, y, y);
 }
 
-// A stride-1 causal convolution (codec.rs:2212) of x [T][C] (+ bias, snake
-// first when alpha is set) into Z [T][N]: pad + round, im2col, one GEMM.
-int32_t causal_conv(S2dCodec *c, const float *x, int T, int C, const float *bias, const float *alpha,
-                    const __half *W, int K, int d, int N, float *Z) {
-    const int pad = (K - 1) * d;
-    pad_f16_kernel<<<grid_for((size_t)(T + pad) * C), 256, 0, c->stream>>>(x, T, C, pad, bias, alpha, c->P);
-    CCK(cudaGetLastError());
+// The GEMM of a stride-1 causal convolution (codec.rs:2212) whose padded f16
+// input P ([(K - 1) d + T][C]) is in place: im2col for K > 1, then Z [T][N].
+int32_t conv_gemm(S2dCodec *c, int T, int C, const __half *W, int K, int d, int N, float *Z) {
     const __half *A = c->P;
     if (K > 1) {
         im2col_kernel<<<grid_for((size_t)T * K * C / 8), 256, 0, c->stream>>>(c->P, T, C, K, d, c->A);
@@ -770,38 +885,73 @@ int32_t causal_conv(S2dCodec *c, const float *x, int T, int C, const float *bias
     return gemm(c, A, W, T, N, K * C, Z);
 }
 
+// P = the padded f16 input of a convolution: f16(snake(x + bias)).
+int32_t pad_input(S2dCodec *c, const float *x, int T, int C, int pad, const float *bias, const float *alpha) {
+    pad_f16_kernel<<<grid_for((size_t)(T + pad) * C / 4), 256, 0, c->stream>>>(x, T, C, pad, bias, alpha, c->P);
+    CCK(cudaGetLastError());
+    return S2D_OK;
+}
+
+// xs / inv = the split of snake(x (+ Z + zb) (+ bias)), rows of C channels.
+int32_t snake_split(S2dCodec *c, const float *x, const float *Z, const float *zb, const float *bias,
+                    const float *alpha, int T, int C) {
+    const unsigned g = (unsigned)((T + 7) / 8);
+    switch (C) {
+    case 1536: snake_split_kernel<24><<<g, 256, 0, c->stream>>>(x, Z, zb, bias, alpha, T, c->xs, c->inv); break;
+    case 768: snake_split_kernel<12><<<g, 256, 0, c->stream>>>(x, Z, zb, bias, alpha, T, c->xs, c->inv); break;
+    case 384: snake_split_kernel<6><<<g, 256, 0, c->stream>>>(x, Z, zb, bias, alpha, T, c->xs, c->inv); break;
+    case 192: snake_split_kernel<3><<<g, 256, 0, c->stream>>>(x, Z, zb, bias, alpha, T, c->xs, c->inv); break;
+    default: return cerr(c, S2D_EINVAL, "snake_split: unsupported channel count " + std::to_string(C));
+    }
+    CCK(cudaGetLastError());
+    return S2D_OK;
+}
+
 // forward_codec_decoder (codec.rs:1941): hidden [L][1024] -> samples [512 L].
+// Elementwise steps ride on the kernels around the GEMMs: the entry conv's
+// bias and each block's snake go into the split of the transposed conv's
+// input, the transposed conv's col2im writes the first unit's conv input,
+// a unit's conv0 bias and snake1 go into conv1's input, and each residual add
+// writes the next unit's conv input (or the next block's split, or the tail).
 int32_t decoder(S2dCodec *c, const float *hidden, int L, float *samples) {
     int32_t rc;
-    // entry conv 1024 -> 1536; its bias is added by the first block's snake
-    if ((rc = causal_conv(c, hidden, L, kHid, nullptr, nullptr, c->entry_w, 7, 1, kEntry, c->Z))) return rc;
-    const float *in = c->Z, *in_bias = c->entry_b;
-    int rows = L, cin = kEntry;
+    // entry conv 1024 -> 1536 (kernel 7), bias left for the split below
+    if ((rc = pad_input(c, hidden, L, kHid, 6, nullptr, nullptr))) return rc;
+    if ((rc = conv_gemm(c, L, kHid, c->entry_w, 7, 1, kEntry, c->Z))) return rc;
+    if ((rc = snake_split(c, c->Z, nullptr, nullptr, c->entry_b, c->block[0].alpha, L, kEntry))) return rc;
+    int rows = L;
     float *x = c->x;
     for (int b = 0; b < kBlocks; ++b) {
         const CodecBlock &k = c->block[b];
-        const int C = kChan[b], s = kRates[b], out = rows * s;
-        // snake, then the transposed conv over every tap and col2im
-        snake_kernel<<<grid_for((size_t)rows * cin), 256, 0, c->stream>>>(in, rows, cin, in_bias, k.alpha, c->x2);
-        CCK(cudaGetLastError());
-        if ((rc = split_gemm(c, c->x2, rows, cin, nullptr, k.wt, k.kernel * C, c->Y2))) return rc;
-        col2im_kernel<<<grid_for((size_t)out * C), 256, 0, c->stream>>>(c->Y2, c->inv, rows, k.kernel, s, C, k.bt, x);
+        const int cin = b == 0 ? kEntry : kChan[b - 1], C = kChan[b], s = kRates[b], out = rows * s;
+        // the transposed conv over every tap, col2im + bias -> x, unit 0's conv input -> P
+        if ((rc = gemm(c, c->xs, k.wt, 2 * rows, k.kernel * C, cin, c->Y2))) return rc;
+        col2im_pad_kernel<<<grid_for(((size_t)out + (k.unit[0].k0 - 1)) * C / 4), 256, 0, c->stream>>>(
+            c->Y2, c->inv, rows, k.kernel, s, C, k.bt, x, k.unit[0].a0, k.unit[0].k0 - 1, c->P);
         CCK(cudaGetLastError());
         // residual units, dilations 1, 3, 9 (codec.rs:2040-2042)
         for (int u = 0; u < 3; ++u) {
             const CodecUnit &n = k.unit[u];
             const int d = u == 0 ? 1 : u == 1 ? 3 : 9;
-            if ((rc = causal_conv(c, x, out, C, nullptr, n.a0, n.w0, n.k0, d, C, c->Z))) return rc;
-            if ((rc = causal_conv(c, c->Z, out, C, n.b0, n.a1, n.w1, n.k1, 1, C, c->x2))) return rc;
-            resid_kernel<<<grid_for((size_t)out * C), 256, 0, c->stream>>>(x, c->x2, out, C, n.b1);
-            CCK(cudaGetLastError());
+            if ((rc = conv_gemm(c, out, C, n.w0, n.k0, d, C, c->Z))) return rc;
+            if ((rc = pad_input(c, c->Z, out, C, n.k1 - 1, n.b0, n.a1))) return rc;
+            if ((rc = conv_gemm(c, out, C, n.w1, n.k1, 1, C, c->x2))) return rc;
+            if (u < 2) {
+                const CodecUnit &nx = k.unit[u + 1];
+                const int pad = (nx.k0 - 1) * (u == 0 ? 3 : 9);
+                resid_pad_kernel<<<grid_for(((size_t)out + pad) * C / 4), 256, 0, c->stream>>>(x, c->x2, n.b1, out, C,
+                                                                                              nx.a0, pad, c->P);
+                CCK(cudaGetLastError());
+            } else if (b + 1 < kBlocks) {
+                if ((rc = snake_split(c, x, c->x2, n.b1, nullptr, c->block[b + 1].alpha, out, C))) return rc;
+            } else {
+                tail_kernel<<<(out + kTailTile - 1) / kTailTile, kTailTile, 0, c->stream>>>(
+                    x, c->x2, n.b1, out, c->tail_alpha, c->out_w, c->out_b, samples);
+                CCK(cudaGetLastError());
+            }
         }
-        in = x, in_bias = nullptr, rows = out, cin = C;
+        rows = out;
     }
-    const size_t smem = (size_t)(kTailTile + 6) * 96 * sizeof(float);
-    tail_kernel<<<(rows + kTailTile - 1) / kTailTile, kTailTile, smem, c->stream>>>(x, rows, c->tail_alpha, c->out_w,
-                                                                                     c->out_b, 96, 7, samples);
-    CCK(cudaGetLastError());
     return S2D_OK;
 }
 

@@ -45,7 +45,8 @@ int32_t s2d_codec_decode_waveform(S2dCodec *c, const int32_t *codes, uint32_t nu
                                   float *samples, size_t capacity, size_t *num_samples, uint32_t *latent_frames);
 
 /* The same decode on device buffers, on `stream` (a cudaStream_t; NULL: the
- * codec's own stream), without host copies or a synchronize: codes_dev
+ * codec's own stream, which does not wait for work on other streams,
+ * including the legacy default stream), without host copies or a synchronize: codes_dev
  * [num_codebooks][n_frames] int32, samples_dev 2048 * n_frames floats.  Codes
  * are checked on the device: an out-of-range code sets the codec's error flag,
  * which the next s2d_codec_sync reports as S2D_EDEVICE. */

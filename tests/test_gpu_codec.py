@@ -120,7 +120,8 @@ def test_decode_is_deterministic_and_the_device_entry_agrees(codec):
     from fish_s2pro_b200.codec import codec_lib
     cd = torch.from_numpy(codes).cuda()
     out = torch.empty(6 * 2048, dtype=torch.float32, device="cuda")
-    s = torch.cuda.current_stream()
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
     assert codec_lib().s2d_codec_decode_waveform_device(codec.handle, cd.data_ptr(), 10, 6, out.data_ptr(),
                                                         s.cuda_stream) == 0
     s.synchronize()
@@ -163,6 +164,7 @@ def test_errors_match_the_reference(codec):
     bad = torch.from_numpy(codes.copy()).cuda()
     bad[3] = 5000
     out = torch.empty(2 * 2048, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()  # the codec's own stream does not wait for torch's
     assert codec_lib().s2d_codec_decode_waveform_device(codec.handle, bad.data_ptr(), 10, 2, out.data_ptr(),
                                                         None) == 0
     assert codec_lib().s2d_codec_sync(codec.handle) == -6
