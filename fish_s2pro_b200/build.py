@@ -21,9 +21,10 @@ LIB = PKG / "libs2d.so"
 SYNTH_LIB = PKG / "libs2d_synth.so"
 
 CUDA_SOURCES = ["s2d_kernels.cu", "s2d_engine.cu", "s2d_prefill.cu", "s2d_decode_attn.cu", "s2d_tcgemm.cu", "s2d_runtime.cu",
-                "s2d_gguf.cpp", "s2d_noalloc.cu", "s2d_tc_attn.cu", "s2d_codec.cu"]
+                "s2d_gguf.cpp", "s2d_noalloc.cu", "s2d_tc_attn.cu", "s2d_codec.cu",
+                "s2d_codec_conv.cu"]
 CUDA_HEADERS = ["s2d_common.cuh", "s2d_kernels.cuh", "s2d_sample.cuh", "s2d_prefill.cuh", "s2d_tcgemm.cuh", "s2d_tc_common.cuh",
-                "s2d_gguf.h"]
+                "s2d_gguf.h", "s2d_codec.cuh"]
 CUDA_LIB = "/usr/local/cuda/lib64"
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

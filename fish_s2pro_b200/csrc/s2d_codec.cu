@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -26,6 +27,7 @@
 
 #include "../../include/s2d.h"
 #include "../../include/s2d_codec.h"
+#include "s2d_codec.cuh"
 #include "s2d_gguf.h"
 #include "s2d_prefill.cuh"
 
@@ -345,18 +347,19 @@ __global__ void __launch_bounds__(256) snake_split_kernel(const float *x, const 
     }
 }
 
-// im2col of a stride-1 causal convolution: A[t][k C + c] = P[t + k d][c] for
-// the taps k < K, 16 bytes at a time (C * 2 is a multiple of 16).
-__global__ void im2col_kernel(const __half *P, int T, int C, int K, int d, __half *A) {
-    const int cv = C / 8, row = K * cv;  // uint4 per row of P / of A
+// im2col of a stride-1 causal convolution: A[t][k Cp + c] = P[t + k d][c] for
+// the taps k < K and c < C, zeros for C <= c < Cp; 16 bytes at a time (C and
+// Cp multiples of 8).
+__global__ void im2col_kernel(const __half *P, int T, int C, int Cp, int K, int d, __half *A) {
+    const int cv = C / 8, cvp = Cp / 8, row = K * cvp;  // uint4 per row of P / per tap of A / per row of A
     const long long total = (long long)T * row;
     const uint4 *src = reinterpret_cast<const uint4 *>(P);
     uint4 *dst = reinterpret_cast<uint4 *>(A);
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         const long long t = i / row;
-        const int r = (int)(i - t * row), k = r / cv, j = r - k * cv;
-        dst[i] = src[(t + (long long)k * d) * cv + j];
+        const int r = (int)(i - t * row), k = r / cvp, j = r - k * cvp;
+        dst[i] = j < cv ? src[(t + (long long)k * d) * cv + j] : make_uint4(0u, 0u, 0u, 0u);
     }
 }
 
@@ -396,8 +399,8 @@ __global__ void col2im_pad_kernel(const float *Y2, const float *inv, int T, int 
     }
 }
 
-// Decoder tail (codec.rs:1978-1998) after the last residual unit: v = x + Z +
-// zb (that unit's output), snake, the causal convolution 96 -> 1 (kernel 7,
+// Decoder tail (codec.rs:1978-1998) after the last residual unit: v = x (+ Z
+// + zb when the unit's residual add is still pending), snake, the causal convolution 96 -> 1 (kernel 7,
 // input rounded to f16) and tanh.  A block of 128 threads stages its 128
 // samples' input rows (and the 6 before) in shared memory as f16 (the
 // rounding the reference applies), rows padded to an odd number of words so
@@ -415,7 +418,9 @@ __global__ void __launch_bounds__(kTailTile) tail_kernel(const float *x, const f
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (src >= 0 && src < T) {
             const size_t o = (size_t)src * kTailC + c;
-            const float4 a = ld4(x + o), z = ld4(Z + o), b = ld4(zb + c), al = ld4(alpha + c);
+            const float4 a = ld4(x + o), al = ld4(alpha + c);
+            const float4 z = Z ? ld4(Z + o) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 b = Z ? ld4(zb + c) : make_float4(0.f, 0.f, 0.f, 0.f);
             v = make_float4(snake(a.x + z.x + b.x, al.x), snake(a.y + z.y + b.y, al.y), snake(a.z + z.z + b.z, al.z),
                             snake(a.w + z.w + b.w, al.w));
         }
@@ -518,8 +523,10 @@ struct S2dCodec {
     float *lat = nullptr, *x = nullptr, *x2 = nullptr, *qkv = nullptr, *att = nullptr, *act = nullptr;
     float *Y2 = nullptr, *Y2b = nullptr, *inv = nullptr, *Z = nullptr;
     __half *xs = nullptr, *P = nullptr, *A = nullptr;
-    int32_t *codes = nullptr, *error = nullptr;
+    int32_t *codes = nullptr, *error = nullptr;  // error[0]: a code out of range; [1]: a tcgen05 wait gave up
     float *samples = nullptr;
+    bool conv_tc = true;  // causal convolutions on the implicit-GEMM tcgen05 kernel (S2D_CODEC_TC)
+    bool conv_one_cta = false;  // ... one CTA per SM with a deeper ring (S2D_CODEC_CONV_CTAS=1)
 };
 
 namespace s2d {
@@ -594,16 +601,18 @@ struct Loader {
         fixes.push_back({off, reinterpret_cast<const void **>(dst)});
     }
     // causal conv weight ggml [k, in, out] (index tap + k (ic + in oc)) as
-    // [out][k in] with column tap * in + ic
+    // [out][k inp] with column tap * inp + ic, inp = in rounded up to 64 and
+    // zeros in the columns past in
     void conv(const GgufTensor *t, int k, int in, int out, const __half **dst) {
         if (!t) return;
-        const size_t off = alloc((size_t)k * in * out * 2);
+        const int inp = (in + 63) / 64 * 64;
+        const size_t off = alloc((size_t)k * inp * out * 2);
         uint16_t *o = reinterpret_cast<uint16_t *>(host.data() + off);
         const uint16_t *s = src(t);
         for (int oc = 0; oc < out; ++oc)
             for (int ic = 0; ic < in; ++ic)
                 for (int tap = 0; tap < k; ++tap)
-                    o[(size_t)oc * k * in + (size_t)tap * in + ic] = s[tap + (size_t)k * (ic + (size_t)in * oc)];
+                    o[(size_t)oc * k * inp + (size_t)tap * inp + ic] = s[tap + (size_t)k * (ic + (size_t)in * oc)];
         fixes.push_back({off, reinterpret_cast<const void **>(dst)});
     }
     // transposed conv weight ggml [k, out, in] (index tap + k (oc + out ic))
@@ -756,11 +765,12 @@ int32_t ensure_ws(S2dCodec *c, uint32_t frames) {
             const int d = u == 0 ? 1 : u == 1 ? 3 : 9;
             const size_t k0 = c->block[b].unit[u].k0, k1 = c->block[b].unit[u].k1;
             pf = std::max(pf, (out + (k0 - 1) * d + k1) * C);
-            af = std::max(af, out * std::max(k0, k1) * C);
+            af = std::max(af, out * std::max(k0, k1) * ((C + 63) / 64 * 64));
         }
         zf = std::max(zf, out * C);
         rows = out, cin = C;
     }
+    if (c->conv_tc) af = 8;  // the implicit-GEMM convolutions need no im2col rows
     const size_t samples = rows;
     struct Part {
         void **p;
@@ -781,7 +791,7 @@ int32_t ensure_ws(S2dCodec *c, uint32_t frames) {
         {(void **)&c->A, af * 2},
         {(void **)&c->codes, T * kBooks * 4},
         {(void **)&c->samples, samples * 4},
-        {(void **)&c->error, 4},
+        {(void **)&c->error, 8},
     };
     size_t total = 0;
     for (auto &p : parts) total += (p.bytes + 255) & ~(size_t)255;
@@ -793,7 +803,7 @@ int32_t ensure_ws(S2dCodec *c, uint32_t frames) {
         *p.p = c->ws + off;
         off += (p.bytes + 255) & ~(size_t)255;
     }
-    CCK(cudaMemset(c->error, 0, 4));
+    CCK(cudaMemset(c->error, 0, 8));
     c->ws_frames = frames, c->ws_bytes = total;
     return S2D_OK;
 }
@@ -874,15 +884,24 @@ int32_t upsample_stage(S2dCodec *c, const CodecUpStage &u, const float *x, int T
 }
 
 // The GEMM of a stride-1 causal convolution (codec.rs:2212) whose padded f16
-// input P ([(K - 1) d + T][C]) is in place: im2col for K > 1, then Z [T][N].
+// input P ([(K - 1) d + T][C]) is in place, into Z [T][N]: the implicit-GEMM
+// tcgen05 kernel, or (S2D_CODEC_TC=0) im2col + cuBLAS.  W is [N][K Cp].
 int32_t conv_gemm(S2dCodec *c, int T, int C, const __half *W, int K, int d, int N, float *Z) {
+    const int Cp = (C + 63) / 64 * 64;
+    if (c->conv_tc) {
+        CodecConv cv;
+        cv.P = c->P, cv.W = W, cv.T = T, cv.C = C, cv.N = N, cv.taps = K, cv.d = d, cv.cpb = Cp / 64, cv.Z = Z;
+        cv.error = c->error + 1, cv.one_cta = c->conv_one_cta;
+        CCK(launch_codec_conv(cv, c->stream));
+        return S2D_OK;
+    }
     const __half *A = c->P;
-    if (K > 1) {
-        im2col_kernel<<<grid_for((size_t)T * K * C / 8), 256, 0, c->stream>>>(c->P, T, C, K, d, c->A);
+    if (K > 1 || Cp != C) {
+        im2col_kernel<<<grid_for((size_t)T * K * Cp / 8), 256, 0, c->stream>>>(c->P, T, C, Cp, K, d, c->A);
         CCK(cudaGetLastError());
         A = c->A;
     }
-    return gemm(c, A, W, T, N, K * C, Z);
+    return gemm(c, A, W, T, N, K * Cp, Z);
 }
 
 // P = the padded f16 input of a convolution: f16(snake(x + bias)).
@@ -984,11 +1003,12 @@ int32_t check_codes(S2dCodec *c, const int32_t *codes, uint32_t ncb, uint32_t n)
 
 int32_t sync_and_check(S2dCodec *c) {
     CCK(cudaStreamSynchronize(c->stream));
-    int32_t flag = 0;
-    CCK(cudaMemcpy(&flag, c->error, 4, cudaMemcpyDeviceToHost));
-    if (flag) {
-        CCK(cudaMemset(c->error, 0, 4));
-        return cerr(c, S2D_EDEVICE, "a codec code was out of range for its codebook");
+    int32_t flag[2] = {0, 0};
+    CCK(cudaMemcpy(flag, c->error, 8, cudaMemcpyDeviceToHost));
+    if (flag[0] || flag[1]) {
+        CCK(cudaMemset(c->error, 0, 8));
+        return cerr(c, S2D_EDEVICE, flag[0] ? "a codec code was out of range for its codebook"
+                                            : "a tensor-core convolution's bounded wait gave up");
     }
     return S2D_OK;
 }
@@ -1021,6 +1041,8 @@ int32_t s2d_codec_open(const char *gguf_path, int32_t device, S2dCodec **out) {
                cublasSetStream(c->blas, c->stream) != CUBLAS_STATUS_SUCCESS) {
         rc = cerr(c, S2D_ECUDA, "cublasCreate failed");
     } else {
+        if (const char *v = getenv("S2D_CODEC_TC")) c->conv_tc = v[0] != '0';
+        if (const char *v = getenv("S2D_CODEC_CONV_CTAS")) c->conv_one_cta = v[0] == '1';
         rc = load(c, g);
     }
     *out = c;  // also on failure, so that the caller can read the message

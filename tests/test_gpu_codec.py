@@ -79,7 +79,7 @@ def test_decode_latents_matches_oracle(codec, codec_oracle_weights, n):
     assert rel_err(got.hidden.reshape(4 * n, 1024), want) < LAT_TOL
 
 
-@pytest.mark.parametrize("L", [1, 4, 9])
+@pytest.mark.parametrize("L", [1, 4, 9, 33])
 def test_decoder_matches_oracle(codec, codec_oracle_weights, L):
     rng = np.random.default_rng(L)
     hidden = rng.standard_normal((L, 1024)).astype(np.float32)
@@ -87,6 +87,18 @@ def test_decoder_matches_oracle(codec, codec_oracle_weights, L):
     assert got.shape == (512 * L,)
     want = co.forward_codec_decoder(hidden.astype(np.float64), codec_oracle_weights)
     assert rel_err(got, want) < PCM_TOL
+
+
+def test_im2col_cublas_route_matches_oracle(codec_gguf, codec_oracle_weights, monkeypatch):
+    """S2D_CODEC_TC=0: the causal convolutions as im2col + cuBLAS instead of
+    the implicit-GEMM tcgen05 kernel, against the same oracle."""
+    from fish_s2pro_b200 import CodecDecoder
+    monkeypatch.setenv("S2D_CODEC_TC", "0")
+    with CodecDecoder.open(codec_gguf) as c:
+        rng = np.random.default_rng(4)
+        hidden = rng.standard_normal((4, 1024)).astype(np.float32)
+        want = co.forward_codec_decoder(hidden.astype(np.float64), codec_oracle_weights)
+        assert rel_err(c.forward_codec_decoder(hidden, 4), want) < PCM_TOL
 
 
 @pytest.mark.parametrize("L", [1, 4])
