@@ -36,4 +36,4 @@ from .s2d import (  # noqa: F401
     transpose_to_time_major,
 )
 from .serve import ServeSession, TtsScheduler  # noqa: F401,E402
-from .codec import CodecDecoder, CodecWaveformResult, pcm_to_wav  # noqa: F401,E402
+from .codec import Codec, CodecDecoder, CodecWaveformResult, pcm_to_wav, read_wav_mono_f32  # noqa: F401,E402

@@ -1,5 +1,6 @@
-"""Seeded synthetic codec GGUF files: the decode tensors of the s2-pro codec
-(fish-speech-codec architecture) with random weights of the real shapes.
+"""Seeded synthetic codec GGUF files: the s2-pro codec's decode and
+reference-audio encode tensors (fish-speech-codec architecture) with random
+weights of the real shapes.
 
 There is no network for the real checkpoint, so tests and the bench decode
 codes through a file of the same layout: tensor names and ggml dims as the
@@ -23,6 +24,36 @@ LAYERS, UPSAMPLE_STAGES = 8, 2
 ENTRY = 1536
 RATES = (8, 8, 4, 2)
 CHANNELS = (768, 384, 192, 96)
+ENC_RATES = (2, 4, 8, 8)
+ENC_CHANNELS = (64, 128, 256, 512, 1024)
+
+
+def _layers(add, module, n):
+    """The transformer layers of a codec module (codec.rs:315-333)."""
+    for layer in range(n):
+        p = f"{module}.layers.{layer}"
+        add(f"{p}.attention.wqkv.weight", [HIDDEN, 3 * HIDDEN], HIDDEN ** -0.5)
+        add(f"{p}.attention.wo.weight", [HIDDEN, HIDDEN], HIDDEN ** -0.5)
+        add(f"{p}.attention_norm.weight", [HIDDEN], 0.1, 1.0)
+        add(f"{p}.ffn_norm.weight", [HIDDEN], 0.1, 1.0)
+        add(f"{p}.feed_forward.w1.weight", [HIDDEN, FFN], HIDDEN ** -0.5)
+        add(f"{p}.feed_forward.w3.weight", [HIDDEN, FFN], HIDDEN ** -0.5)
+        add(f"{p}.feed_forward.w2.weight", [FFN, HIDDEN], FFN ** -0.5)
+        add(f"{p}.attention_layer_scale.gamma", [HIDDEN], 0.02, 0.1)
+        add(f"{p}.ffn_layer_scale.gamma", [HIDDEN], 0.02, 0.1)
+
+
+def _convnext(add, p):
+    """The ConvNeXt block of an upsample or downsample stage (codec.rs:429-447)."""
+    add(f"{p}.1.gamma", [HIDDEN], 0.02, 0.1)
+    add(f"{p}.1.dwconv.conv.weight", [7, 1, HIDDEN], 7 ** -0.5)
+    add(f"{p}.1.dwconv.conv.bias", [HIDDEN], 0.02)
+    add(f"{p}.1.norm.weight", [HIDDEN], 0.1, 1.0)
+    add(f"{p}.1.norm.bias", [HIDDEN], 0.02)
+    add(f"{p}.1.pwconv1.weight", [HIDDEN, EXPANDED], HIDDEN ** -0.5)
+    add(f"{p}.1.pwconv1.bias", [EXPANDED], 0.02)
+    add(f"{p}.1.pwconv2.weight", [EXPANDED, HIDDEN], EXPANDED ** -0.5)
+    add(f"{p}.1.pwconv2.bias", [HIDDEN], 0.02)
 
 
 def _tensors():
@@ -40,31 +71,44 @@ def _tensors():
         add(f"{p}.out_proj.weight", [1, PROJ, HIDDEN], PROJ ** -0.5)
         add(f"{p}.out_proj.bias", [HIDDEN], 0.02)
         add(f"{p}.codebook.weight", [PROJ, n], 1.0)
-    for layer in range(LAYERS):
-        p = f"quantizer.post_module.layers.{layer}"
-        add(f"{p}.attention.wqkv.weight", [HIDDEN, 3 * HIDDEN], HIDDEN ** -0.5)
-        add(f"{p}.attention.wo.weight", [HIDDEN, HIDDEN], HIDDEN ** -0.5)
-        add(f"{p}.attention_norm.weight", [HIDDEN], 0.1, 1.0)
-        add(f"{p}.ffn_norm.weight", [HIDDEN], 0.1, 1.0)
-        add(f"{p}.feed_forward.w1.weight", [HIDDEN, FFN], HIDDEN ** -0.5)
-        add(f"{p}.feed_forward.w3.weight", [HIDDEN, FFN], HIDDEN ** -0.5)
-        add(f"{p}.feed_forward.w2.weight", [FFN, HIDDEN], FFN ** -0.5)
-        add(f"{p}.attention_layer_scale.gamma", [HIDDEN], 0.02, 0.1)
-        add(f"{p}.ffn_layer_scale.gamma", [HIDDEN], 0.02, 0.1)
+    _layers(add, "quantizer.post_module", LAYERS)
     add("quantizer.post_module.norm.weight", [HIDDEN], 0.1, 1.0)
     for i in range(UPSAMPLE_STAGES):
         p = f"quantizer.upsample.{i}"
         add(f"{p}.0.conv.weight", [2, HIDDEN, HIDDEN], HIDDEN ** -0.5)
         add(f"{p}.0.conv.bias", [HIDDEN], 0.02)
-        add(f"{p}.1.gamma", [HIDDEN], 0.02, 0.1)
-        add(f"{p}.1.dwconv.conv.weight", [7, 1, HIDDEN], 7 ** -0.5)
-        add(f"{p}.1.dwconv.conv.bias", [HIDDEN], 0.02)
-        add(f"{p}.1.norm.weight", [HIDDEN], 0.1, 1.0)
-        add(f"{p}.1.norm.bias", [HIDDEN], 0.02)
-        add(f"{p}.1.pwconv1.weight", [HIDDEN, EXPANDED], HIDDEN ** -0.5)
-        add(f"{p}.1.pwconv1.bias", [EXPANDED], 0.02)
-        add(f"{p}.1.pwconv2.weight", [EXPANDED, HIDDEN], EXPANDED ** -0.5)
-        add(f"{p}.1.pwconv2.bias", [HIDDEN], 0.02)
+        _convnext(add, p)
+    # the reference-audio encoder (codec.rs:1323-1390, 1473-1584)
+    add("encoder.block.0.conv.weight", [7, 1, 64], 7 ** -0.5)
+    add("encoder.block.0.conv.bias", [64], 0.02)
+    for i, (r, c) in enumerate(zip(ENC_RATES, ENC_CHANNELS[:-1]), start=1):
+        p = f"encoder.block.{i}.block"
+        co = ENC_CHANNELS[i]
+        for u in range(3):
+            q = f"{p}.{u}"
+            add(f"{q}.block.0.alpha", [1, c, 1], 0.1, 1.0)
+            add(f"{q}.block.1.conv.weight", [7, c, c], 0.7 * (7 * c) ** -0.5)
+            add(f"{q}.block.1.conv.bias", [c], 0.02)
+            add(f"{q}.block.2.alpha", [1, c, 1], 0.1, 1.0)
+            add(f"{q}.block.3.conv.weight", [1, c, c], 0.5 * c ** -0.5)
+            add(f"{q}.block.3.conv.bias", [c], 0.02)
+        add(f"{p}.3.alpha", [1, c, 1], 0.1, 1.0)
+        add(f"{p}.4.conv.weight", [2 * r, c, co], (2 * r * c) ** -0.5)
+        add(f"{p}.4.conv.bias", [co], 0.02)
+        if i == len(ENC_RATES):
+            _layers(add, f"{p}.5", 4)
+            add(f"{p}.5.norm.weight", [HIDDEN], 0.1, 1.0)
+    add("encoder.block.5.alpha", [1, HIDDEN, 1], 0.1, 1.0)
+    add("encoder.block.6.conv.weight", [3, HIDDEN, HIDDEN], (3 * HIDDEN) ** -0.5)
+    add("encoder.block.6.conv.bias", [HIDDEN], 0.02)
+    # the quantizer's encode side: downsample stages and pre module (codec.rs:357-391, 450-494)
+    for i in range(UPSAMPLE_STAGES):
+        p = f"quantizer.downsample.{i}"
+        add(f"{p}.0.conv.weight", [2, HIDDEN, HIDDEN], (2 * HIDDEN) ** -0.5)
+        add(f"{p}.0.conv.bias", [HIDDEN], 0.02)
+        _convnext(add, p)
+    _layers(add, "quantizer.pre_module", LAYERS)
+    add("quantizer.pre_module.norm.weight", [HIDDEN], 0.1, 1.0)
     add("decoder.model.0.conv.weight", [7, HIDDEN, ENTRY], (7 * HIDDEN) ** -0.5)
     add("decoder.model.0.conv.bias", [ENTRY], 0.02)
     c_in = ENTRY
@@ -94,7 +138,7 @@ def _gguf_string(s: str) -> bytes:
 
 
 def write_codec_gguf(path: str | os.PathLike, seed: int = 1234) -> Path:
-    """Write the synthetic codec file (about 370 MB) to `path`."""
+    """Write the synthetic codec file (about 770 MB) to `path`."""
     path = Path(path)
     specs = _tensors()
     rng = np.random.default_rng(seed)
@@ -130,7 +174,7 @@ def cached_codec_gguf(directory: str | os.PathLike | None = None, seed: int = 12
     from .synth import default_model_dir
     d = Path(directory) if directory else default_model_dir()
     d.mkdir(parents=True, exist_ok=True)
-    p = d / f"codec_synth_{seed}.gguf"
+    p = d / f"codec_synth_v2_{seed}.gguf"
     if not p.exists():
         write_codec_gguf(p, seed)
     return p

@@ -104,41 +104,54 @@ __global__ void qkv_rope_kernel(const float *Y2, const float *inv, int T, const 
     }
 }
 
-// Query row t of head h over keys max(0, t + 1 - 128) .. t
+// Query row t of head h over keys max(0, t + 1 - WIN) .. t
 // (codec.rs:3270-3297 with gqa_decode_attention, attention.rs:208, and
-// softmax_in_place, attention.rs:296): one block of 128 threads, a thread per
-// visible position for the scores, two half-blocks over positions for P V.
+// softmax_in_place, attention.rs:296; WIN 128 in the post and pre modules,
+// 512 in the encoder): one block of 128 threads, WIN / 128 visible positions
+// per thread for the scores, two half-blocks over positions for P V.
+template <int WIN>
 __global__ void __launch_bounds__(kWin) window_attn_kernel(const float *qkv, int T, float *out) {
+    constexpr int PER = WIN / kWin;
     const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-    __shared__ float q[kHd], p[kWin], red[kWin / 32], part[2][kHd];
+    __shared__ float q[kHd], p[WIN], red[kWin / 32], part[2][kHd];
     constexpr int N = 3 * kHid;
-    const int lo = max(0, t + 1 - kWin), n = t + 1 - lo;
+    const int lo = max(0, t + 1 - WIN), n = t + 1 - lo;
     if (tid < kHd) q[tid] = qkv[(size_t)t * N + h * kHd + tid];
     __syncthreads();
-    float s = -INFINITY;
-    if (tid < n) {
-        const float4 *k = reinterpret_cast<const float4 *>(qkv + (size_t)(lo + tid) * N + kHid + h * kHd);
-        float acc = 0.f;
+    float s[PER], m = -INFINITY;
 #pragma unroll
-        for (int d = 0; d < kHd / 4; ++d) {
-            const float4 kv = k[d];
-            acc += q[4 * d] * kv.x + q[4 * d + 1] * kv.y + q[4 * d + 2] * kv.z + q[4 * d + 3] * kv.w;
+    for (int e = 0; e < PER; ++e) {
+        const int j = tid + kWin * e;
+        s[e] = -INFINITY;
+        if (j < n) {
+            const float4 *k = reinterpret_cast<const float4 *>(qkv + (size_t)(lo + j) * N + kHid + h * kHd);
+            float acc = 0.f;
+#pragma unroll
+            for (int d = 0; d < kHd / 4; ++d) {
+                const float4 kv = k[d];
+                acc += q[4 * d] * kv.x + q[4 * d + 1] * kv.y + q[4 * d + 2] * kv.z + q[4 * d + 3] * kv.w;
+            }
+            s[e] = acc * 0.125f;  // 1 / sqrt(64)
         }
-        s = acc * 0.125f;  // 1 / sqrt(64)
+        m = fmaxf(m, s[e]);
     }
-    float m = s;
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((tid & 31) == 0) red[tid >> 5] = m;
     __syncthreads();
     m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     __syncthreads();
-    const float e = tid < n ? expf(s - m) : 0.f;
-    float sum = e;
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+        s[e] = tid + kWin * e < n ? expf(s[e] - m) : 0.f;
+        sum += s[e];
+    }
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if ((tid & 31) == 0) red[tid >> 5] = sum;
     __syncthreads();
     sum = red[0] + red[1] + red[2] + red[3];
-    p[tid] = e / sum;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) p[tid + kWin * e] = s[e] / sum;
     __syncthreads();
     const int d = tid & (kHd - 1), half = tid >> 6;
     float acc = 0.f;
@@ -270,11 +283,12 @@ __global__ void pad_f16_kernel(const float *x, int T, int C, int pad, const floa
 }
 
 // The last two steps of a residual unit and the first of the next
-// (codec.rs:2085-2160): x += Z + bias (the unit's output, written back), and
+// (codec.rs:2085-2160): x += Z + bias (the unit's output, written back; with
+// assign x = Z + bias, a strided conv's output starting the next block), and
 // the next unit's padded conv input P[pad + t] = f16(snake(x, alpha)),
 // P[0 .. pad) = 0.
 __global__ void resid_pad_kernel(float *x, const float *Z, const float *bias, int T, int C, const float *alpha,
-                                 int pad, __half *P) {
+                                 int pad, __half *P, bool assign) {
     const int C4 = C / 4;
     const long long total = (long long)(T + pad) * C4;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
@@ -284,13 +298,120 @@ __global__ void resid_pad_kernel(float *x, const float *Z, const float *bias, in
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         if (row >= pad) {
             float *xr = x + (row - pad) * C + c;
-            float4 v = ld4(xr);
-            const float4 z = ld4(Z + (row - pad) * C + c), b = ld4(bias + c), a = ld4(alpha + c);
+            float4 v = assign ? make_float4(0.f, 0.f, 0.f, 0.f) : ld4(xr);
+            const float4 z = ld4(Z + (row - pad) * C + c), b = ld4(bias + c);
             v.x += z.x + b.x, v.y += z.y + b.y, v.z += z.z + b.z, v.w += z.w + b.w;
             *reinterpret_cast<float4 *>(xr) = v;
-            s = make_float4(snake(v.x, a.x), snake(v.y, a.y), snake(v.z, a.z), snake(v.w, a.w));
+            if (P) {
+                const float4 a = ld4(alpha + c);
+                s = make_float4(snake(v.x, a.x), snake(v.y, a.y), snake(v.z, a.z), snake(v.w, a.w));
+            }
         }
-        st_half4(P + row * C + c, s.x, s.y, s.z, s.w);
+        if (P) st_half4(P + row * C + c, s.x, s.y, s.z, s.w);
+    }
+}
+
+// The encoder's entry conv (codec.rs:1112-1124): 1 -> 64 channels, kernel 7,
+// causal, input rounded to f16: y[t][c] = b[c] + sum_k f16(x[t + k - 6]) w[c][k].
+__global__ void enc_entry_kernel(const float *x, int T, const float *w, const float *b, float *y) {
+    const long long total = (long long)T * 64;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long t = i >> 6;
+        const int c = (int)(i & 63);
+        float acc = b[c];
+#pragma unroll
+        for (int k = 0; k < 7; ++k) {
+            const long long src = t + k - 6;
+            if (src >= 0) acc += __half2float(__float2half_rn(x[src])) * w[c * 7 + k];
+        }
+        y[i] = acc;
+    }
+}
+
+struct VqArgs {
+    const __half *in_w[kBooks];  // [8][1024]
+    const __half *in_b[kBooks];  // [8]
+};
+
+// rvq_encode_latents_nearest (codec.rs:2598) with nearest_code_for_residual
+// (codec.rs:2453-2505): one block per frame; per codebook in order, the
+// residual's in_proj (+ bias), the codebook row of the largest cosine
+// similarity (the first on ties), then residual -= that code's out_proj
+// projection (+ bias, summed as rvq_kernel sums it).  codes [10][T],
+// l2[t] = the final residual's norm.
+constexpr int kVqThreads = 256;
+__global__ void __launch_bounds__(kVqThreads) vq_kernel(VqArgs v, RvqArgs a, const float *lat, int T,
+                                                        int32_t *codes, float *l2) {
+    __shared__ float r[kHid], proj[kProj], bs[kVqThreads / 32];
+    __shared__ int bi[kVqThreads / 32];
+    __shared__ float red[kVqThreads / 32];
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < kHid; i += kVqThreads) r[i] = lat[(size_t)t * kHid + i];
+    __syncthreads();
+    for (int cb = 0; cb < kBooks; ++cb) {
+        // in_proj: warp j < 8 takes output j
+        if (warp < kProj) {
+            const __half *wr = v.in_w[cb] + (size_t)warp * kHid;
+            float acc = 0.f;
+            for (int i = lane; i < kHid; i += 32) acc += r[i] * __half2float(wr[i]);
+            for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) proj[warp] = acc + __half2float(v.in_b[cb][warp]);
+        }
+        __syncthreads();
+        float pn = 0.f;
+#pragma unroll
+        for (int j = 0; j < kProj; ++j) pn += proj[j] * proj[j];
+        pn = sqrtf(fmaxf(pn, 1e-12f));
+        float pu[kProj];
+#pragma unroll
+        for (int j = 0; j < kProj; ++j) pu[j] = proj[j] / pn;
+        // the best row of this thread's rows, then of the block (first index on ties)
+        float best = -INFINITY;
+        int besti = 0x7fffffff;
+        for (int k = tid; k < a.size[cb]; k += kVqThreads) {
+            const __half *row = a.book[cb] + (size_t)k * kProj;
+            float cr[kProj], cn = 0.f;
+#pragma unroll
+            for (int j = 0; j < kProj; ++j) cr[j] = __half2float(row[j]), cn += cr[j] * cr[j];
+            cn = sqrtf(fmaxf(cn, 1e-12f));
+            float sc = 0.f;
+#pragma unroll
+            for (int j = 0; j < kProj; ++j) sc += pu[j] * (cr[j] / cn);
+            if (sc > best) best = sc, besti = k;
+        }
+        for (int o = 16; o; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+            if (ob > best || (ob == best && oi < besti)) best = ob, besti = oi;
+        }
+        if (lane == 0) bs[warp] = best, bi[warp] = besti;
+        __syncthreads();
+        best = bs[0], besti = bi[0];
+        for (int w = 1; w < kVqThreads / 32; ++w)
+            if (bs[w] > best || (bs[w] == best && bi[w] < besti)) best = bs[w], besti = bi[w];
+        if (tid == 0) codes[(size_t)cb * T + t] = besti;
+        // residual -= the code's projection
+        const __half *code = a.book[cb] + (size_t)besti * kProj;
+        for (int c = tid; c < kHid; c += kVqThreads) {
+            const __half *w = a.oproj[cb] + (size_t)c * kProj;
+            float p = 0.f;
+#pragma unroll
+            for (int j = 0; j < kProj; ++j) p = __fadd_rn(p, __fmul_rn(__half2float(code[j]), __half2float(w[j])));
+            p = __fadd_rn(p, __half2float(a.obias[cb][c]));
+            r[c] -= p;
+        }
+        __syncthreads();
+    }
+    float ss = 0.f;
+    for (int i = tid; i < kHid; i += kVqThreads) ss += r[i] * r[i];
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kVqThreads / 32; ++w) tot += red[w];
+        l2[t] = sqrtf(tot);
     }
 }
 
@@ -493,6 +614,12 @@ struct CodecLayer {
     const __half *wqkv, *wo, *w1, *w3, *w2;
     const float *an, *fn, *ga, *gf;
 };
+struct CodecEncBlock {
+    CodecUnit unit[3];
+    const float *alpha, *down_b;
+    const __half *down_w;  // [Co][K C], K = 2 x stride: read as 2 taps of stride x C channels
+    int stride;
+};
 struct CodecUpStage {
     const __half *wt, *pw1, *pw2;  // wt [2 x 1024][1024]
     const float *bt, *dw, *dwb, *lnw, *lnb, *pw1b, *pw2b, *gamma;
@@ -516,6 +643,24 @@ struct S2dCodec {
     s2d::CodecBlock block[s2d::kBlocks]{};
     const float *tail_alpha = nullptr, *out_w = nullptr;
     float out_b = 0.f;
+    // the reference-audio encoder (codec.rs:1056), when the file holds it
+    bool has_encoder = false;
+    const float *enc_entry_w = nullptr, *enc_entry_b = nullptr;  // [64][7], [64]
+    s2d::CodecEncBlock enc[s2d::kBlocks]{};
+    s2d::CodecLayer enc_layer[4]{};
+    const float *enc_norm = nullptr, *enc_tail_alpha = nullptr, *enc_out_b = nullptr;
+    const __half *enc_out_w = nullptr;  // [1024][3 x 1024]
+    s2d::CodecUpStage down[s2d::kUpStages]{};  // wt: the stride-2 conv as [1024][2 x 1024]
+    s2d::CodecLayer pre_layer[s2d::kLayers]{};
+    const float *pre_norm = nullptr;
+    s2d::VqArgs vq{};
+    size_t enc_samples = 0;  // the encoder workspace's capacity in padded samples
+    uint8_t *enc_ws = nullptr;
+    size_t enc_ws_bytes = 0;
+    float *eaudio = nullptr, *ex = nullptr, *ez = nullptr, *ez2 = nullptr;
+    __half *eP = nullptr;
+    int32_t *ecodes = nullptr;
+    float *el2 = nullptr;
     // workspace, sized for `ws_frames` code frames
     uint32_t ws_frames = 0;
     uint8_t *ws = nullptr;
@@ -735,6 +880,80 @@ int32_t load(S2dCodec *c, const Gguf &g) {
         L.floats(w, &c->out_w);
     }
     if (const GgufTensor *ob = L.get("decoder.model.6.conv.bias", D{1})) c->out_b = h2f_host(L.src(ob)[0]);
+    // the reference-audio encoder and the quantizer's encode side (codec.rs:1519-1584,
+    // 546-680, 455-494, and in_proj of 2356-2413), loaded when the file has them
+    c->has_encoder = g.tensor("encoder.block.0.conv.weight") != nullptr;
+    if (c->has_encoder && L.err.empty()) {
+        L.f32(L.get("encoder.block.0.conv.weight", D{7, 1, 64}), &c->enc_entry_w);  // index tap + 7 c
+        L.f32(L.get("encoder.block.0.conv.bias", D{64}), &c->enc_entry_b);
+        constexpr int kEncRates[kBlocks] = {2, 4, 8, 8};
+        constexpr int kEncChan[kBlocks + 1] = {64, 128, 256, 512, 1024};
+        for (int b = 0; b < kBlocks; ++b) {
+            const std::string p = "encoder.block." + std::to_string(b + 1) + ".block";
+            const int C = kEncChan[b], Co = kEncChan[b + 1], st = kEncRates[b];
+            CodecEncBlock &k = c->enc[b];
+            k.stride = st;
+            for (int u = 0; u < 3; ++u) {
+                const std::string q = p + "." + std::to_string(u);
+                CodecUnit &n = k.unit[u];
+                n.k0 = 7, n.k1 = 1;
+                L.f32(L.get(q + ".block.0.alpha", D{1, (uint64_t)C, 1}), &n.a0);
+                L.conv(L.get(q + ".block.1.conv.weight", D{7, (uint64_t)C, (uint64_t)C}), 7, C, C, &n.w0);
+                L.f32(L.get(q + ".block.1.conv.bias", D{(uint64_t)C}), &n.b0);
+                L.f32(L.get(q + ".block.2.alpha", D{1, (uint64_t)C, 1}), &n.a1);
+                L.conv(L.get(q + ".block.3.conv.weight", D{1, (uint64_t)C, (uint64_t)C}), 1, C, C, &n.w1);
+                L.f32(L.get(q + ".block.3.conv.bias", D{(uint64_t)C}), &n.b1);
+            }
+            L.f32(L.get(p + ".3.alpha", D{1, (uint64_t)C, 1}), &k.alpha);
+            // kernel 2 x stride (codec.rs:40): [oc][tap C + ic] is also [oc][j (stride C) + r C + ic]
+            L.conv(L.get(p + ".4.conv.weight", D{(uint64_t)(2 * st), (uint64_t)C, (uint64_t)Co}), 2 * st, C, Co,
+                   &k.down_w);
+            L.f32(L.get(p + ".4.conv.bias", D{(uint64_t)Co}), &k.down_b);
+        }
+        auto layers = [&](const std::string &module, CodecLayer *out, int n) {
+            for (int l = 0; l < n; ++l) {
+                const std::string q = module + ".layers." + std::to_string(l);
+                CodecLayer &y = out[l];
+                L.f16(L.get(q + ".attention.wqkv.weight", D{H, 3 * H}), &y.wqkv);
+                L.f16(L.get(q + ".attention.wo.weight", D{H, H}), &y.wo);
+                L.f32(L.get(q + ".attention_norm.weight", D{H}), &y.an);
+                L.f32(L.get(q + ".ffn_norm.weight", D{H}), &y.fn);
+                L.f16(L.get(q + ".feed_forward.w1.weight", D{H, kFfn}), &y.w1);
+                L.f16(L.get(q + ".feed_forward.w3.weight", D{H, kFfn}), &y.w3);
+                L.f16(L.get(q + ".feed_forward.w2.weight", D{kFfn, H}), &y.w2);
+                L.f32(L.get(q + ".attention_layer_scale.gamma", D{H}), &y.ga);
+                L.f32(L.get(q + ".ffn_layer_scale.gamma", D{H}), &y.gf);
+            }
+        };
+        layers("encoder.block.4.block.5", c->enc_layer, 4);
+        L.f32(L.get("encoder.block.4.block.5.norm.weight", D{H}), &c->enc_norm);
+        L.f32(L.get("encoder.block.5.alpha", D{1, H, 1}), &c->enc_tail_alpha);
+        L.conv(L.get("encoder.block.6.conv.weight", D{3, H, H}), 3, kHid, kHid, &c->enc_out_w);
+        L.f32(L.get("encoder.block.6.conv.bias", D{H}), &c->enc_out_b);
+        for (int st = 0; st < kUpStages; ++st) {
+            const std::string p = "quantizer.downsample." + std::to_string(st);
+            CodecUpStage &u = c->down[st];
+            L.conv(L.get(p + ".0.conv.weight", D{2, H, H}), 2, kHid, kHid, &u.wt);
+            L.f32(L.get(p + ".0.conv.bias", D{H}), &u.bt);
+            L.f32(L.get(p + ".1.gamma", D{H}), &u.gamma);
+            L.f32(L.get(p + ".1.dwconv.conv.weight", D{kDw, 1, H}), &u.dw);
+            L.f32(L.get(p + ".1.dwconv.conv.bias", D{H}), &u.dwb);
+            L.f32(L.get(p + ".1.norm.weight", D{H}), &u.lnw);
+            L.f32(L.get(p + ".1.norm.bias", D{H}), &u.lnb);
+            L.f16(L.get(p + ".1.pwconv1.weight", D{H, kExp}), &u.pw1);
+            L.f32(L.get(p + ".1.pwconv1.bias", D{kExp}), &u.pw1b);
+            L.f16(L.get(p + ".1.pwconv2.weight", D{kExp, H}), &u.pw2);
+            L.f32(L.get(p + ".1.pwconv2.bias", D{H}), &u.pw2b);
+        }
+        layers("quantizer.pre_module", c->pre_layer, kLayers);
+        L.f32(L.get("quantizer.pre_module.norm.weight", D{H}), &c->pre_norm);
+        for (int cb = 0; cb < kBooks; ++cb) {
+            const std::string p = cb == 0 ? "quantizer.semantic_quantizer.quantizers.0"
+                                          : "quantizer.quantizer.quantizers." + std::to_string(cb - 1);
+            L.f16(L.get(p + ".in_proj.weight", D{1, H, kProj}), &c->vq.in_w[cb]);  // [8][1024]
+            L.f16(L.get(p + ".in_proj.bias", D{kProj}), &c->vq.in_b[cb]);
+        }
+    }
     if (!L.err.empty()) return cerr(c, S2D_EINVAL, "codec weights: " + L.err);
 
     CCK(cudaMalloc(&c->arena, L.host.size()));
@@ -779,11 +998,11 @@ int32_t ensure_ws(S2dCodec *c, uint32_t frames) {
         {(void **)&c->lat, T * kHid * 4},
         {(void **)&c->x, xf * 4},
         {(void **)&c->x2, xf * 4},
-        {(void **)&c->qkv, T * 3 * kHid * 4},
+        {(void **)&c->qkv, L * 3 * kHid * 4},
         {(void **)&c->att, L * kHid * 4},
         {(void **)&c->act, L * kExp * 4},
         {(void **)&c->Y2, yf * 4},
-        {(void **)&c->Y2b, 2 * T * (size_t)kFfn * 4},
+        {(void **)&c->Y2b, 2 * L * (size_t)kFfn * 4},
         {(void **)&c->inv, std::max(2 * rows, (size_t)L) * 4},
         {(void **)&c->Z, zf * 4},
         {(void **)&c->xs, xsf * 2},
@@ -842,15 +1061,21 @@ int32_t epilogue(S2dCodec *c, int epi, const float *Y2, const float *Y2b, int T,
     return S2D_OK;
 }
 
-// forward_codec_post_module (codec.rs:986) on x [T][1024], in place; the final
-// RMSNorm lands in `out`.
-int32_t post_module(S2dCodec *c, float *x, int T, float *out) {
+// n codec transformer layers (codec.rs:3229, attention window `window`) on
+// x [T][1024], in place; the module's final RMSNorm lands in `out`
+// (forward_codec_post_module, codec.rs:986; the pre module, codec.rs:1038;
+// the encoder's last block, codec.rs:1836).
+int32_t transformer(S2dCodec *c, const CodecLayer *layers, int n, int window, float *x, int T, const float *norm,
+                    float *out) {
     int32_t rc;
-    for (int l = 0; l < kLayers; ++l) {
-        const CodecLayer &y = c->layer[l];
+    for (int l = 0; l < n; ++l) {
+        const CodecLayer &y = layers[l];
         if ((rc = split_gemm(c, x, T, kHid, y.an, y.wqkv, 3 * kHid, c->Y2))) return rc;
         qkv_rope_kernel<<<T, 256, 0, c->stream>>>(c->Y2, c->inv, T, c->rope_freq, c->qkv);
-        window_attn_kernel<<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
+        if (window == 512)
+            window_attn_kernel<512><<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
+        else
+            window_attn_kernel<kWin><<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
         CCK(cudaGetLastError());
         if ((rc = split_gemm(c, c->att, T, kHid, nullptr, y.wo, kHid, c->Y2))) return rc;
         if ((rc = epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T, kHid, nullptr, 1, y.ga, x, x))) return rc;
@@ -862,8 +1087,24 @@ int32_t post_module(S2dCodec *c, float *x, int T, float *out) {
         if ((rc = epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T, kHid, nullptr, 1, y.gf, x, x))) return rc;
     }
     // the final RMSNorm: split_rows writes the normalised rows to `out`
-    CCK(launch_split_rows(x, kHid, T, kHid, c->post_norm, kNormEps, c->xs, c->inv, out, c->stream));
+    CCK(launch_split_rows(x, kHid, T, kHid, norm, kNormEps, c->xs, c->inv, out, c->stream));
     return S2D_OK;
+}
+
+int32_t post_module(S2dCodec *c, float *x, int T, float *out) {
+    return transformer(c, c->layer, kLayers, kWin, x, T, c->post_norm, out);
+}
+
+// The ConvNeXt block of an upsample or downsample stage (codec.rs:3438,
+// 3392) on y [T][1024], in place.
+int32_t convnext(S2dCodec *c, const CodecUpStage &u, float *y, int T) {
+    int32_t rc;
+    dwconv_ln_kernel<<<T, 256, 0, c->stream>>>(y, T, u.dw, u.dwb, u.lnw, u.lnb, c->att);
+    CCK(cudaGetLastError());
+    if ((rc = split_gemm(c, c->att, T, kHid, nullptr, u.pw1, kExp, c->Y2))) return rc;
+    if ((rc = epilogue(c, CE_GELU, c->Y2, nullptr, T, kExp, u.pw1b, kExp, nullptr, nullptr, c->act))) return rc;
+    if ((rc = split_gemm(c, c->act, T, kExp, nullptr, u.pw2, kHid, c->Y2))) return rc;
+    return epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T, kHid, u.pw2b, kHid, u.gamma, y, y);
 }
 
 // One upsample stage (codec.rs:3338): x [T][1024] -> y [2T][1024].
@@ -874,30 +1115,27 @@ int32_t upsample_stage(S2dCodec *c, const CodecUpStage &u, const float *x, int T
     // columns [k 1024, (k + 1) 1024), so [T][2048] is already [2T][1024]
     if ((rc = split_gemm(c, x, T, kHid, nullptr, u.wt, kUp * kHid, c->Y2))) return rc;
     if ((rc = epilogue(c, CE_STORE, c->Y2, nullptr, T, kUp * kHid, u.bt, kHid, nullptr, nullptr, y))) return rc;
-    // ConvNeXt block (codec.rs:3438)
-    dwconv_ln_kernel<<<T2, 256, 0, c->stream>>>(y, T2, u.dw, u.dwb, u.lnw, u.lnb, c->att);
-    CCK(cudaGetLastError());
-    if ((rc = split_gemm(c, c->att, T2, kHid, nullptr, u.pw1, kExp, c->Y2))) return rc;
-    if ((rc = epilogue(c, CE_GELU, c->Y2, nullptr, T2, kExp, u.pw1b, kExp, nullptr, nullptr, c->act))) return rc;
-    if ((rc = split_gemm(c, c->act, T2, kExp, nullptr, u.pw2, kHid, c->Y2))) return rc;
-    return epilogue(c, CE_SCALE_RESID, c->Y2, nullptr, T2, kHid, u.pw2b, kHid, u.gamma, y, y);
+    return convnext(c, u, y, T2);
 }
 
 // The GEMM of a stride-1 causal convolution (codec.rs:2212) whose padded f16
 // input P ([(K - 1) d + T][C]) is in place, into Z [T][N]: the implicit-GEMM
 // tcgen05 kernel, or (S2D_CODEC_TC=0) im2col + cuBLAS.  W is [N][K Cp].
-int32_t conv_gemm(S2dCodec *c, int T, int C, const __half *W, int K, int d, int N, float *Z) {
+int32_t conv_gemm(S2dCodec *c, int T, int C, const __half *W, int K, int d, int N, float *Z,
+                  const __half *P = nullptr) {
     const int Cp = (C + 63) / 64 * 64;
+    if (!P) P = c->P;
     if (c->conv_tc) {
         CodecConv cv;
-        cv.P = c->P, cv.W = W, cv.T = T, cv.C = C, cv.N = N, cv.taps = K, cv.d = d, cv.cpb = Cp / 64, cv.Z = Z;
+        cv.P = P, cv.W = W, cv.T = T, cv.C = C, cv.N = N, cv.taps = K, cv.d = d, cv.cpb = Cp / 64, cv.Z = Z;
         cv.error = c->error + 1, cv.one_cta = c->conv_one_cta;
         CCK(launch_codec_conv(cv, c->stream));
         return S2D_OK;
     }
-    const __half *A = c->P;
+    const __half *A = P;
     if (K > 1 || Cp != C) {
-        im2col_kernel<<<grid_for((size_t)T * K * Cp / 8), 256, 0, c->stream>>>(c->P, T, C, Cp, K, d, c->A);
+        if (P != c->P) return cerr(c, S2D_EINVAL, "the im2col route covers the decoder only");
+        im2col_kernel<<<grid_for((size_t)T * K * Cp / 8), 256, 0, c->stream>>>(P, T, C, Cp, K, d, c->A);
         CCK(cudaGetLastError());
         A = c->A;
     }
@@ -905,8 +1143,10 @@ int32_t conv_gemm(S2dCodec *c, int T, int C, const __half *W, int K, int d, int 
 }
 
 // P = the padded f16 input of a convolution: f16(snake(x + bias)).
-int32_t pad_input(S2dCodec *c, const float *x, int T, int C, int pad, const float *bias, const float *alpha) {
-    pad_f16_kernel<<<grid_for((size_t)(T + pad) * C / 4), 256, 0, c->stream>>>(x, T, C, pad, bias, alpha, c->P);
+int32_t pad_input(S2dCodec *c, const float *x, int T, int C, int pad, const float *bias, const float *alpha,
+                  __half *P = nullptr) {
+    pad_f16_kernel<<<grid_for((size_t)(T + pad) * C / 4), 256, 0, c->stream>>>(x, T, C, pad, bias, alpha,
+                                                                                P ? P : c->P);
     CCK(cudaGetLastError());
     return S2D_OK;
 }
@@ -959,7 +1199,7 @@ int32_t decoder(S2dCodec *c, const float *hidden, int L, float *samples) {
                 const CodecUnit &nx = k.unit[u + 1];
                 const int pad = (nx.k0 - 1) * (u == 0 ? 3 : 9);
                 resid_pad_kernel<<<grid_for(((size_t)out + pad) * C / 4), 256, 0, c->stream>>>(x, c->x2, n.b1, out, C,
-                                                                                              nx.a0, pad, c->P);
+                                                                                              nx.a0, pad, c->P, false);
                 CCK(cudaGetLastError());
             } else if (b + 1 < kBlocks) {
                 if ((rc = snake_split(c, x, c->x2, n.b1, nullptr, c->block[b + 1].alpha, out, C))) return rc;
@@ -971,6 +1211,136 @@ int32_t decoder(S2dCodec *c, const float *hidden, int L, float *samples) {
         }
         rows = out;
     }
+    return S2D_OK;
+}
+
+// ---- reference-audio encoder (codec.rs:1056) --------------------------------
+
+constexpr int kEncChan[kBlocks + 1] = {64, 128, 256, 512, 1024};
+constexpr int kFrameLength = 2048;  // codec.rs:46
+
+int32_t ensure_enc_ws(S2dCodec *c, size_t S) {
+    if (S <= c->enc_samples) return S2D_OK;
+    const size_t frames = S / kFrameLength;
+    struct Part {
+        void **p;
+        size_t bytes;
+    } parts[] = {
+        {(void **)&c->eaudio, S * 4},
+        {(void **)&c->ex, S * 64 * 4},
+        {(void **)&c->ez, S * 64 * 4},
+        {(void **)&c->ez2, S * 64 * 4},
+        {(void **)&c->eP, (S * 64 + 64 * 1024) * 2},
+        {(void **)&c->ecodes, frames * kBooks * 4},
+        {(void **)&c->el2, frames * 4},
+    };
+    size_t total = 0;
+    for (auto &p : parts) total += (p.bytes + 255) & ~(size_t)255;
+    if (c->enc_ws) cudaFree(c->enc_ws);
+    c->enc_ws = nullptr, c->enc_samples = 0, c->enc_ws_bytes = 0;
+    CCK(cudaMalloc(&c->enc_ws, total));
+    size_t off = 0;
+    for (auto &p : parts) {
+        *p.p = c->enc_ws + off;
+        off += (p.bytes + 255) & ~(size_t)255;
+    }
+    c->enc_samples = S, c->enc_ws_bytes = total;
+    return S2D_OK;
+}
+
+int32_t resid_pad(S2dCodec *c, float *x, const float *Z, const float *bias, int T, int C, const float *alpha, int pad,
+                  __half *P, bool assign) {
+    resid_pad_kernel<<<grid_for(((size_t)T + pad) * C / 4), 256, 0, c->stream>>>(x, Z, bias, T, C, alpha, pad, P,
+                                                                                  assign);
+    CCK(cudaGetLastError());
+    return S2D_OK;
+}
+
+// forward_codec_encoder_frontend (codec.rs:1104) on c->eaudio [S] (S a
+// multiple of 2,048, zero padded): the output conv's rows without their bias
+// (c->enc_out_b) in c->ez [S / 512][1024].
+int32_t encoder_frontend(S2dCodec *c, int S) {
+    int32_t rc;
+    enc_entry_kernel<<<grid_for((size_t)S * 64), 256, 0, c->stream>>>(c->eaudio, S, c->enc_entry_w, c->enc_entry_b,
+                                                                      c->ex);
+    CCK(cudaGetLastError());
+    if ((rc = pad_input(c, c->ex, S, 64, 6, nullptr, c->enc[0].unit[0].a0, c->eP))) return rc;
+    int rows = S;
+    for (int b = 0; b < kBlocks; ++b) {
+        const CodecEncBlock &k = c->enc[b];
+        const int C = kEncChan[b], Co = kEncChan[b + 1], st = k.stride;
+        // residual units, dilations 1, 3, 9 (codec.rs:1749-1790); the last
+        // one's residual add writes the down conv's input: snake, then
+        // `stride` zero rows of left padding (kernel 2 x stride - stride)
+        for (int u = 0; u < 3; ++u) {
+            const CodecUnit &n = k.unit[u];
+            const int d = u == 0 ? 1 : u == 1 ? 3 : 9;
+            if ((rc = conv_gemm(c, rows, C, n.w0, n.k0, d, C, c->ez, c->eP))) return rc;
+            if ((rc = pad_input(c, c->ez, rows, C, n.k1 - 1, n.b0, n.a1, c->eP))) return rc;
+            if ((rc = conv_gemm(c, rows, C, n.w1, n.k1, 1, C, c->ez2, c->eP))) return rc;
+            if (u < 2) {
+                const CodecUnit &nx = k.unit[u + 1];
+                rc = resid_pad(c, c->ex, c->ez2, n.b1, rows, C, nx.a0, (nx.k0 - 1) * (u == 0 ? 3 : 9), c->eP, false);
+            } else {
+                rc = resid_pad(c, c->ex, c->ez2, n.b1, rows, C, k.alpha, st, c->eP, false);
+            }
+            if (rc) return rc;
+        }
+        // the strided down conv (codec.rs:1808-1820): rows of `stride` x C
+        // channels, two taps
+        if ((rc = conv_gemm(c, rows / st, st * C, k.down_w, 2, 1, Co, c->ez, c->eP))) return rc;
+        rows /= st;
+        if (b + 1 < kBlocks)
+            rc = resid_pad(c, c->ex, c->ez, k.down_b, rows, Co, c->enc[b + 1].unit[0].a0, 6, c->eP, true);
+        else
+            rc = resid_pad(c, c->ex, c->ez, k.down_b, rows, Co, nullptr, 0, nullptr, true);
+        if (rc) return rc;
+    }
+    // the last block's 4 transformer layers (window 512) and norm, the tail
+    // snake and the output conv (kernel 3)
+    if ((rc = transformer(c, c->enc_layer, 4, 512, c->ex, rows, c->enc_norm, c->ez2))) return rc;
+    if ((rc = pad_input(c, c->ez2, rows, kHid, 2, nullptr, c->enc_tail_alpha, c->eP))) return rc;
+    return conv_gemm(c, rows, kHid, c->enc_out_w, 3, 1, kHid, c->ez, c->eP);
+}
+
+// forward_codec_quantizer_encode_stage (codec.rs:1020): h [L][1024] (+ hb)
+// -> two downsample stages (stride-2 conv + ConvNeXt) -> pre module -> out
+// [L / 4][1024].  L a multiple of 4.
+int32_t quantizer_encode(S2dCodec *c, const float *h, const float *hb, int L, float *out) {
+    int32_t rc;
+    const float *in = h, *in_b = hb;
+    float *y[2] = {c->x, c->x2};
+    int rows = L;
+    for (int st = 0; st < kUpStages; ++st) {
+        // kernel 2 = stride 2, no padding: one tap over rows of 2 x 1024
+        if ((rc = pad_input(c, in, rows, kHid, 0, in_b, nullptr, c->eP))) return rc;
+        if ((rc = conv_gemm(c, rows / 2, 2 * kHid, c->down[st].wt, 1, 1, kHid, c->ez, c->eP))) return rc;
+        rows /= 2;
+        if ((rc = resid_pad(c, y[st], c->ez, c->down[st].bt, rows, kHid, nullptr, 0, nullptr, true))) return rc;
+        if ((rc = convnext(c, c->down[st], y[st], rows))) return rc;
+        in = y[st], in_b = nullptr;
+    }
+    return transformer(c, c->pre_layer, kLayers, kWin, y[1], rows, c->pre_norm, out);
+}
+
+int32_t check_encoder(S2dCodec *c) {
+    if (!c || !c->arena) return cerr(c, S2D_ESTATE, "codec is not loaded");
+    if (!c->has_encoder) return cerr(c, S2D_EINVAL, "the codec file holds no reference-audio encoder");
+    if (!c->conv_tc) return cerr(c, S2D_EINVAL, "the reference-audio encoder runs on the tcgen05 convolutions only");
+    return S2D_OK;
+}
+
+// Zero-padded copy of the audio into the encoder workspace; S = padded samples.
+int32_t load_audio(S2dCodec *c, const float *audio, size_t n, size_t *S) {
+    if (!audio && n) return cerr(c, S2D_EINVAL, "audio is null");
+    if (n > 0xffffffffull) return cerr(c, S2D_EINVAL, "encoder input sample count overflows u32");
+    const size_t padded = n == 0 ? kFrameLength : (n + kFrameLength - 1) / kFrameLength * kFrameLength;  // codec.rs:1926
+    int32_t rc;
+    if ((rc = ensure_enc_ws(c, padded))) return rc;
+    if ((rc = ensure_ws(c, (uint32_t)(padded / kFrameLength)))) return rc;
+    CCK(cudaMemsetAsync(c->eaudio, 0, padded * 4, c->stream));
+    if (n) CCK(cudaMemcpyAsync(c->eaudio, audio, n * 4, cudaMemcpyHostToDevice, c->stream));
+    *S = padded;
     return S2D_OK;
 }
 
@@ -1053,6 +1423,7 @@ void s2d_codec_close(S2dCodec *c) {
     if (!c) return;
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->ws) cudaFree(c->ws);
+    if (c->enc_ws) cudaFree(c->enc_ws);
     if (c->arena) cudaFree(c->arena);
     if (c->blas) cublasDestroy(c->blas);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -1153,8 +1524,89 @@ int32_t s2d_codec_decoder(S2dCodec *c, const float *hidden, uint32_t n_frames, u
 int32_t s2d_codec_memory(const S2dCodec *c, size_t *weight_bytes, size_t *workspace_bytes) {
     if (!c) return S2D_EINVAL;
     if (weight_bytes) *weight_bytes = c->arena_bytes;
-    if (workspace_bytes) *workspace_bytes = c->ws_bytes;
+    if (workspace_bytes) *workspace_bytes = c->ws_bytes + c->enc_ws_bytes;
     return S2D_OK;
+}
+
+int32_t s2d_codec_has_encoder(const S2dCodec *c) { return c && c->has_encoder ? 1 : 0; }
+
+int32_t s2d_codec_encode_reference_audio(S2dCodec *c, const float *audio, size_t n_samples, int32_t *codes,
+                                         size_t capacity, uint32_t *quantizer_frames, uint32_t *encoder_frames,
+                                         uint32_t *padded_samples, float *final_residual_l2) {
+    int32_t rc;
+    if ((rc = check_encoder(c))) return rc;
+    const size_t need = (n_samples == 0 ? 1 : (n_samples + kFrameLength - 1) / kFrameLength) * kBooks;
+    if (!codes || capacity < need)
+        return cerr(c, S2D_EINVAL, "codes buffer holds " + std::to_string(capacity) + " codes, the audio needs " +
+                                       std::to_string(need));
+    size_t S = 0;
+    if ((rc = load_audio(c, audio, n_samples, &S))) return rc;
+    if ((rc = encoder_frontend(c, (int)S))) return rc;
+    const int L = (int)(S / 512), T = L / 4;
+    if ((rc = quantizer_encode(c, c->ez, c->enc_out_b, L, c->lat))) return rc;
+    vq_kernel<<<T, kVqThreads, 0, c->stream>>>(c->vq, c->rvq, c->lat, T, c->ecodes, c->el2);
+    CCK(cudaGetLastError());
+    CCK(cudaMemcpyAsync(codes, c->ecodes, (size_t)T * kBooks * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (final_residual_l2)
+        CCK(cudaMemcpyAsync(final_residual_l2, c->el2, (size_t)T * 4, cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = sync_and_check(c))) return rc;
+    if (quantizer_frames) *quantizer_frames = (uint32_t)T;
+    if (encoder_frames) *encoder_frames = (uint32_t)L;
+    if (padded_samples) *padded_samples = (uint32_t)S;
+    return S2D_OK;
+}
+
+int32_t s2d_codec_encoder_frontend(S2dCodec *c, const float *audio, size_t n_samples, float *hidden, size_t capacity,
+                                   uint32_t *frames, uint32_t *padded_samples) {
+    int32_t rc;
+    if ((rc = check_encoder(c))) return rc;
+    const size_t S_need = n_samples == 0 ? kFrameLength : (n_samples + kFrameLength - 1) / kFrameLength * kFrameLength;
+    if (!hidden || capacity < S_need / 512 * kHid)
+        return cerr(c, S2D_EINVAL, "hidden buffer too small: the audio needs " + std::to_string(S_need / 512 * kHid));
+    size_t S = 0;
+    if ((rc = load_audio(c, audio, n_samples, &S))) return rc;
+    if ((rc = encoder_frontend(c, (int)S))) return rc;
+    const int L = (int)(S / 512);
+    // the output conv's bias
+    if ((rc = resid_pad(c, c->ez2, c->ez, c->enc_out_b, L, kHid, nullptr, 0, nullptr, true))) return rc;
+    CCK(cudaMemcpyAsync(hidden, c->ez2, (size_t)L * kHid * 4, cudaMemcpyDeviceToHost, c->stream));
+    if ((rc = sync_and_check(c))) return rc;
+    if (frames) *frames = (uint32_t)L;
+    if (padded_samples) *padded_samples = (uint32_t)S;
+    return S2D_OK;
+}
+
+int32_t s2d_codec_quantizer_encode(S2dCodec *c, const float *hidden, uint32_t n_frames, float *out) {
+    int32_t rc;
+    if ((rc = check_encoder(c))) return rc;
+    if (!hidden || !out) return cerr(c, S2D_EINVAL, "null buffer");
+    if (n_frames < 4 || n_frames % 4)
+        return cerr(c, S2D_EINVAL, "codec quantizer encode needs a multiple of 4 frames (two stride-2 downsample "
+                                   "stages), got " + std::to_string(n_frames));
+    const int L = (int)n_frames;
+    if ((rc = ensure_enc_ws(c, (size_t)L * 512))) return rc;
+    if ((rc = ensure_ws(c, n_frames / 4))) return rc;
+    CCK(cudaMemcpyAsync(c->ez2, hidden, (size_t)L * kHid * 4, cudaMemcpyHostToDevice, c->stream));
+    if ((rc = quantizer_encode(c, c->ez2, nullptr, L, c->lat))) return rc;
+    CCK(cudaMemcpyAsync(out, c->lat, (size_t)(L / 4) * kHid * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+int32_t s2d_codec_vq_encode(S2dCodec *c, const float *latents, uint32_t n_frames, int32_t *codes,
+                            float *final_residual_l2) {
+    int32_t rc;
+    if ((rc = check_encoder(c))) return rc;
+    if (!latents || !codes) return cerr(c, S2D_EINVAL, "null buffer");
+    if (n_frames == 0) return cerr(c, S2D_EINVAL, "no frames");
+    if ((rc = ensure_ws(c, n_frames))) return rc;
+    if ((rc = ensure_enc_ws(c, (size_t)n_frames * kFrameLength))) return rc;
+    CCK(cudaMemcpyAsync(c->lat, latents, (size_t)n_frames * kHid * 4, cudaMemcpyHostToDevice, c->stream));
+    vq_kernel<<<n_frames, kVqThreads, 0, c->stream>>>(c->vq, c->rvq, c->lat, (int)n_frames, c->ecodes, c->el2);
+    CCK(cudaGetLastError());
+    CCK(cudaMemcpyAsync(codes, c->ecodes, (size_t)n_frames * kBooks * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (final_residual_l2)
+        CCK(cudaMemcpyAsync(final_residual_l2, c->el2, (size_t)n_frames * 4, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
 }
 
 }  // extern "C"

@@ -11,7 +11,7 @@ namespace s2d {
 // (s2d_codec_conv.cu): Z [T][N] f32 = sum over taps k < taps and channels c < C
 // of P[t + k d][c] . W[n][k (64 cpb) + c], P the padded f16 input
 // [T + (taps - 1) d][C], W [N][taps 64 cpb] f16 with zero columns past C in
-// each tap.  N a multiple of 96, 192 or 256.
+// each tap.  N a multiple of 64 or 96.
 struct CodecConv {
     const __half *P = nullptr, *W = nullptr;
     int T = 0, C = 0, N = 0, taps = 1, d = 1, cpb = 1;

@@ -187,7 +187,9 @@ cudaError_t launch_nt(const CodecConv &cv, cudaStream_t s) {
 
 }  // namespace
 
-int codec_conv_tile(int N) { return N % 256 == 0 ? 256 : N % 192 == 0 ? 192 : N % 96 == 0 ? 96 : 0; }
+int codec_conv_tile(int N) {
+    return N % 256 == 0 ? 256 : N % 192 == 0 ? 192 : N % 128 == 0 ? 128 : N % 96 == 0 ? 96 : N % 64 == 0 ? 64 : 0;
+}
 
 bool codec_conv_supported(const CodecConv &cv) {
     auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -202,12 +204,16 @@ cudaError_t launch_codec_conv(const CodecConv &cv, cudaStream_t s) {
     if (cv.one_cta) switch (codec_conv_tile(cv.N)) {
         case 256: return launch_nt<256, 1>(cv, s);
         case 192: return launch_nt<192, 1>(cv, s);
-        default: return launch_nt<96, 1>(cv, s);
+        case 128: return launch_nt<128, 1>(cv, s);
+        case 96: return launch_nt<96, 1>(cv, s);
+        default: return launch_nt<64, 1>(cv, s);
         }
     switch (codec_conv_tile(cv.N)) {
     case 256: return launch_nt<256, 2>(cv, s);
     case 192: return launch_nt<192, 2>(cv, s);
-    default: return launch_nt<96, 2>(cv, s);
+    case 128: return launch_nt<128, 2>(cv, s);
+    case 96: return launch_nt<96, 2>(cv, s);
+    default: return launch_nt<64, 2>(cv, s);
     }
 }
 

@@ -1,4 +1,5 @@
-/* s2d_codec.h -- C ABI of the sm_100a codec decode: RVQ codes -> 44.1 kHz PCM.
+/* s2d_codec.h -- C ABI of the sm_100a codec: RVQ codes -> 44.1 kHz PCM, and
+ * reference audio -> prompt codes.
  *
  * The step after the Dual-AR token loop: the codebook-major codes that
  * s2d_generate_codes returns go through the codec's RVQ lookup, its 8-layer
@@ -65,9 +66,33 @@ int32_t s2d_codec_decode_latents(S2dCodec *c, const float *latents, uint32_t n_f
  * -> samples [512 n_frames]. */
 int32_t s2d_codec_decoder(S2dCodec *c, const float *hidden, uint32_t n_frames, uint32_t hidden_dim, float *samples);
 
-/* Device bytes held by the weights and by the workspace sized for the
- * largest decode so far. */
+/* Device bytes held by the weights and by the workspaces sized for the
+ * largest decode and encode so far. */
 int32_t s2d_codec_memory(const S2dCodec *c, size_t *weight_bytes, size_t *workspace_bytes);
+
+/* ---- reference-audio encoder: 44.1 kHz mono PCM -> prompt codes ----
+ * Present when the codec file holds the encoder, the quantizer's downsample
+ * stages and pre module (a full s2-pro codec GGUF does); 1 if so, else 0. */
+int32_t s2d_codec_has_encoder(const S2dCodec *c);
+
+/* encode_reference_audio (codec.rs:1056): audio [n_samples] -> codes
+ * [10][quantizer_frames] int32 (codebook-major, the layout decode_waveform
+ * takes), quantizer_frames = ceil(n_samples / 2048) (one for no samples).
+ * final_residual_l2 (optional) receives quantizer_frames floats. */
+int32_t s2d_codec_encode_reference_audio(S2dCodec *c, const float *audio, size_t n_samples, int32_t *codes,
+                                         size_t capacity, uint32_t *quantizer_frames, uint32_t *encoder_frames,
+                                         uint32_t *padded_samples, float *final_residual_l2);
+/* forward_codec_encoder_frontend (codec.rs:1087): audio -> hidden
+ * [frames = padded_samples / 512][1024]. */
+int32_t s2d_codec_encoder_frontend(S2dCodec *c, const float *audio, size_t n_samples, float *hidden, size_t capacity,
+                                   uint32_t *frames, uint32_t *padded_samples);
+/* forward_codec_quantizer_encode_stage (codec.rs:1020): hidden [n_frames][1024]
+ * -> [n_frames / 4][1024]; n_frames a multiple of 4. */
+int32_t s2d_codec_quantizer_encode(S2dCodec *c, const float *hidden, uint32_t n_frames, float *out);
+/* rvq_encode_latents_nearest (codec.rs:2598): latents [n_frames][1024] ->
+ * codes [10][n_frames], final_residual_l2 [n_frames] (optional). */
+int32_t s2d_codec_vq_encode(S2dCodec *c, const float *latents, uint32_t n_frames, int32_t *codes,
+                            float *final_residual_l2);
 
 #ifdef __cplusplus
 }

@@ -59,7 +59,8 @@ _GGUF_SCALAR = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7
 def read_gguf(path):
     """(metadata dict, {name: (ggml dims, flat f16 / f32 array)}) of a GGUF
     v3 file; tensors of other types are skipped."""
-    data = Path(path).read_bytes()
+    mm = np.memmap(path, dtype=np.uint8, mode="r")
+    data = bytes(mm[:min(mm.size, 4 << 20)])  # the header (tensor directory) lies in the first MiB
     off = 0
 
     def take(fmt):
@@ -106,14 +107,28 @@ def read_gguf(path):
     tensors = {}
     for name, dims, t, rel in infos:
         n = int(np.prod(dims))
+        o = start + rel
         if t == 1:
-            a = np.frombuffer(data, np.float16, n, start + rel)
+            a = mm[o:o + 2 * n].view(np.float16)
         elif t == 0:
-            a = np.frombuffer(data, np.float32, n, start + rel)
+            a = mm[o:o + 4 * n].view(np.float32)
         else:
             continue
         tensors[name] = (dims, a)
     return meta, tensors
+
+
+def f16_to_f32(a):
+    """IEEE half -> float by bit manipulation (numpy's own f16 cast is slow
+    for hundreds of millions of values); exact for every f16 value."""
+    h = np.asarray(a).view(np.uint16).astype(np.uint32)
+    sign = (h & 0x8000) << 16
+    e = (h >> 10) & 0x1F
+    m = h & 0x3FF
+    normal = (sign | ((e + 112) << 23) | (m << 13)).view(np.float32)
+    special = (sign | 0x7F800000 | (m << 13)).view(np.float32)
+    sub = (m.astype(np.float32) * np.float32(2.0 ** -24)) * np.where(sign != 0, np.float32(-1), np.float32(1))
+    return np.where(e == 0, sub, np.where(e == 31, special, normal))
 
 
 class CodecWeights:
@@ -138,7 +153,7 @@ class CodecWeights:
         if dims is not None and list(d) != list(dims):
             raise CodecOracleError(f"{name}: expected {dims}, got {d}")
         if name not in self._f64:
-            self._f64[name] = a.astype(self.dtype)
+            self._f64[name] = (f16_to_f32(a) if a.dtype == np.float16 else np.asarray(a)).astype(self.dtype)
         return self._f64[name]
 
     def quantizer(self, cb):
@@ -212,15 +227,16 @@ def silu(x):
     return x / (1.0 + np.exp(-x))
 
 
-def transformer_layer(x, w: CodecWeights, layer, module="quantizer.post_module"):
-    """codec.rs:3229 forward_codec_transformer_layer_with_window, window 128."""
+def transformer_layer(x, w: CodecWeights, layer, module="quantizer.post_module", window=WINDOW):
+    """codec.rs:3229 forward_codec_transformer_layer_with_window (window 128
+    for the post and pre modules, 512 in the encoder)."""
     p = f"{module}.layers.{layer}"
     T = x.shape[0]
     h = rms_norm(x, w.get(f"{p}.attention_norm.weight", [HIDDEN]), NORM_EPS)
     qkv = h @ w.get(f"{p}.attention.wqkv.weight", [HIDDEN, 3 * HIDDEN]).reshape(3 * HIDDEN, HIDDEN).T
     q, k, v = qkv[:, :HIDDEN], qkv[:, HIDDEN:2 * HIDDEN], qkv[:, 2 * HIDDEN:]
     pos = np.arange(T)
-    att = windowed_attention(rope_normal(q, pos), rope_normal(k, pos), v)
+    att = windowed_attention(rope_normal(q, pos), rope_normal(k, pos), v, window)
     o = att @ w.get(f"{p}.attention.wo.weight", [HIDDEN, HIDDEN]).reshape(HIDDEN, HIDDEN).T
     x = x + o * w.get(f"{p}.attention_layer_scale.gamma", [HIDDEN])
     h = rms_norm(x, w.get(f"{p}.ffn_norm.weight", [HIDDEN]), NORM_EPS)
@@ -394,3 +410,138 @@ def pcm_to_wav(samples, sample_rate=SAMPLE_RATE):
     hdr = b"RIFF" + struct.pack("<I", 44 + 2 * n) + b"WAVEfmt " + struct.pack(
         "<IHHIIHH", 16, 1, 1, sample_rate, sample_rate * 2, 2, 16) + b"data" + struct.pack("<I", 2 * n)
     return hdr + pcm.tobytes()
+
+
+# ---- reference-audio encoder: PCM -> prompt codes (codec.rs:1056-1212, 1740-1940) ----
+
+ENCODER_RATES = (2, 4, 8, 8)
+ENCODER_CHANNELS = (64, 128, 256, 512, 1024)
+ENCODER_WINDOW = 512
+FRAME_LENGTH = 2048
+
+
+def causal_conv1d_strided(x, weight, dims, bias, stride):
+    """codec.rs:2212 causal_conv_1d_frame_major at dilation 1 and any stride:
+    left padding kernel - stride, the extra right padding of
+    extra_padding_for_conv1d (codec.rs:2191), the padded input rounded to f16."""
+    kernel, in_ch, out_ch = dims
+    W = weight.reshape(out_ch, in_ch, kernel)
+    F = x.shape[0]
+    pad = max(kernel - stride, 0)
+    n = np.ceil(np.float32(F - kernel + pad) / np.float32(stride) + np.float32(1.0))
+    ideal = max(int(n) - 1, 0) * stride + max(kernel - pad, 0)
+    extra = max(ideal - F, 0)
+    P = F + pad + extra
+    xp = round_f16(np.concatenate([np.zeros((pad, in_ch), x.dtype), x, np.zeros((extra, in_ch), x.dtype)]))
+    out = max(P - kernel, 0) // stride + 1
+    y = np.tile(bias, (out, 1))
+    for k in range(kernel):
+        src = xp[k:k + (out - 1) * stride + 1:stride]
+        y[:src.shape[0]] += src @ W[:, :, k].T
+    return y
+
+
+def pad_sample_count(n, frame_length=FRAME_LENGTH):
+    """codec.rs:1926: up to a multiple of the frame length (one frame for no samples)."""
+    return frame_length if n == 0 else (n + frame_length - 1) // frame_length * frame_length
+
+
+def encoder_block(x, w: CodecWeights, i):
+    """codec.rs:1740 forward_codec_encoder_block: residual units (dilations
+    1, 3, 9), snake, strided down conv, and for the last block 4 transformer
+    layers (window 512) + RMSNorm."""
+    p = f"encoder.block.{i}.block"
+    C, Co, s = ENCODER_CHANNELS[i - 1], ENCODER_CHANNELS[i], ENCODER_RATES[i - 1]
+    for u, d in zip((0, 1, 2), (1, 3, 9)):
+        x = residual_unit(x, w, f"{p}.{u}", C, d)
+    x = snake(x, w.get(f"{p}.3.alpha", [1, C, 1]))
+    k = w.t[f"{p}.4.conv.weight"][0][0] if f"{p}.4.conv.weight" in w.t else 2 * s
+    x = causal_conv1d_strided(x, w.get(f"{p}.4.conv.weight", [k, C, Co]), [k, C, Co], w.get(f"{p}.4.conv.bias", [Co]),
+                              s)
+    if i == len(ENCODER_RATES):
+        for layer in range(4):
+            x = transformer_layer(x, w, layer, module=f"{p}.5", window=ENCODER_WINDOW)
+        x = rms_norm(x, w.get(f"{p}.5.norm.weight", [HIDDEN]), NORM_EPS)
+    return x
+
+
+def forward_codec_encoder_frontend(audio, w: CodecWeights):
+    """codec.rs:1104: pad to a multiple of 2,048 samples, entry conv 1 -> 64
+    (kernel 7), 4 encoder blocks (/2, /4, /8, /8), snake, output conv
+    1024 -> 1024 (kernel 3).  Returns (hidden [frames][1024], padded samples)."""
+    audio = np.asarray(audio, np.float32).astype(w.dtype)
+    n = pad_sample_count(audio.size)
+    x = np.zeros((n, 1), w.dtype)
+    x[:audio.size, 0] = audio
+    x = causal_conv1d(x, w.get("encoder.block.0.conv.weight", [7, 1, 64]), [7, 1, 64],
+                      w.get("encoder.block.0.conv.bias", [64]))
+    for i in range(1, len(ENCODER_RATES) + 1):
+        x = encoder_block(x, w, i)
+    x = snake(x, w.get("encoder.block.5.alpha", [1, HIDDEN, 1]))
+    x = causal_conv1d(x, w.get("encoder.block.6.conv.weight", [3, HIDDEN, HIDDEN]), [3, HIDDEN, HIDDEN],
+                      w.get("encoder.block.6.conv.bias", [HIDDEN]))
+    return x, n
+
+
+def downsample_stage(x, w: CodecWeights, i):
+    """codec.rs:3360: conv (kernel 2, stride 2), then the ConvNeXt block of codec.rs:3392."""
+    p = f"quantizer.downsample.{i}"
+    H, E = HIDDEN, CONVNEXT_EXPANDED
+    if x.shape[0] < 2:
+        raise CodecOracleError("codec downsample requires at least 2 frames")
+    y = causal_conv1d_strided(x, w.get(f"{p}.0.conv.weight", [2, H, H]), [2, H, H], w.get(f"{p}.0.conv.bias", [H]),
+                              2)
+    if y.shape[0] != (x.shape[0] - 2) // 2 + 1:  # an odd frame count (codec.rs:3382, 3398)
+        raise CodecOracleError("codec downsample convnext input length mismatch")
+    h = depthwise_causal_conv1d(y, w.get(f"{p}.1.dwconv.conv.weight", [CONVNEXT_KERNEL, 1, H]),
+                                w.get(f"{p}.1.dwconv.conv.bias", [H]))
+    h = layer_norm(h, w.get(f"{p}.1.norm.weight", [H]), w.get(f"{p}.1.norm.bias", [H]), CONVNEXT_EPS)
+    h = gelu_erf(h @ w.get(f"{p}.1.pwconv1.weight", [H, E]).reshape(E, H).T + w.get(f"{p}.1.pwconv1.bias", [E]))
+    h = h @ w.get(f"{p}.1.pwconv2.weight", [E, H]).reshape(H, E).T + w.get(f"{p}.1.pwconv2.bias", [H])
+    return y + h * w.get(f"{p}.1.gamma", [H])
+
+
+def forward_codec_quantizer_encode_stage(x, w: CodecWeights):
+    """codec.rs:1020: two downsample stages (/4 frames), the 8-layer pre
+    module (window 128) and its RMSNorm."""
+    for i in range(UPSAMPLE_STAGES):
+        x = downsample_stage(x, w, i)
+    for layer in range(LAYERS):
+        x = transformer_layer(x, w, layer, module="quantizer.pre_module")
+    return rms_norm(x, w.get("quantizer.pre_module.norm.weight", [HIDDEN]), NORM_EPS)
+
+
+def rvq_encode_latents_nearest(lat, w: CodecWeights, margins=False):
+    """codec.rs:2598 + nearest_code_for_residual (2453-2505): per frame and
+    codebook in order, in_proj of the residual (+ bias), the codebook row of
+    the largest cosine similarity (first on ties), residual -= that code's
+    out_proj projection.  Returns (codes [10][frames], final residual L2
+    [frames]) and, with margins, each choice's score gap to the runner-up."""
+    F = lat.shape[0]
+    codes = np.zeros((1 + RESIDUAL_QUANTIZERS, F), np.int64)
+    gaps = np.zeros((1 + RESIDUAL_QUANTIZERS, F))
+    res = lat.astype(w.dtype).copy()
+    for cb in range(1 + RESIDUAL_QUANTIZERS):
+        book, wo, bo = w.quantizer(cb)
+        p = "quantizer.semantic_quantizer.quantizers.0" if cb == 0 else f"quantizer.quantizer.quantizers.{cb - 1}"
+        wi = w.get(f"{p}.in_proj.weight", [1, HIDDEN, PROJ]).reshape(PROJ, HIDDEN)
+        bi = w.get(f"{p}.in_proj.bias", [PROJ])
+        proj = res @ wi.T + bi
+        pn = np.sqrt(np.maximum((proj * proj).sum(axis=1, keepdims=True), 1e-12))
+        rn = np.sqrt(np.maximum((book * book).sum(axis=1), 1e-12))
+        score = (proj / pn) @ (book / rn[:, None]).T
+        best = np.argmax(score, axis=1)
+        codes[cb] = best
+        srt = np.sort(score, axis=1)
+        gaps[cb] = srt[:, -1] - srt[:, -2]
+        res = res - (book[best] @ wo.T + bo)
+    l2 = np.sqrt((res * res).sum(axis=1))
+    return (codes, l2, gaps) if margins else (codes, l2)
+
+
+def encode_reference_audio(audio, w: CodecWeights):
+    """codec.rs:1056: encoder frontend, quantizer encode stage, nearest-code RVQ."""
+    h, padded = forward_codec_encoder_frontend(audio, w)
+    q = forward_codec_quantizer_encode_stage(h, w)
+    codes, l2 = rvq_encode_latents_nearest(q, w)
+    return codes, l2, h.shape[0], q.shape[0], padded

@@ -160,7 +160,7 @@ def test_library_exports_the_codec_entry_points():
     build.build_runtime()
     lib = ctypes.CDLL(str(s2d.LIB_PATH))
     syms = _header_symbols()
-    assert len(syms) == 10
+    assert len(syms) == 15
     assert not [s for s in syms if not hasattr(lib, s)]
     assert sorted(codec.CODEC_SIGNATURES) == syms
 
@@ -189,3 +189,95 @@ def test_python_mirror_checks_lengths_before_the_library():
         c.rvq_decode_latents(np.zeros(100, np.float32), 1)
     with pytest.raises(S2dError, match="decoder input length mismatch"):
         c.forward_codec_decoder(np.zeros(100, np.float32), 1)
+
+
+# ---- reference-audio encoder ------------------------------------------------
+
+def fixture_pcm(n=2048):
+    """codec.rs:4194-4196 / 4264-4266: ((i % 97) - 48) / 4096."""
+    return ((np.arange(n) % 97).astype(np.float32) - 48.0) / 4096.0
+
+
+def _strided_conv_loop(x, weight, dims, bias, stride):
+    """causal_conv_1d_frame_major (codec.rs:2212-2293) as the reference loops it."""
+    kernel, in_ch, out_ch = dims
+    F = x.shape[0]
+    pad = kernel - stride
+    n = np.ceil(np.float32(F - kernel + pad) / np.float32(stride) + np.float32(1.0))
+    extra = max((max(int(n) - 1, 0)) * stride + (kernel - pad) - F, 0)
+    xp = np.zeros((F + pad + extra, in_ch))
+    xp[pad:pad + F] = x
+    xp = xp.astype(np.float32).astype(np.float16).astype(np.float64)
+    out = (xp.shape[0] - kernel) // stride + 1
+    y = np.zeros((out, out_ch))
+    for t in range(out):
+        for oc in range(out_ch):
+            s = bias[oc]
+            for tap in range(kernel):
+                src = t * stride + tap
+                if src >= xp.shape[0]:
+                    continue
+                for ic in range(in_ch):
+                    s += xp[src, ic] * weight[tap + kernel * (ic + in_ch * oc)]
+            y[t, oc] = s
+    return y
+
+
+@pytest.mark.parametrize("kernel,stride,F", [(4, 2, 12), (16, 8, 32), (2, 2, 10), (4, 2, 7)])
+def test_strided_conv_matches_reference_loop(kernel, stride, F):
+    rng = np.random.default_rng(kernel + stride + F)
+    cin, cout = 3, 4
+    x = rng.standard_normal((F, cin))
+    w = rng.standard_normal(kernel * cin * cout)
+    b = rng.standard_normal(cout)
+    got = co.causal_conv1d_strided(x, w, [kernel, cin, cout], b, stride)
+    np.testing.assert_allclose(got, _strided_conv_loop(x, w, [kernel, cin, cout], b, stride), rtol=1e-12, atol=1e-12)
+
+
+def test_fixture_pcm_through_the_oracle_encoder(codec_oracle_weights):
+    """codec.rs:4189-4218 and 4258-4276: 2,048 samples -> 4 encoder frames -> 1
+    quantizer frame of 10 in-range codes; codec.rs:4096-4122: 8 latent frames
+    of ((i % 97) - 48) / 512 -> 2 frames through the quantizer encode stage."""
+    w = codec_oracle_weights
+    h, padded = co.forward_codec_encoder_frontend(fixture_pcm(), w)
+    assert padded == 2048 and h.shape == (4, 1024) and np.isfinite(h).all() and (np.abs(h) > 0).any()
+    codes, l2, enc_frames, q_frames, padded = co.encode_reference_audio(fixture_pcm(), w)
+    assert (enc_frames, q_frames, padded) == (4, 1, 2048) and codes.shape == (10, 1)
+    assert 0 <= codes[0, 0] < 4096 and all(0 <= c < 1024 for c in codes[1:, 0]) and np.isfinite(l2).all()
+    lat = (((np.arange(8 * 1024) % 97) - 48.0) / 512.0).reshape(8, 1024)
+    q = co.forward_codec_quantizer_encode_stage(lat, w)
+    assert q.shape == (2, 1024) and np.isfinite(q).all() and (np.abs(q) > 0).any()
+    assert co.pad_sample_count(0) == 2048 and co.pad_sample_count(2049) == 4096
+
+
+def _wav(fmt, ch, rate, bits, data, extra_chunk=b""):
+    fmt_chunk = struct.pack("<HHIIHH", fmt, ch, rate, rate * ch * bits // 8, ch * bits // 8, bits)
+    body = b"WAVE" + extra_chunk + b"fmt " + struct.pack("<I", 16) + fmt_chunk + b"data" + \
+        struct.pack("<I", len(data)) + data + (b"\0" if len(data) % 2 else b"")
+    return b"RIFF" + struct.pack("<I", len(body)) + body
+
+
+def test_wav_reader_follows_the_reference():
+    """wav.rs:41-170: formats, odd-length chunks, channel averaging, errors."""
+    from fish_s2pro_b200 import S2dError, read_wav_mono_f32
+    from fish_s2pro_b200.codec import pcm_to_wav
+    s = np.array([0.0, 0.5, -0.25, 0.999], np.float32)
+    got = read_wav_mono_f32(pcm_to_wav(s))
+    assert np.array_equal(got, (s * 32767).astype(np.int16).astype(np.float32) / 32768)
+    assert np.array_equal(read_wav_mono_f32(_wav(1, 1, 44100, 8, bytes([0, 128, 255]))),
+                          np.array([-1.0, 0.0, 127 / 128], np.float32))
+    assert np.allclose(read_wav_mono_f32(_wav(1, 1, 44100, 24, bytes([0, 0, 0x80, 0xff, 0xff, 0x7f]))),
+                       [-1.0, 8388607 / 8388608])
+    assert np.array_equal(read_wav_mono_f32(_wav(3, 1, 44100, 32, np.array([0.25, -2.0], "<f4").tobytes())),
+                          np.array([0.25, -2.0], np.float32))
+    stereo = np.array([1000, 3000, -2000, 0], "<i2").tobytes()
+    assert np.allclose(read_wav_mono_f32(_wav(1, 2, 44100, 16, stereo, extra_chunk=b"LIST\x03\0\0\0abc\0")),
+                       [2000 / 32768, -1000 / 32768])
+    with pytest.raises(S2dError, match="expected 44100 Hz"):
+        read_wav_mono_f32(_wav(1, 1, 16000, 16, b"\0\0"))
+    with pytest.raises(S2dError, match="unsupported WAV format"):
+        read_wav_mono_f32(_wav(1, 1, 44100, 12, b"\0\0"))
+    with pytest.raises(S2dError, match="no samples"):
+        read_wav_mono_f32(_wav(1, 1, 44100, 16, b""))
+    with pytest.raises(S2dError, match="not a RIFF"):
+        read_wav_mono_f32(b"RIFX0000WAVE")

@@ -183,3 +183,107 @@ def test_errors_match_the_reference(codec):
     assert codec_lib().s2d_codec_sync(codec.handle) == 0  # the flag is cleared
     # and the codec still decodes
     assert codec.decode_waveform(codes, 10, 2).num_samples == 4096
+
+
+# ---- reference-audio encoder (codec.rs:1056) ----------------------------------
+
+@pytest.fixture(scope="module")
+def w32(codec_gguf):
+    return co.CodecWeights(codec_gguf, np.float32)
+
+
+def pcm(n, seed):
+    rng = np.random.default_rng(seed)
+    t = np.arange(n)
+    return (0.3 * np.sin(t * 0.031) + 0.2 * np.sin(t * 0.0071 + 1.0) + 0.05 * rng.standard_normal(n)).astype(np.float32)
+
+
+@pytest.mark.parametrize("n", [2048, 5000])
+def test_encoder_frontend_matches_oracle(codec, codec_oracle_weights, w32, n):
+    """Entry conv, 4 blocks (residual units, strided down convs as two-tap
+    implicit GEMMs over rows of stride x C channels), the last block's
+    transformer (window 512), tail conv: within 3x (+1e-4) of the float32
+    oracle's distance from the float64 oracle, as for the decoder."""
+    from test_codec_oracle import fixture_pcm
+    audio = fixture_pcm(n) if n == 2048 else pcm(n, 1)
+    got = codec.forward_codec_encoder_frontend(audio)
+    frames = (n + 2047) // 2048 * 4
+    assert (got.input_samples, got.padded_samples, got.output_frames) == (n, frames * 512, frames)
+    want, padded = co.forward_codec_encoder_frontend(audio, codec_oracle_weights)
+    e32 = rel_err(co.forward_codec_encoder_frontend(audio, w32)[0], want)
+    egpu = rel_err(got.hidden.reshape(frames, 1024), want)
+    assert egpu < 3 * e32 + 1e-4 and egpu < PCM_TOL, (egpu, e32)
+
+
+@pytest.mark.parametrize("n", [8, 16])
+def test_quantizer_encode_stage_matches_oracle(codec, codec_oracle_weights, w32, n):
+    """Two stride-2 downsample stages (one-tap implicit GEMMs over rows of
+    2 x 1024) with their ConvNeXt blocks, and the 8-layer pre module; the
+    8-frame input is the reference fixture's (codec.rs:4107-4110)."""
+    if n == 8:
+        lat = (((np.arange(8 * 1024) % 97) - 48.0) / 512.0).reshape(8, 1024).astype(np.float32)
+    else:
+        lat = np.random.default_rng(n).standard_normal((n, 1024)).astype(np.float32)
+    got = codec.forward_codec_quantizer_encode_stage(lat, n)
+    assert (got.input_frames, got.output_frames) == (n, n // 4)
+    want = co.forward_codec_quantizer_encode_stage(lat.astype(np.float64), codec_oracle_weights)
+    e32 = rel_err(co.forward_codec_quantizer_encode_stage(lat, w32), want)
+    egpu = rel_err(got.hidden.reshape(n // 4, 1024), want)
+    assert egpu < 3 * e32 + 1e-5 and egpu < 1e-3, (egpu, e32)
+
+
+def test_vq_encode_matches_oracle(codec, codec_oracle_weights):
+    """Nearest-code search: per frame the codes equal the oracle's in order;
+    a codebook may differ only where the oracle's best two cosine scores are
+    within 1e-4 (a near tie), after which the frame's later codebooks follow
+    a different residual and are not compared."""
+    n = 24
+    lat = co.forward_codec_quantizer_encode_stage(
+        np.random.default_rng(5).standard_normal((4 * n, 1024)), codec_oracle_weights)
+    got = codec.rvq_encode_latents_nearest(lat.astype(np.float32), n)
+    want, l2, gaps = co.rvq_encode_latents_nearest(lat.astype(np.float32).astype(np.float64), codec_oracle_weights,
+                                                   margins=True)
+    gc = got.codes.reshape(10, n)
+    exact = 0
+    for f in range(n):
+        same = True
+        for cb in range(10):
+            if gc[cb, f] != want[cb, f]:
+                assert gaps[cb, f] < 1e-4, (f, cb, gaps[cb, f])
+                same = False
+                break
+        if same:
+            exact += 1
+            assert abs(got.final_residual_l2[f] - l2[f]) <= 1e-5 * l2[f]
+    assert exact >= n - 2
+
+
+def test_encode_reference_audio_chains_the_stages(codec, tmp_path):
+    """The one-call encode equals its three stages run one by one, its codes
+    are in range, decode back to 2,048 samples a frame, and the WAV entry
+    reads the file as the reference does."""
+    from fish_s2pro_b200.codec import pcm_to_wav
+    audio = pcm(4500, 3)
+    r = codec.encode_reference_audio(audio)
+    assert (r.input_samples, r.padded_samples, r.encoder_frames, r.quantizer_frames) == (4500, 6144, 12, 3)
+    fe = codec.forward_codec_encoder_frontend(audio)
+    q = codec.forward_codec_quantizer_encode_stage(fe.hidden, fe.output_frames)
+    v = codec.rvq_encode_latents_nearest(q.hidden, q.output_frames)
+    assert np.array_equal(r.codes, v.codes) and np.array_equal(r.final_residual_l2, v.final_residual_l2)
+    codes = r.codes.reshape(10, 3)
+    assert (0 <= codes[0]).all() and (codes[0] < 4096).all() and (0 <= codes[1:]).all() and (codes[1:] < 1024).all()
+    assert codec.decode_waveform(r.codes, 10, 3).num_samples == 3 * 2048
+    wav = tmp_path / "ref.wav"
+    wav.write_bytes(pcm_to_wav(audio))
+    from fish_s2pro_b200 import read_wav_mono_f32
+    assert np.array_equal(codec.encode_reference_wav_file(wav).codes,
+                          codec.encode_reference_audio(read_wav_mono_f32(wav)).codes)
+
+
+def test_encoder_edge_cases(codec):
+    from fish_s2pro_b200 import S2dError
+    assert codec.has_encoder
+    r = codec.encode_reference_audio(np.zeros(0, np.float32))  # no samples: one padded frame
+    assert (r.padded_samples, r.quantizer_frames) == (2048, 1) and r.codes.size == 10
+    with pytest.raises(S2dError, match="multiple of 4"):
+        codec.forward_codec_quantizer_encode_stage(np.zeros(6 * 1024, np.float32), 6)
