@@ -578,6 +578,31 @@ def run_codec(args, d: Dist, frames=512, steps=None, warmup=None):
                    "parallelism": f"replicas x{d.world}"},
         "clocks": ck,
     }
+    # the reference-audio encoder (PCM -> prompt codes), end to end through
+    # encode_reference_audio: 10 s of audio in, codes out
+    if c.has_encoder:
+        n_audio = 441000
+        audio = (0.3 * np.sin(np.arange(n_audio) * 0.031) +
+                 0.05 * np.random.default_rng(7 + d.rank).standard_normal(n_audio)).astype(np.float32)
+        for _ in range(2):
+            r = c.encode_reference_audio(audio)
+        d.barrier()
+        t0 = time.perf_counter()
+        enc_steps = 5
+        for _ in range(enc_steps):
+            r = c.encode_reference_audio(audio)
+        t1 = time.perf_counter()
+        d.barrier()
+        enc_s = d.max((t1 - t0) / enc_steps)
+        line["encode"] = {
+            "metric": "encode_samples_per_s", "value": round(d.sum(n_audio) / enc_s), "unit": "samples/s",
+            "ms_per_call": round(enc_s * 1e3, 3), "realtime_factor": round(d.sum(n_audio) / enc_s / 44100.0, 1),
+            "steps": enc_steps,
+            "config": {"workload": f"encode_reference_audio of {n_audio} samples (10 s) -> {r.quantizer_frames} "
+                                   "frames x 10 codes, host PCM in and host codes out (wall clock, synchronised)"},
+            "e2e": {"value": round(d.sum(n_audio) / enc_s), "unit": "samples/s", "h2d_bytes_per_step": int(audio.nbytes),
+                    "d2h_bytes_per_step": int(r.codes.nbytes + r.final_residual_l2.nbytes)},
+        }
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         # the float64 numpy oracle on one code frame, all host threads (BLAS)
         from oracle import codec_oracle as co
@@ -592,6 +617,15 @@ def run_codec(args, d: Dist, frames=512, steps=None, warmup=None):
         line["cpu_baseline"] = {"value": round(2048 / dt, 1), "unit": "samples/s", "cores": os.cpu_count(),
                                 "kind": "port", "sample": "one code frame (2,048 samples) through the float64 "
                                                           "numpy codec oracle, twice"}
+        if "encode" in line:
+            clip = np.asarray(audio[:4096])
+            co.encode_reference_audio(clip, w64)  # converts the encoder weights once
+            t0 = time.perf_counter()
+            co.encode_reference_audio(clip, w64)
+            dt = time.perf_counter() - t0
+            line["encode"]["cpu_baseline"] = {
+                "value": round(4096 / dt, 1), "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": "4,096 samples (2 code frames) through the float64 numpy encoder oracle, once"}
     c.close()
     return line
 
