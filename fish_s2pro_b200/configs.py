@@ -111,6 +111,16 @@ def tiny(seed: int = 0, linear_type: int = GGML_F16) -> ModelConfig:
                        linear_type=linear_type, seed=seed)
 
 
+def tiny_codec(seed: int = 0) -> ModelConfig:
+    """A tiny Dual-AR whose codes the s2-pro codec decodes: 2 Slow-AR layers
+    (d 512), 4096 text + 4096 semantic ids, 1 Fast-AR layer, 10 codebooks x
+    1024 (the codec's residual codebook size).  For end-to-end pipeline tests."""
+    return ModelConfig(name="tinycodec", slow_layers=2, d=512, heads=8, kv_heads=2, head_dim=64,
+                       ffn=1536, vocab=8192, sem_begin=4096, sem_end=8191, fast_layers=1,
+                       fast_heads=4, fast_kv_heads=2, fast_head_dim=64, fast_ffn=768,
+                       num_codebooks=10, codebook_size=1024, context_length=4096, seed=seed)
+
+
 def s2pro(seed: int = 1, linear_type: int = GGML_F16, slow_layers: int = 36,
           fast_layers: int = 4) -> ModelConfig:
     """C2..C5 shapes: 36 Slow-AR layers, d 2560, 32/8 heads x 128, FFN 9728,

@@ -42,3 +42,32 @@ def codec_gguf(model_dir):
 def codec_oracle_weights(codec_gguf):
     from oracle import codec_oracle
     return codec_oracle.CodecWeights(codec_gguf)
+
+
+def synthetic_tokenizer_json(path):
+    """A tokenizer.json of the reference's shape for the tests: the 256
+    byte-level symbols (ids 0..255 in byte order), a few merges, and the
+    special tokens build_prompt needs, all below the tiny models' 4096 text ids
+    (<|im_end|> = 4000, the tiny models' end id)."""
+    import json
+    from fish_s2pro_b200.text import bytes_to_unicode
+    table = bytes_to_unicode()
+    vocab = {table[b]: b for b in range(256)}
+    sp = chr(0x120)  # the byte-level space
+    merges = [("h", "e"), ("l", "l"), ("he", "ll"), (sp, "w"), ("o", "r"), (sp + "w", "or")]
+    for i, (a, b) in enumerate(merges):
+        vocab[a + b] = 256 + i
+    added = [{"id": 3000, "content": "<|im_start|>", "special": True},
+             {"id": 4000, "content": "<|im_end|>", "special": True},
+             {"id": 3001, "content": "<|voice|>", "special": True},
+             {"id": 3002, "content": "<|speaker:0|>", "special": True},
+             {"id": 3003, "content": "plain", "special": False}]
+    doc = {"added_tokens": added, "model": {"type": "BPE", "vocab": vocab,
+                                            "merges": [f"{a} {b}" for a, b in merges]}}
+    path.write_text(json.dumps(doc))
+    return path
+
+
+@pytest.fixture(scope="session")
+def tokenizer_json(tmp_path_factory):
+    return synthetic_tokenizer_json(tmp_path_factory.mktemp("tok") / "tokenizer.json")
