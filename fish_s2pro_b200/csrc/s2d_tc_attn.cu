@@ -286,12 +286,24 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             tc_fence_before();
             mb_arrive(&sh.s_empty[b]);
             const int nvis = valid ? min(kTaTile, prow + 1 - j * kTaTile) : 0;  // positions < nvis visible
-            const bool full = nvis >= kTaTile;
+            // all of the warp's rows see the whole tile: no masks (the max is
+            // exact in any order, so four independent chains change nothing)
+            const bool fullw = __all_sync(0xffffffffu, nvis >= kTaTile);
             float mx = -INFINITY;
+            if (fullw) {
+                float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                if (full || i < nvis) mx = fmaxf(mx, s0[i]);
-                if (full || i + 32 < nvis) mx = fmaxf(mx, s1[i]);
+                for (int i = 0; i < 32; i += 2) {
+                    m4[0] = fmaxf(m4[0], s0[i]), m4[1] = fmaxf(m4[1], s0[i + 1]);
+                    m4[2] = fmaxf(m4[2], s1[i]), m4[3] = fmaxf(m4[3], s1[i + 1]);
+                }
+                mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    if (i < nvis) mx = fmaxf(mx, s0[i]);
+                    if (i + 32 < nvis) mx = fmaxf(mx, s1[i]);
+                }
             }
             mx *= qdown;
             // P buffer pb is free once P V of tile j - 2 is done; with j >= 1
@@ -331,24 +343,34 @@ __global__ void __launch_bounds__(kTaThreads, 1)
             lrow *= corr;
             mrow = mnew;
             // P = 2^(s - mrow) of this thread's 32 columns into P buffer pb
+            // (ch is warp-uniform: each half has its own code, no selects)
             const uint32_t p_hi = sbase + kOffP + (uint32_t)pb * 2 * kPMat;
-            float acc = 0.f;
+            auto write_p = [&](const float(&sv)[32], int c0) {
+                float a4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float x[8];
+                for (int c = 0; c < 4; ++c) {
+                    float x[8];
+                    if (fullw) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int i = 32 * ch + 8 * c + e;
-                    const float sv = ch ? s1[8 * c + e] : s0[8 * c + e];  // constant indices: no local array
-                    x[e] = full || i < nvis ? exp2f(fmaf(sv, qdown, -mrow)) : 0.f;
-                    acc += x[e];
+                        for (int e = 0; e < 8; ++e) x[e] = exp2f(fmaf(sv[8 * c + e], qdown, -mrow));
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            x[e] = c0 + 8 * c + e < nvis ? exp2f(fmaf(sv[8 * c + e], qdown, -mrow)) : 0.f;
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) a4[e & 3] += x[e];
+                    uint4 hi, lo;
+                    split8(x, hi, lo);
+                    st_shared16(p_hi + sw128(r, 4 * ch + c), hi);
+                    st_shared16(p_hi + kPMat + sw128(r, 4 * ch + c), lo);
                 }
-                uint4 hi, lo;
-                split8(x, hi, lo);
-                st_shared16(p_hi + sw128(r, 4 * ch + c), hi);
-                st_shared16(p_hi + kPMat + sw128(r, 4 * ch + c), lo);
-            }
-            lrow += acc;
+                lrow += (a4[0] + a4[1]) + (a4[2] + a4[3]);
+            };
+            if (ch)
+                write_p(s1, 32);
+            else
+                write_p(s0, 0);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             fence_proxy_async_smem();
