@@ -14,7 +14,9 @@
  * hidden frame-major [frames][1024] float; samples float in [-1, 1], 512 per
  * latent frame (2,048 per code frame).
  *
- * Status codes are the S2D_* codes of s2d.h.
+ * Status codes are the S2D_* codes of s2d.h.  A handle serves one call at a
+ * time (its workspace and stream are shared by every call); open one handle
+ * per thread to decode in parallel.
  */
 #ifndef S2D_CODEC_H
 #define S2D_CODEC_H
