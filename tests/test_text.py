@@ -96,3 +96,40 @@ def test_load_prompt_codes(tmp_path):
     p.write_text(json.dumps({"prompt_text": "hi", "num_codebooks": 2, "cols": 3, "codes": [1, 2]}))
     with pytest.raises(S2dError, match="length mismatch"):
         load_prompt_codes(p)
+
+
+def test_pipeline_load_reports_missing_files(tmp_path, tokenizer_json):
+    """pipeline.rs:258 require_file: each of the three files is checked
+    before anything is loaded (no GPU needed)."""
+    from fish_s2pro_b200 import Pipeline
+    lm, codec = tmp_path / "lm.gguf", tmp_path / "codec.gguf"
+    with pytest.raises(S2dError, match="transformer GGUF not found"):
+        Pipeline.load(lm, codec, tokenizer_json)
+    lm.write_bytes(b"GGUF")
+    with pytest.raises(S2dError, match="codec GGUF not found"):
+        Pipeline.load(lm, codec, tokenizer_json)
+    codec.write_bytes(b"GGUF")
+    with pytest.raises(S2dError, match="tokenizer not found"):
+        Pipeline.load(lm, codec, tmp_path / "tokenizer.json")
+
+
+def test_synthetic_codec_file_has_the_reference_shapes():
+    """The synthetic codec's tensor list: the names and ggml dims the
+    reference's loaders check (codec.rs:2386-2413, 860-910, 736-820,
+    1640-1679, 1519-1584), and kernel 2 x stride for every strided conv."""
+    from fish_s2pro_b200.codec_synth import _tensors
+    t = {name: dims for name, dims, _, _ in _tensors()}
+    assert t["quantizer.semantic_quantizer.quantizers.0.codebook.weight"] == [8, 4096]
+    assert t["quantizer.quantizer.quantizers.8.codebook.weight"] == [8, 1024]
+    assert t["quantizer.post_module.layers.7.attention.wqkv.weight"] == [1024, 3072]
+    assert t["quantizer.upsample.1.0.conv.weight"] == [2, 1024, 1024]
+    assert t["decoder.model.0.conv.weight"] == [7, 1024, 1536]
+    assert t["decoder.model.6.conv.weight"] == [7, 96, 1] and t["decoder.model.5.alpha"] == [1, 96, 1]
+    for i, (r, c, ci) in enumerate(zip((8, 8, 4, 2), (768, 384, 192, 96), (1536, 768, 384, 192)), start=1):
+        assert t[f"decoder.model.{i}.block.1.conv.weight"] == [2 * r, c, ci]
+    assert t["encoder.block.0.conv.weight"] == [7, 1, 64] and t["encoder.block.6.conv.weight"] == [3, 1024, 1024]
+    for i, (k, c, co) in enumerate(zip((4, 8, 16, 16), (64, 128, 256, 512), (128, 256, 512, 1024)), start=1):
+        assert t[f"encoder.block.{i}.block.4.conv.weight"] == [k, c, co]
+    assert t["encoder.block.4.block.5.layers.3.feed_forward.w2.weight"] == [3072, 1024]
+    assert t["quantizer.downsample.0.0.conv.weight"] == [2, 1024, 1024]
+    assert sum(1 for n in t if n.startswith("decoder.")) == 89  # the reference registry's decoder count
