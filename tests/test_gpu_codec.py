@@ -287,3 +287,23 @@ def test_encoder_edge_cases(codec):
     assert (r.padded_samples, r.quantizer_frames) == (2048, 1) and r.codes.size == 10
     with pytest.raises(S2dError, match="multiple of 4"):
         codec.forward_codec_quantizer_encode_stage(np.zeros(6 * 1024, np.float32), 6)
+
+
+def test_decode_is_causal_at_full_size(codec):
+    """A size-independent property at the bench's scale: every stage is causal
+    (left-padded convolutions, windowed causal attention, transposed
+    convolutions that write forward), so the first k frames' samples of a
+    512-frame decode (multi-wave convolution grids, sliced GEMMs) equal the
+    decode of those k frames alone, which the oracle tests pin, up to the
+    f32-level spread of the f16-rounded stack."""
+    codes = random_codes(512, 77).reshape(10, 512)
+    full = codec.decode_waveform(codes.reshape(-1), 10, 512).samples
+    for k in (3, 40):
+        head = codec.decode_waveform(np.ascontiguousarray(codes[:, :k]).reshape(-1), 10, k).samples
+        assert rel_err(full[:k * 2048], head.astype(np.float64)) < PCM_TOL, k
+    # and the rows past the first k do depend on the later codes
+    other = codes.copy()
+    other[:, 40:] = random_codes(472, 78).reshape(10, 472)
+    alt = codec.decode_waveform(other.reshape(-1), 10, 512).samples
+    assert rel_err(alt[:40 * 2048], full[:40 * 2048].astype(np.float64)) < PCM_TOL
+    assert np.max(np.abs(alt[41 * 2048:] - full[41 * 2048:])) > 1e-2
