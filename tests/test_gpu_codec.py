@@ -307,3 +307,15 @@ def test_decode_is_causal_at_full_size(codec):
     alt = codec.decode_waveform(other.reshape(-1), 10, 512).samples
     assert rel_err(alt[:40 * 2048], full[:40 * 2048].astype(np.float64)) < PCM_TOL
     assert np.max(np.abs(alt[41 * 2048:] - full[41 * 2048:])) > 1e-2
+
+
+def test_encode_is_causal_at_full_size(codec):
+    """The encoder is causal too, so the first frames' codes of a 10 s clip
+    (the bench's size) match the encode of the clip's first 4 frames of
+    samples; a code may differ only by a near tie of the nearest-code search
+    after f32-level differences, so at least 95% must agree."""
+    audio = pcm(441000, 9)
+    full = codec.encode_reference_audio(audio).codes.reshape(10, -1)
+    head = codec.encode_reference_audio(audio[:4 * 2048]).codes.reshape(10, 4)
+    assert full.shape == (10, 216)
+    assert np.mean(full[:, :4] == head) >= 0.95
