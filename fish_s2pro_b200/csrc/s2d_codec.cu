@@ -161,6 +161,75 @@ __global__ void __launch_bounds__(kWin) window_attn_kernel(const float *qkv, int
     if (tid < kHd) out[(size_t)t * kHid + h * kHd + tid] = part[0][tid] + part[1][tid];
 }
 
+// The same attention with the key / value rows shared by a tile of 32 query
+// frames: each chunk of 32 positions of the tile's window is staged in shared
+// memory once, and every warp runs an online softmax for 4 frames over it
+// (lane = position for the scores, lane = two head dims for P V).  The
+// per-frame kernel above re-reads up to WIN rows from L2 for every frame.
+constexpr int kWaFrames = 32, kWaChunk = 32;
+__global__ void __launch_bounds__(256) window_attn_tiled_kernel(const float *qkv, int T, int window, float *out) {
+    __shared__ float qs[kWaFrames][kHd], ks[kWaChunk][kHd + 1];
+    __shared__ __align__(8) float vs[kWaChunk][kHd];
+    constexpr int N = 3 * kHid;
+    const int t0 = blockIdx.x * kWaFrames, h = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < kWaFrames * kHd; i += blockDim.x) {
+        const int f = i / kHd, d = i % kHd, t = t0 + f;
+        qs[f][d] = t < T ? qkv[(size_t)t * N + h * kHd + d] : 0.f;
+    }
+    const int p_lo = max(0, t0 - window + 1), p_hi = min(T, t0 + kWaFrames) - 1;
+    float m[4], l[4], o[4][2];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) m[q] = -INFINITY, l[q] = 0.f, o[q][0] = 0.f, o[q][1] = 0.f;
+    for (int p0 = p_lo; p0 <= p_hi; p0 += kWaChunk) {
+        __syncthreads();  // the previous chunk (and the q rows) are in place / consumed
+        for (int i = threadIdx.x; i < kWaChunk * kHd; i += blockDim.x) {
+            const int j = i / kHd, d = i % kHd, p = p0 + j;
+            const bool in = p <= p_hi;
+            ks[j][d] = in ? qkv[(size_t)p * N + kHid + h * kHd + d] : 0.f;
+            vs[j][d] = in ? qkv[(size_t)p * N + 2 * kHid + h * kHd + d] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int f = warp * 4 + q, t = t0 + f, p = p0 + lane;
+            const bool vis = t < T && p <= t && p >= t - window + 1 && p <= p_hi;
+            float sc = -INFINITY;
+            if (vis) {
+                float acc = 0.f;
+#pragma unroll 16
+                for (int d = 0; d < kHd; ++d) acc += qs[f][d] * ks[lane][d];
+                sc = acc * 0.125f;  // 1 / sqrt(64)
+            }
+            float cm = sc;
+            for (int off = 16; off; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, off));
+            if (cm == -INFINITY) continue;  // nothing of this chunk is visible to frame t (warp-uniform)
+            const float mn = fmaxf(m[q], cm);
+            const float corr = m[q] == -INFINITY ? 0.f : expf(m[q] - mn);
+            const float e = vis ? expf(sc - mn) : 0.f;
+            float es = e;
+            for (int off = 16; off; off >>= 1) es += __shfl_xor_sync(0xffffffffu, es, off);
+            l[q] = l[q] * corr + es;
+            float a0 = o[q][0] * corr, a1 = o[q][1] * corr;
+#pragma unroll 8
+            for (int j = 0; j < kWaChunk; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, e, j);
+                const float2 v = *reinterpret_cast<const float2 *>(&vs[j][2 * lane]);
+                a0 += pj * v.x, a1 += pj * v.y;
+            }
+            o[q][0] = a0, o[q][1] = a1, m[q] = mn;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int t = t0 + warp * 4 + q;
+        if (t < T) {
+            float *dst = out + (size_t)t * kHid + h * kHd + 2 * lane;
+            dst[0] = o[q][0] / l[q];
+            dst[1] = o[q][1] / l[q];
+        }
+    }
+}
+
 enum CodecEpi { CE_STORE = 0, CE_GELU = 1, CE_SWIGLU = 2, CE_SCALE_RESID = 3 };
 
 // erf by Abramowitz & Stegun 7.1.26, the form codec.rs:3890 uses.
@@ -672,6 +741,7 @@ struct S2dCodec {
     float *samples = nullptr;
     bool conv_tc = true;  // causal convolutions on the implicit-GEMM tcgen05 kernel (S2D_CODEC_TC)
     bool conv_one_cta = false;  // ... one CTA per SM with a deeper ring (S2D_CODEC_CONV_CTAS=1)
+    bool attn_tiled = true;     // windowed attention over 32-frame tiles (S2D_CODEC_ATTN_TILED=0: per frame)
 };
 
 namespace s2d {
@@ -1072,7 +1142,10 @@ int32_t transformer(S2dCodec *c, const CodecLayer *layers, int n, int window, fl
         const CodecLayer &y = layers[l];
         if ((rc = split_gemm(c, x, T, kHid, y.an, y.wqkv, 3 * kHid, c->Y2))) return rc;
         qkv_rope_kernel<<<T, 256, 0, c->stream>>>(c->Y2, c->inv, T, c->rope_freq, c->qkv);
-        if (window == 512)
+        if (c->attn_tiled)
+            window_attn_tiled_kernel<<<dim3((T + kWaFrames - 1) / kWaFrames, kHeads), 256, 0, c->stream>>>(
+                c->qkv, T, window, c->att);
+        else if (window == 512)
             window_attn_kernel<512><<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
         else
             window_attn_kernel<kWin><<<dim3(T, kHeads), kWin, 0, c->stream>>>(c->qkv, T, c->att);
@@ -1413,6 +1486,7 @@ int32_t s2d_codec_open(const char *gguf_path, int32_t device, S2dCodec **out) {
     } else {
         if (const char *v = getenv("S2D_CODEC_TC")) c->conv_tc = v[0] != '0';
         if (const char *v = getenv("S2D_CODEC_CONV_CTAS")) c->conv_one_cta = v[0] == '1';
+        if (const char *v = getenv("S2D_CODEC_ATTN_TILED")) c->attn_tiled = v[0] != '0';
         rc = load(c, g);
     }
     *out = c;  // also on failure, so that the caller can read the message

@@ -68,13 +68,26 @@ def test_rvq_lookup_is_bit_exact(codec, codec_oracle_weights, n, seed):
     assert np.array_equal(got.latents.reshape(n, 1024), rvq_f32(codes, n, codec_oracle_weights))
 
 
-@pytest.mark.parametrize("n", [1, 2, 5, 136])
+@pytest.mark.parametrize("n", [1, 2, 5, 33, 136])
 def test_decode_latents_matches_oracle(codec, codec_oracle_weights, n):
     """Post module (8 windowed-attention layers; 136 frames cross the
     128-frame window) and the two upsample stages."""
     lat = co.rvq_lookup_codes(random_codes(n, 10 + n), 10, n, codec_oracle_weights)
     got = codec.rvq_decode_latents(lat.astype(np.float32), n)
     assert (got.input_frames, got.output_frames, got.hidden_dim) == (n, 4 * n, 1024)
+    want = co.rvq_decode_latents(lat.astype(np.float32).astype(np.float64), codec_oracle_weights)
+    assert rel_err(got.hidden.reshape(4 * n, 1024), want) < LAT_TOL
+
+
+def test_per_frame_attention_route_matches_oracle(codec_gguf, codec_oracle_weights, monkeypatch):
+    """S2D_CODEC_ATTN_TILED=0: the windowed attention one block per frame and
+    head instead of over 32-frame tiles, across the 128-frame window."""
+    from fish_s2pro_b200 import CodecDecoder
+    monkeypatch.setenv("S2D_CODEC_ATTN_TILED", "0")
+    n = 136
+    lat = co.rvq_lookup_codes(random_codes(n, 10 + n), 10, n, codec_oracle_weights)
+    with CodecDecoder.open(codec_gguf) as c:
+        got = c.rvq_decode_latents(lat.astype(np.float32), n)
     want = co.rvq_decode_latents(lat.astype(np.float32).astype(np.float64), codec_oracle_weights)
     assert rel_err(got.hidden.reshape(4 * n, 1024), want) < LAT_TOL
 
